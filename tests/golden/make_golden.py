@@ -1,0 +1,242 @@
+"""Generate golden vectors from the reference's own CPU code path.
+
+Run in the build container, where the reference tree is importable:
+
+    python tests/golden/make_golden.py [/path/to/reference]
+
+It imports ``geoembodied`` read-only (PYTHONDONTWRITEBYTECODE) and records, for seeded
+inputs, what the reference's public entry points return on the CPU:
+
+* ``functional.fps.farthest_point_sampling`` (-> ``csrc._fps_iterative_fallback``)
+* ``functional.knn.knn`` (-> ``csrc._knn_bruteforce``)
+* ``functional.radius_graph.radius_graph`` (-> ``_radius_graph_single/_batched``)
+* ``functional.segment_reduce.sort_and_build_csr`` / ``segment_reduce`` (+ autograd)
+* ``torch.scatter_reduce(include_self=False)`` mean/amax (+ autograd), the semantics
+  the reference's callers use for segment mean/max.
+
+Inputs that would make the CPU path and the CUDA kernels disagree for reasons the
+reference itself documents (exact distance ties, pairs at the radius boundary where
+``cdist``'s matmul rounding differs, radius truncation by near-tied distances) are
+rejected and re-drawn, so each fixture pins the restated algorithm unambiguously.
+Large arrays are regenerated from their seed in the tests; the fixtures hold the
+outputs (and small inputs) only.
+"""
+
+from __future__ import annotations
+
+import hashlib
+import os
+import sys
+from pathlib import Path
+
+import numpy as np
+
+os.environ["PYTHONDONTWRITEBYTECODE"] = "1"
+sys.dont_write_bytecode = True
+
+HERE = Path(__file__).resolve().parent
+sys.path.insert(0, str(HERE.parent.parent))
+
+import torch  # noqa: E402
+
+from tests.golden import inputs  # noqa: E402
+
+
+def _ref(root: str):
+    sys.path.insert(0, root)
+    import importlib
+
+    mods = [importlib.import_module(f"geoembodied.functional.{m}") for m in ("fps", "knn", "radius_graph",
+                                                                           "segment_reduce")]
+    return tuple(mods)
+
+
+def sha(a: np.ndarray) -> str:
+    return hashlib.sha256(np.ascontiguousarray(a).tobytes()).hexdigest()
+
+
+def strictly_increasing_rows(d: np.ndarray, valid: np.ndarray) -> bool:
+    for r in range(d.shape[0]):
+        v = d[r][valid[r]]
+        if v.size > 1 and not np.all(np.diff(v.astype(np.float64)) > 0):
+            return False
+    return True
+
+
+def gen_fps(F, out):
+    # config 1: B=4 x N=2048 U[-1,1]^3 seed 0, FPS -> 512 (ptr path)
+    pos, ptr = inputs.config1_points()
+    idx = F.farthest_point_sampling(torch.from_numpy(pos), 512, ptr=torch.from_numpy(ptr))
+    out["fps_c1_idx"] = idx.numpy().astype(np.int32)
+    # variable-size clouds, k < n everywhere (k >= n takes an arange shortcut on the CPU
+    # path only, csrc/__init__.py:634-636)
+    g = torch.Generator().manual_seed(7)
+    sizes = [300, 257, 97, 1030]
+    posv = (torch.randn(sum(sizes), 3, generator=g) * 0.7).numpy().astype(np.float32)
+    ptrv = np.concatenate([[0], np.cumsum(sizes)]).astype(np.int64)
+    idxv = F.farthest_point_sampling(torch.from_numpy(posv), 64, ptr=torch.from_numpy(ptrv))
+    out["fps_var_pos"] = posv
+    out["fps_var_ptr"] = ptrv
+    out["fps_var_idx"] = idxv.numpy().astype(np.int32)
+    # single cloud path (functional/fps.py:121-162)
+    poss = posv[:300]
+    out["fps_single_idx"] = F.farthest_point_sampling(torch.from_numpy(poss), 50).numpy().astype(np.int32)
+
+
+def gen_knn(K, out, fps_idx):
+    pos, ptr = inputs.config1_points()
+    q = pos[fps_idx.astype(np.int64)]
+    ptr_q = np.arange(0, 4 * 512 + 1, 512, dtype=np.int64)
+    idx, d = K.knn(torch.from_numpy(q), torch.from_numpy(pos), torch.from_numpy(ptr_q), torch.from_numpy(ptr), 16)
+    idx, d = idx.numpy(), d.numpy()
+    assert strictly_increasing_rows(d, idx >= 0), "config-1 KNN has a distance tie; fixture would be ambiguous"
+    out["knn_c1_idx"] = idx.astype(np.int32)
+    out["knn_c1_dist"] = d
+    # variable sizes incl. a source cloud smaller than k, and an empty query cloud
+    for seed in range(100, 200):
+        g = torch.Generator().manual_seed(seed)
+        qs, ss = [40, 0, 25, 60], [500, 30, 9, 333]
+        qv = torch.rand(sum(qs), 3, generator=g).numpy().astype(np.float32)
+        sv = torch.rand(sum(ss), 3, generator=g).numpy().astype(np.float32)
+        pq = np.concatenate([[0], np.cumsum(qs)]).astype(np.int64)
+        ps = np.concatenate([[0], np.cumsum(ss)]).astype(np.int64)
+        ok = True
+        res = {}
+        for k in (1, 5, 16, 33, 70):
+            i2, d2 = K.knn(torch.from_numpy(qv), torch.from_numpy(sv), torch.from_numpy(pq), torch.from_numpy(ps), k)
+            i2, d2 = i2.numpy(), d2.numpy()
+            if not strictly_increasing_rows(d2, i2 >= 0):
+                ok = False
+                break
+            res[k] = (i2, d2)
+        if ok:
+            break
+    else:
+        raise RuntimeError("no tie-free KNN fixture found")
+    out["knn_var_q"] = qv
+    out["knn_var_s"] = sv
+    out["knn_var_ptr_q"] = pq
+    out["knn_var_ptr_s"] = ps
+    for k, (i2, d2) in res.items():
+        out[f"knn_var_k{k}_idx"] = i2.astype(np.int32)
+        out[f"knn_var_k{k}_dist"] = d2
+
+
+def _radius_safe(x: np.ndarray, B: int, r: float, K: int, mask=None) -> bool:
+    """No pair near the boundary; no truncation (in-radius degree <= K)."""
+    n = x.shape[0] // B
+    r2 = np.float64(np.float32(r)) ** 2
+    for b in range(B):
+        p = x[b * n:(b + 1) * n].astype(np.float64)
+        d = ((p[:, None, :] - p[None, :, :]) ** 2).sum(-1)
+        if np.any(np.abs(d - r2) < 1e-4 * r2):
+            return False
+        valid = np.ones(n, bool) if mask is None else mask[b * n:(b + 1) * n]
+        inr = (d < r2) & valid[None, :] & valid[:, None]
+        np.fill_diagonal(inr, False)
+        if inr.sum(0).max() > K - 1:
+            return False
+    return True
+
+
+def gen_radius(R, out):
+    # batched equal-size clouds (functional/radius_graph.py:70-85, :204-275)
+    for seed in range(300, 400):
+        g = torch.Generator().manual_seed(seed)
+        B, n, r, K = 4, 200, 0.22, 32
+        x = (torch.rand(B * n, 3, generator=g) * 2 - 1).numpy().astype(np.float32)
+        mask = (torch.rand(B * n, generator=g) > 0.1).numpy()
+        if _radius_safe(x, B, r, K) and _radius_safe(x, B, r, K, mask):
+            break
+    else:
+        raise RuntimeError("no radius fixture without boundary pairs found")
+    batch = torch.arange(B).repeat_interleave(n)
+    out["rad_x"] = x
+    out["rad_mask"] = mask
+    out["rad_meta"] = np.array([B, n, K], np.int64)
+    out["rad_r"] = np.array([r], np.float64)
+    for loop in (False, True):
+        for use_mask in (False, True):
+            row, col = R.radius_graph(torch.from_numpy(x), r, max_num_neighbors=K, batch=batch, loop=loop,
+                                      mask=torch.from_numpy(mask) if use_mask else None, num_batch_elements=B)
+            tag = f"rad_b_loop{int(loop)}_mask{int(use_mask)}"
+            out[tag + "_row"] = row.numpy().astype(np.int32)
+            out[tag + "_col"] = col.numpy().astype(np.int32)
+    # single cloud (functional/radius_graph.py:278-335)
+    xs = x[:n]
+    row, col = R.radius_graph(torch.from_numpy(xs), r, max_num_neighbors=K)
+    out["rad_single_row"] = row.numpy().astype(np.int32)
+    out["rad_single_col"] = col.numpy().astype(np.int32)
+    # known-answer tests of tests/test_phase1.py:258-299
+    kat = np.array([[0.0, 0.0, 0.0], [0.1, 0.0, 0.0], [10.0, 0.0, 0.0]], np.float32)
+    row, col = R.radius_graph(torch.from_numpy(kat), r=1.0)
+    out["rad_kat3_row"] = row.numpy().astype(np.int32)
+    out["rad_kat3_col"] = col.numpy().astype(np.int32)
+
+
+def gen_segment(S, out, knn_idx):
+    # config 1 edge CSR: dst = centroid (2048), 16 edges each, msg ~ N(0,1) [32768, 64]
+    col, msg = inputs.config1_segment_inputs()
+    cs, pm, ns, ne = S.sort_and_build_csr(torch.from_numpy(col), 2048)
+    m = torch.from_numpy(msg).requires_grad_(True)
+    o = S.segment_reduce(m, cs, pm, ns, ne, 2048)
+    gout = inputs.config1_grad_out()
+    o.backward(torch.from_numpy(gout))
+    out["seg_c1_sum_sha"] = np.frombuffer(sha(o.detach().numpy()).encode(), np.uint8)
+    out["seg_c1_sum_head"] = o.detach().numpy()[:64]
+    out["seg_c1_sum_grad_sha"] = np.frombuffer(sha(m.grad.numpy()).encode(), np.uint8)
+    mx = torch.from_numpy(msg).requires_grad_(True)
+    ref = torch.zeros(2048, 64).scatter_reduce(0, torch.from_numpy(col)[:, None].expand(-1, 64), mx, "amax",
+                                              include_self=False)
+    ref.backward(torch.from_numpy(gout))
+    out["seg_c1_max_sha"] = np.frombuffer(sha(ref.detach().numpy()).encode(), np.uint8)
+    out["seg_c1_max_head"] = ref.detach().numpy()[:64]
+    out["seg_c1_max_grad_sha"] = np.frombuffer(sha(mx.grad.numpy()).encode(), np.uint8)
+
+    # random CSR incl. empty nodes and ties (small, full fixture)
+    g = torch.Generator().manual_seed(42)
+    N, E, C = 500, 3000, 32
+    colr = torch.randint(0, N, (E,), generator=g)
+    msgr = torch.randn(E, C, generator=g)
+    msgr[5, :] = msgr[6, :]  # duplicate rows -> max ties if they share a node
+    colr[5] = colr[6]
+    cs, pm, ns, ne = S.sort_and_build_csr(colr, N)
+    out["seg_r_col"] = colr.numpy()
+    out["seg_r_msg"] = msgr.numpy()
+    out["seg_r_cs"] = cs.numpy()
+    out["seg_r_perm"] = pm.numpy()
+    out["seg_r_ns"] = ns.numpy()
+    out["seg_r_ne"] = ne.numpy()
+    gr = torch.randn(N, C, generator=g)
+    out["seg_r_gout"] = gr.numpy()
+    m = msgr.clone().requires_grad_(True)
+    o = S.segment_reduce(m, cs, pm, ns, ne, N)
+    o.backward(gr)
+    out["seg_r_sum"] = o.detach().numpy()
+    out["seg_r_sum_grad"] = m.grad.numpy()
+    for red, tname in (("mean", "mean"), ("max", "amax")):
+        for dt in (torch.float32, torch.bfloat16):
+            m = msgr.to(dt).clone().requires_grad_(True)
+            ref = torch.zeros(N, C, dtype=dt).scatter_reduce(0, colr[:, None].expand(-1, C), m, tname,
+                                                             include_self=False)
+            ref.backward(gr.to(dt))
+            tag = f"seg_r_{red}_{'f32' if dt == torch.float32 else 'bf16'}"
+            out[tag] = ref.detach().float().numpy()
+            out[tag + "_grad"] = m.grad.float().numpy()
+
+
+def main():
+    root = sys.argv[1] if len(sys.argv) > 1 else "/root/reference"
+    F, K, R, S = _ref(root)
+    torch.set_num_threads(os.cpu_count() or 1)
+    out = {}
+    gen_fps(F, out)
+    gen_knn(K, out, out["fps_c1_idx"])
+    gen_radius(R, out)
+    gen_segment(S, out, out["knn_c1_idx"])
+    np.savez_compressed(HERE / "golden_cpu.npz", **out)
+    print("wrote", HERE / "golden_cpu.npz", sum(v.nbytes for v in out.values()) / 1e6, "MB raw")
+
+
+if __name__ == "__main__":
+    main()
