@@ -1,0 +1,254 @@
+"""Operator entry points of the B200 build -- the drop-in for ``geoembodied.csrc``.
+
+Same names, arguments, dtypes and return values as the reference dispatcher
+(geoembodied/csrc/__init__.py:120-597); every call runs the sm_100a kernels of
+libgdl_b200.so on the current CUDA stream. Differences, all deliberate:
+
+* no CPU fallback and no JIT compile step: CPU tensors raise ``GdlError``; the library is
+  built once by ``python -m gdl_b200.build``;
+* ``fps_cuda`` takes ``tie_break`` ("reference" = bit-identical to the reference kernel,
+  "lowest_index" = torch.argmax order);
+* ``radius_graph_cuda`` returns the edges grouped by destination with ascending sources (the
+  reference's order is that of its atomic counter, i.e. arbitrary) and accepts clouds of any
+  sizes through ``radius_graph_csr``;
+* segment reduce also offers mean and max (``segment_reduce_cuda``).
+"""
+
+from __future__ import annotations
+
+from typing import Optional, Tuple
+
+import torch
+
+from .. import _native as nat
+
+__all__ = [
+    "get_radius_graph_backend", "radius_graph_cuda", "radius_graph_csr",
+    "segment_reduce_available", "sort_and_build_csr_cuda", "segment_reduce_sum_cuda", "segment_reduce_cuda",
+    "segment_reduce_backward_cuda", "knn_available", "knn_cuda", "knn_self_cuda", "fps_available", "fps_cuda",
+]
+
+
+def _available() -> bool:
+    try:
+        nat.load()
+    except Exception:
+        return False
+    return torch.cuda.is_available()
+
+
+def get_radius_graph_backend() -> str:
+    """'cuda' when the B200 library is usable (reference: csrc/__init__.py:120-127)."""
+    return "cuda" if _available() else "unavailable"
+
+
+def segment_reduce_available() -> bool:
+    return _available()
+
+
+def knn_available() -> bool:
+    return _available()
+
+
+def fps_available() -> bool:
+    return _available()
+
+
+# --------------------------------------------------------------------------- FPS
+def fps_cuda(pos: torch.Tensor, ptr: torch.Tensor, k_per_batch: torch.Tensor, *,
+             tie_break: str = "reference") -> torch.Tensor:
+    """Farthest point sampling per cloud (reference: csrc/__init__.py:566-597,
+    fps_kernel.cu:160-209). Returns int64 global indices, cloud b's picks at offset
+    sum_{c<b} k_c; a cloud with k > n yields n indices followed by -1.
+
+    One device->host copy of ``ptr``/``k_per_batch`` sizes the output (the reference
+    also synchronises once, fps_kernel.cu:183); pass CPU tensors to avoid it.
+    """
+    dev = nat.require_cuda(pos, what="fps_cuda")
+    pos = pos.contiguous().float()
+    host = torch.cat([ptr.reshape(-1).to(torch.int64), k_per_batch.reshape(-1).to(torch.int64)]).cpu()
+    B = ptr.numel() - 1
+    ptr_h, k_h = host[: B + 1], host[B + 1:]
+    total = int(k_h.clamp(min=0).sum()) if B > 0 else 0
+    if total <= 0 or pos.shape[0] == 0:
+        return torch.empty(0, dtype=torch.int64, device=dev)
+    max_n = int((ptr_h[1:] - ptr_h[:-1]).max())
+    ptr_d = ptr_h.to(dev, non_blocking=True) if not ptr.is_cuda else ptr.to(torch.int64).contiguous()
+    k_d = k_h.to(dev, non_blocking=True) if not k_per_batch.is_cuda else k_per_batch.to(torch.int64).contiguous()
+    out = torch.empty(total, dtype=torch.int64, device=dev)
+    L = nat.load()
+    ws = nat.workspace(L.gdl_fps_workspace_size(pos.shape[0], max_n), dev)
+    nat.check(L.gdl_fps(pos.data_ptr(), ptr_d.data_ptr(), k_d.data_ptr(), B, pos.shape[0], max_n,
+                        nat.TIE[tie_break], out.data_ptr(), ws.data_ptr(), ws.numel(), nat.stream(dev)), "gdl_fps")
+    return out
+
+
+# --------------------------------------------------------------------------- KNN
+def knn_cuda(query: torch.Tensor, source: torch.Tensor, ptr_q: torch.Tensor, ptr_s: torch.Tensor,
+             k: int) -> Tuple[torch.Tensor, torch.Tensor]:
+    """Batched brute-force KNN (reference: csrc/__init__.py:376-410, knn_kernel.cu:200-291).
+
+    Returns (indices [N_q, k] int64 global, -1 padded; dists [N_q, k] f32 squared, 1e30
+    padded), ordered exactly like the reference kernel (at most 64 real neighbours).
+    No host synchronisation.
+    """
+    dev = nat.require_cuda(query, source, what="knn_cuda")
+    query = query.contiguous().float()
+    source = source.contiguous().float()
+    ptr_q = ptr_q.to(device=dev, dtype=torch.int64).contiguous()
+    ptr_s = ptr_s.to(device=dev, dtype=torch.int64).contiguous()
+    K = int(k)
+    nq = query.shape[0]
+    if nq == 0 or K <= 0:
+        return (torch.empty(0, K, dtype=torch.int64, device=dev), torch.empty(0, K, dtype=torch.float32, device=dev))
+    B = ptr_q.numel() - 1
+    if ptr_s.numel() != ptr_q.numel():
+        raise nat.GdlError("knn_cuda: ptr_q and ptr_s must have the same length (B+1)")
+    idx = torch.empty(nq, K, dtype=torch.int64, device=dev)
+    dist = torch.empty(nq, K, dtype=torch.float32, device=dev)
+    L = nat.load()
+    max_src = source.shape[0]
+    ws = nat.workspace(L.gdl_knn_workspace_size(nq, B, K, max_src), dev)
+    nat.check(L.gdl_knn(query.data_ptr(), source.data_ptr() if source.numel() else None, ptr_q.data_ptr(),
+                        ptr_s.data_ptr(), B, nq, K, max_src, idx.data_ptr(), dist.data_ptr(), ws.data_ptr(),
+                        ws.numel(), nat.stream(dev)), "gdl_knn")
+    return idx, dist
+
+
+def knn_self_cuda(points: torch.Tensor, ptr: torch.Tensor, k: int) -> Tuple[torch.Tensor, torch.Tensor]:
+    """Self-KNN, self included (reference: csrc/__init__.py:413-432)."""
+    return knn_cuda(points, points, ptr, ptr, k)
+
+
+# --------------------------------------------------------------------------- radius graph
+def radius_graph_csr(x: torch.Tensor, r: float, ptr: torch.Tensor, *, max_num_neighbors: int = 32,
+                     loop: bool = False, mask: Optional[torch.Tensor] = None, with_dst: bool = True):
+    """Radius graph of packed clouds as a destination CSR, without a host sync.
+
+    Returns (row_ptr [N+1] int64, src [cap] int64, dst [cap] int64 or None); the first
+    row_ptr[N] entries of src/dst are the edges (row=src=neighbour, col=dst=query),
+    grouped by destination with ascending sources. cap = N * bucket(max_num_neighbors).
+    """
+    dev = nat.require_cuda(x, what="radius_graph")
+    x = x.contiguous().float()
+    N = x.shape[0]
+    ptr = ptr.to(device=dev, dtype=torch.int64).contiguous()
+    B = ptr.numel() - 1
+    cap_k = 16 if max_num_neighbors <= 16 else 32 if max_num_neighbors <= 32 else 64
+    row_ptr = torch.empty(N + 1, dtype=torch.int64, device=dev)
+    src = torch.empty(max(N * cap_k, 1), dtype=torch.int64, device=dev)
+    dst = torch.empty_like(src) if with_dst else None
+    m = None
+    if mask is not None and mask.numel() > 0:
+        m = mask.to(device=dev).contiguous()
+        m = m.view(torch.uint8) if m.dtype == torch.bool else m.to(torch.uint8)
+    L = nat.load()
+    ws = nat.workspace(L.gdl_radius_graph_workspace_size(N, B, int(max_num_neighbors)), dev)
+    nat.check(L.gdl_radius_graph(x.data_ptr() if N else None, ptr.data_ptr(), B, N, float(r), int(max_num_neighbors),
+                                 int(bool(loop)), nat.ptr(m), row_ptr.data_ptr(), src.data_ptr(), nat.ptr(dst),
+                                 ws.data_ptr(), ws.numel(), nat.stream(dev)), "gdl_radius_graph")
+    return row_ptr, src, dst
+
+
+def radius_graph_cuda(x: torch.Tensor, r: float, *, max_num_neighbors: int = 32, loop: bool = False,
+                      mask: Optional[torch.Tensor] = None, batch_size: Optional[int] = None,
+                      points_per_batch: Optional[int] = None) -> Tuple[torch.Tensor, torch.Tensor]:
+    """(row, col) int64 edges, global indices (reference: csrc/__init__.py:130-186,
+    radius_graph_kernel.cu:253-467). Equal-size batches via batch_size/points_per_batch
+    like the reference; one device->host read of the edge count."""
+    dev = nat.require_cuda(x, what="radius_graph_cuda")
+    N = x.shape[0]
+    if batch_size is not None and batch_size > 1:
+        assert points_per_batch is not None, "points_per_batch required when batch_size > 1"
+        ptr = torch.arange(0, batch_size + 1, dtype=torch.int64) * int(points_per_batch)
+    else:
+        ptr = torch.tensor([0, N], dtype=torch.int64)
+    row_ptr, src, dst = radius_graph_csr(x, r, ptr.to(dev), max_num_neighbors=max_num_neighbors, loop=loop, mask=mask)
+    E = int(row_ptr[N].item())
+    return src[:E], dst[:E]
+
+
+# --------------------------------------------------------------------------- segment reduce
+def sort_and_build_csr_cuda(col: torch.Tensor, N: int):
+    """Stable sort by destination + CSR offsets (reference: csrc/__init__.py:261-277,
+    segment_reduce_kernel.cu:100-169). Returns (col_sorted, perm, node_start, node_end) int32."""
+    dev = nat.require_cuda(col, what="sort_and_build_csr_cuda")
+    col = col.to(torch.int64).contiguous()
+    E = col.numel()
+    cs = torch.empty(E, dtype=torch.int32, device=dev)
+    pm = torch.empty(E, dtype=torch.int32, device=dev)
+    ns = torch.empty(N, dtype=torch.int32, device=dev)
+    ne = torch.empty(N, dtype=torch.int32, device=dev)
+    L = nat.load()
+    ws = nat.workspace(L.gdl_sort_and_build_csr_workspace_size(E, N), dev)
+    nat.check(L.gdl_sort_and_build_csr(col.data_ptr() if E else None, E, int(N), cs.data_ptr() if E else None,
+                                       pm.data_ptr() if E else None, ns.data_ptr() if N else None,
+                                       ne.data_ptr() if N else None, ws.data_ptr(), ws.numel(), nat.stream(dev)),
+              "gdl_sort_and_build_csr")
+    return cs, pm, ns, ne
+
+
+def segment_reduce_cuda(msg: torch.Tensor, perm: Optional[torch.Tensor], node_start: torch.Tensor,
+                        node_end: torch.Tensor, N: int, reduce: str = "sum", *, with_arg: bool = False):
+    """out [N, C] float32 = reduce over slots [node_start[n], node_end[n]) of msg[perm[slot]].
+
+    msg float32 or bfloat16 (fp32 accumulation). perm None = identity. For reduce="max"
+    and with_arg, also returns arg [N, C] int32 (slot of the unique maximum, -1 if tied).
+    """
+    dev = nat.require_cuda(msg, node_start, node_end, what="segment_reduce")
+    if msg.dtype not in nat.DTYPE:
+        msg = msg.float()
+    msg = msg.contiguous()
+    if msg.dim() == 1:
+        msg = msg.unsqueeze(1)
+    E, C = msg.shape
+    out = torch.empty(N, C, dtype=torch.float32, device=dev)
+    arg = torch.empty(N, C, dtype=torch.int32, device=dev) if (reduce == "max" and with_arg) else None
+    ns = node_start.to(torch.int32).contiguous()
+    ne = node_end.to(torch.int32).contiguous()
+    pm = None if perm is None else perm.to(torch.int32).contiguous()
+    L = nat.load()
+    ws = nat.workspace(L.gdl_segment_reduce_workspace_size(E, N), dev)
+    if N > 0 and C > 0:
+        nat.check(L.gdl_segment_reduce(msg.data_ptr() if E else None, nat.DTYPE[msg.dtype], E, C, nat.ptr(pm),
+                                       ns.data_ptr(), ne.data_ptr(), int(N), nat.REDUCE[reduce], out.data_ptr(),
+                                       nat.ptr(arg), ws.data_ptr(), ws.numel(), nat.stream(dev)),
+                  "gdl_segment_reduce")
+    return (out, arg) if with_arg else out
+
+
+def segment_reduce_sum_cuda(msg: torch.Tensor, perm: torch.Tensor, node_start: torch.Tensor,
+                            node_end: torch.Tensor, N: int) -> torch.Tensor:
+    """Deterministic segment sum (reference: csrc/__init__.py:280-302)."""
+    return segment_reduce_cuda(msg, perm, node_start, node_end, N, "sum")
+
+
+def segment_reduce_backward_cuda(grad_out: torch.Tensor, msg: torch.Tensor, out: Optional[torch.Tensor],
+                                 arg: Optional[torch.Tensor], perm: Optional[torch.Tensor], node_start: torch.Tensor,
+                                 node_end: torch.Tensor, N: int, reduce: str = "sum",
+                                 grad_msg: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """Gradient w.r.t. msg (msg's shape and dtype): grad_msg[perm[j]] for every slot j of every
+    segment (the reference's gather + un-permute, functional/segment_reduce.py:142-158).
+
+    Rows that no slot references are zero (or keep ``grad_msg``'s contents when it is given;
+    a CSR from sort_and_build_csr references every row exactly once).
+    """
+    dev = nat.require_cuda(grad_out, node_start, node_end, what="segment_reduce_backward")
+    E = msg.shape[0]
+    C = grad_out.shape[1] if grad_out.dim() == 2 else 1
+    if grad_msg is None:
+        grad_msg = torch.zeros(msg.shape, dtype=msg.dtype, device=dev)
+    if E == 0 or C == 0 or N == 0:
+        return grad_msg
+    go = grad_out.float().contiguous()
+    m = msg.contiguous()
+    pm = None if perm is None else perm.to(torch.int32).contiguous()
+    ns = node_start.to(torch.int32).contiguous()
+    ne = node_end.to(torch.int32).contiguous()
+    L = nat.load()
+    ws = nat.workspace(L.gdl_segment_reduce_workspace_size(E, N), dev)
+    nat.check(L.gdl_segment_reduce_backward(go.data_ptr(), m.data_ptr(), nat.DTYPE[msg.dtype], nat.ptr(out),
+                                            nat.ptr(arg), E, C, nat.ptr(pm), ns.data_ptr(), ne.data_ptr(), int(N),
+                                            nat.REDUCE[reduce], grad_msg.data_ptr(), ws.data_ptr(), ws.numel(),
+                                            nat.stream(dev)), "gdl_segment_reduce_backward")
+    return grad_msg

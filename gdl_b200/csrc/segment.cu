@@ -1,0 +1,645 @@
+// segment.cu -- CSR build and deterministic segment reduce (sum / mean / max, fwd + bwd).
+//
+// Reference: geoembodied/csrc/segment_reduce_kernel.cu (sort_and_build_csr :100-169,
+// segment_reduce_sum_kernel :66-93) and the autograd in
+// geoembodied/functional/segment_reduce.py:112-158, 211-279.
+//
+// Layout in HBM: msg [rows, C] row-major (f32 or bf16), out [N, C] f32, CSR as int32
+// node_start / node_end over "slots" (sorted positions), perm[slot] = msg row.
+//
+// Forward, short segments (<= kLongSegment slots): a group of G lanes owns one segment; each
+// lane owns VEC consecutive channels and folds the segment's rows in slot order, so a sum is
+// ((0 + m0) + m1) + ... exactly like the reference kernel (one thread per channel). Rows are
+// fetched with 8/16-byte vector loads, U slots in flight. Long segments are queued and
+// handled one CTA each: row groups fold contiguous slot ranges, partials combined in a fixed
+// order (deterministic, not the reference's rounding).
+// Backward: the same segment-to-group mapping; each group writes its segment's gradient rows
+// grad_msg[perm[j]] (what the reference's gather + un-permute computes, segment_reduce.py:
+// 142-158), VEC channels per lane. Max uses the forward's arg and re-reads msg only for
+// tied maxima, whose gradient is shared evenly (torch's amax rule).
+#include <initializer_list>
+
+#include "common.cuh"
+#include "radix.cuh"
+
+namespace gdl {
+
+constexpr int kLongSegment = 4096;
+constexpr int kSegThreads = 256;
+constexpr int kUnroll = 4;
+
+// ----------------------------------------------------------------- vector loads as f32
+template <typename T, int VEC>
+struct VecIO;
+
+template <>
+struct VecIO<float, 4> {
+    static __device__ __forceinline__ void load(const float *p, float *v) {
+        float4 t = __ldg(reinterpret_cast<const float4 *>(p));
+        v[0] = t.x; v[1] = t.y; v[2] = t.z; v[3] = t.w;
+    }
+    static __device__ __forceinline__ void store(float *p, const float *v) {
+        *reinterpret_cast<float4 *>(p) = make_float4(v[0], v[1], v[2], v[3]);
+    }
+};
+template <>
+struct VecIO<float, 2> {
+    static __device__ __forceinline__ void load(const float *p, float *v) {
+        float2 t = __ldg(reinterpret_cast<const float2 *>(p));
+        v[0] = t.x; v[1] = t.y;
+    }
+    static __device__ __forceinline__ void store(float *p, const float *v) {
+        *reinterpret_cast<float2 *>(p) = make_float2(v[0], v[1]);
+    }
+};
+template <>
+struct VecIO<float, 1> {
+    static __device__ __forceinline__ void load(const float *p, float *v) { v[0] = __ldg(p); }
+    static __device__ __forceinline__ void store(float *p, const float *v) { *p = v[0]; }
+};
+template <>
+struct VecIO<uint16_t, 8> {
+    static __device__ __forceinline__ void load(const uint16_t *p, float *v) {
+        uint4 t = __ldg(reinterpret_cast<const uint4 *>(p));
+        const uint32_t w[4] = {t.x, t.y, t.z, t.w};
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            v[2 * i] = __uint_as_float(w[i] << 16);
+            v[2 * i + 1] = __uint_as_float(w[i] & 0xffff0000u);
+        }
+    }
+    static __device__ __forceinline__ void store(uint16_t *p, const float *v) {
+        uint32_t w[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+            w[i] = (uint32_t)f32_to_bf16_bits(v[2 * i]) | ((uint32_t)f32_to_bf16_bits(v[2 * i + 1]) << 16);
+        *reinterpret_cast<uint4 *>(p) = make_uint4(w[0], w[1], w[2], w[3]);
+    }
+};
+template <>
+struct VecIO<uint16_t, 4> {
+    static __device__ __forceinline__ void load(const uint16_t *p, float *v) {
+        uint2 t = __ldg(reinterpret_cast<const uint2 *>(p));
+        v[0] = __uint_as_float(t.x << 16); v[1] = __uint_as_float(t.x & 0xffff0000u);
+        v[2] = __uint_as_float(t.y << 16); v[3] = __uint_as_float(t.y & 0xffff0000u);
+    }
+    static __device__ __forceinline__ void store(uint16_t *p, const float *v) {
+        uint2 t;
+        t.x = (uint32_t)f32_to_bf16_bits(v[0]) | ((uint32_t)f32_to_bf16_bits(v[1]) << 16);
+        t.y = (uint32_t)f32_to_bf16_bits(v[2]) | ((uint32_t)f32_to_bf16_bits(v[3]) << 16);
+        *reinterpret_cast<uint2 *>(p) = t;
+    }
+};
+template <>
+struct VecIO<uint16_t, 2> {
+    static __device__ __forceinline__ void load(const uint16_t *p, float *v) {
+        uint32_t t = __ldg(reinterpret_cast<const unsigned int *>(p));
+        v[0] = __uint_as_float(t << 16); v[1] = __uint_as_float(t & 0xffff0000u);
+    }
+    static __device__ __forceinline__ void store(uint16_t *p, const float *v) {
+        *reinterpret_cast<uint32_t *>(p) = (uint32_t)f32_to_bf16_bits(v[0]) | ((uint32_t)f32_to_bf16_bits(v[1]) << 16);
+    }
+};
+template <>
+struct VecIO<uint16_t, 1> {
+    static __device__ __forceinline__ void load(const uint16_t *p, float *v) { v[0] = bf16_bits_to_f32(__ldg(p)); }
+    static __device__ __forceinline__ void store(uint16_t *p, const float *v) { *p = f32_to_bf16_bits(v[0]); }
+};
+
+// ----------------------------------------------------------------- reduction state
+// max keeps (best, slot of first best, #values equal to best (saturating), NaN seen)
+struct MaxState {
+    float best;
+    int arg;
+    int cnt;
+    bool nan;
+    __device__ __forceinline__ void init() { best = __int_as_float(0xff800000); arg = -1; cnt = 0; nan = false; }
+    __device__ __forceinline__ void push(float v, int slot) {
+        if (v != v) { nan = true; return; }
+        if (cnt == 0 || v > best) { best = v; arg = slot; cnt = 1; }
+        else if (v == best) { cnt = cnt < 2 ? cnt + 1 : 2; }
+    }
+    __device__ __forceinline__ void merge(const MaxState &o) {  // o covers later slots
+        nan = nan || o.nan;
+        if (o.cnt == 0) return;
+        if (cnt == 0 || o.best > best) { best = o.best; arg = o.arg; cnt = o.cnt; }
+        else if (o.best == best) { cnt = (cnt + o.cnt) < 2 ? cnt + o.cnt : 2; }
+    }
+    __device__ __forceinline__ float value() const { return nan ? __int_as_float(0x7fc00000) : (cnt == 0 ? 0.0f : best); }
+    __device__ __forceinline__ int arg_out() const { return (nan || cnt != 1) ? -1 : arg; }
+};
+
+template <typename T, int VEC, int G, int RED>
+__global__ void __launch_bounds__(kSegThreads) seg_fwd_short_kernel(
+    const T *__restrict__ msg, int64_t C, const int32_t *__restrict__ perm, const int32_t *__restrict__ ns,
+    const int32_t *__restrict__ ne, int64_t N, float *__restrict__ out, int32_t *__restrict__ arg,
+    int32_t *__restrict__ long_list, int32_t *__restrict__ long_count) {
+    constexpr int kGroups = kSegThreads / G;
+    const int lig = threadIdx.x % G;
+    const int64_t n = (int64_t)blockIdx.x * kGroups + threadIdx.x / G;
+    if (n >= N) return;
+    const int s = ns[n], e = ne[n];
+    if (e - s > kLongSegment) {
+        if (lig == 0) long_list[atomicAdd(long_count, 1)] = (int32_t)n;
+        return;
+    }
+    for (int64_t c0 = 0; c0 < C; c0 += (int64_t)G * VEC) {
+        const int64_t c = c0 + (int64_t)lig * VEC;
+        if (c >= C) continue;
+        float acc[VEC];
+        MaxState mx[RED == GDL_REDUCE_MAX ? VEC : 1];
+#pragma unroll
+        for (int v = 0; v < VEC; ++v) {
+            acc[v] = 0.0f;
+            if (RED == GDL_REDUCE_MAX) mx[v].init();
+        }
+        int j = s;
+        for (; j + kUnroll <= e; j += kUnroll) {
+            float x[kUnroll][VEC];
+#pragma unroll
+            for (int u = 0; u < kUnroll; ++u) {
+                const int64_t row = perm ? (int64_t)__ldg(perm + j + u) : (int64_t)(j + u);
+                VecIO<T, VEC>::load(msg + row * C + c, x[u]);
+            }
+#pragma unroll
+            for (int u = 0; u < kUnroll; ++u)
+#pragma unroll
+                for (int v = 0; v < VEC; ++v) {
+                    if (RED == GDL_REDUCE_MAX) mx[v].push(x[u][v], j + u);
+                    else acc[v] = add_ftz(acc[v], x[u][v]);
+                }
+        }
+        for (; j < e; ++j) {
+            float x[VEC];
+            const int64_t row = perm ? (int64_t)__ldg(perm + j) : (int64_t)j;
+            VecIO<T, VEC>::load(msg + row * C + c, x);
+#pragma unroll
+            for (int v = 0; v < VEC; ++v) {
+                if (RED == GDL_REDUCE_MAX) mx[v].push(x[v], j);
+                else acc[v] = add_ftz(acc[v], x[v]);
+            }
+        }
+        float o[VEC];
+#pragma unroll
+        for (int v = 0; v < VEC; ++v) {
+            if (RED == GDL_REDUCE_MAX) {
+                o[v] = mx[v].value();
+                if (arg) arg[n * C + c + v] = mx[v].arg_out();
+            } else if (RED == GDL_REDUCE_MEAN) {
+                o[v] = (e > s) ? __fdiv_rn(acc[v], (float)(e - s)) : 0.0f;
+            } else {
+                o[v] = acc[v];
+            }
+        }
+        VecIO<float, VEC>::store(out + n * C + c, o);
+    }
+}
+
+// one CTA per queued long segment; row group rg folds a contiguous slot range
+template <typename T, int VEC, int G, int RED>
+__global__ void __launch_bounds__(kSegThreads) seg_fwd_long_kernel(
+    const T *__restrict__ msg, int64_t C, const int32_t *__restrict__ perm, const int32_t *__restrict__ ns,
+    const int32_t *__restrict__ ne, float *__restrict__ out, int32_t *__restrict__ arg,
+    const int32_t *__restrict__ long_list, const int32_t *__restrict__ long_count) {
+    constexpr int kRG = kSegThreads / G;
+    __shared__ float part[kRG][G * VEC];
+    __shared__ int part_arg[RED == GDL_REDUCE_MAX ? kRG : 1][RED == GDL_REDUCE_MAX ? G * VEC : 1];
+    __shared__ int part_cnt[RED == GDL_REDUCE_MAX ? kRG : 1][RED == GDL_REDUCE_MAX ? G * VEC : 1];
+    __shared__ unsigned char part_nan[RED == GDL_REDUCE_MAX ? kRG : 1][RED == GDL_REDUCE_MAX ? G * VEC : 1];
+    if ((int)blockIdx.x >= *long_count) return;
+    const int64_t n = long_list[blockIdx.x];
+    const int s = ns[n], e = ne[n];
+    const int deg = e - s;
+    const int rg = threadIdx.x / G, lig = threadIdx.x % G;
+    const int chunk = (deg + kRG - 1) / kRG;
+    const int j0 = s + rg * chunk;
+    const int j1 = min(j0 + chunk, e);
+    for (int64_t c0 = 0; c0 < C; c0 += (int64_t)G * VEC) {
+        const int64_t c = c0 + (int64_t)lig * VEC;
+        const bool active = c < C;
+        float acc[VEC];
+        MaxState mx[RED == GDL_REDUCE_MAX ? VEC : 1];
+#pragma unroll
+        for (int v = 0; v < VEC; ++v) {
+            acc[v] = 0.0f;
+            if (RED == GDL_REDUCE_MAX) mx[v].init();
+        }
+        if (active) {
+            int j = j0;
+            for (; j + kUnroll <= j1; j += kUnroll) {
+                float x[kUnroll][VEC];
+#pragma unroll
+                for (int u = 0; u < kUnroll; ++u) {
+                    const int64_t row = perm ? (int64_t)__ldg(perm + j + u) : (int64_t)(j + u);
+                    VecIO<T, VEC>::load(msg + row * C + c, x[u]);
+                }
+#pragma unroll
+                for (int u = 0; u < kUnroll; ++u)
+#pragma unroll
+                    for (int v = 0; v < VEC; ++v) {
+                        if (RED == GDL_REDUCE_MAX) mx[v].push(x[u][v], j + u);
+                        else acc[v] = add_ftz(acc[v], x[u][v]);
+                    }
+            }
+            for (; j < j1; ++j) {
+                float x[VEC];
+                const int64_t row = perm ? (int64_t)__ldg(perm + j) : (int64_t)j;
+                VecIO<T, VEC>::load(msg + row * C + c, x);
+#pragma unroll
+                for (int v = 0; v < VEC; ++v) {
+                    if (RED == GDL_REDUCE_MAX) mx[v].push(x[v], j);
+                    else acc[v] = add_ftz(acc[v], x[v]);
+                }
+            }
+        }
+#pragma unroll
+        for (int v = 0; v < VEC; ++v) {
+            const int k = lig * VEC + v;
+            if (RED == GDL_REDUCE_MAX) {
+                part[rg][k] = mx[v].best;
+                part_arg[rg][k] = mx[v].arg;
+                part_cnt[rg][k] = mx[v].cnt;
+                part_nan[rg][k] = mx[v].nan;
+            } else {
+                part[rg][k] = acc[v];
+            }
+        }
+        __syncthreads();
+        for (int k = threadIdx.x; k < G * VEC; k += kSegThreads) {
+            const int64_t ch = c0 + k;
+            if (ch < C) {
+                if (RED == GDL_REDUCE_MAX) {
+                    MaxState m;
+                    m.init();
+                    for (int r = 0; r < kRG; ++r) {
+                        MaxState o;
+                        o.best = part[r][k]; o.arg = part_arg[r][k]; o.cnt = part_cnt[r][k]; o.nan = part_nan[r][k];
+                        m.merge(o);
+                    }
+                    out[n * C + ch] = m.value();
+                    if (arg) arg[n * C + ch] = m.arg_out();
+                } else {
+                    float a = 0.0f;
+                    for (int r = 0; r < kRG; ++r) a = add_ftz(a, part[r][k]);
+                    out[n * C + ch] = (RED == GDL_REDUCE_MEAN) ? __fdiv_rn(a, (float)deg) : a;
+                }
+            }
+        }
+        __syncthreads();
+    }
+}
+
+// gradient of one (segment, VEC channels) for slots [j0, j1) of segment n
+template <typename T, int VEC, int RED>
+__device__ __forceinline__ void seg_bwd_range(const float *__restrict__ grad_out, const T *__restrict__ msg,
+                                              const float *__restrict__ out, const int32_t *__restrict__ arg,
+                                              int64_t C, const int32_t *__restrict__ perm, int64_t n, int s, int e,
+                                              int j0, int j1, int64_t c, T *__restrict__ grad_msg) {
+    float g[VEC], base[VEC];
+    VecIO<float, VEC>::load(grad_out + n * C + c, g);
+    int a[VEC];
+    float mx[VEC];
+#pragma unroll
+    for (int v = 0; v < VEC; ++v) {
+        if (RED == GDL_REDUCE_SUM) {
+            base[v] = g[v];
+        } else if (RED == GDL_REDUCE_MEAN) {
+            base[v] = __fdiv_rn(g[v], (float)(e - s));
+        } else {
+            a[v] = arg ? arg[n * C + c + v] : -1;
+            mx[v] = out[n * C + c + v];
+            base[v] = g[v];
+            if (a[v] < 0) {  // tied (or NaN) maximum: share among every slot equal to it
+                int t = 0;
+                for (int k = s; k < e; ++k) {
+                    float x;
+                    const int64_t rk = perm ? (int64_t)__ldg(perm + k) : (int64_t)k;
+                    VecIO<T, 1>::load(msg + rk * C + c + v, &x);
+                    t += (x == mx[v]);
+                }
+                base[v] = __fdiv_rn(g[v], (float)t);
+            }
+        }
+    }
+    for (int j = j0; j < j1; ++j) {
+        const int64_t row = perm ? (int64_t)__ldg(perm + j) : (int64_t)j;
+        float val[VEC];
+        if (RED == GDL_REDUCE_MAX) {
+            float x[VEC];
+            bool need = false;
+#pragma unroll
+            for (int v = 0; v < VEC; ++v) need |= a[v] < 0;
+            if (need) VecIO<T, VEC>::load(msg + row * C + c, x);
+#pragma unroll
+            for (int v = 0; v < VEC; ++v) {
+                const bool hit = a[v] >= 0 ? (a[v] == j) : (x[v] == mx[v]);
+                val[v] = (hit ? 1.0f : 0.0f) * base[v];  // torch: mask * share
+            }
+        } else {
+#pragma unroll
+            for (int v = 0; v < VEC; ++v) val[v] = base[v];
+        }
+        VecIO<T, VEC>::store(grad_msg + row * C + c, val);
+    }
+}
+
+template <typename T, int VEC, int G, int RED>
+__global__ void __launch_bounds__(kSegThreads) seg_bwd_short_kernel(
+    const float *__restrict__ grad_out, const T *__restrict__ msg, const float *__restrict__ out,
+    const int32_t *__restrict__ arg, int64_t C, const int32_t *__restrict__ perm, const int32_t *__restrict__ ns,
+    const int32_t *__restrict__ ne, int64_t N, T *__restrict__ grad_msg, int32_t *__restrict__ long_list,
+    int32_t *__restrict__ long_count) {
+    constexpr int kGroups = kSegThreads / G;
+    const int lig = threadIdx.x % G;
+    const int64_t n = (int64_t)blockIdx.x * kGroups + threadIdx.x / G;
+    if (n >= N) return;
+    const int s = ns[n], e = ne[n];
+    if (e <= s) return;
+    if (e - s > kLongSegment) {
+        if (lig == 0) long_list[atomicAdd(long_count, 1)] = (int32_t)n;
+        return;
+    }
+    for (int64_t c0 = 0; c0 < C; c0 += (int64_t)G * VEC) {
+        const int64_t c = c0 + (int64_t)lig * VEC;
+        if (c < C) seg_bwd_range<T, VEC, RED>(grad_out, msg, out, arg, C, perm, n, s, e, s, e, c, grad_msg);
+    }
+}
+
+template <typename T, int VEC, int G, int RED>
+__global__ void __launch_bounds__(kSegThreads) seg_bwd_long_kernel(
+    const float *__restrict__ grad_out, const T *__restrict__ msg, const float *__restrict__ out,
+    const int32_t *__restrict__ arg, int64_t C, const int32_t *__restrict__ perm, const int32_t *__restrict__ ns,
+    const int32_t *__restrict__ ne, T *__restrict__ grad_msg, const int32_t *__restrict__ long_list,
+    const int32_t *__restrict__ long_count) {
+    constexpr int kRG = kSegThreads / G;
+    if ((int)blockIdx.x >= *long_count) return;
+    const int64_t n = long_list[blockIdx.x];
+    const int s = ns[n], e = ne[n];
+    const int rg = threadIdx.x / G, lig = threadIdx.x % G;
+    const int chunk = (e - s + kRG - 1) / kRG;
+    const int j0 = s + rg * chunk;
+    const int j1 = min(j0 + chunk, e);
+    if (j0 >= j1) return;
+    for (int64_t c0 = 0; c0 < C; c0 += (int64_t)G * VEC) {
+        const int64_t c = c0 + (int64_t)lig * VEC;
+        if (c < C) seg_bwd_range<T, VEC, RED>(grad_out, msg, out, arg, C, perm, n, s, e, j0, j1, c, grad_msg);
+    }
+}
+
+// ----------------------------------------------------------------- CSR build kernels
+__global__ void csr_keys_kernel(const int64_t *__restrict__ col, int64_t E, uint32_t *__restrict__ keys) {
+    const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < E) keys[i] = (uint32_t)(int32_t)col[i];
+}
+
+// segment_reduce_kernel.cu:30-50: boundaries of runs of equal destinations
+__global__ void csr_offsets_kernel(const int32_t *__restrict__ cs, int64_t E, int64_t N, int32_t *__restrict__ ns,
+                                   int32_t *__restrict__ ne) {
+    const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= E) return;
+    const int32_t v = cs[i];
+    if (v < 0 || v >= N) return;
+    if (i == 0 || cs[i - 1] != v) ns[v] = (int32_t)i;
+    if (i == E - 1 || cs[i + 1] != v) ne[v] = (int32_t)(i + 1);
+}
+
+// ----------------------------------------------------------------- host dispatch
+struct SegShape {
+    int vec;
+    int group;
+};
+
+template <typename T>
+static SegShape seg_shape(int64_t C, uintptr_t align_bits) {
+    // widest vector that divides C and the row alignment; lanes per segment = C / VEC
+    const int maxv = 16 / (int)sizeof(T);
+    int vec = 1;
+    for (int v = maxv; v >= 1; v >>= 1) {
+        if (C % v == 0 && (align_bits % (v * sizeof(T))) == 0) { vec = v; break; }
+    }
+    // prefer filling a warp over the widest vector when a row is narrower than 32 vectors
+    while (vec > 1 && (C / vec) < 32 && (C / (vec / 2)) <= 32 && (sizeof(T) * vec / 2) >= 4) vec >>= 1;
+    int64_t lanes = C / vec;
+    int g = 1;
+    while (g < lanes && g < 32) g <<= 1;
+    return {vec, g};
+}
+
+// narrow a shape until its VEC-wide f32 accesses (out / grad_out rows) are aligned too
+static SegShape fit_f32_side(SegShape sh, int64_t C, uintptr_t alf) {
+    while (sh.vec > 1 && (sh.vec > 4 || alf % (uintptr_t)(sh.vec * 4) != 0)) sh.vec >>= 1;
+    int64_t lanes = C / sh.vec;
+    int g = 1;
+    while (g < lanes && g < 32) g <<= 1;
+    sh.group = g;
+    return sh;
+}
+
+// largest power of two dividing every address and row stride given (the vector width a
+// kernel may use for all of them); null pointers do not constrain it
+static uintptr_t common_align(std::initializer_list<uintptr_t> vals) {
+    uintptr_t a = 0;
+    for (uintptr_t v : vals) a |= v;
+    if (a == 0) return 256;
+    a &= (~a + 1);  // lowest set bit
+    return a > 256 ? 256 : a;
+}
+
+template <typename T, int VEC, int G, int RED>
+static void launch_fwd(const void *msg, int64_t C, const int32_t *perm, const int32_t *ns, const int32_t *ne,
+                       int64_t N, float *out, int32_t *arg, int32_t *long_list, int32_t *long_count,
+                       int64_t max_long, cudaStream_t st) {
+    constexpr int groups = kSegThreads / G;
+    const int64_t blocks = (N + groups - 1) / groups;
+    seg_fwd_short_kernel<T, VEC, G, RED><<<(unsigned)blocks, kSegThreads, 0, st>>>(
+        (const T *)msg, C, perm, ns, ne, N, out, arg, long_list, long_count);
+    if (max_long > 0)
+        seg_fwd_long_kernel<T, VEC, G, RED><<<(unsigned)max_long, kSegThreads, 0, st>>>(
+            (const T *)msg, C, perm, ns, ne, out, arg, long_list, long_count);
+}
+
+template <typename T, int VEC, int RED>
+static void launch_fwd_g(int G, const void *msg, int64_t C, const int32_t *perm, const int32_t *ns,
+                         const int32_t *ne, int64_t N, float *out, int32_t *arg, int32_t *ll, int32_t *lc,
+                         int64_t ml, cudaStream_t st) {
+    switch (G) {
+    case 1: launch_fwd<T, VEC, 1, RED>(msg, C, perm, ns, ne, N, out, arg, ll, lc, ml, st); break;
+    case 2: launch_fwd<T, VEC, 2, RED>(msg, C, perm, ns, ne, N, out, arg, ll, lc, ml, st); break;
+    case 4: launch_fwd<T, VEC, 4, RED>(msg, C, perm, ns, ne, N, out, arg, ll, lc, ml, st); break;
+    case 8: launch_fwd<T, VEC, 8, RED>(msg, C, perm, ns, ne, N, out, arg, ll, lc, ml, st); break;
+    case 16: launch_fwd<T, VEC, 16, RED>(msg, C, perm, ns, ne, N, out, arg, ll, lc, ml, st); break;
+    default: launch_fwd<T, VEC, 32, RED>(msg, C, perm, ns, ne, N, out, arg, ll, lc, ml, st); break;
+    }
+}
+
+template <typename T, int RED>
+static void launch_fwd_v(SegShape sh, const void *msg, int64_t C, const int32_t *perm, const int32_t *ns,
+                         const int32_t *ne, int64_t N, float *out, int32_t *arg, int32_t *ll, int32_t *lc,
+                         int64_t ml, cudaStream_t st) {
+    switch (sh.vec) {
+    case 4: launch_fwd_g<T, 4, RED>(sh.group, msg, C, perm, ns, ne, N, out, arg, ll, lc, ml, st); break;
+    case 2: launch_fwd_g<T, 2, RED>(sh.group, msg, C, perm, ns, ne, N, out, arg, ll, lc, ml, st); break;
+    default: launch_fwd_g<T, 1, RED>(sh.group, msg, C, perm, ns, ne, N, out, arg, ll, lc, ml, st); break;
+    }
+}
+
+template <typename T, int VEC, int G, int RED>
+static void launch_bwd(const float *go, const void *msg, const float *out, const int32_t *arg, int64_t C,
+                       const int32_t *perm, const int32_t *ns, const int32_t *ne, int64_t N, void *gm, int32_t *ll,
+                       int32_t *lc, int64_t ml, cudaStream_t st) {
+    constexpr int groups = kSegThreads / G;
+    const int64_t blocks = (N + groups - 1) / groups;
+    seg_bwd_short_kernel<T, VEC, G, RED><<<(unsigned)blocks, kSegThreads, 0, st>>>(
+        go, (const T *)msg, out, arg, C, perm, ns, ne, N, (T *)gm, ll, lc);
+    if (ml > 0)
+        seg_bwd_long_kernel<T, VEC, G, RED><<<(unsigned)ml, kSegThreads, 0, st>>>(go, (const T *)msg, out, arg, C, perm,
+                                                                                 ns, ne, (T *)gm, ll, lc);
+}
+
+template <typename T, int VEC, int RED>
+static void launch_bwd_g(int G, const float *go, const void *msg, const float *out, const int32_t *arg, int64_t C,
+                         const int32_t *perm, const int32_t *ns, const int32_t *ne, int64_t N, void *gm, int32_t *ll,
+                         int32_t *lc, int64_t ml, cudaStream_t st) {
+    switch (G) {
+    case 1: launch_bwd<T, VEC, 1, RED>(go, msg, out, arg, C, perm, ns, ne, N, gm, ll, lc, ml, st); break;
+    case 2: launch_bwd<T, VEC, 2, RED>(go, msg, out, arg, C, perm, ns, ne, N, gm, ll, lc, ml, st); break;
+    case 4: launch_bwd<T, VEC, 4, RED>(go, msg, out, arg, C, perm, ns, ne, N, gm, ll, lc, ml, st); break;
+    case 8: launch_bwd<T, VEC, 8, RED>(go, msg, out, arg, C, perm, ns, ne, N, gm, ll, lc, ml, st); break;
+    case 16: launch_bwd<T, VEC, 16, RED>(go, msg, out, arg, C, perm, ns, ne, N, gm, ll, lc, ml, st); break;
+    default: launch_bwd<T, VEC, 32, RED>(go, msg, out, arg, C, perm, ns, ne, N, gm, ll, lc, ml, st); break;
+    }
+}
+
+template <typename T, int RED>
+static void launch_bwd_v(SegShape sh, const float *go, const void *msg, const float *out, const int32_t *arg,
+                         int64_t C, const int32_t *perm, const int32_t *ns, const int32_t *ne, int64_t N, void *gm,
+                         int32_t *ll, int32_t *lc, int64_t ml, cudaStream_t st) {
+    switch (sh.vec) {
+    case 4: launch_bwd_g<T, 4, RED>(sh.group, go, msg, out, arg, C, perm, ns, ne, N, gm, ll, lc, ml, st); break;
+    case 2: launch_bwd_g<T, 2, RED>(sh.group, go, msg, out, arg, C, perm, ns, ne, N, gm, ll, lc, ml, st); break;
+    default: launch_bwd_g<T, 1, RED>(sh.group, go, msg, out, arg, C, perm, ns, ne, N, gm, ll, lc, ml, st); break;
+    }
+}
+
+}  // namespace gdl
+
+using namespace gdl;
+
+static inline size_t al256(size_t b) { return (b + 255) & ~size_t(255); }
+
+extern "C" size_t gdl_sort_and_build_csr_workspace_size(int64_t num_edges, int64_t num_nodes) {
+    (void)num_nodes;
+    const int64_t E = num_edges > 0 ? num_edges : 1;
+    return al256(sizeof(uint32_t) * E) + radix_scratch_bytes(E, 1) + 256;
+}
+
+extern "C" int gdl_sort_and_build_csr(const int64_t *col, int64_t num_edges, int64_t num_nodes, int32_t *col_sorted,
+                                      int32_t *perm, int32_t *node_start, int32_t *node_end, void *workspace,
+                                      size_t workspace_bytes, void *stream) {
+    cudaStream_t st = (cudaStream_t)stream;
+    GDL_RETURN_IF(num_edges < 0 || num_nodes < 0, GDL_ERR_INVALID);
+    GDL_RETURN_IF(num_edges >= INT32_MAX || num_nodes >= INT32_MAX, GDL_ERR_OVERFLOW);
+    if (num_nodes > 0) {
+        GDL_RETURN_IF(!node_start || !node_end, GDL_ERR_INVALID);
+        GDL_CUDA_TRY(cudaMemsetAsync(node_start, 0, sizeof(int32_t) * num_nodes, st));
+        GDL_CUDA_TRY(cudaMemsetAsync(node_end, 0, sizeof(int32_t) * num_nodes, st));
+    }
+    if (num_edges == 0) return GDL_OK;
+    GDL_RETURN_IF(!col || !col_sorted || !perm, GDL_ERR_INVALID);
+    GDL_RETURN_IF(!workspace || workspace_bytes < gdl_sort_and_build_csr_workspace_size(num_edges, num_nodes),
+                  GDL_ERR_WORKSPACE);
+    char *p = (char *)workspace;
+    uint32_t *keys = (uint32_t *)p;
+    p += al256(sizeof(uint32_t) * num_edges);
+    RadixScratch rs = radix_carve(p, num_edges, 1);
+    csr_keys_kernel<<<(unsigned)((num_edges + 255) / 256), 256, 0, st>>>(col, num_edges, keys);
+    int bits = 1;
+    while (bits < 32 && ((int64_t)1 << bits) < num_nodes) ++bits;
+    const int passes = (bits + 7) / 8;
+    GDL_CUDA_TRY(radix_sort_pairs(keys, nullptr, (uint32_t *)col_sorted, perm, num_edges, nullptr, 1, passes, nullptr,
+                                  rs, st));
+    csr_offsets_kernel<<<(unsigned)((num_edges + 255) / 256), 256, 0, st>>>(col_sorted, num_edges, num_nodes,
+                                                                            node_start, node_end);
+    GDL_CUDA_TRY(cudaGetLastError());
+    return GDL_OK;
+}
+
+extern "C" size_t gdl_segment_reduce_workspace_size(int64_t num_rows, int64_t num_nodes) {
+    (void)num_nodes;
+    const int64_t max_long = num_rows / (kLongSegment + 1) + 1;
+    return al256(sizeof(int32_t)) + al256(sizeof(int32_t) * max_long);
+}
+
+extern "C" int gdl_segment_reduce(const void *msg, int32_t dtype, int64_t num_rows, int64_t C, const int32_t *perm,
+                                  const int32_t *node_start, const int32_t *node_end, int64_t num_nodes,
+                                  int32_t reduce, float *out, int32_t *arg_out, void *workspace,
+                                  size_t workspace_bytes, void *stream) {
+    cudaStream_t st = (cudaStream_t)stream;
+    GDL_RETURN_IF(num_rows < 0 || C <= 0 || num_nodes < 0, GDL_ERR_INVALID);
+    GDL_RETURN_IF(dtype != GDL_DTYPE_F32 && dtype != GDL_DTYPE_BF16, GDL_ERR_INVALID);
+    GDL_RETURN_IF(reduce < GDL_REDUCE_SUM || reduce > GDL_REDUCE_MAX, GDL_ERR_INVALID);
+    GDL_RETURN_IF(num_rows >= INT32_MAX, GDL_ERR_OVERFLOW);
+    if (num_nodes == 0) return GDL_OK;
+    GDL_RETURN_IF(!out || !node_start || !node_end || (num_rows > 0 && !msg), GDL_ERR_INVALID);
+    GDL_RETURN_IF(!workspace || workspace_bytes < gdl_segment_reduce_workspace_size(num_rows, num_nodes),
+                  GDL_ERR_WORKSPACE);
+    int32_t *long_count = (int32_t *)workspace;
+    int32_t *long_list = (int32_t *)((char *)workspace + al256(sizeof(int32_t)));
+    const int64_t max_long = num_rows / (kLongSegment + 1) + 1;
+    GDL_CUDA_TRY(cudaMemsetAsync(long_count, 0, sizeof(int32_t), st));
+    const int64_t esz = dtype == GDL_DTYPE_BF16 ? 2 : 4;
+    const uintptr_t al = common_align({(uintptr_t)msg, (uintptr_t)(C * esz), (uintptr_t)out, (uintptr_t)(C * 4)});
+    if (dtype == GDL_DTYPE_F32) {
+        SegShape sh = seg_shape<float>(C, al);
+        if (reduce == GDL_REDUCE_SUM) launch_fwd_v<float, GDL_REDUCE_SUM>(sh, msg, C, perm, node_start, node_end, num_nodes, out, arg_out, long_list, long_count, max_long, st);
+        else if (reduce == GDL_REDUCE_MEAN) launch_fwd_v<float, GDL_REDUCE_MEAN>(sh, msg, C, perm, node_start, node_end, num_nodes, out, arg_out, long_list, long_count, max_long, st);
+        else launch_fwd_v<float, GDL_REDUCE_MAX>(sh, msg, C, perm, node_start, node_end, num_nodes, out, arg_out, long_list, long_count, max_long, st);
+    } else {
+        // out rows are f32: the vector width must also suit them
+        SegShape sh = fit_f32_side(seg_shape<uint16_t>(C, al), C,
+                                   common_align({(uintptr_t)out, (uintptr_t)(C * 4)}));
+        if (reduce == GDL_REDUCE_SUM) launch_fwd_v<uint16_t, GDL_REDUCE_SUM>(sh, msg, C, perm, node_start, node_end, num_nodes, out, arg_out, long_list, long_count, max_long, st);
+        else if (reduce == GDL_REDUCE_MEAN) launch_fwd_v<uint16_t, GDL_REDUCE_MEAN>(sh, msg, C, perm, node_start, node_end, num_nodes, out, arg_out, long_list, long_count, max_long, st);
+        else launch_fwd_v<uint16_t, GDL_REDUCE_MAX>(sh, msg, C, perm, node_start, node_end, num_nodes, out, arg_out, long_list, long_count, max_long, st);
+    }
+    GDL_CUDA_TRY(cudaGetLastError());
+    return GDL_OK;
+}
+
+extern "C" int gdl_segment_reduce_backward(const float *grad_out, const void *msg, int32_t dtype, const float *out,
+                                           const int32_t *arg, int64_t num_rows, int64_t C, const int32_t *perm,
+                                           const int32_t *node_start, const int32_t *node_end, int64_t num_nodes,
+                                           int32_t reduce, void *grad_msg, void *workspace, size_t workspace_bytes,
+                                           void *stream) {
+    cudaStream_t st = (cudaStream_t)stream;
+    GDL_RETURN_IF(num_rows < 0 || C <= 0 || num_nodes < 0, GDL_ERR_INVALID);
+    GDL_RETURN_IF(dtype != GDL_DTYPE_F32 && dtype != GDL_DTYPE_BF16, GDL_ERR_INVALID);
+    GDL_RETURN_IF(reduce < GDL_REDUCE_SUM || reduce > GDL_REDUCE_MAX, GDL_ERR_INVALID);
+    GDL_RETURN_IF(num_rows >= INT32_MAX, GDL_ERR_OVERFLOW);
+    if (num_nodes == 0 || num_rows == 0) return GDL_OK;
+    GDL_RETURN_IF(!grad_out || !grad_msg || !node_start || !node_end, GDL_ERR_INVALID);
+    GDL_RETURN_IF(reduce == GDL_REDUCE_MAX && (!msg || !out), GDL_ERR_INVALID);
+    GDL_RETURN_IF(!workspace || workspace_bytes < gdl_segment_reduce_workspace_size(num_rows, num_nodes),
+                  GDL_ERR_WORKSPACE);
+    int32_t *long_count = (int32_t *)workspace;
+    int32_t *long_list = (int32_t *)((char *)workspace + al256(sizeof(int32_t)));
+    const int64_t max_long = num_rows / (kLongSegment + 1) + 1;
+    GDL_CUDA_TRY(cudaMemsetAsync(long_count, 0, sizeof(int32_t), st));
+    const int64_t esz = dtype == GDL_DTYPE_BF16 ? 2 : 4;
+    const uintptr_t al = common_align({(uintptr_t)grad_out, (uintptr_t)(C * 4), (uintptr_t)grad_msg,
+                                       (uintptr_t)(C * esz), (uintptr_t)msg});
+    SegShape sh = dtype == GDL_DTYPE_F32 ? seg_shape<float>(C, al) : seg_shape<uint16_t>(C, al);
+    sh = fit_f32_side(sh, C, common_align({(uintptr_t)grad_out, (uintptr_t)(C * 4)}));
+    const int32_t *a = arg;
+    if (dtype == GDL_DTYPE_F32) {
+        if (reduce == GDL_REDUCE_SUM) launch_bwd_v<float, GDL_REDUCE_SUM>(sh, grad_out, msg, out, a, C, perm, node_start, node_end, num_nodes, grad_msg, long_list, long_count, max_long, st);
+        else if (reduce == GDL_REDUCE_MEAN) launch_bwd_v<float, GDL_REDUCE_MEAN>(sh, grad_out, msg, out, a, C, perm, node_start, node_end, num_nodes, grad_msg, long_list, long_count, max_long, st);
+        else launch_bwd_v<float, GDL_REDUCE_MAX>(sh, grad_out, msg, out, a, C, perm, node_start, node_end, num_nodes, grad_msg, long_list, long_count, max_long, st);
+    } else {
+        if (reduce == GDL_REDUCE_SUM) launch_bwd_v<uint16_t, GDL_REDUCE_SUM>(sh, grad_out, msg, out, a, C, perm, node_start, node_end, num_nodes, grad_msg, long_list, long_count, max_long, st);
+        else if (reduce == GDL_REDUCE_MEAN) launch_bwd_v<uint16_t, GDL_REDUCE_MEAN>(sh, grad_out, msg, out, a, C, perm, node_start, node_end, num_nodes, grad_msg, long_list, long_count, max_long, st);
+        else launch_bwd_v<uint16_t, GDL_REDUCE_MAX>(sh, grad_out, msg, out, a, C, perm, node_start, node_end, num_nodes, grad_msg, long_list, long_count, max_long, st);
+    }
+    GDL_CUDA_TRY(cudaGetLastError());
+    return GDL_OK;
+}

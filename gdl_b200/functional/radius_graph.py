@@ -1,0 +1,65 @@
+"""Radius graph -- drop-in for ``geoembodied.functional.radius_graph``
+(reference: geoembodied/functional/radius_graph.py:19-105, 338-358)."""
+
+from __future__ import annotations
+
+from typing import Optional, Tuple
+
+import torch
+from torch import Tensor
+
+from .. import csrc
+
+
+def _ptr_from_batch(batch: Tensor, B: Optional[int]):
+    batch = batch.to(torch.int64)
+    nb = int(B) if B is not None else int(batch.max().item()) + 1
+    counts = torch.bincount(batch, minlength=nb)
+    ptr = torch.zeros(nb + 1, dtype=torch.int64, device=batch.device)
+    ptr[1:] = counts.cumsum(0)
+    return ptr
+
+
+def radius_graph_csr(x: Tensor, r: float, ptr: Tensor, *, max_num_neighbors: int = 32, loop: bool = False,
+                     mask: Optional[Tensor] = None):
+    """Edges of packed clouds as a destination CSR (row_ptr [N+1], src, dst); the first
+    row_ptr[N] entries of src/dst are valid. No host synchronisation."""
+    return csrc.radius_graph_csr(x, r, ptr, max_num_neighbors=max_num_neighbors, loop=loop, mask=mask)
+
+
+def radius_graph(x: Tensor, r: float, *, max_num_neighbors: int = 32, batch: Optional[Tensor] = None,
+                 loop: bool = False, mask: Optional[Tensor] = None,
+                 num_batch_elements: Optional[int] = None) -> Tuple[Tensor, Tensor]:
+    """(row, col) int64 with ||x[row] - x[col]|| < r; row = source (neighbour), col = target.
+
+    Each target keeps its bucket(max_num_neighbors) in {16, 32, 64} nearest in-radius
+    points of its own cloud, selected exactly as the reference CUDA kernel does. Clouds come
+    from ``batch`` (any sizes, any order), else ``num_batch_elements`` equal-size clouds,
+    else one cloud. Edges are grouped by target, sources ascending.
+    """
+    N = x.shape[0]
+    if batch is not None:
+        batch = batch.to(torch.int64)
+        sorted_ok = N < 2 or bool((batch[1:] >= batch[:-1]).all())
+        order = None if sorted_ok else torch.argsort(batch, stable=True)
+        xb = x if order is None else x[order]
+        mb = mask if (mask is None or order is None) else mask[order]
+        ptr = _ptr_from_batch(batch if order is None else batch[order], num_batch_elements)
+    else:
+        order, xb, mb = None, x, mask
+        B = num_batch_elements if num_batch_elements is not None else 1
+        ptr = torch.arange(B + 1, dtype=torch.int64, device=x.device) * (N // B)
+    row_ptr, src, dst = csrc.radius_graph_csr(xb, r, ptr, max_num_neighbors=max_num_neighbors, loop=loop, mask=mb)
+    E = int(row_ptr[N].item())
+    row, col = src[:E], dst[:E]
+    if order is not None:
+        row, col = order[row], order[col]
+    return row, col
+
+
+def compute_edge_vectors(x: Tensor, row: Tensor, col: Tensor) -> Tuple[Tensor, Tensor, Tensor]:
+    """(diff = x[col] - x[row], |diff| clamped at 1e-8, diff / |diff|) -- the reference's
+    formula (radius_graph.py:338-358), evaluated with torch ops."""
+    diff = x[col] - x[row]
+    dist = diff.norm(dim=-1, keepdim=True).clamp(min=1e-8)
+    return diff, dist.squeeze(-1), diff / dist

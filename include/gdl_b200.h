@@ -1,0 +1,161 @@
+/*
+ * gdl_b200.h -- C ABI of the B200 (sm_100a) point-cloud graph operators.
+ *
+ * Drop-in native layer for GeoEmbodied's hot path (illusionaryshelter/GDL,
+ * geoembodied/csrc): farthest-point sampling, KNN, radius graph, CSR build and
+ * segment reduce (sum / mean / max, forward and backward).
+ *
+ * Conventions
+ *  - Every pointer argument is DEVICE memory unless the comment says otherwise. Inputs
+ *    are borrowed; outputs are written in place; nothing is freed.
+ *  - `stream` is a cudaStream_t passed as void*; every kernel runs on it and no entry
+ *    point synchronises the host, except where a comment says so.
+ *  - Scratch memory is caller-provided (`workspace`, `workspace_bytes`); each operator
+ *    that needs it has a *_workspace_size() query evaluated on the host. A workspace
+ *    must be 256-byte aligned and may be reused once the stream has moved past the call.
+ *  - Return value: a gdl_status for argument and launch errors. The kernels contain no
+ *    spin-waits; launches are asynchronous, so execution faults surface at the caller's
+ *    next synchronisation like any CUDA error.
+ *  - Clouds are packed CSR-style: cloud b owns points [ptr[b], ptr[b+1]); ptr is int64.
+ */
+#ifndef GDL_B200_H
+#define GDL_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef enum {
+    GDL_OK = 0,
+    GDL_ERR_INVALID = 1,     /* bad argument: null pointer, negative size, bad enum       */
+    GDL_ERR_WORKSPACE = 2,   /* workspace smaller than *_workspace_size()                  */
+    GDL_ERR_CUDA = 3,        /* CUDA runtime / launch error                                */
+    GDL_ERR_UNSUPPORTED = 4, /* device is not sm_100 (B200) or configuration not supported */
+    GDL_ERR_OVERFLOW = 5,    /* a size exceeds the 32-bit index range of a kernel          */
+    GDL_ERR_TIMEOUT = 6      /* a bounded device-side wait gave up                         */
+} gdl_status;
+
+enum { GDL_TIE_REFERENCE = 0, GDL_TIE_LOWEST_INDEX = 1 };
+enum { GDL_REDUCE_SUM = 0, GDL_REDUCE_MEAN = 1, GDL_REDUCE_MAX = 2 };
+enum { GDL_DTYPE_F32 = 0, GDL_DTYPE_BF16 = 1 };
+
+/* Library version (major*10000 + minor*100 + patch). */
+int gdl_version(void);
+
+/* Human-readable name of a gdl_status. */
+const char *gdl_status_string(int status);
+
+/* GDL_OK if `device` is an sm_100 GPU this library was built for. */
+int gdl_check_device(int device);
+
+/* ------------------------------------------------------------------------------ FPS
+ * Replaces fps_cuda(pos, ptr, k_per_batch) -- geoembodied/csrc/fps_kernel.cu:160-209,
+ * Python dispatch geoembodied/csrc/__init__.py:566-597.
+ *
+ * pos          [n_points, 3] f32
+ * ptr          [num_clouds + 1] i64
+ * k_per_cloud  [num_clouds] i64, samples requested per cloud
+ * out_idx      [sum(max(k_b, 0))] i64: cloud b's picks start at sum_{c<b} max(k_c, 0);
+ *              min(k_b, n_b) global indices in selection order, then -1 padding.
+ * n_points     rows of pos.
+ * max_cloud_points  host-side upper bound of max_b n_b (selects the kernel variant: one CTA
+ *              per cloud up to 8192 points, a thread-block cluster up to 131072, else a
+ *              streaming CTA that keeps the running minima in the workspace).
+ * tie_break    GDL_TIE_REFERENCE: the reference kernel's argmax reduction order
+ *              (bit-identical to fps_kernel<512>); GDL_TIE_LOWEST_INDEX: torch.argmax.
+ * Seed is the first point of each cloud; distances use the reference's rounding.
+ */
+size_t gdl_fps_workspace_size(int64_t n_points, int64_t max_cloud_points);
+int gdl_fps(const float *pos, const int64_t *ptr, const int64_t *k_per_cloud, int32_t num_clouds, int64_t n_points,
+            int64_t max_cloud_points, int32_t tie_break, int64_t *out_idx, void *workspace, size_t workspace_bytes,
+            void *stream);
+
+/* ------------------------------------------------------------------------------ KNN
+ * Replaces knn_cuda(query, source, ptr_q, ptr_s, k) and knn_self_cuda(points, ptr, k)
+ * -- geoembodied/csrc/knn_kernel.cu:200-308, dispatch csrc/__init__.py:376-432.
+ *
+ * query [n_query, 3] f32, source [*, 3] f32, ptr_q / ptr_s [num_clouds + 1] i64.
+ * out_idx [n_query, k] i64 global source indices, -1 padded; out_dist [n_query, k] f32
+ * squared distances, 1e30 padded. At most min(k, 64) neighbours per query (the reference's
+ * MinK<64> bucket), ascending distance; equal distances are ordered exactly as the
+ * reference's heap orders them. Queries outside every [ptr_q[b], ptr_q[b+1]) keep padding.
+ * max_cloud_sources: host-side upper bound of max_b (ptr_s[b+1] - ptr_s[b]).
+ */
+size_t gdl_knn_workspace_size(int64_t n_query, int32_t num_clouds, int32_t k, int64_t max_cloud_sources);
+int gdl_knn(const float *query, const float *source, const int64_t *ptr_q, const int64_t *ptr_s,
+            int32_t num_clouds, int64_t n_query, int32_t k, int64_t max_cloud_sources, int64_t *out_idx,
+            float *out_dist, void *workspace, size_t workspace_bytes, void *stream);
+
+/* ----------------------------------------------------------------------- radius graph
+ * Replaces radius_graph_cuda(points, radius, max_num_neighbors, mask, loop) and
+ * radius_graph_cuda_batched(...) -- geoembodied/csrc/radius_graph_kernel.cu:253-467,
+ * dispatch csrc/__init__.py:130-186 -- for any number of variable-size clouds at once.
+ *
+ * x [n_points, 3] f32, ptr [num_clouds + 1] i64, mask [n_points] u8 (nullable, 0 = padding).
+ * Per query: the bucket(max_num_neighbors) in {16, 32, 64} nearest points of its own
+ * cloud with squared distance < r^2 (r = (float)radius), found on the reference's
+ * per-cloud cell grid with its scan order and heap, so the edge SET equals the
+ * reference's. Edges are emitted as a CSR over destinations:
+ *   out_row_ptr [n_points + 1] i64  (edges of destination q: [row_ptr[q], row_ptr[q+1]))
+ *   out_src     [capacity] i64      (row: the neighbour, ascending within a destination)
+ *   out_dst     [capacity] i64      (col: the query; nullable)
+ * capacity = n_points * bucket(max_num_neighbors). The edge count is out_row_ptr[n_points].
+ */
+size_t gdl_radius_graph_workspace_size(int64_t n_points, int32_t num_clouds, int32_t max_num_neighbors);
+int gdl_radius_graph(const float *x, const int64_t *ptr, int32_t num_clouds, int64_t n_points, double radius,
+                     int32_t max_num_neighbors, int32_t loop, const uint8_t *mask, int64_t *out_row_ptr,
+                     int64_t *out_src, int64_t *out_dst, void *workspace, size_t workspace_bytes, void *stream);
+
+/* -------------------------------------------------------------------------- CSR build
+ * Replaces sort_and_build_csr(col, N) -- geoembodied/csrc/segment_reduce_kernel.cu:100-169.
+ * col [num_edges] i64 in [0, num_nodes). Stable sort by destination:
+ * col_sorted / perm [num_edges] i32 (perm = original edge id of each sorted slot),
+ * node_start / node_end [num_nodes] i32; nodes without edges get 0 / 0.
+ */
+size_t gdl_sort_and_build_csr_workspace_size(int64_t num_edges, int64_t num_nodes);
+int gdl_sort_and_build_csr(const int64_t *col, int64_t num_edges, int64_t num_nodes, int32_t *col_sorted,
+                           int32_t *perm, int32_t *node_start, int32_t *node_end, void *workspace,
+                           size_t workspace_bytes, void *stream);
+
+/* ------------------------------------------------------------------- segment reduce
+ * Replaces segment_reduce_sum(msg, perm, node_start, node_end, N) --
+ * geoembodied/csrc/segment_reduce_kernel.cu:176-210 -- and adds mean and max
+ * (torch.scatter_reduce(include_self=False) semantics, used by the reference's callers
+ * at nn/modules/invariant_attention.py:215-220 and nn/modules/se3_net.py:226-270).
+ *
+ * msg [num_rows, C] f32 or bf16 (dtype); perm [*] i32 row of each sorted slot (nullable:
+ * slot j is row j); node_start / node_end [num_nodes] i32. out [num_nodes, C] f32:
+ *   sum  : ((0 + m_0) + m_1) + ... in slot order (bit-identical to the reference kernel)
+ *          for segments of up to 4096 slots; longer ones use a fixed-order tree.
+ *   mean : sum / degree;  max : elementwise maximum (NaN propagates); empty -> 0.
+ * arg_out [num_nodes, C] i32 (max only, nullable): slot of the unique maximum, -1 when
+ * tied (or empty); consumed by the backward.
+ */
+size_t gdl_segment_reduce_workspace_size(int64_t num_rows, int64_t num_nodes);
+int gdl_segment_reduce(const void *msg, int32_t dtype, int64_t num_rows, int64_t C, const int32_t *perm,
+                       const int32_t *node_start, const int32_t *node_end, int64_t num_nodes, int32_t reduce,
+                       float *out, int32_t *arg_out, void *workspace, size_t workspace_bytes, void *stream);
+
+/* Backward of gdl_segment_reduce (the reference's autograd: gather grad_out by destination,
+ * un-permute -- geoembodied/functional/segment_reduce.py:142-158, 259-270): for every slot j
+ * of node n,
+ *   grad_msg[perm[j]] = grad_out[n]                              (sum)
+ *                     = grad_out[n] / degree(n)                  (mean)
+ *                     = (msg == out[n]) * grad_out[n] / ties     (max; ties = #maxima)
+ * `arg`/`out` come from the max forward (msg is re-read only for tied maxima). Rows that no
+ * slot references are left untouched. grad_msg has msg's dtype (bf16 rounded to nearest even).
+ * Uses the same workspace size as gdl_segment_reduce.
+ */
+int gdl_segment_reduce_backward(const float *grad_out, const void *msg, int32_t dtype, const float *out,
+                                const int32_t *arg, int64_t num_rows, int64_t C, const int32_t *perm,
+                                const int32_t *node_start, const int32_t *node_end, int64_t num_nodes, int32_t reduce,
+                                void *grad_msg, void *workspace, size_t workspace_bytes, void *stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* GDL_B200_H */

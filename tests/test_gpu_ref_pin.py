@@ -1,0 +1,134 @@
+"""Pin against the reference's own CUDA kernels, run on the same B200.
+
+The reference extensions are built from the unmodified sources by oracle/build_ref.py
+(output in oracle/_ref, shipped with the repository snapshot). These tests
+
+1. pin the squared-distance rounding of the reference kernels by comparing the distances
+   its KNN returns bit-for-bit with each candidate rounding of the CPU checker;
+2. compare every B200 operator with the corresponding reference kernel on seeded inputs,
+   including inputs built to produce exact distance ties (points on a coarse lattice),
+   where the reference's heap / reduction order decides the result.
+
+Integer outputs must be identical; sums too (same sequential fold).
+"""
+
+import numpy as np
+import pytest
+import torch
+
+from tests import ref_cuda
+
+pytestmark = [pytest.mark.gpu,
+              pytest.mark.skipif(not torch.cuda.is_available(), reason="needs a CUDA device")]
+
+DEV = "cuda"
+
+
+@pytest.fixture(scope="module")
+def ref():
+    if not ref_cuda.available():
+        pytest.skip("reference CUDA extensions not built (oracle/build_ref.py)")
+    return {n: ref_cuda.load(n) for n in ("fps", "knn", "radius_graph", "segment_reduce")}
+
+
+def _clouds(seed, sizes, kind="uniform", scale=1.0):
+    g = torch.Generator().manual_seed(seed)
+    n = int(sum(sizes))
+    if kind == "lattice":  # exact ties everywhere
+        x = torch.randint(0, 6, (n, 3), generator=g).float() * 0.25 * scale
+    elif kind == "dup":  # many duplicated points
+        base = torch.rand(max(n // 8, 1), 3, generator=g) * scale
+        x = base[torch.randint(0, base.shape[0], (n,), generator=g)]
+    else:
+        x = (torch.rand(n, 3, generator=g) * 2 - 1) * scale
+    ptr = torch.tensor(np.concatenate([[0], np.cumsum(sizes)]), dtype=torch.int64)
+    return x.contiguous(), ptr
+
+
+def test_distance_rounding_pinned(ref, oracle):
+    """The KNN distances of the reference kernel equal exactly one CPU rounding mode."""
+    match = {m: True for m in oracle.DIST_MODES}
+    for seed, scale in [(0, 1.0), (1, 1e-3), (2, 37.0), (3, 1e4)]:
+        x, ptr = _clouds(seed, [700, 300], scale=scale)
+        q, pq = _clouds(seed + 100, [200, 100], scale=scale)
+        idx, d = ref["knn"].knn_cuda(q.to(DEV), x.to(DEV), pq.to(DEV), ptr.to(DEV), 8)
+        idx, d = idx.cpu().numpy(), d.cpu().numpy()
+        qn, xn = q.numpy(), x.numpy()
+        for name, mode in oracle.DIST_MODES.items():
+            valid = idx >= 0
+            qi = np.repeat(np.arange(qn.shape[0]), idx.shape[1]).reshape(idx.shape)
+            # recompute the reference's selected pairs with this mode
+            dd = np.array([oracle.knn(qn[a:a + 1], xn[b:b + 1], [0, 1], [0, 1], 1, dist=mode)[1][0, 0]
+                           for a, b in zip(qi[valid][:400], idx[valid][:400])], np.float32)
+            if not np.array_equal(dd.view(np.uint32), d[valid][:400].view(np.uint32)):
+                match[name] = False
+    winners = [m for m, ok in match.items() if ok]
+    print("distance modes matching the reference kernel:", winners)
+    assert oracle.DIST_CUDA in [oracle.DIST_MODES[w] for w in winners], winners
+
+
+@pytest.mark.parametrize("kind", ["uniform", "lattice", "dup"])
+@pytest.mark.parametrize("tie", ["reference"])
+def test_fps_vs_reference_kernel(ref, kind, tie):
+    from gdl_b200 import csrc
+
+    for seed, sizes, k in [(0, [2048] * 4, 512), (1, [300, 1000, 7, 5000], 200), (2, [9000], 700)]:
+        x, ptr = _clouds(seed, sizes, kind)
+        kk = torch.clamp(ptr[1:] - ptr[:-1], max=k)
+        want = ref["fps"].fps_cuda(x.to(DEV), ptr.to(DEV), kk.to(DEV)).cpu()
+        got = csrc.fps_cuda(x.to(DEV), ptr, kk, tie_break=tie).cpu()
+        assert torch.equal(got, want), f"{kind} seed {seed}: first diff at {(got != want).nonzero()[:3]}"
+
+
+@pytest.mark.parametrize("kind", ["uniform", "lattice", "dup"])
+@pytest.mark.parametrize("k", [1, 4, 7, 16, 32, 64, 80])
+def test_knn_vs_reference_kernel(ref, kind, k):
+    from gdl_b200 import csrc
+
+    x, ptr = _clouds(11, [1500, 40, 3000], kind)
+    q, pq = _clouds(12, [300, 10, 700], kind)
+    wi, wd = ref["knn"].knn_cuda(q.to(DEV), x.to(DEV), pq.to(DEV), ptr.to(DEV), k)
+    gi, gd = csrc.knn_cuda(q.to(DEV), x.to(DEV), pq.to(DEV), ptr.to(DEV), k)
+    assert torch.equal(gi.cpu(), wi.cpu())
+    assert torch.equal(gd.cpu().view(torch.int32), wd.cpu().view(torch.int32))
+
+
+def _edge_set(row, col):
+    r = row.cpu().numpy().astype(np.int64)
+    c = col.cpu().numpy().astype(np.int64)
+    return np.unique(c * (1 << 32) + r)
+
+
+@pytest.mark.parametrize("kind", ["uniform", "lattice", "dup"])
+@pytest.mark.parametrize("max_nn", [16, 32, 64])
+@pytest.mark.parametrize("loop", [False, True])
+def test_radius_vs_reference_kernel(ref, kind, max_nn, loop):
+    from gdl_b200 import csrc
+
+    B, n = 3, 1500
+    x, _ = _clouds(21, [B * n], kind)
+    g = torch.Generator().manual_seed(5)
+    mask = torch.rand(B * n, generator=g) > 0.15
+    for r in (0.15, 0.4):
+        for m in (None, mask):
+            mt = torch.empty(0, dtype=torch.bool) if m is None else m
+            wr, wc = ref["radius_graph"].radius_graph_cuda_batched(x.to(DEV), r, max_nn, mt.to(DEV), loop, B, n)
+            gr, gc = csrc.radius_graph_cuda(x.to(DEV), r, max_num_neighbors=max_nn, loop=loop, mask=m,
+                                            batch_size=B, points_per_batch=n)
+            assert np.array_equal(_edge_set(gr, gc), _edge_set(wr, wc)), (kind, r, m is not None)
+
+
+def test_csr_and_sum_vs_reference_kernel(ref):
+    from gdl_b200 import csrc
+
+    g = torch.Generator().manual_seed(3)
+    for N, E, C in [(500, 3000, 32), (70000, 400000, 64), (1, 50, 6), (5000, 0, 8)]:
+        col = torch.randint(0, N, (E,), generator=g).to(DEV)
+        msg = torch.randn(E, C, generator=g).to(DEV)
+        want = ref["segment_reduce"].sort_and_build_csr(col, N)
+        got = csrc.sort_and_build_csr_cuda(col, N)
+        for a, b in zip(got, want):
+            assert torch.equal(a.cpu(), b.cpu())
+        ws = ref["segment_reduce"].segment_reduce_sum(msg, want[1], want[2], want[3], N)
+        gs = csrc.segment_reduce_sum_cuda(msg, got[1], got[2], got[3], N)
+        assert torch.equal(gs.cpu().view(torch.int32), ws.cpu().view(torch.int32))
