@@ -26,7 +26,6 @@ import argparse
 import json
 import os
 import statistics
-import subprocess
 import sys
 import threading
 import time
@@ -85,40 +84,52 @@ class C2:
         self.ws_rad = nat.workspace(L.gdl_radius_graph_workspace_size(self.nc, self.B, self.NN), dev)
         self.ws_seg = nat.workspace(L.gdl_segment_reduce_workspace_size(self.cap, self.nc), dev)
 
-    # kernels of this library launched per step (fps 1; radius 25: grid, keys, radix sort
-    # 1 + 4 x 4, gather, query, scan 3, compact; segment fwd 2 + bwd 2)
-    launches_per_step = 1 + 25 + 2 + 2
+        # static intermediates, so that every stage can be captured as its own CUDA graph
+        self.cent = torch.empty(self.nc, 3, dtype=torch.float32, device=dev)  # written by FPS
+        self.row_ptr32 = torch.zeros(self.nc + 1, dtype=torch.int32, device=dev)
+        self.ns, self.ne = self.row_ptr32[:-1], self.row_ptr32[1:]
+        self.src32 = torch.zeros(self.cap, dtype=torch.int32, device=dev)
 
-    def step(self, ev=None):
-        L, s = self.L, torch.cuda.current_stream(self.dev).cuda_stream
-        rec = (lambda i: ev[i].record()) if ev else (lambda i: None)
-        rec(0)
-        nat.check(L.gdl_fps(self.pos.data_ptr(), self.ptr.data_ptr(), self.k.data_ptr(), self.B, self.n_points,
-                            self.N, 0, self.idx.data_ptr(), self.ws_fps.data_ptr(), self.ws_fps.numel(), s), "fps")
-        rec(1)
-        cent = self.pos.index_select(0, self.idx)
-        rec(2)
-        nat.check(L.gdl_radius_graph(cent.data_ptr(), self.cptr.data_ptr(), self.B, self.nc, self.R, self.NN, 0, None,
-                                     self.row_ptr.data_ptr(), self.src.data_ptr(), self.dst.data_ptr(),
-                                     self.ws_rad.data_ptr(), self.ws_rad.numel(), s), "radius")
-        rec(3)
-        ns = self.row_ptr[:-1].to(torch.int32)
-        ne = self.row_ptr[1:].to(torch.int32)
-        src32 = self.src.to(torch.int32)
-        rec(4)
-        # messages = source-point features gathered by the CSR (perm = src), mean per destination
-        nat.check(L.gdl_segment_reduce(self.feat.data_ptr(), 0, self.nc, self.C, src32.data_ptr(), ns.data_ptr(),
-                                       ne.data_ptr(), self.nc, 1, self.out.data_ptr(), None, self.ws_seg.data_ptr(),
-                                       self.ws_seg.numel(), s), "segment mean")
-        rec(5)
+    # kernels of this library launched per step (fps 1; radius graph 2 (fused per-cloud kernel
+    # + compaction); segment fwd 2 + bwd 2)
+    launches_per_step = 1 + 2 + 2 + 2
+
+    def _s(self):
+        return torch.cuda.current_stream(self.dev).cuda_stream
+
+    def stage_fps(self):
+        nat.check(self.L.gdl_fps(self.pos.data_ptr(), self.ptr.data_ptr(), self.k.data_ptr(), self.B, self.n_points,
+                                 self.N, 0, self.idx.data_ptr(), self.cent.data_ptr(), self.ws_fps.data_ptr(),
+                                 self.ws_fps.numel(), self._s()), "fps")
+
+    def stage_radius(self):
+        nat.check(self.L.gdl_radius_graph(self.cent.data_ptr(), self.cptr.data_ptr(), self.B, self.nc, self.K, self.R,
+                                          self.NN, 0, None, self.row_ptr.data_ptr(), self.src.data_ptr(),
+                                          self.dst.data_ptr(), self.row_ptr32.data_ptr(), self.src32.data_ptr(),
+                                          self.ws_rad.data_ptr(), self.ws_rad.numel(), self._s()), "radius")
+
+    def stage_seg_fwd(self):
+        # messages = source-point features gathered through the CSR (perm = src), mean per destination
+        nat.check(self.L.gdl_segment_reduce(self.feat.data_ptr(), 0, self.nc, self.C, self.src32.data_ptr(),
+                                            self.ns.data_ptr(), self.ne.data_ptr(), self.nc, 1, self.out.data_ptr(),
+                                            None, self.ws_seg.data_ptr(), self.ws_seg.numel(), self._s()),
+                  "segment mean")
+
+    def stage_seg_bwd(self):
         # gradient w.r.t. the per-edge messages (slot-indexed rows)
-        nat.check(L.gdl_segment_reduce_backward(self.gout.data_ptr(), None, 0, None, None, self.cap, self.C, None,
-                                                ns.data_ptr(), ne.data_ptr(), self.nc, 1, self.gmsg.data_ptr(),
-                                                self.ws_seg.data_ptr(), self.ws_seg.numel(), s), "segment mean bwd")
-        rec(6)
-        return self.out
+        nat.check(self.L.gdl_segment_reduce_backward(self.gout.data_ptr(), None, 0, None, None, self.cap, self.C, None,
+                                                     self.ns.data_ptr(), self.ne.data_ptr(), self.nc, 1,
+                                                     self.gmsg.data_ptr(), self.ws_seg.data_ptr(),
+                                                     self.ws_seg.numel(), self._s()), "segment mean bwd")
 
-    stages = {"fps": (0, 1), "radius_graph": (2, 3), "segment_mean_fwd": (4, 5), "segment_mean_bwd": (5, 6)}
+    def stage_list(self):
+        return [("fps", self.stage_fps), ("radius_graph", self.stage_radius),
+                ("segment_mean_fwd", self.stage_seg_fwd), ("segment_mean_bwd", self.stage_seg_bwd)]
+
+    def step(self):
+        for _, fn in self.stage_list():
+            fn()
+        return self.out
 
     def stage_bytes(self, E):
         """algorithmic bytes per launch of each stage"""
@@ -134,11 +145,11 @@ class C2:
         """Public API, host buffers in and out."""
         pos = self.pos_h.to(self.dev, non_blocking=True)
         feat = self.feat_h.to(self.dev, non_blocking=True)
-        idx = F.farthest_point_sampling(pos, self.K, ptr=self.ptr_h)
-        cent = pos[idx]
-        row_ptr, src, _ = F.radius_graph_csr(cent, self.R, self.cptr, max_num_neighbors=self.NN)
-        ns, ne = row_ptr[:-1], row_ptr[1:]
-        out = csrc.segment_reduce_cuda(feat, src, ns, ne, self.nc, "mean")
+        idx, cent = csrc.fps_cuda(pos, self.ptr_h, self.k_h, return_pos=True)
+        row_ptr, src, _, rp32, src32 = csrc.radius_graph_csr(cent, self.R, self.cptr_h, max_num_neighbors=self.NN,
+                                                             int32_csr=True)
+        ns, ne = rp32[:-1], rp32[1:]
+        out = csrc.segment_reduce_cuda(feat, src32, ns, ne, self.nc, "mean")
         g = csrc.segment_reduce_backward_cuda(self.gout, self.gmsg, None, None, None, ns, ne, self.nc, "mean",
                                               grad_msg=self.gmsg)
         host = out.to("cpu", non_blocking=True)
@@ -166,52 +177,51 @@ CONFIGS = {"c2": C2}
 
 # ----------------------------------------------------------------------------- helpers
 class ClockSampler:
-    """nvidia-smi samples (200 ms) of this GPU while the timed region runs."""
+    """NVML samples (every 10 ms) of this GPU's SM clock and throttle reasons while the
+    timed region runs."""
 
-    FIELDS = "index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active," \
-             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown," \
-             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap"
+    REASONS = {"hw_slowdown": 0x8, "hw_thermal_slowdown": 0x40, "sw_thermal_slowdown": 0x20,
+               "sw_power_cap": 0x4, "hw_power_brake_slowdown": 0x80}
 
-    def __init__(self, gpu_index: int):
-        self.idx = gpu_index
-        self.rows = []
-        self.proc = None
+    def __init__(self, gpu_index: int, period_s: float = 0.01):
+        self.idx, self.period = gpu_index, period_s
+        self.sm, self.reasons, self.max_mhz = [], set(), None
+        self._stop = threading.Event()
+
+    def _sample(self, nv, h):
+        self.sm.append(nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM))
+        r = nv.nvmlDeviceGetCurrentClocksEventReasons(h)
+        for name, bit in self.REASONS.items():
+            if r & bit:
+                self.reasons.add(name)
+
+    def _run(self):
+        try:
+            import pynvml as nv
+
+            nv.nvmlInit()
+            h = nv.nvmlDeviceGetHandleByIndex(self.idx)
+            self.max_mhz = nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM)
+            self._sample(nv, h)
+            while not self._stop.wait(self.period):
+                self._sample(nv, h)
+            self._sample(nv, h)
+        except Exception as e:  # no NVML: report nothing rather than guess
+            self.error = repr(e)
 
     def __enter__(self):
-        try:
-            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.idx}", f"--query-gpu={self.FIELDS}",
-                                          "--format=csv,noheader,nounits", "-lms", "200"],
-                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
-            self.thread = threading.Thread(target=self._read, daemon=True)
-            self.thread.start()
-        except Exception:
-            self.proc = None
+        self.thread = threading.Thread(target=self._run, daemon=True)
+        self.thread.start()
+        time.sleep(0.02)
         return self
 
-    def _read(self):
-        for line in self.proc.stdout:
-            self.rows.append([c.strip() for c in line.split(",")])
-
     def __exit__(self, *a):
-        if self.proc:
-            self.proc.terminate()
-            try:
-                self.proc.wait(timeout=5)
-            except Exception:
-                self.proc.kill()
+        self._stop.set()
+        self.thread.join(timeout=5)
 
     def summary(self):
-        sm = [float(r[1]) for r in self.rows if len(r) >= 9 and r[1].replace(".", "").isdigit()]
-        mx = [float(r[2]) for r in self.rows if len(r) >= 9 and r[2].replace(".", "").isdigit()]
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        reasons = set()
-        for r in self.rows:
-            if len(r) >= 9:
-                for n, v in zip(names, r[5:9]):
-                    if v.strip().lower() == "active":
-                        reasons.add(n)
-        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
-                "reasons": sorted(reasons), "samples": len(self.rows)}
+        return {"sm_mhz": statistics.median(self.sm) if self.sm else None, "sm_max_mhz": self.max_mhz,
+                "reasons": sorted(self.reasons), "samples": len(self.sm)}
 
 
 def measured_peak():
@@ -306,50 +316,71 @@ def run_ours(args, cfg_cls):
     torch.cuda.set_device(dev)
     cfg = cfg_cls(dev, seed=1000 * rank)
     flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
-    nev = 7
+    stages = cfg.stage_list()
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(len(stages) + 1)]
     for _ in range(max(args.warmup, 3)):
         cfg.step()
     torch.cuda.synchronize(dev)
+
+    # each stage captured as one CUDA graph; events between the replays time the stages
+    runners = [fn for _, fn in stages]
+    launch = "eager"
+    if not args.eager:
+        try:
+            graphs = []
+            for _, fn in stages:
+                g = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(g):
+                    fn()
+                graphs.append(g)
+            runners = [g.replay for g in graphs]
+            launch = "one CUDA graph per stage"
+        except Exception as e:  # keep going eagerly, say so in the line
+            print(f"[bench] graph capture failed, eager launches: {e!r}", file=sys.stderr)
+        torch.cuda.synchronize(dev)
 
     def barrier():
         if ws > 1:
             torch.distributed.barrier()
         torch.cuda.synchronize(dev)
 
-    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(nev)] for _ in range(args.steps)]
-    step_ms = []
+    step_ms, stage_acc = [], [0.0] * len(stages)
     barrier()
     with ClockSampler(dev.index if dev.index is not None else 0) as clk:
-        for i in range(args.steps):
+        for _ in range(args.steps):
             flush.zero_()
-            cfg.step(evs[i])
-        torch.cuda.synchronize(dev)
+            ev[0].record()
+            for i, run in enumerate(runners):
+                run()
+                ev[i + 1].record()
+            ev[-1].synchronize()
+            step_ms.append(ev[0].elapsed_time(ev[-1]))
+            for i in range(len(stages)):
+                stage_acc[i] += ev[i].elapsed_time(ev[i + 1])
     barrier()
-    for e in evs:
-        step_ms.append(e[0].elapsed_time(e[-1]))
     total_ms = sum(step_ms)
-    stage_ms = {k: sum(e[b].elapsed_time(e[c]) for e in evs) / args.steps for k, (b, c) in cfg.stages.items()}
+    stage_ms = {name: stage_acc[i] / args.steps for i, (name, _) in enumerate(stages)}
     E = int(cfg.row_ptr[-1].item())
 
-    # end-to-end through the public API
-    for _ in range(2):
-        cfg.e2e_step()
-    barrier()
-    t0 = time.perf_counter()
-    e2e_steps = max(3, min(args.steps, 20))
-    for _ in range(e2e_steps):
-        cfg.e2e_step()
-    e2e_ms = 1000 * (time.perf_counter() - t0) / e2e_steps
+    # end-to-end through the public API, host buffers in and out
+    e2e_ms = None
+    if not args.no_e2e:
+        for _ in range(2):
+            cfg.e2e_step()
+        barrier()
+        e2e_steps = max(3, min(args.steps, 50))
+        t0 = time.perf_counter()
+        for _ in range(e2e_steps):
+            cfg.e2e_step()
+        e2e_ms = 1000 * (time.perf_counter() - t0) / e2e_steps
 
-    t = torch.tensor([total_ms, e2e_ms], dtype=torch.float64, device=dev)
+    t = torch.tensor([total_ms, e2e_ms or 0.0], dtype=torch.float64, device=dev)
     if ws > 1:
         torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
-    total_ms, e2e_ms = float(t[0]), float(t[1])
+    total_ms, e2e_ms = float(t[0]), (float(t[1]) if e2e_ms is not None else None)
     pts = cfg.B * cfg.N
     value = ws * pts * args.steps / (total_ms / 1000)
-    e2e_val = ws * pts / (e2e_ms / 1000)
 
-    line = None
     if rank == 0:
         peak, peak_kind = measured_peak()
         dom = max(stage_ms, key=stage_ms.get)
@@ -359,23 +390,26 @@ def run_ours(args, cfg_cls):
             "metric": cfg.metric, "value": value, "unit": "points/s", "n_gpus": ws, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": total_ms / args.steps, "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-            "config": {"workload": f"{cfg.name}: {cfg.B} clouds x {cfg.N} points per rank", "clouds": cfg.B,
+            "config": {"workload": f"{cfg.name}: {cfg.B} clouds x {cfg.N} points per GPU", "clouds": cfg.B,
                        "points_per_cloud": cfg.N, "edges": E, "l2": "flushed between steps (256 MiB write)",
+                       "launch": launch,
                        "parallelism": f"clouds sharded over {ws} GPU(s), no collective in a step"},
             "stage_ms": stage_ms,
             "roofline": {"kernel": dom, "bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak, "traffic": ncu_traffic(dom),
-                         "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured"
-                         else "fallback 6.65 TB/s",
+                         "peak_source": (f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured"
+                                         else "fallback 6.65 TB/s"),
                          "algorithmic_bytes_per_launch": algo},
-            "e2e": {"value": e2e_val, "unit": "points/s", "h2d_bytes_per_step": cfg.e2e_h2d,
-                    "d2h_bytes_per_step": cfg.e2e_d2h},
             "gpu_launches": cfg.launches_per_step * args.steps,
             "clocks": clk.summary(),
         }
+        if e2e_ms is not None:
+            line["e2e"] = {"value": ws * pts / (e2e_ms / 1000), "unit": "points/s",
+                           "h2d_bytes_per_step": cfg.e2e_h2d, "d2h_bytes_per_step": cfg.e2e_d2h}
         if not args.no_cpu_baseline:
             line["cpu_baseline"] = cpu_baseline(cfg, seconds=args.cpu_seconds)
         print(json.dumps(line), flush=True)
+    runners = None
     if ws > 1:
         torch.distributed.barrier()
         torch.distributed.destroy_process_group()
@@ -385,12 +419,14 @@ def run_ours(args, cfg_cls):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--config", default="c2", choices=sorted(CONFIGS))
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--eager", action="store_true", help="launch kernels one by one instead of a CUDA graph")
     args = ap.parse_args()
     cfg_cls = CONFIGS[args.config]
     if args.impl == "reference":

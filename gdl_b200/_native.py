@@ -25,11 +25,13 @@ PROTOTYPES = {
     "gdl_status_string": (ctypes.c_char_p, [ctypes.c_int]),
     "gdl_check_device": (ctypes.c_int, [ctypes.c_int]),
     "gdl_fps_workspace_size": (_SZ, [_I64, _I64]),
-    "gdl_fps": (ctypes.c_int, [_P, _P, _P, _I32, _I64, _I64, _I32, _P, _P, _SZ, _P]),
+    "gdl_fps": (ctypes.c_int, [_P, _P, _P, _I32, _I64, _I64, _I32, _P, _P, _P, _SZ, _P]),
     "gdl_knn_workspace_size": (_SZ, [_I64, _I32, _I32, _I64]),
     "gdl_knn": (ctypes.c_int, [_P, _P, _P, _P, _I32, _I64, _I32, _I64, _P, _P, _P, _SZ, _P]),
     "gdl_radius_graph_workspace_size": (_SZ, [_I64, _I32, _I32]),
-    "gdl_radius_graph": (ctypes.c_int, [_P, _P, _I32, _I64, ctypes.c_double, _I32, _I32, _P, _P, _P, _P, _P, _SZ, _P]),
+    "gdl_radius_graph": (ctypes.c_int,
+                         [_P, _P, _I32, _I64, _I64, ctypes.c_double, _I32, _I32, _P, _P, _P, _P, _P, _P, _P, _SZ,
+                          _P]),
     "gdl_sort_and_build_csr_workspace_size": (_SZ, [_I64, _I64]),
     "gdl_sort_and_build_csr": (ctypes.c_int, [_P, _I64, _I64, _P, _P, _P, _P, _P, _SZ, _P]),
     "gdl_segment_reduce_workspace_size": (_SZ, [_I64, _I64]),

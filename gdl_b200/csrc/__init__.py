@@ -56,13 +56,14 @@ def fps_available() -> bool:
 
 # --------------------------------------------------------------------------- FPS
 def fps_cuda(pos: torch.Tensor, ptr: torch.Tensor, k_per_batch: torch.Tensor, *,
-             tie_break: str = "reference") -> torch.Tensor:
+             tie_break: str = "reference", return_pos: bool = False):
     """Farthest point sampling per cloud (reference: csrc/__init__.py:566-597,
     fps_kernel.cu:160-209). Returns int64 global indices, cloud b's picks at offset
     sum_{c<b} k_c; a cloud with k > n yields n indices followed by -1.
 
     One device->host copy of ``ptr``/``k_per_batch`` sizes the output (the reference
-    also synchronises once, fps_kernel.cu:183); pass CPU tensors to avoid it.
+    also synchronises once, fps_kernel.cu:183); pass CPU tensors to avoid it. With
+    ``return_pos`` also returns the picked coordinates [total, 3] (written by the kernel).
     """
     dev = nat.require_cuda(pos, what="fps_cuda")
     pos = pos.contiguous().float()
@@ -71,16 +72,19 @@ def fps_cuda(pos: torch.Tensor, ptr: torch.Tensor, k_per_batch: torch.Tensor, *,
     ptr_h, k_h = host[: B + 1], host[B + 1:]
     total = int(k_h.clamp(min=0).sum()) if B > 0 else 0
     if total <= 0 or pos.shape[0] == 0:
-        return torch.empty(0, dtype=torch.int64, device=dev)
+        e = torch.empty(0, dtype=torch.int64, device=dev)
+        return (e, torch.empty(0, 3, device=dev)) if return_pos else e
     max_n = int((ptr_h[1:] - ptr_h[:-1]).max())
     ptr_d = ptr_h.to(dev, non_blocking=True) if not ptr.is_cuda else ptr.to(torch.int64).contiguous()
     k_d = k_h.to(dev, non_blocking=True) if not k_per_batch.is_cuda else k_per_batch.to(torch.int64).contiguous()
     out = torch.empty(total, dtype=torch.int64, device=dev)
+    opos = torch.empty(total, 3, dtype=torch.float32, device=dev) if return_pos else None
     L = nat.load()
     ws = nat.workspace(L.gdl_fps_workspace_size(pos.shape[0], max_n), dev)
     nat.check(L.gdl_fps(pos.data_ptr(), ptr_d.data_ptr(), k_d.data_ptr(), B, pos.shape[0], max_n,
-                        nat.TIE[tie_break], out.data_ptr(), ws.data_ptr(), ws.numel(), nat.stream(dev)), "gdl_fps")
-    return out
+                        nat.TIE[tie_break], out.data_ptr(), nat.ptr(opos), ws.data_ptr(), ws.numel(),
+                        nat.stream(dev)), "gdl_fps")
+    return (out, opos) if return_pos else out
 
 
 # --------------------------------------------------------------------------- KNN
@@ -122,32 +126,42 @@ def knn_self_cuda(points: torch.Tensor, ptr: torch.Tensor, k: int) -> Tuple[torc
 
 # --------------------------------------------------------------------------- radius graph
 def radius_graph_csr(x: torch.Tensor, r: float, ptr: torch.Tensor, *, max_num_neighbors: int = 32,
-                     loop: bool = False, mask: Optional[torch.Tensor] = None, with_dst: bool = True):
+                     loop: bool = False, mask: Optional[torch.Tensor] = None, with_dst: bool = True,
+                     max_cloud_points: Optional[int] = None, int32_csr: bool = False):
     """Radius graph of packed clouds as a destination CSR, without a host sync.
 
     Returns (row_ptr [N+1] int64, src [cap] int64, dst [cap] int64 or None); the first
     row_ptr[N] entries of src/dst are the edges (row=src=neighbour, col=dst=query),
     grouped by destination with ascending sources. cap = N * bucket(max_num_neighbors).
+    ``max_cloud_points`` (taken from ``ptr`` when it is a CPU tensor) lets clouds of up to
+    4096 points use the fused one-CTA-per-cloud kernels. ``int32_csr`` appends
+    (row_ptr32 [N+1], src32 [cap]) int32 copies, the layout segment_reduce_cuda consumes.
     """
     dev = nat.require_cuda(x, what="radius_graph")
     x = x.contiguous().float()
     N = x.shape[0]
+    if max_cloud_points is None:
+        max_cloud_points = int((ptr[1:] - ptr[:-1]).max()) if (not ptr.is_cuda and ptr.numel() > 1) else 0
     ptr = ptr.to(device=dev, dtype=torch.int64).contiguous()
     B = ptr.numel() - 1
     cap_k = 16 if max_num_neighbors <= 16 else 32 if max_num_neighbors <= 32 else 64
     row_ptr = torch.empty(N + 1, dtype=torch.int64, device=dev)
     src = torch.empty(max(N * cap_k, 1), dtype=torch.int64, device=dev)
     dst = torch.empty_like(src) if with_dst else None
+    rp32 = torch.empty(N + 1, dtype=torch.int32, device=dev) if int32_csr else None
+    src32 = torch.empty(src.numel(), dtype=torch.int32, device=dev) if int32_csr else None
     m = None
     if mask is not None and mask.numel() > 0:
         m = mask.to(device=dev).contiguous()
         m = m.view(torch.uint8) if m.dtype == torch.bool else m.to(torch.uint8)
     L = nat.load()
     ws = nat.workspace(L.gdl_radius_graph_workspace_size(N, B, int(max_num_neighbors)), dev)
-    nat.check(L.gdl_radius_graph(x.data_ptr() if N else None, ptr.data_ptr(), B, N, float(r), int(max_num_neighbors),
+    nat.check(L.gdl_radius_graph(x.data_ptr() if N else None, ptr.data_ptr(), B, N, int(max_cloud_points), float(r),
+                                 int(max_num_neighbors),
                                  int(bool(loop)), nat.ptr(m), row_ptr.data_ptr(), src.data_ptr(), nat.ptr(dst),
-                                 ws.data_ptr(), ws.numel(), nat.stream(dev)), "gdl_radius_graph")
-    return row_ptr, src, dst
+                                 nat.ptr(rp32), nat.ptr(src32), ws.data_ptr(), ws.numel(), nat.stream(dev)),
+              "gdl_radius_graph")
+    return (row_ptr, src, dst, rp32, src32) if int32_csr else (row_ptr, src, dst)
 
 
 def radius_graph_cuda(x: torch.Tensor, r: float, *, max_num_neighbors: int = 32, loop: bool = False,
@@ -163,7 +177,7 @@ def radius_graph_cuda(x: torch.Tensor, r: float, *, max_num_neighbors: int = 32,
         ptr = torch.arange(0, batch_size + 1, dtype=torch.int64) * int(points_per_batch)
     else:
         ptr = torch.tensor([0, N], dtype=torch.int64)
-    row_ptr, src, dst = radius_graph_csr(x, r, ptr.to(dev), max_num_neighbors=max_num_neighbors, loop=loop, mask=mask)
+    row_ptr, src, dst = radius_graph_csr(x, r, ptr, max_num_neighbors=max_num_neighbors, loop=loop, mask=mask)
     E = int(row_ptr[N].item())
     return src[:E], dst[:E]
 

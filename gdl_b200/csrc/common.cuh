@@ -48,13 +48,13 @@ __device__ __forceinline__ float fma_ftz(float a, float b, float c) {
 
 // Squared distance with the rounding of the reference kernels' `dx*dx + dy*dy + dz*dz`
 // (fps_kernel.cu:91-94, knn_kernel.cu:149-152, radius_graph_kernel.cu:224-227) as nvcc
-// contracts it: fma(dz, dz, fma(dy, dy, dx*dx)), flush-to-zero. Pinned against the
-// distances the reference KNN kernel returns on a B200.
+// contracts it: fma(dz, dz, fma(dx, dx, dy*dy)), flush-to-zero. Pinned bit-for-bit against
+// the distances the reference KNN kernel returns on a B200 (the other contractions differ).
 __device__ __forceinline__ float dist2(float ax, float ay, float az, float bx, float by, float bz) {
     const float dx = sub_ftz(ax, bx);
     const float dy = sub_ftz(ay, by);
     const float dz = sub_ftz(az, bz);
-    return fma_ftz(dz, dz, fma_ftz(dy, dy, mul_ftz(dx, dx)));
+    return fma_ftz(dz, dz, fma_ftz(dx, dx, mul_ftz(dy, dy)));
 }
 
 // ---------------------------------------------------------------- warp helpers
@@ -140,5 +140,50 @@ struct MinKHeap {
         }
     }
 };
+
+// The same heap as free functions over caller-owned arrays, so the counter stays in a
+// register while only the arrays live in local memory.
+__device__ __forceinline__ void heap_sift_down(float *d, int *id, int cap, int at) {
+    for (;;) {
+        int l = 2 * at + 1, r = 2 * at + 2, g = at;
+        if (l < cap && d[l] > d[g]) g = l;
+        if (r < cap && d[r] > d[g]) g = r;
+        if (g == at) break;
+        const float td = d[at];
+        d[at] = d[g];
+        d[g] = td;
+        const int ti = id[at];
+        id[at] = id[g];
+        id[g] = ti;
+        at = g;
+    }
+}
+
+__device__ __forceinline__ void heap_add(float *d, int *id, int &count, int cap, float dist, int idx) {
+    if (count >= cap) {
+        if (dist >= d[0]) return;
+        d[0] = dist;
+        id[0] = idx;
+        heap_sift_down(d, id, cap, 0);
+    } else {
+        d[count] = dist;
+        id[count] = idx;
+        ++count;
+        if (count == cap)
+            for (int j = cap / 2 - 1; j >= 0; --j) heap_sift_down(d, id, cap, j);
+    }
+}
+
+__device__ __forceinline__ void sort_ints(int *v, int count) {  // ascending insertion sort
+    for (int a = 1; a < count; ++a) {
+        const int x = v[a];
+        int c = a - 1;
+        while (c >= 0 && v[c] > x) {
+            v[c + 1] = v[c];
+            --c;
+        }
+        v[c + 1] = x;
+    }
+}
 
 }  // namespace gdl

@@ -7,14 +7,20 @@
 // next pick is the argmax. Ties go by a 32-bit priority: either the reference kernel's
 // reduction order (GDL_TIE_REFERENCE, see fps_priority) or the lowest index.
 //
-// Design (B200): a cloud's points and running minima stay in REGISTERS for the whole run
-// (P points per thread); the argmax is a packed 64-bit key (min_d bits, ~priority) reduced with
-// two redux.sync per warp, the warp winners go to a double-buffered shared-memory slot array,
-// one __syncthreads per step, and every warp then reduces the slots redundantly (no second
-// barrier). Clouds above one CTA's register budget use a thread-block cluster (up to 16 CTAs,
-// one per SM): each warp writes its winner straight into every CTA's slot array through
-// distributed shared memory and one cluster barrier per step publishes them. Larger clouds
-// fall back to a CTA that streams points from HBM with min_d in a workspace.
+// Design (B200). The step is a pure latency chain (one argmax per selected point), so the
+// kernel minimises the work between two picks:
+//  * a cloud's coordinates and running minima stay in REGISTERS for the whole run (P points
+//    per thread); a float4 copy of the coordinates in shared memory serves the winner lookup;
+//  * the argmax is a single u64 key (min_d bits << 32 | ~priority): a tree max over the
+//    thread's P keys, two redux.sync per warp, warp winners into a double-buffered slot
+//    array, one __syncthreads, then every warp reduces the slots itself (no second barrier;
+//    a shared-memory u64 atomicMax measured ~300 cycles slower per step here);
+//  * the winner's local index is decoded from its priority (a bijection) and its coordinates
+//    read back from shared memory.
+// Clouds above one CTA's register budget run on a thread-block cluster (up to 16 CTAs, one per
+// SM): each CTA's winner record goes to every CTA of the cluster through distributed shared
+// memory and one cluster barrier per step publishes it. Larger clouds fall back to a CTA that
+// streams points from HBM with min_d in a workspace.
 #include <cooperative_groups.h>
 
 #include "common.cuh"
@@ -34,31 +40,25 @@ __device__ __forceinline__ uint32_t fps_priority(uint32_t i, int tie) {
     return ((__brev(w) >> 28) << 27) | ((__brev(l) >> 27) << 22) | (rj & 0x3fffffu);
 }
 
-struct Cand {  // one warp's (or CTA's) best point
-    uint32_t hi;  // bits of min_d (>= 0, so ordered like the float)
-    uint32_t lo;  // ~priority
-    float x, y, z;
-    int32_t idx;  // local index
-};
-
-__device__ __forceinline__ bool key_gt(uint32_t ahi, uint32_t alo, uint32_t bhi, uint32_t blo) {
-    return ahi > bhi || (ahi == bhi && alo > blo);
+// inverse of fps_priority
+__device__ __forceinline__ uint32_t fps_index(uint32_t prio, int tie) {
+    if (tie == GDL_TIE_LOWEST_INDEX) return prio;
+    const uint32_t w = __brev((prio >> 27) & 15u) >> 28, l = __brev((prio >> 22) & 31u) >> 27;
+    return ((prio & 0x3fffffu) << 9) | (w << 5) | l;
 }
 
-// Reduce a candidate across the warp; every lane returns the winner.
-__device__ __forceinline__ Cand warp_argmax(Cand c) {
-    const uint32_t mhi = __reduce_max_sync(0xffffffffu, c.hi);
-    const uint32_t mlo = __reduce_max_sync(0xffffffffu, c.hi == mhi ? c.lo : 0u);
-    const unsigned win = __ballot_sync(0xffffffffu, c.hi == mhi && c.lo == mlo);
-    const int src = __ffs(win) - 1;
-    Cand r;
-    r.hi = mhi;
-    r.lo = mlo;
-    r.x = __shfl_sync(0xffffffffu, c.x, src);
-    r.y = __shfl_sync(0xffffffffu, c.y, src);
-    r.z = __shfl_sync(0xffffffffu, c.z, src);
-    r.idx = __shfl_sync(0xffffffffu, c.idx, src);
-    return r;
+__device__ __forceinline__ uint64_t make_key(float m, uint32_t np) {
+    return ((uint64_t)__float_as_uint(m) << 32) | np;
+}
+
+__device__ __forceinline__ uint64_t umax64(uint64_t a, uint64_t b) { return a > b ? a : b; }
+
+// max over the warp of a u64 key (hi word first, then lo among the hi winners)
+__device__ __forceinline__ uint64_t warp_max_key(uint64_t k) {
+    const uint32_t hi = (uint32_t)(k >> 32);
+    const uint32_t mhi = __reduce_max_sync(0xffffffffu, hi);
+    const uint32_t mlo = __reduce_max_sync(0xffffffffu, hi == mhi ? (uint32_t)k : 0u);
+    return ((uint64_t)mhi << 32) | mlo;
 }
 
 // out offset of cloud b = sum_{c<b} max(k_c, 0)
@@ -74,17 +74,37 @@ __device__ __forceinline__ int64_t block_out_offset(const int64_t *__restrict__ 
     return t;
 }
 
-// Per-thread register state: P points (strided by THREADS inside a chunk of THREADS*P points).
-template <int P>
+// one selection: global index (and, when requested, its coordinates)
+__device__ __forceinline__ void emit(int64_t *__restrict__ out, float *__restrict__ out_pos, int64_t slot,
+                                     int64_t start, int64_t idx, float x, float y, float z) {
+    out[slot] = start + idx;
+    if (out_pos) {
+        out_pos[3 * slot] = x;
+        out_pos[3 * slot + 1] = y;
+        out_pos[3 * slot + 2] = z;
+    }
+}
+
+// slots [actual, kb) of a cloud that asked for more points than it has: -1 (and 0 coordinates)
+__device__ __forceinline__ void pad_outputs(int64_t *__restrict__ out, float *__restrict__ out_pos, int64_t o0,
+                                            int64_t actual, int64_t kb, int threads) {
+    for (int64_t j = actual + threadIdx.x; j < kb; j += threads) {
+        out[o0 + j] = -1;
+        if (out_pos) out_pos[3 * (o0 + j)] = out_pos[3 * (o0 + j) + 1] = out_pos[3 * (o0 + j) + 2] = 0.0f;
+    }
+}
+
+// Per-thread register state: P points i = base + threadIdx.x + j * THREADS.
+template <int THREADS, int P>
 struct PointRegs {
     float x[P], y[P], z[P], md[P];
-    uint32_t np[P];  // ~priority, 0 for padding lanes
+    uint32_t np[P];  // ~priority; 0 marks a padding slot (never wins)
 
-    __device__ __forceinline__ void load(const float *__restrict__ pos, int64_t start, int n, int chunk_base,
-                                         int threads, int tie) {
+    __device__ __forceinline__ void load(const float *__restrict__ pos, int64_t start, int n, int base, int tie,
+                                         float4 *__restrict__ sxyz) {
 #pragma unroll
         for (int j = 0; j < P; ++j) {
-            const int i = chunk_base + (int)threadIdx.x + j * threads;
+            const int i = base + (int)threadIdx.x + j * THREADS;
             if (i < n) {
                 const float *p = pos + 3 * (start + i);
                 x[j] = p[0];
@@ -92,39 +112,29 @@ struct PointRegs {
                 z[j] = p[2];
                 md[j] = 1e30f;
                 np[j] = ~fps_priority((uint32_t)i, tie);
+                sxyz[i - base] = make_float4(x[j], y[j], z[j], 0.0f);
             } else {
                 x[j] = y[j] = z[j] = 0.0f;
-                md[j] = -1.0f;
+                md[j] = 0.0f;
                 np[j] = 0u;
             }
         }
     }
 
-    // update minima against (sx, sy, sz), return this thread's best candidate
-    __device__ __forceinline__ Cand step(float sx, float sy, float sz, int chunk_base, int threads) {
-        Cand c;
-        c.hi = 0u;
-        c.lo = 0u;
-        c.x = c.y = c.z = 0.0f;
-        c.idx = 0;
+    // update the minima against (sx, sy, sz); this thread's best key (tree max over P)
+    __device__ __forceinline__ uint64_t step(float sx, float sy, float sz) {
+        uint64_t k[P];
 #pragma unroll
         for (int j = 0; j < P; ++j) {
-            if (np[j] != 0u) {
-                const float d = dist2(x[j], y[j], z[j], sx, sy, sz);
-                const float m = fminf(d, md[j]);
-                md[j] = m;
-                const uint32_t h = __float_as_uint(m);
-                if (key_gt(h, np[j], c.hi, c.lo)) {
-                    c.hi = h;
-                    c.lo = np[j];
-                    c.x = x[j];
-                    c.y = y[j];
-                    c.z = z[j];
-                    c.idx = chunk_base + (int)threadIdx.x + j * threads;
-                }
-            }
+            const float m = fminf(dist2(x[j], y[j], z[j], sx, sy, sz), md[j]);
+            md[j] = m;
+            k[j] = np[j] ? make_key(m, np[j]) : 0ull;
         }
-        return c;
+#pragma unroll
+        for (int w = 1; w < P; w <<= 1)
+#pragma unroll
+            for (int j = 0; j + w < P; j += 2 * w) k[j] = umax64(k[j], k[j + w]);
+        return k[0];
     }
 };
 
@@ -133,9 +143,10 @@ template <int THREADS, int P>
 __global__ void __launch_bounds__(THREADS) fps_cta_kernel(const float *__restrict__ pos,
                                                           const int64_t *__restrict__ ptr,
                                                           const int64_t *__restrict__ kpc, int tie,
-                                                          int64_t *__restrict__ out) {
+                                                          int64_t *__restrict__ out, float *__restrict__ out_pos) {
     constexpr int NW = THREADS / 32;
-    __shared__ Cand slots[2][NW];
+    extern __shared__ float4 sxyz[];  // [THREADS * P]
+    __shared__ unsigned long long slots[2][NW];
     __shared__ int64_t red[NW];
     const int b = blockIdx.x;
     const int64_t start = ptr[b];
@@ -144,37 +155,45 @@ __global__ void __launch_bounds__(THREADS) fps_cta_kernel(const float *__restric
     const int64_t o0 = block_out_offset(kpc, b, red);
     if (kb <= 0) return;
     const int64_t actual = n <= 0 ? 0 : (kb < n ? kb : n);
-    for (int64_t j = actual + threadIdx.x; j < kb; j += THREADS) out[o0 + j] = -1;
+    pad_outputs(out, out_pos, o0, actual, kb, THREADS);
     if (actual <= 0) return;
 
-    PointRegs<P> pr;
-    pr.load(pos, start, n, 0, THREADS, tie);
-    if (threadIdx.x == 0) out[o0] = start;
-    float sx = pos[3 * start], sy = pos[3 * start + 1], sz = pos[3 * start + 2];
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    PointRegs<THREADS, P> pr;
+    pr.load(pos, start, n, 0, tie, sxyz);
+    __syncthreads();
+    float4 s = sxyz[0];
+    if (threadIdx.x == 0) emit(out, out_pos, o0, start, 0, s.x, s.y, s.z);
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     for (int64_t k = 1; k < actual; ++k) {
-        Cand c = warp_argmax(pr.step(sx, sy, sz, 0, THREADS));
+        const uint64_t wk = warp_max_key(pr.step(s.x, s.y, s.z));
         const int par = (int)(k & 1);
-        if (lane == 0) slots[par][warp] = c;
+        if (lane == 0) slots[par][warp] = wk;
         __syncthreads();
-        Cand s = lane < NW ? slots[par][lane] : Cand{0u, 0u, 0.0f, 0.0f, 0.0f, 0};
-        s = warp_argmax(s);
-        sx = s.x;
-        sy = s.y;
-        sz = s.z;
-        if (threadIdx.x == 0) out[o0 + k] = start + s.idx;
+        // every warp reduces the warp winners itself: no second barrier; the other parity
+        // buffer takes step k+1's writes while slow warps still read this one
+        const uint64_t best = warp_max_key(lane < NW ? slots[par][lane] : 0ull);
+        const uint32_t idx = fps_index(~(uint32_t)best, tie);
+        s = sxyz[idx];
+        if (threadIdx.x == 0) emit(out, out_pos, o0 + k, start, idx, s.x, s.y, s.z);
     }
 }
 
 // ------------------------------------------------------------------ cluster per cloud
+struct Rec {  // one CTA's best point
+    unsigned long long key;
+    float x, y, z, pad;
+};
+
 template <int THREADS, int P>
 __global__ void __launch_bounds__(THREADS) fps_cluster_kernel(const float *__restrict__ pos,
                                                               const int64_t *__restrict__ ptr,
                                                               const int64_t *__restrict__ kpc, int tie,
-                                                              int64_t *__restrict__ out) {
-    constexpr int NW = THREADS / 32;
+                                                              int64_t *__restrict__ out, float *__restrict__ out_pos) {
     constexpr int kMaxCluster = 16;
-    __shared__ Cand slots[2][kMaxCluster * NW];
+    constexpr int NW = THREADS / 32;
+    extern __shared__ float4 sxyz[];  // this CTA's THREADS * P points
+    __shared__ unsigned long long slots[2][NW];
+    __shared__ Rec recs[2][kMaxCluster];
     __shared__ int64_t red[NW];
     cg::cluster_group cluster = cg::this_cluster();
     const int cs = (int)cluster.num_blocks();
@@ -185,36 +204,48 @@ __global__ void __launch_bounds__(THREADS) fps_cluster_kernel(const float *__res
     const int64_t kb = kpc[b];
     const int64_t o0 = block_out_offset(kpc, b, red);
     const int64_t actual = (kb <= 0 || n <= 0) ? 0 : (kb < n ? kb : n);
-    if (rank == 0)
-        for (int64_t j = actual + threadIdx.x; j < kb; j += THREADS) out[o0 + j] = -1;
-    // every CTA of the cluster runs the same number of steps (uniform exit)
-    const int chunk_base = rank * THREADS * P;
-    PointRegs<P> pr;
-    pr.load(pos, start, n, chunk_base, THREADS, tie);
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int nslots = cs * NW;
-    if (actual > 0 && rank == 0 && threadIdx.x == 0) out[o0] = start;
-    float sx = actual > 0 ? pos[3 * start] : 0.0f, sy = actual > 0 ? pos[3 * start + 1] : 0.0f,
-          sz = actual > 0 ? pos[3 * start + 2] : 0.0f;
-    cluster.sync();  // all CTAs resident before remote shared-memory writes
+    if (rank == 0) pad_outputs(out, out_pos, o0, actual, kb, THREADS);
+    const int base = rank * THREADS * P;
+    PointRegs<THREADS, P> pr;
+    pr.load(pos, start, n, base, tie, sxyz);
+    float sx = 0.0f, sy = 0.0f, sz = 0.0f;
+    if (actual > 0) {
+        sx = pos[3 * start];
+        sy = pos[3 * start + 1];
+        sz = pos[3 * start + 2];
+        if (rank == 0 && threadIdx.x == 0) emit(out, out_pos, o0, start, 0, sx, sy, sz);
+    }
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    cluster.sync();  // every CTA resident and initialised before remote writes
     for (int64_t k = 1; k < actual; ++k) {
-        Cand c = warp_argmax(pr.step(sx, sy, sz, chunk_base, THREADS));
+        const uint64_t wk = warp_max_key(pr.step(sx, sy, sz));
         const int par = (int)(k & 1);
-        if (lane < cs) {  // lane q publishes this warp's winner into CTA q's slot array
-            Cand *dst = cluster.map_shared_rank(&slots[par][rank * NW + warp], lane);
-            *dst = c;
+        if (lane == 0) slots[par][warp] = wk;
+        __syncthreads();
+        if (warp == 0) {  // this CTA's winner, published into every CTA's record slot [rank]
+            const unsigned long long key = warp_max_key(lane < NW ? slots[par][lane] : 0ull);
+            Rec r;
+            r.key = key;
+            if (key != 0ull) {
+                const float4 c = sxyz[fps_index(~(uint32_t)key, tie) - base];
+                r.x = c.x;
+                r.y = c.y;
+                r.z = c.z;
+            } else {
+                r.x = r.y = r.z = 0.0f;
+            }
+            r.pad = 0.0f;
+            if (lane < cs) *cluster.map_shared_rank(&recs[par][rank], lane) = r;
         }
         cluster.sync();
-        Cand s = Cand{0u, 0u, 0.0f, 0.0f, 0.0f, 0};
-        for (int q = lane; q < nslots; q += 32) {
-            const Cand t = slots[par][q];
-            if (key_gt(t.hi, t.lo, s.hi, s.lo)) s = t;
-        }
-        s = warp_argmax(s);
-        sx = s.x;
-        sy = s.y;
-        sz = s.z;
-        if (rank == 0 && threadIdx.x == 0) out[o0 + k] = start + s.idx;
+        const unsigned long long mine = lane < cs ? recs[par][lane].key : 0ull;
+        const uint64_t best = warp_max_key(mine);
+        const int src = __ffs(__ballot_sync(0xffffffffu, lane < cs && mine == best)) - 1;
+        const Rec w = recs[par][src];
+        sx = w.x;
+        sy = w.y;
+        sz = w.z;
+        if (rank == 0 && threadIdx.x == 0) emit(out, out_pos, o0 + k, start, fps_index(~(uint32_t)best, tie), sx, sy, sz);
     }
     cluster.sync();  // no CTA leaves while a peer may still write into it
 }
@@ -227,9 +258,10 @@ __global__ void __launch_bounds__(kStreamThreads) fps_stream_kernel(const float 
                                                                     const int64_t *__restrict__ ptr,
                                                                     const int64_t *__restrict__ kpc, int tie,
                                                                     float *__restrict__ mind,
-                                                                    int64_t *__restrict__ out) {
+                                                                    int64_t *__restrict__ out,
+                                                                    float *__restrict__ out_pos) {
     constexpr int NW = kStreamThreads / 32;
-    __shared__ Cand slots[2][NW];
+    __shared__ unsigned long long slots[2][NW];
     __shared__ int64_t red[NW];
     const int b = blockIdx.x;
     const int64_t start = ptr[b];
@@ -238,41 +270,44 @@ __global__ void __launch_bounds__(kStreamThreads) fps_stream_kernel(const float 
     const int64_t o0 = block_out_offset(kpc, b, red);
     if (kb <= 0) return;
     const int64_t actual = n <= 0 ? 0 : (kb < n ? kb : n);
-    for (int64_t j = actual + threadIdx.x; j < kb; j += kStreamThreads) out[o0 + j] = -1;
+    pad_outputs(out, out_pos, o0, actual, kb, kStreamThreads);
     if (actual <= 0) return;
     float *md = mind + start;
     for (int64_t i = threadIdx.x; i < n; i += kStreamThreads) md[i] = 1e30f;
-    if (threadIdx.x == 0) out[o0] = start;
-    float sx = pos[3 * start], sy = pos[3 * start + 1], sz = pos[3 * start + 2];
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     __syncthreads();
+    float sx = pos[3 * start], sy = pos[3 * start + 1], sz = pos[3 * start + 2];
+    if (threadIdx.x == 0) emit(out, out_pos, o0, start, 0, sx, sy, sz);
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     for (int64_t k = 1; k < actual; ++k) {
-        Cand c{0u, 0u, 0.0f, 0.0f, 0.0f, 0};
+        uint64_t best = 0ull;
         for (int64_t i = threadIdx.x; i < n; i += kStreamThreads) {
             const float *p = pos + 3 * (start + i);
-            const float px = p[0], py = p[1], pz = p[2];
-            const float m = fminf(dist2(px, py, pz, sx, sy, sz), md[i]);
+            const float m = fminf(dist2(p[0], p[1], p[2], sx, sy, sz), md[i]);
             md[i] = m;
-            const uint32_t h = __float_as_uint(m), l = ~fps_priority((uint32_t)i, tie);
-            if (key_gt(h, l, c.hi, c.lo)) c = Cand{h, l, px, py, pz, (int32_t)i};
+            best = umax64(best, make_key(m, ~fps_priority((uint32_t)i, tie)));
         }
-        c = warp_argmax(c);
+        const uint64_t wk = warp_max_key(best);
         const int par = (int)(k & 1);
-        if (lane == 0) slots[par][warp] = c;
+        if (lane == 0) slots[par][warp] = wk;
         __syncthreads();
-        Cand s = slots[par][lane];
-        s = warp_argmax(s);
-        sx = s.x;
-        sy = s.y;
-        sz = s.z;
-        if (threadIdx.x == 0) out[o0 + k] = start + s.idx;
+        const int64_t idx = fps_index(~(uint32_t)warp_max_key(slots[par][lane]), tie);
+        sx = pos[3 * (start + idx)];
+        sy = pos[3 * (start + idx) + 1];
+        sz = pos[3 * (start + idx) + 2];
+        if (threadIdx.x == 0) emit(out, out_pos, o0 + k, start, idx, sx, sy, sz);
     }
 }
 
 template <int T, int P>
 static cudaError_t launch_cta(int B, const float *pos, const int64_t *ptr, const int64_t *kpc, int tie, int64_t *out,
-                              cudaStream_t st) {
-    fps_cta_kernel<T, P><<<B, T, 0, st>>>(pos, ptr, kpc, tie, out);
+                              float *out_pos, cudaStream_t st) {
+    const size_t smem = sizeof(float4) * T * P;
+    auto kern = fps_cta_kernel<T, P>;
+    if (smem > 48 * 1024) {
+        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        if (e != cudaSuccess) return e;
+    }
+    kern<<<B, T, smem, st>>>(pos, ptr, kpc, tie, out, out_pos);
     return cudaGetLastError();
 }
 
@@ -281,16 +316,19 @@ constexpr int kClusterP = 16;
 constexpr int64_t kCtaCapacity = (int64_t)kClusterThreads * kClusterP;  // points per CTA
 
 static cudaError_t launch_cluster(int B, int cs, const float *pos, const int64_t *ptr, const int64_t *kpc, int tie,
-                                  int64_t *out, cudaStream_t st) {
+                                  int64_t *out, float *out_pos, cudaStream_t st) {
     auto kern = fps_cluster_kernel<kClusterThreads, kClusterP>;
+    const size_t smem = sizeof(float4) * kCtaCapacity;
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
     if (cs > 8) {
-        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+        e = cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
         if (e != cudaSuccess) return e;
     }
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((unsigned)(B * cs));
     cfg.blockDim = dim3(kClusterThreads);
-    cfg.dynamicSmemBytes = 0;
+    cfg.dynamicSmemBytes = smem;
     cfg.stream = st;
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeClusterDimension;
@@ -300,9 +338,9 @@ static cudaError_t launch_cluster(int B, int cs, const float *pos, const int64_t
     cfg.attrs = attr;
     cfg.numAttrs = 1;
     int max_clusters = 0;
-    cudaError_t e = cudaOccupancyMaxActiveClusters(&max_clusters, kern, &cfg);
+    e = cudaOccupancyMaxActiveClusters(&max_clusters, kern, &cfg);
     if (e != cudaSuccess || max_clusters < 1) return e != cudaSuccess ? e : cudaErrorInvalidConfiguration;
-    return cudaLaunchKernelEx(&cfg, kern, pos, ptr, kpc, tie, out);
+    return cudaLaunchKernelEx(&cfg, kern, pos, ptr, kpc, tie, out, out_pos);
 }
 
 }  // namespace gdl
@@ -317,7 +355,7 @@ extern "C" size_t gdl_fps_workspace_size(int64_t n_points, int64_t max_cloud_poi
 
 extern "C" int gdl_fps(const float *pos, const int64_t *ptr, const int64_t *k_per_cloud, int32_t num_clouds,
                        int64_t n_points, int64_t max_cloud_points, int32_t tie_break, int64_t *out_idx,
-                       void *workspace, size_t workspace_bytes, void *stream) {
+                       float *out_pos, void *workspace, size_t workspace_bytes, void *stream) {
     cudaStream_t st = (cudaStream_t)stream;
     GDL_RETURN_IF(num_clouds < 0 || max_cloud_points < 0 || n_points < 0, GDL_ERR_INVALID);
     GDL_RETURN_IF(tie_break != GDL_TIE_REFERENCE && tie_break != GDL_TIE_LOWEST_INDEX, GDL_ERR_INVALID);
@@ -326,20 +364,20 @@ extern "C" int gdl_fps(const float *pos, const int64_t *ptr, const int64_t *k_pe
     GDL_RETURN_IF(max_cloud_points >= INT32_MAX, GDL_ERR_OVERFLOW);
     const int64_t m = max_cloud_points;
     cudaError_t e;
-    if (m <= 512) e = launch_cta<128, 4>(num_clouds, pos, ptr, k_per_cloud, tie_break, out_idx, st);
-    else if (m <= 1024) e = launch_cta<256, 4>(num_clouds, pos, ptr, k_per_cloud, tie_break, out_idx, st);
-    else if (m <= 2048) e = launch_cta<256, 8>(num_clouds, pos, ptr, k_per_cloud, tie_break, out_idx, st);
-    else if (m <= 4096) e = launch_cta<256, 16>(num_clouds, pos, ptr, k_per_cloud, tie_break, out_idx, st);
-    else if (m <= kCtaCapacity) e = launch_cta<kClusterThreads, kClusterP>(num_clouds, pos, ptr, k_per_cloud, tie_break, out_idx, st);
+    if (m <= 512) e = launch_cta<128, 4>(num_clouds, pos, ptr, k_per_cloud, tie_break, out_idx, out_pos, st);
+    else if (m <= 1024) e = launch_cta<256, 4>(num_clouds, pos, ptr, k_per_cloud, tie_break, out_idx, out_pos, st);
+    else if (m <= 2048) e = launch_cta<256, 8>(num_clouds, pos, ptr, k_per_cloud, tie_break, out_idx, out_pos, st);
+    else if (m <= 4096) e = launch_cta<256, 16>(num_clouds, pos, ptr, k_per_cloud, tie_break, out_idx, out_pos, st);
+    else if (m <= kCtaCapacity) e = launch_cta<kClusterThreads, kClusterP>(num_clouds, pos, ptr, k_per_cloud, tie_break, out_idx, out_pos, st);
     else {
         const int cs = (int)((m + kCtaCapacity - 1) / kCtaCapacity);
         e = cudaErrorInvalidConfiguration;
-        if (cs <= 16) e = launch_cluster(num_clouds, cs, pos, ptr, k_per_cloud, tie_break, out_idx, st);
+        if (cs <= 16) e = launch_cluster(num_clouds, cs, pos, ptr, k_per_cloud, tie_break, out_idx, out_pos, st);
         if (e != cudaSuccess) {
             (void)cudaGetLastError();  // clear a refused cluster launch, use the streaming kernel
             GDL_RETURN_IF(!workspace || workspace_bytes < sizeof(float) * (size_t)n_points, GDL_ERR_WORKSPACE);
             fps_stream_kernel<<<num_clouds, kStreamThreads, 0, st>>>(pos, ptr, k_per_cloud, tie_break,
-                                                                     (float *)workspace, out_idx);
+                                                                     (float *)workspace, out_idx, out_pos);
             e = cudaGetLastError();
         }
     }

@@ -162,8 +162,9 @@ __global__ void __launch_bounds__(kQueryThreads) rg_query_kernel(
     const int qc[3] = {cell_coord(qx, g.mn[0], inv), cell_coord(qy, g.mn[1], inv), cell_coord(qz, g.mn[2], inv)};
     const int zlo = qc[2] - 1 < 0 ? 0 : qc[2] - 1;
     const int zhi = qc[2] + 1 > g.res[2] - 1 ? g.res[2] - 1 : qc[2] + 1;
-    MinKHeap h;
-    h.init(cap);
+    float hd[64];
+    int hid[64];
+    int cnt = 0;
     if (zlo <= zhi) {
         for (int dx = -1; dx <= 1; ++dx) {
             const int cx = qc[0] + dx;
@@ -179,40 +180,482 @@ __global__ void __launch_bounds__(kQueryThreads) rg_query_kernel(
                     if (!loop && o == (int)q) continue;
                     const float4 s = sorted_pts[j];
                     const float d = dist2(qx, qy, qz, s.x, s.y, s.z);
-                    if (d < r_sq) h.add(d, o);
+                    if (d < r_sq) heap_add(hd, hid, cnt, cap, d, o);
                 }
             }
         }
     }
-    // kept set, ascending source index
-    int *keep = h.i;
-    for (int a = 1; a < h.count; ++a) {
-        const int v = keep[a];
-        int c = a - 1;
-        while (c >= 0 && keep[c] > v) {
-            keep[c + 1] = keep[c];
-            --c;
-        }
-        keep[c + 1] = v;
-    }
+    sort_ints(hid, cnt);  // kept set, ascending source index
     int32_t *dst = padded + q * cap;
-    for (int a = 0; a < h.count; ++a) dst[a] = keep[a];
-    counts[q] = h.count;
+    for (int a = 0; a < cnt; ++a) dst[a] = hid[a];
+    counts[q] = cnt;
 }
 
 __global__ void rg_compact_kernel(const int32_t *__restrict__ counts, const int32_t *__restrict__ padded, int64_t n,
                                   int cap, const int64_t *__restrict__ row_ptr, int64_t *__restrict__ src,
-                                  int64_t *__restrict__ dst) {
+                                  int64_t *__restrict__ dst, int32_t *__restrict__ row_ptr32,
+                                  int32_t *__restrict__ src32) {
     // one warp per query row: lanes copy the row's entries
     const int64_t q = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
     const int lane = threadIdx.x & 31;
-    if (q >= n) return;
+    if (q > n) return;
+    if (row_ptr32 && lane == 0) row_ptr32[q] = (int32_t)row_ptr[q];
+    if (q == n) return;
     const int c = counts[q];
     const int64_t o = row_ptr[q];
     for (int a = lane; a < c; a += 32) {
-        src[o + a] = padded[q * cap + a];
+        const int32_t v = padded[q * cap + a];
+        src[o + a] = v;
+        if (src32) src32[o + a] = v;
         if (dst) dst[o + a] = q;
     }
+}
+
+// ------------------------------------------------------------------ small clouds, fused
+// One CTA per cloud of at most kSmallMax points does the whole pipeline in shared memory:
+// bbox + grid parameters, cell keys, a stable LSD radix sort of (cell, index) (warp match +
+// per-warp digit counters, as in radix.cuh), the sorted coordinates, and every query with the
+// exact MinK heap. A second kernel turns the per-query counts into the global CSR.
+constexpr int kSmallThreads = 512;
+constexpr int kSmallMax = 4096;
+constexpr int kSmallWarps = kSmallThreads / 32;
+constexpr int kSmallItems = kSmallMax / kSmallThreads;  // keys per thread in a pass
+
+constexpr int kSmallCells = 16384;  // dense cell-start table when the grid has at most this many cells
+
+struct SmallSmem {
+    uint32_t key[2][kSmallMax];
+    int32_t val[2][kSmallMax];
+    float4 pts[kSmallMax];
+    int32_t cell_start[kSmallCells + 1];
+    uint32_t warp_cnt[kSmallWarps][256];
+    uint32_t digit_base[256];
+    float red[6][kSmallWarps];
+    GridParams g;
+    int32_t warp_tot[kSmallWarps];
+};
+
+__device__ __forceinline__ GridParams grid_from_bbox(const float *lo, const float *hi, float inv_cell, int64_t n) {
+    GridParams g;
+    int64_t cells = 1;
+    for (int a = 0; a < 3; ++a) {
+        // host arithmetic of the reference, in IEEE single precision (:283-297)
+        const float mn = __fsub_rn(lo[a], 1e-5f), mx = __fadd_rn(hi[a], 1e-5f);
+        const float c = ceilf(__fmul_rn(__fsub_rn(mx, mn), inv_cell));
+        const int r = (c >= 1023.0f) ? 1024 : (int)c + 1;
+        g.mn[a] = mn;
+        g.res[a] = r < 1 ? 1 : r;
+        cells *= g.res[a];
+    }
+    g.ncells = (int)cells;
+    g.ok = n > 1;
+    return g;
+}
+
+// grid = num_clouds * split: CTA (b, part) rebuilds cloud b's grid in shared memory and answers
+// queries [part * chunk, (part + 1) * chunk). Rows go to `padded` row-major (cap entries per
+// query), unsorted; counts[q] entries each.
+__global__ void __launch_bounds__(kSmallThreads) rg_small_kernel(
+    const float *__restrict__ x, const int64_t *__restrict__ ptr, const uint8_t *__restrict__ mask, float r_sq,
+    float inv, int loop, int cap, int split, int64_t n_all, int32_t *__restrict__ counts,
+    int32_t *__restrict__ padded, int32_t *__restrict__ cloud_tot) {
+    extern __shared__ __align__(16) unsigned char smem_raw[];
+    SmallSmem &S = *reinterpret_cast<SmallSmem *>(smem_raw);
+    const int b = blockIdx.x / split, part = blockIdx.x % split;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int64_t s0 = ptr[b];
+    const int n = (int)(ptr[b + 1] - s0);
+
+    // 1. bbox of all points of the cloud (masked ones included, :281-288)
+    float lo[3] = {__int_as_float(0x7f800000), __int_as_float(0x7f800000), __int_as_float(0x7f800000)};
+    float hi[3] = {__int_as_float(0xff800000), __int_as_float(0xff800000), __int_as_float(0xff800000)};
+    for (int i = tid; i < n; i += kSmallThreads)
+#pragma unroll
+        for (int a = 0; a < 3; ++a) {
+            const float v = x[3 * (s0 + i) + a];
+            lo[a] = fminf(lo[a], v);
+            hi[a] = fmaxf(hi[a], v);
+        }
+#pragma unroll
+    for (int a = 0; a < 3; ++a)
+        for (int o = 16; o > 0; o >>= 1) {
+            lo[a] = fminf(lo[a], __shfl_xor_sync(0xffffffffu, lo[a], o));
+            hi[a] = fmaxf(hi[a], __shfl_xor_sync(0xffffffffu, hi[a], o));
+        }
+    if (lane == 0)
+        for (int a = 0; a < 3; ++a) {
+            S.red[a][warp] = lo[a];
+            S.red[3 + a][warp] = hi[a];
+        }
+    __syncthreads();
+    if (tid == 0) {
+        for (int a = 0; a < 3; ++a)
+            for (int w = 1; w < kSmallWarps; ++w) {
+                S.red[a][0] = fminf(S.red[a][0], S.red[a][w]);
+                S.red[3 + a][0] = fmaxf(S.red[3 + a][0], S.red[3 + a][w]);
+            }
+        const float l3[3] = {S.red[0][0], S.red[1][0], S.red[2][0]};
+        const float h3[3] = {S.red[3][0], S.red[4][0], S.red[5][0]};
+        S.g = grid_from_bbox(l3, h3, inv, n);
+    }
+    __syncthreads();
+    const GridParams g = S.g;
+
+    // 2. cell keys (masked points last, :107-111), padded to items * kSmallThreads slots
+    const int items = (n + kSmallThreads - 1) / kSmallThreads;  // keys per thread in a pass
+    for (int i = tid; i < items * kSmallThreads; i += kSmallThreads) {
+        uint32_t key = 0xffffffffu;  // padding sorts after everything
+        if (i < n) {
+            if (!g.ok || (mask && !mask[s0 + i])) {
+                key = (uint32_t)g.ncells;
+            } else {
+                int c[3];
+#pragma unroll
+                for (int a = 0; a < 3; ++a) {
+                    const int v = cell_coord(x[3 * (s0 + i) + a], g.mn[a], inv);
+                    c[a] = v < 0 ? 0 : (v > g.res[a] - 1 ? g.res[a] - 1 : v);
+                }
+                key = (uint32_t)((c[0] * g.res[1] + c[1]) * g.res[2] + c[2]);
+            }
+        }
+        S.key[0][i] = key;
+        S.val[0][i] = i;
+    }
+    int bits = 0;
+    while (bits < 31 && ((int64_t)1 << bits) <= (int64_t)g.ncells) ++bits;
+    const int passes = (bits + 7) / 8;
+    // padding keys are 0xffffffff: they stay last as long as the digits of the passes run
+    // order them after every real key, which holds because real keys < 2^bits
+
+    // 3. stable LSD radix sort in shared memory
+    int src = 0;
+    const unsigned lt_mask = (1u << lane) - 1u;
+    for (int p = 0; p < passes; ++p) {
+        const int shift = 8 * p;
+        __syncthreads();
+        for (int d = tid; d < kSmallWarps * 256; d += kSmallThreads) (&S.warp_cnt[0][0])[d] = 0;
+        __syncthreads();
+        uint32_t key[kSmallItems], dig[kSmallItems], rank[kSmallItems];
+        int32_t val[kSmallItems];
+#pragma unroll
+        for (int it = 0; it < kSmallItems; ++it) {
+            if (it >= items) break;
+            const int idx = warp * 32 * items + it * 32 + lane;
+            key[it] = S.key[src][idx];
+            val[it] = S.val[src][idx];
+            dig[it] = (key[it] >> shift) & 255u;
+            const unsigned peers = __match_any_sync(0xffffffffu, dig[it]);
+            const unsigned before = __popc(peers & lt_mask);
+            const uint32_t base = S.warp_cnt[warp][dig[it]];
+            __syncwarp();
+            if (before == 0) S.warp_cnt[warp][dig[it]] = base + __popc(peers);
+            __syncwarp();
+            rank[it] = base + before;
+        }
+        __syncthreads();
+        if (tid < 256) {  // per digit: exclusive prefix over warps, digit total
+            uint32_t run = 0;
+            for (int w = 0; w < kSmallWarps; ++w) {
+                const uint32_t c = S.warp_cnt[w][tid];
+                S.warp_cnt[w][tid] = run;
+                run += c;
+            }
+            S.digit_base[tid] = run;
+        }
+        __syncthreads();
+        if (tid < 32) {  // exclusive scan of the 256 digit totals by one warp
+            uint32_t v[8], t = 0;
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                v[j] = S.digit_base[tid * 8 + j];
+                t += v[j];
+            }
+            uint32_t inc = t;
+            for (int o = 1; o < 32; o <<= 1) {
+                const uint32_t y = __shfl_up_sync(0xffffffffu, inc, o);
+                if (tid >= o) inc += y;
+            }
+            uint32_t run = inc - t;
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                const uint32_t c = v[j];
+                S.digit_base[tid * 8 + j] = run;
+                run += c;
+            }
+        }
+        __syncthreads();
+#pragma unroll
+        for (int it = 0; it < kSmallItems; ++it) {
+            if (it >= items) break;
+            const uint32_t dst = S.digit_base[dig[it]] + S.warp_cnt[warp][dig[it]] + rank[it];
+            S.key[src ^ 1][dst] = key[it];
+            S.val[src ^ 1][dst] = val[it];
+        }
+        src ^= 1;
+    }
+    __syncthreads();
+    // 4. sorted coordinates; first sorted position of every cell (dense table: a cell's points
+    // are [cell_start[c], cell_start[c+1]); empty cells take the next cell's start)
+    const uint32_t *keys = S.key[src];
+    const int32_t *vals = S.val[src];
+    const bool dense = g.ncells < kSmallCells;
+    if (dense)
+        for (int c = tid; c <= g.ncells; c += kSmallThreads) S.cell_start[c] = n;
+    for (int j = tid; j < n; j += kSmallThreads) {  // .w carries the point's local index
+        const int v = vals[j];
+        const int64_t o = s0 + v;
+        S.pts[j] = make_float4(x[3 * o], x[3 * o + 1], x[3 * o + 2], __int_as_float(v));
+    }
+    __syncthreads();
+    if (dense) {
+        for (int j = tid; j < n; j += kSmallThreads)
+            // masked points carry key ncells: their run start is the end of the last cell
+            if (keys[j] <= (uint32_t)g.ncells && (j == 0 || keys[j - 1] != keys[j])) S.cell_start[keys[j]] = j;
+        __syncthreads();
+        // suffix minimum cell_start[c] = min(cell_start[c..ncells]): each thread folds a span of
+        // consecutive cells from the top, then one block-wide suffix scan of the span minima
+        const int total = g.ncells + 1, span = (total + kSmallThreads - 1) / kSmallThreads;
+        const int c0 = tid * span, c1 = min(c0 + span, total);
+        int m = 0x7fffffff;
+        for (int c = c1 - 1; c >= c0; --c) m = min(m, S.cell_start[c]);
+        // inclusive suffix scan over threads (higher tid = higher cells)
+        const int lane_ = tid & 31, w = tid >> 5;
+        int suf = m;
+        for (int o = 1; o < 32; o <<= 1) {
+            const int y = __shfl_down_sync(0xffffffffu, suf, o);
+            if (lane_ + o < 32) suf = min(suf, y);
+        }
+        if (lane_ == 0) S.warp_tot[w] = suf;
+        __syncthreads();
+        int above = 0x7fffffff;  // minimum over all later threads
+        for (int ww = w + 1; ww < kSmallWarps; ++ww) above = min(above, S.warp_tot[ww]);
+        int after = __shfl_down_sync(0xffffffffu, suf, 1);
+        if (lane_ == 31) after = 0x7fffffff;
+        int run = min(above, after);
+        for (int c = c1 - 1; c >= c0; --c) {
+            run = min(run, S.cell_start[c]);
+            S.cell_start[c] = run;
+        }
+    }
+    __syncthreads();
+
+    // 5. queries, one warp each. Lanes 0-8 fetch the sorted-position ranges of the 9 z-columns
+    // of the 27-cell neighbourhood ((dx, dy) order, empty outside the grid); a warp scan makes
+    // them one candidate list that the lanes test 32 at a time; ballot/popc place the accepted
+    // sources, in scan order, into the query's padded row. Rows are sorted at compaction. A
+    // query with more than `cap` sources in range replays the reference heap on lane 0.
+    int my_total = 0;
+    const int chunk = (n + split - 1) / split;
+    const int qend = min(n, (part + 1) * chunk);
+    for (int q = part * chunk + warp; q < qend; q += kSmallWarps) {
+        int kept = 0;
+        if (g.ok && !(mask && !mask[s0 + q])) {
+            const float qx = x[3 * (s0 + q)], qy = x[3 * (s0 + q) + 1], qz = x[3 * (s0 + q) + 2];
+            const int qc0 = cell_coord(qx, g.mn[0], inv), qc1 = cell_coord(qy, g.mn[1], inv),
+                      qc2 = cell_coord(qz, g.mn[2], inv);
+            const int zlo = qc2 - 1 < 0 ? 0 : qc2 - 1;
+            const int zhi = qc2 + 1 > g.res[2] - 1 ? g.res[2] - 1 : qc2 + 1;
+            int j0 = 0, len = 0;
+            if (lane < 9) {
+                const int cx = qc0 + lane / 3 - 1, cy = qc1 + lane % 3 - 1;
+                if (zlo <= zhi && cx >= 0 && cx < g.res[0] && cy >= 0 && cy < g.res[1]) {
+                    const int colc = (cx * g.res[1] + cy) * g.res[2];
+                    int e;
+                    if (dense) {
+                        j0 = S.cell_start[colc + zlo];
+                        e = S.cell_start[colc + zhi + 1];
+                    } else {
+                        const uint32_t klo = (uint32_t)(colc + zlo), khi = (uint32_t)(colc + zhi) + 1u;
+                        int lo = 0, hi = n;
+                        while (lo < hi) {
+                            const int m = (lo + hi) >> 1;
+                            if (keys[m] < klo) lo = m + 1;
+                            else hi = m;
+                        }
+                        j0 = lo;
+                        hi = n;
+                        while (lo < hi) {
+                            const int m = (lo + hi) >> 1;
+                            if (keys[m] < khi) lo = m + 1;
+                            else hi = m;
+                        }
+                        e = lo;
+                    }
+                    len = e - j0;
+                }
+            }
+            int inc = len;  // inclusive prefix of the column lengths
+            for (int o = 1; o < 16; o <<= 1) {
+                const int y = __shfl_up_sync(0xffffffffu, inc, o);
+                if (lane >= o) inc += y;
+            }
+            const int total = __shfl_sync(0xffffffffu, inc, 8);
+            const int excl = inc - len;
+            // every lane takes the 9 (first candidate number, start) pairs, full-warp shuffles
+            // outside any divergent branch
+            int cex[9], cj[9];
+#pragma unroll
+            for (int c = 0; c < 9; ++c) {
+                cex[c] = __shfl_sync(0xffffffffu, excl, c);
+                cj[c] = __shfl_sync(0xffffffffu, j0, c);
+            }
+            int32_t *row = padded + (s0 + q) * cap;
+            for (int base = 0; base < total; base += 32) {
+                const int t = base + lane;
+                bool ok = false;
+                int o = 0;
+                if (t < total) {
+                    int j = 0;
+#pragma unroll
+                    for (int c = 0; c < 9; ++c)  // column holding candidate t
+                        if (t >= cex[c]) j = cj[c] + (t - cex[c]);
+                    const float4 sp = S.pts[j];
+                    o = __float_as_int(sp.w);
+                    ok = (loop || o != q) && dist2(qx, qy, qz, sp.x, sp.y, sp.z) < r_sq;
+                }
+                const unsigned hits = __ballot_sync(0xffffffffu, ok);
+                const int pos = kept + __popc(hits & lt_mask);
+                if (ok && pos < cap) row[pos] = (int32_t)(s0 + o);
+                kept += __popc(hits);
+            }
+            if (kept > cap) {  // the reference heap decides which `cap` stay, in scan order
+                int cjl[9];
+#pragma unroll
+                for (int c = 0; c < 9; ++c) cjl[c] = __shfl_sync(0xffffffffu, len, c);
+                if (lane == 0) {
+                    float hd[64];
+                    int hid[64];
+                    int hc = 0;
+#pragma unroll
+                    for (int c = 0; c < 9; ++c)
+                        for (int j = cj[c]; j < cj[c] + cjl[c]; ++j) {
+                            const float4 sp = S.pts[j];
+                            const int o = __float_as_int(sp.w);
+                            if (!loop && o == q) continue;
+                            const float d = dist2(qx, qy, qz, sp.x, sp.y, sp.z);
+                            if (d < r_sq) heap_add(hd, hid, hc, cap, d, o);
+                        }
+                    for (int a2 = 0; a2 < hc; ++a2) row[a2] = (int32_t)(s0 + hid[a2]);
+                }
+                __syncwarp();
+                kept = cap;
+            }
+        }
+        if (lane == 0) {
+            counts[s0 + q] = kept;
+            my_total += kept;
+        }
+    }
+    for (int o = 16; o > 0; o >>= 1) my_total += __shfl_xor_sync(0xffffffffu, my_total, o);
+    if (lane == 0) S.warp_tot[warp] = my_total;
+    __syncthreads();
+    if (tid == 0) {
+        int t = 0;
+        for (int w = 0; w < kSmallWarps; ++w) t += S.warp_tot[w];
+        atomicAdd(&cloud_tot[b], t);  // the parts of a cloud add up (integer: order-free)
+    }
+}
+
+// Sort one query's kept sources (count <= 64, in padded[0, c)) ascending with a warp bitonic
+// sort (two keys per lane) and write them at o.
+__device__ __forceinline__ void warp_sort_emit(const int32_t *__restrict__ col, int64_t stride, int c, int64_t o,
+                                               int64_t q, int64_t *__restrict__ src, int64_t *__restrict__ dstv,
+                                               int32_t *__restrict__ src32) {
+    const int lane = threadIdx.x & 31;
+    int a = lane < c ? col[lane * stride] : 0x7fffffff;
+    int b = lane + 32 < c ? col[(lane + 32) * stride] : 0x7fffffff;
+    if (c > 1 && c <= 32) {  // one value per lane: bitonic sort over the 32 lanes
+        for (int size = 2; size <= 32; size <<= 1)
+            for (int stride2 = size >> 1; stride2 > 0; stride2 >>= 1) {
+                const int p = __shfl_xor_sync(0xffffffffu, a, stride2);
+                const bool asc = (lane & size) == 0 || size == 32;
+                const bool lower = (lane & stride2) == 0;
+                a = (lower == asc) ? min(a, p) : max(a, p);
+            }
+    } else if (c > 32) {
+        // bitonic sort of the 64 values held as (a = element lane, b = element lane + 32)
+        for (int size = 2; size <= 64; size <<= 1) {
+            for (int stride = size >> 1; stride > 0; stride >>= 1) {
+                if (stride == 32) {  // partner is the other register of the same lane
+                    const bool up = true;  // size == 64: whole sequence ascending
+                    const int lo = min(a, b), hi = max(a, b);
+                    a = up ? lo : hi;
+                    b = up ? hi : lo;
+                } else {
+#pragma unroll
+                    for (int r = 0; r < 2; ++r) {
+                        int v = r == 0 ? a : b;
+                        const int idx = lane + 32 * r;
+                        const int p = __shfl_xor_sync(0xffffffffu, v, stride);
+                        const bool asc = ((idx & size) == 0);
+                        const bool lower = (idx & stride) == 0;
+                        v = (lower == asc) ? min(v, p) : max(v, p);
+                        if (r == 0) a = v;
+                        else b = v;
+                    }
+                }
+            }
+        }
+    }
+    if (lane < c) {
+        src[o + lane] = a;
+        if (src32) src32[o + lane] = a;
+        if (dstv) dstv[o + lane] = q;
+    }
+    if (lane + 32 < c) {
+        src[o + lane + 32] = b;
+        if (src32) src32[o + lane + 32] = b;
+        if (dstv) dstv[o + lane + 32] = q;
+    }
+}
+
+// grid = num_clouds * split. Every CTA of cloud b takes the cloud's global edge offset (sum of the
+// earlier clouds' totals) and scans the cloud's counts; it writes row_ptr and the edges of its
+// own query part, one warp per row: bitonic sort of the row's sources, then the copy.
+__global__ void __launch_bounds__(kSmallThreads) rg_small_compact_kernel(
+    const int64_t *__restrict__ ptr, int32_t B, int split, int64_t n_all, int cap, const int32_t *__restrict__ counts,
+    const int32_t *__restrict__ padded, const int32_t *__restrict__ cloud_tot, int64_t *__restrict__ row_ptr,
+    int64_t *__restrict__ src, int64_t *__restrict__ dstv, int32_t *__restrict__ row_ptr32,
+    int32_t *__restrict__ src32) {
+    __shared__ int64_t warp_sums[32];
+    __shared__ int64_t total;
+    __shared__ int64_t offs[kSmallMax];
+    const int b = blockIdx.x / split, part = blockIdx.x % split;
+    const int tid = threadIdx.x, warp = tid >> 5;
+    int64_t base = 0;
+    for (int c = tid; c < b; c += kSmallThreads) base += cloud_tot[c];
+    (void)block_exclusive_scan<int64_t>(base, warp_sums, &total);
+    base = total;
+    const int64_t s0 = ptr[b], s1 = ptr[b + 1];
+    const int n = (int)(s1 - s0);
+    int64_t carry = base;
+    for (int q0 = 0; q0 < n; q0 += kSmallThreads) {  // offsets of the whole cloud
+        const int q = q0 + tid;
+        const int c = q < n ? counts[s0 + q] : 0;
+        const int64_t off = block_exclusive_scan<int64_t>(c, warp_sums, &total) + carry;
+        if (q < n) offs[q] = off;
+        carry += total;
+    }
+    __syncthreads();
+    const int chunk = (n + split - 1) / split;
+    const int qb = part * chunk, qe = min(n, qb + chunk);
+    for (int q = qb + tid; q < qe; q += kSmallThreads) {
+        const int64_t gq = s0 + q;
+        row_ptr[gq] = offs[q];
+        if (row_ptr32) row_ptr32[gq] = (int32_t)offs[q];
+    }
+    for (int q = qb + warp; q < qe; q += kSmallWarps)  // one warp sorts and writes a row
+        warp_sort_emit(padded + (s0 + q) * cap, 1, counts[s0 + q], offs[q], s0 + q, src, dstv, src32);
+    if (b == 0 && part == 0)  // points before the first cloud have no edges
+        for (int64_t q = tid; q < ptr[0]; q += kSmallThreads) {
+            row_ptr[q] = 0;
+            if (row_ptr32) row_ptr32[q] = 0;
+        }
+    if (b == B - 1 && part == split - 1)  // the end of the last cloud, and points after it
+        for (int64_t q = s1 + tid; q <= n_all; q += kSmallThreads) {
+            row_ptr[q] = carry;
+            if (row_ptr32) row_ptr32[q] = (int32_t)carry;
+        }
 }
 
 struct RadiusWs {
@@ -222,6 +665,7 @@ struct RadiusWs {
     int32_t *sorted_idx, *counts, *padded;
     float4 *sorted_pts;
     int64_t *scan_scratch;
+    int32_t *cloud_tot;
     RadixScratch rs;
 };
 
@@ -243,6 +687,7 @@ static size_t radius_ws(int64_t n, int32_t B, int cap, char *base, RadiusWs *w) 
     t.padded = (int32_t *)take(sizeof(int32_t) * nn * cap);
     t.sorted_pts = (float4 *)take(sizeof(float4) * nn);
     t.scan_scratch = (int64_t *)take(sizeof(int64_t) * (scan_blocks(nn) + 1));
+    t.cloud_tot = (int32_t *)take(sizeof(int32_t) * (B > 0 ? B : 1));
     const size_t rbytes = radix_scratch_bytes(nn, B > 0 ? B : 1);
     char *rb = take(rbytes);
     if (base) t.rs = radix_carve(rb, nn, B > 0 ? B : 1);
@@ -259,9 +704,10 @@ extern "C" size_t gdl_radius_graph_workspace_size(int64_t n_points, int32_t num_
 }
 
 extern "C" int gdl_radius_graph(const float *x, const int64_t *ptr, int32_t num_clouds, int64_t n_points,
-                                double radius, int32_t max_num_neighbors, int32_t loop, const uint8_t *mask,
-                                int64_t *out_row_ptr, int64_t *out_src, int64_t *out_dst, void *workspace,
-                                size_t workspace_bytes, void *stream) {
+                                int64_t max_cloud_points, double radius, int32_t max_num_neighbors, int32_t loop,
+                                const uint8_t *mask, int64_t *out_row_ptr, int64_t *out_src, int64_t *out_dst,
+                                int32_t *out_row_ptr32, int32_t *out_src32, void *workspace, size_t workspace_bytes,
+                                void *stream) {
     cudaStream_t st = (cudaStream_t)stream;
     GDL_RETURN_IF(num_clouds < 0 || n_points < 0, GDL_ERR_INVALID);
     GDL_RETURN_IF(!out_row_ptr, GDL_ERR_INVALID);
@@ -269,6 +715,7 @@ extern "C" int gdl_radius_graph(const float *x, const int64_t *ptr, int32_t num_
     const float r = (float)radius;  // radius_graph_kernel.cu:266
     if (n_points == 0 || num_clouds == 0 || !(r > 0.0f)) {
         GDL_CUDA_TRY(cudaMemsetAsync(out_row_ptr, 0, sizeof(int64_t) * (n_points + 1), st));
+        if (out_row_ptr32) GDL_CUDA_TRY(cudaMemsetAsync(out_row_ptr32, 0, sizeof(int32_t) * (n_points + 1), st));
         return GDL_OK;
     }
     GDL_RETURN_IF(!x || !ptr || !out_src, GDL_ERR_INVALID);
@@ -279,6 +726,21 @@ extern "C" int gdl_radius_graph(const float *x, const int64_t *ptr, int32_t num_
     radius_ws(n_points, num_clouds, cap, (char *)workspace, &w);
     const float r_sq = r * r;           // :274
     const float inv = 1.0f / r;         // :276 (host IEEE division)
+    if (max_cloud_points > 0 && max_cloud_points <= kSmallMax) {  // fused per-cloud path
+        const size_t smem = sizeof(SmallSmem);
+        // spread each cloud over several CTAs so that small batches still fill the GPU
+        int split = (int)((2 * kSmCount) / num_clouds);
+        split = split < 1 ? 1 : (split > 8 ? 8 : split);
+        GDL_CUDA_TRY(cudaFuncSetAttribute(rg_small_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+        GDL_CUDA_TRY(cudaMemsetAsync(w.cloud_tot, 0, sizeof(int32_t) * num_clouds, st));
+        rg_small_kernel<<<num_clouds * split, kSmallThreads, smem, st>>>(x, ptr, mask, r_sq, inv, loop, cap, split,
+                                                                         n_points, w.counts, w.padded, w.cloud_tot);
+        rg_small_compact_kernel<<<num_clouds * split, kSmallThreads, 0, st>>>(
+            ptr, num_clouds, split, n_points, cap, w.counts, w.padded, w.cloud_tot, out_row_ptr, out_src, out_dst,
+            out_row_ptr32, out_src32);
+        GDL_CUDA_TRY(cudaGetLastError());
+        return GDL_OK;
+    }
     const unsigned g256 = (unsigned)((n_points + 255) / 256);
     GDL_CUDA_TRY(cudaMemsetAsync(w.key_bits, 0, sizeof(int32_t), st));
     rg_grid_kernel<<<num_clouds, kGridThreads, 0, st>>>(x, ptr, inv, w.gp, w.key_bits);
@@ -291,8 +753,8 @@ extern "C" int gdl_radius_graph(const float *x, const int64_t *ptr, int32_t num_
         w.counts, w.padded);
     GDL_CUDA_TRY((exclusive_scan<int32_t, int64_t>(w.counts, out_row_ptr, n_points, w.scan_scratch,
                                                    out_row_ptr + n_points, st)));
-    rg_compact_kernel<<<(unsigned)((n_points * 32 + 255) / 256), 256, 0, st>>>(w.counts, w.padded, n_points, cap,
-                                                                             out_row_ptr, out_src, out_dst);
+    rg_compact_kernel<<<(unsigned)(((n_points + 1) * 32 + 255) / 256), 256, 0, st>>>(
+        w.counts, w.padded, n_points, cap, out_row_ptr, out_src, out_dst, out_row_ptr32, out_src32);
     GDL_CUDA_TRY(cudaGetLastError());
     return GDL_OK;
 }

@@ -12,10 +12,11 @@ from .. import csrc
 
 
 def _ptr_from_batch(batch: Tensor, B: Optional[int]):
+    """CSR offsets of a sorted batch vector, on the host (one device->host copy)."""
     batch = batch.to(torch.int64)
-    nb = int(B) if B is not None else int(batch.max().item()) + 1
-    counts = torch.bincount(batch, minlength=nb)
-    ptr = torch.zeros(nb + 1, dtype=torch.int64, device=batch.device)
+    nb = int(B) if B is not None else (int(batch.max().item()) + 1 if batch.numel() else 0)
+    counts = torch.bincount(batch, minlength=nb).cpu()
+    ptr = torch.zeros(nb + 1, dtype=torch.int64)
     ptr[1:] = counts.cumsum(0)
     return ptr
 
@@ -23,7 +24,8 @@ def _ptr_from_batch(batch: Tensor, B: Optional[int]):
 def radius_graph_csr(x: Tensor, r: float, ptr: Tensor, *, max_num_neighbors: int = 32, loop: bool = False,
                      mask: Optional[Tensor] = None):
     """Edges of packed clouds as a destination CSR (row_ptr [N+1], src, dst); the first
-    row_ptr[N] entries of src/dst are valid. No host synchronisation."""
+    row_ptr[N] entries of src/dst are valid. No host synchronisation (pass ``ptr`` as a
+    CPU tensor to let small clouds use the fused kernels)."""
     return csrc.radius_graph_csr(x, r, ptr, max_num_neighbors=max_num_neighbors, loop=loop, mask=mask)
 
 
@@ -48,7 +50,7 @@ def radius_graph(x: Tensor, r: float, *, max_num_neighbors: int = 32, batch: Opt
     else:
         order, xb, mb = None, x, mask
         B = num_batch_elements if num_batch_elements is not None else 1
-        ptr = torch.arange(B + 1, dtype=torch.int64, device=x.device) * (N // B)
+        ptr = torch.arange(B + 1, dtype=torch.int64) * (N // B)
     row_ptr, src, dst = csrc.radius_graph_csr(xb, r, ptr, max_num_neighbors=max_num_neighbors, loop=loop, mask=mb)
     E = int(row_ptr[N].item())
     row, col = src[:E], dst[:E]

@@ -66,12 +66,14 @@ int gdl_check_device(int device);
  *              streaming CTA that keeps the running minima in the workspace).
  * tie_break    GDL_TIE_REFERENCE: the reference kernel's argmax reduction order
  *              (bit-identical to fps_kernel<512>); GDL_TIE_LOWEST_INDEX: torch.argmax.
+ * out_pos      [same slots, 3] f32 (nullable): coordinates of each pick (0 for padding), which
+ *              saves the caller a gather of pos[out_idx].
  * Seed is the first point of each cloud; distances use the reference's rounding.
  */
 size_t gdl_fps_workspace_size(int64_t n_points, int64_t max_cloud_points);
 int gdl_fps(const float *pos, const int64_t *ptr, const int64_t *k_per_cloud, int32_t num_clouds, int64_t n_points,
-            int64_t max_cloud_points, int32_t tie_break, int64_t *out_idx, void *workspace, size_t workspace_bytes,
-            void *stream);
+            int64_t max_cloud_points, int32_t tie_break, int64_t *out_idx, float *out_pos, void *workspace,
+            size_t workspace_bytes, void *stream);
 
 /* ------------------------------------------------------------------------------ KNN
  * Replaces knn_cuda(query, source, ptr_q, ptr_s, k) and knn_self_cuda(points, ptr, k)
@@ -102,12 +104,19 @@ int gdl_knn(const float *query, const float *source, const int64_t *ptr_q, const
  *   out_row_ptr [n_points + 1] i64  (edges of destination q: [row_ptr[q], row_ptr[q+1]))
  *   out_src     [capacity] i64      (row: the neighbour, ascending within a destination)
  *   out_dst     [capacity] i64      (col: the query; nullable)
+ *   out_row_ptr32 [n_points + 1], out_src32 [capacity] i32 (nullable): the same CSR in the
+ *               int32 layout the segment reduce consumes (node_start = row_ptr32[:-1],
+ *               node_end = row_ptr32[1:], perm = src32 to gather source rows).
  * capacity = n_points * bucket(max_num_neighbors). The edge count is out_row_ptr[n_points].
+ * max_cloud_points: host-side upper bound of the largest cloud, or 0 if unknown; clouds of at
+ * most 4096 points take a fused path (one CTA per cloud, 2 launches in total).
  */
 size_t gdl_radius_graph_workspace_size(int64_t n_points, int32_t num_clouds, int32_t max_num_neighbors);
-int gdl_radius_graph(const float *x, const int64_t *ptr, int32_t num_clouds, int64_t n_points, double radius,
-                     int32_t max_num_neighbors, int32_t loop, const uint8_t *mask, int64_t *out_row_ptr,
-                     int64_t *out_src, int64_t *out_dst, void *workspace, size_t workspace_bytes, void *stream);
+int gdl_radius_graph(const float *x, const int64_t *ptr, int32_t num_clouds, int64_t n_points,
+                     int64_t max_cloud_points, double radius, int32_t max_num_neighbors, int32_t loop,
+                     const uint8_t *mask, int64_t *out_row_ptr, int64_t *out_src, int64_t *out_dst,
+                     int32_t *out_row_ptr32, int32_t *out_src32, void *workspace, size_t workspace_bytes,
+                     void *stream);
 
 /* -------------------------------------------------------------------------- CSR build
  * Replaces sort_and_build_csr(col, N) -- geoembodied/csrc/segment_reduce_kernel.cu:100-169.

@@ -34,9 +34,10 @@ DIST_MODES = {
     "fma_xyz": DIST_FMA_XYZ,
 }
 # Rounding of the reference CUDA kernels' `dx*dx + dy*dy + dz*dz` under nvcc -O3
-# --use_fast_math for sm_100a; pinned on a B200 against the reference KNN's returned
-# distances (tests/test_gpu_ref_pin.py).
-DIST_CUDA = DIST_FMA_ZYX
+# --use_fast_math for sm_100a: fma(dz, dz, fma(dx, dx, dy*dy)) with flush-to-zero. Pinned on
+# a B200: of the candidate modes only this one reproduces, bit for bit, every distance the
+# reference KNN kernel returned (tests/test_gpu_ref_pin.py::test_distance_rounding_pinned).
+DIST_CUDA = DIST_FMA_ZXY
 
 TIE_REFERENCE = 0
 TIE_LOWEST_INDEX = 1

@@ -124,14 +124,18 @@ def test_knn_full_size_config4_sample(oracle):
 @pytest.mark.parametrize("max_nn", [16, 20, 32, 64])
 @pytest.mark.parametrize("loop", [False, True])
 @pytest.mark.parametrize("kind", ["uniform", "lattice"])
-def test_radius_matches_oracle(oracle, max_nn, loop, kind):
-    x, ptr = _rand_clouds(max_nn, [1, 0, 400, 2500, 3000], kind)
+@pytest.mark.parametrize("path", ["fused", "general"])
+def test_radius_matches_oracle(oracle, max_nn, loop, kind, path):
+    sizes = [1, 0, 400, 2500, 3000] if path == "fused" else [1, 0, 400, 2500, 9000]
+    x, ptr = _rand_clouds(max_nn, sizes, kind)
     rng = np.random.default_rng(1)
     mask = rng.random(x.shape[0]) > 0.1
     for r in (0.12, 0.35):
         for m in (None, mask):
             wrp, wsrc = oracle.radius_graph(x, ptr, r, max_nn, loop, m, dist=oracle.DIST_CUDA)
-            rp, src, dst = csrc.radius_graph_csr(torch.from_numpy(x).to(DEV), r, torch.from_numpy(ptr).to(DEV),
+            # a CPU ptr tells the wrapper the largest cloud (fused kernels up to 4096 points)
+            pt = torch.from_numpy(ptr) if path == "fused" else torch.from_numpy(ptr).to(DEV)
+            rp, src, dst = csrc.radius_graph_csr(torch.from_numpy(x).to(DEV), r, pt,
                                                  max_num_neighbors=max_nn, loop=loop,
                                                  mask=None if m is None else torch.from_numpy(m).to(DEV))
             rp = rp.cpu().numpy()

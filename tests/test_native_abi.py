@@ -52,7 +52,7 @@ def test_host_only_queries(lib):
 
 def test_argument_validation_without_gpu(lib):
     # invalid arguments are rejected before any CUDA call
-    assert lib.gdl_fps(None, None, None, 1, 10, 10, 7, None, None, 0, None) == 1
+    assert lib.gdl_fps(None, None, None, 1, 10, 10, 7, None, None, None, 0, None) == 1
     assert lib.gdl_segment_reduce(None, 5, 1, 1, None, None, None, 1, 0, None, None, None, 0, None) == 1
     assert lib.gdl_knn(None, None, None, None, 1, 10, 4, 10, None, None, None, 0, None) == 1
 
