@@ -129,20 +129,34 @@ struct MaxState {
     __device__ __forceinline__ int arg_out() const { return (nan || cnt != 1) ? -1 : arg; }
 };
 
+// Queue segment n for the one-CTA-per-segment kernel; true if it was queued. A full queue
+// (a CSR with more slots than rows can hold more long segments than it was sized for) leaves
+// the segment to its lane group. Called by all G lanes of the group.
+template <int G>
+__device__ __forceinline__ bool queue_long(int64_t n, int lig, int32_t *long_list, int32_t *long_count,
+                                           int64_t max_long) {
+    int queued = 0;
+    if (lig == 0) {
+        const int idx = atomicAdd(long_count, 1);
+        queued = idx < max_long;
+        if (queued) long_list[idx] = (int32_t)n;
+    }
+    const int lane = threadIdx.x & 31, leader = lane & ~(G - 1);
+    const unsigned gmask = G == 32 ? 0xffffffffu : (((1u << G) - 1u) << leader);
+    return __shfl_sync(gmask, queued, leader) != 0;
+}
+
 template <typename T, int VEC, int G, int RED>
 __global__ void __launch_bounds__(kSegThreads) seg_fwd_short_kernel(
     const T *__restrict__ msg, int64_t C, const int32_t *__restrict__ perm, const int32_t *__restrict__ ns,
     const int32_t *__restrict__ ne, int64_t N, float *__restrict__ out, int32_t *__restrict__ arg,
-    int32_t *__restrict__ long_list, int32_t *__restrict__ long_count) {
+    int32_t *__restrict__ long_list, int32_t *__restrict__ long_count, int64_t max_long) {
     constexpr int kGroups = kSegThreads / G;
     const int lig = threadIdx.x % G;
     const int64_t n = (int64_t)blockIdx.x * kGroups + threadIdx.x / G;
     if (n >= N) return;
     const int s = ns[n], e = ne[n];
-    if (e - s > kLongSegment) {
-        if (lig == 0) long_list[atomicAdd(long_count, 1)] = (int32_t)n;
-        return;
-    }
+    if (e - s > kLongSegment && queue_long<G>(n, lig, long_list, long_count, max_long)) return;
     for (int64_t c0 = 0; c0 < C; c0 += (int64_t)G * VEC) {
         const int64_t c = c0 + (int64_t)lig * VEC;
         if (c >= C) continue;
@@ -201,6 +215,7 @@ __global__ void __launch_bounds__(kSegThreads) seg_fwd_long_kernel(
     const T *__restrict__ msg, int64_t C, const int32_t *__restrict__ perm, const int32_t *__restrict__ ns,
     const int32_t *__restrict__ ne, float *__restrict__ out, int32_t *__restrict__ arg,
     const int32_t *__restrict__ long_list, const int32_t *__restrict__ long_count) {
+    // launched with max_long CTAs: entries beyond the queue's capacity were handled in place
     constexpr int kRG = kSegThreads / G;
     __shared__ float part[kRG][G * VEC];
     __shared__ int part_arg[RED == GDL_REDUCE_MAX ? kRG : 1][RED == GDL_REDUCE_MAX ? G * VEC : 1];
@@ -348,17 +363,14 @@ __global__ void __launch_bounds__(kSegThreads) seg_bwd_short_kernel(
     const float *__restrict__ grad_out, const T *__restrict__ msg, const float *__restrict__ out,
     const int32_t *__restrict__ arg, int64_t C, const int32_t *__restrict__ perm, const int32_t *__restrict__ ns,
     const int32_t *__restrict__ ne, int64_t N, T *__restrict__ grad_msg, int32_t *__restrict__ long_list,
-    int32_t *__restrict__ long_count) {
+    int32_t *__restrict__ long_count, int64_t max_long) {
     constexpr int kGroups = kSegThreads / G;
     const int lig = threadIdx.x % G;
     const int64_t n = (int64_t)blockIdx.x * kGroups + threadIdx.x / G;
     if (n >= N) return;
     const int s = ns[n], e = ne[n];
     if (e <= s) return;
-    if (e - s > kLongSegment) {
-        if (lig == 0) long_list[atomicAdd(long_count, 1)] = (int32_t)n;
-        return;
-    }
+    if (e - s > kLongSegment && queue_long<G>(n, lig, long_list, long_count, max_long)) return;
     for (int64_t c0 = 0; c0 < C; c0 += (int64_t)G * VEC) {
         const int64_t c = c0 + (int64_t)lig * VEC;
         if (c < C) seg_bwd_range<T, VEC, RED>(grad_out, msg, out, arg, C, perm, n, s, e, s, e, c, grad_msg);
@@ -452,7 +464,7 @@ static void launch_fwd(const void *msg, int64_t C, const int32_t *perm, const in
     constexpr int groups = kSegThreads / G;
     const int64_t blocks = (N + groups - 1) / groups;
     seg_fwd_short_kernel<T, VEC, G, RED><<<(unsigned)blocks, kSegThreads, 0, st>>>(
-        (const T *)msg, C, perm, ns, ne, N, out, arg, long_list, long_count);
+        (const T *)msg, C, perm, ns, ne, N, out, arg, long_list, long_count, max_long);
     if (max_long > 0)
         seg_fwd_long_kernel<T, VEC, G, RED><<<(unsigned)max_long, kSegThreads, 0, st>>>(
             (const T *)msg, C, perm, ns, ne, out, arg, long_list, long_count);
@@ -490,7 +502,7 @@ static void launch_bwd(const float *go, const void *msg, const float *out, const
     constexpr int groups = kSegThreads / G;
     const int64_t blocks = (N + groups - 1) / groups;
     seg_bwd_short_kernel<T, VEC, G, RED><<<(unsigned)blocks, kSegThreads, 0, st>>>(
-        go, (const T *)msg, out, arg, C, perm, ns, ne, N, (T *)gm, ll, lc);
+        go, (const T *)msg, out, arg, C, perm, ns, ne, N, (T *)gm, ll, lc, ml);
     if (ml > 0)
         seg_bwd_long_kernel<T, VEC, G, RED><<<(unsigned)ml, kSegThreads, 0, st>>>(go, (const T *)msg, out, arg, C, perm,
                                                                                  ns, ne, (T *)gm, ll, lc);
@@ -643,3 +655,4 @@ extern "C" int gdl_segment_reduce_backward(const float *grad_out, const void *ms
     GDL_CUDA_TRY(cudaGetLastError());
     return GDL_OK;
 }
+

@@ -253,6 +253,28 @@ def test_segment_long_segments(oracle, reduce):
     assert np.array_equal(again.view(np.uint32), got.view(np.uint32))
 
 
+@pytest.mark.parametrize("reduce", ["sum", "max"])
+def test_segment_long_queue_overflow(oracle, reduce):
+    """More slots than rows (perm gathers rows repeatedly): more long segments than the queue
+    was sized for; the overflow is folded in place (sum in reference order, bit-exact)."""
+    rng = np.random.default_rng(9)
+    rows, C = 300, 8
+    msg = rng.standard_normal((rows, C)).astype(np.float32)
+    lens = [5000, 4500, 6000, 3, 0, 7000]
+    ns = np.concatenate([[0], np.cumsum(lens)[:-1]]).astype(np.int32)
+    ne = (ns + np.array(lens)).astype(np.int32)
+    perm = rng.integers(0, rows, int(sum(lens))).astype(np.int32)
+    want = oracle.segment_reduce(msg, perm, ns, ne, len(lens), reduce)
+    got = csrc.segment_reduce_cuda(torch.from_numpy(msg).to(DEV), torch.from_numpy(perm).to(DEV),
+                                   torch.from_numpy(ns).to(DEV), torch.from_numpy(ne).to(DEV), len(lens),
+                                   reduce).cpu().numpy()
+    if reduce == "max":
+        assert np.array_equal(got, want)
+    else:
+        scale = np.array([np.abs(msg[perm[a:b]]).sum(0) for a, b in zip(ns, ne)])
+        assert np.all(np.abs(got - want) <= 1e-5 * scale + 1e-6)
+
+
 def test_segment_golden_and_reference_kats(golden, oracle):
     col = torch.from_numpy(golden["seg_r_col"]).to(DEV)
     msg = torch.from_numpy(golden["seg_r_msg"]).to(DEV)
