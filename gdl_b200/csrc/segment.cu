@@ -18,6 +18,7 @@
 // 142-158), VEC channels per lane. Max uses the forward's arg and re-reads msg only for
 // tied maxima, whose gradient is shared evenly (torch's amax rule).
 #include <initializer_list>
+#include <mutex>
 
 #include "common.cuh"
 #include "radix.cuh"
@@ -656,3 +657,82 @@ extern "C" int gdl_segment_reduce_backward(const float *grad_out, const void *ms
     return GDL_OK;
 }
 
+// ---------------------------------------------------------------------------------------------
+// Segment reduce without any allocation.
+//
+// Some callers cannot allocate device memory at the moment they reduce: code that runs while a
+// CUDA graph is being captured with a static memory plan, plugin hosts (inference engines,
+// real-time robot control loops) that forbid cudaMalloc / cudaFree on their enqueue path, or
+// programs with no allocator bound to the device at all. gdl_segment_reduce asks them for a
+// workspace; this variant instead keeps its only scratch -- the queue of segments longer than
+// kLongSegment slots -- in a fixed array compiled into the library. Every GPU that loads the
+// library holds that array (64 KiB) until the process exits.
+//
+// The array is shared by every call on a device and keeps whatever the last call left in it:
+// the queue counter is cleared by each call, and two calls whose kernels overlap on the GPU
+// (different streams, no ordering between them) race on it and must not be issued.
+namespace gdl {
+
+constexpr int kNoAllocSlots = 16384;  // the counter, padding to 256 bytes, then the queue
+constexpr int kNoAllocQueue = kNoAllocSlots - 64;
+// largest input whose long segments all fit the queue (with at most one slot per row)
+constexpr int64_t kNoAllocMaxRows = (int64_t)kNoAllocQueue * (kLongSegment + 1);
+constexpr int kNoAllocMaxDevices = 64;
+
+static __device__ __align__(256) int32_t g_seg_noalloc_scratch[kNoAllocSlots];
+
+// device address of g_seg_noalloc_scratch, looked up once per device with that device current
+static int32_t *g_noalloc_ptr[kNoAllocMaxDevices];
+static std::mutex g_noalloc_mutex;
+
+static int noalloc_scratch(int32_t **out) {
+    int dev = 0;
+    GDL_CUDA_TRY(cudaGetDevice(&dev));
+    GDL_RETURN_IF(dev < 0 || dev >= kNoAllocMaxDevices, GDL_ERR_UNSUPPORTED);
+    std::lock_guard<std::mutex> lock(g_noalloc_mutex);
+    if (!g_noalloc_ptr[dev]) {
+        void *p = nullptr;
+        GDL_CUDA_TRY(cudaGetSymbolAddress(&p, g_seg_noalloc_scratch));
+        g_noalloc_ptr[dev] = (int32_t *)p;
+    }
+    *out = g_noalloc_ptr[dev];
+    return GDL_OK;
+}
+
+}  // namespace gdl
+
+extern "C" int gdl_segment_reduce_noalloc(const void *msg, int32_t dtype, int64_t num_rows, int64_t C,
+                                          const int32_t *perm, const int32_t *node_start, const int32_t *node_end,
+                                          int64_t num_nodes, int32_t reduce, float *out, int32_t *arg_out,
+                                          void *stream) {
+    cudaStream_t st = (cudaStream_t)stream;
+    GDL_RETURN_IF(num_rows < 0 || C <= 0 || num_nodes < 0, GDL_ERR_INVALID);
+    GDL_RETURN_IF(num_rows > kNoAllocMaxRows, GDL_ERR_OVERFLOW);  // queue would not fit the array
+    GDL_RETURN_IF(dtype != GDL_DTYPE_F32 && dtype != GDL_DTYPE_BF16, GDL_ERR_INVALID);
+    GDL_RETURN_IF(reduce < GDL_REDUCE_SUM || reduce > GDL_REDUCE_MAX, GDL_ERR_INVALID);
+    if (num_nodes == 0) return GDL_OK;
+    GDL_RETURN_IF(!out || !node_start || !node_end || (num_rows > 0 && !msg), GDL_ERR_INVALID);
+    int32_t *scratch = nullptr;
+    const int rc = noalloc_scratch(&scratch);
+    if (rc != GDL_OK) return rc;
+    int32_t *long_count = scratch;
+    int32_t *long_list = scratch + 64;  // 256-byte offset
+    const int64_t want = num_rows / (kLongSegment + 1) + 1;
+    const int64_t max_long = want < kNoAllocQueue ? want : kNoAllocQueue;
+    GDL_CUDA_TRY(cudaMemsetAsync(long_count, 0, sizeof(int32_t), st));
+    const int64_t esz = dtype == GDL_DTYPE_BF16 ? 2 : 4;
+    const uintptr_t al = common_align({(uintptr_t)msg, (uintptr_t)(C * esz), (uintptr_t)out, (uintptr_t)(C * 4)});
+    if (dtype == GDL_DTYPE_F32) {
+        SegShape sh = seg_shape<float>(C, al);
+        if (reduce == GDL_REDUCE_SUM) launch_fwd_v<float, GDL_REDUCE_SUM>(sh, msg, C, perm, node_start, node_end, num_nodes, out, arg_out, long_list, long_count, max_long, st);
+        else if (reduce == GDL_REDUCE_MEAN) launch_fwd_v<float, GDL_REDUCE_MEAN>(sh, msg, C, perm, node_start, node_end, num_nodes, out, arg_out, long_list, long_count, max_long, st);
+        else launch_fwd_v<float, GDL_REDUCE_MAX>(sh, msg, C, perm, node_start, node_end, num_nodes, out, arg_out, long_list, long_count, max_long, st);
+    } else {
+        SegShape sh = fit_f32_side(seg_shape<uint16_t>(C, al), C, common_align({(uintptr_t)out, (uintptr_t)(C * 4)}));
+        if (reduce == GDL_REDUCE_SUM) launch_fwd_v<uint16_t, GDL_REDUCE_SUM>(sh, msg, C, perm, node_start, node_end, num_nodes, out, arg_out, long_list, long_count, max_long, st);
+        else if (reduce == GDL_REDUCE_MEAN) launch_fwd_v<uint16_t, GDL_REDUCE_MEAN>(sh, msg, C, perm, node_start, node_end, num_nodes, out, arg_out, long_list, long_count, max_long, st);
+        else launch_fwd_v<uint16_t, GDL_REDUCE_MAX>(sh, msg, C, perm, node_start, node_end, num_nodes, out, arg_out, long_list, long_count, max_long, st);
+    }
+    GDL_CUDA_TRY(cudaGetLastError());
+    return GDL_OK;
+}

@@ -163,6 +163,25 @@ int gdl_segment_reduce_backward(const float *grad_out, const void *msg, int32_t 
                                 const int32_t *node_start, const int32_t *node_end, int64_t num_nodes, int32_t reduce,
                                 void *grad_msg, void *workspace, size_t workspace_bytes, void *stream);
 
+/* Segment reduce that allocates nothing (no counterpart in the reference).
+ * For callers that may not allocate device memory while they run -- a CUDA graph being
+ * captured under a fixed memory plan, plugin or real-time hosts whose enqueue path forbids
+ * cudaMalloc / cudaFree, programs without an allocator for the device. Same arguments and
+ * results as gdl_segment_reduce, minus the workspace: its scratch (the queue of segments longer
+ * than 4096 slots) lives in a 64 KiB array built into the library, which every GPU that loads
+ * the library keeps until the process exits.
+ *  - num_rows must not exceed 66,863,040 (16,320 queued segments x 4,097 slots); larger inputs
+ *    return GDL_ERR_OVERFLOW.
+ *  - The first call on a device looks up the array's device address (cudaGetSymbolAddress) with
+ *    that device current; make that first call before any stream capture.
+ *  - All calls on a device share the array. Each call clears the part that must start at zero,
+ *    but calls whose kernels may overlap on the GPU (unordered streams) race and must not be
+ *    issued; order them on one stream or with events.
+ */
+int gdl_segment_reduce_noalloc(const void *msg, int32_t dtype, int64_t num_rows, int64_t C, const int32_t *perm,
+                               const int32_t *node_start, const int32_t *node_end, int64_t num_nodes, int32_t reduce,
+                               float *out, int32_t *arg_out, void *stream);
+
 #ifdef __cplusplus
 }
 #endif
