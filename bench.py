@@ -8,6 +8,11 @@ inputs with the shapes of the reference's use cases; see gdl_b200/synthetic.py):
   c2 (default)  16 clouds x 2048 points: FPS -> 512 centroids per cloud, radius graph
                 (r = 0.2, 32 neighbours) over the centroids, segment mean of 128-channel
                 features over that graph, forward and backward.
+  c1            4 clouds x 2048 uniform points: FPS -> 512, KNN k=16, segment sum and max
+                (64 channels).
+  c3            32 GMM clouds x 8192 points: FPS chain 8192 -> 2048 -> 512 -> 128, KNN k=32
+                per level, segment max over gathered bf16 features, forward and backward.
+  c4            64 source/target pairs x 16384 points: KNN k=1, residual segment sum.
   c5            8 clouds x 131072 LiDAR points: FPS -> 16384, radius graph (r = 1 m, 64),
                 segment sum of 64-channel features.
 
@@ -289,6 +294,178 @@ class C1:
         O.segment_reduce(self.msg_h.numpy(), None, ns, ns + self.KNN, self.nq, "max")
 
 
+class C3:
+    """32 GMM clouds x 8192 points: FPS chain 8192 -> 2048 -> 512 -> 128, KNN k=32 of each
+    level's centroids into the previous level's points, segment max over the gathered bf16
+    features of those points (C = 64 / 128 / 256, fp32 compare), forward and backward."""
+    name = "c3"
+    metric = ("points/sec (FPS chain 8192->2048->512->128 + KNN k=32 per level + bf16 segment max fwd+bwd), "
+              "config 3")
+    B, N, KNN = 32, 8192, 32
+    LEVELS = (2048, 512, 128)
+    CH = (64, 128, 256)
+    # per level: fps 1; knn tiles + pad + fast + merge + exact replay 5; gather 1; segment max fwd 2
+    # (short + long pass) and bwd 2
+    launches_per_step = 3 * (1 + 5 + 1 + 2 + 2)
+    points_per_step = property(lambda self: self.B * self.N)
+
+    def _sizes(self):
+        return (self.N,) + self.LEVELS
+
+    def _host_init(self, seed, pin=True):
+        pos, ptr = synthetic.c3_points(seed=seed, B=self.B, N=self.N)
+        sz = self._sizes()
+        self.pos_h = torch.from_numpy(pos)
+        self.lptr_h = [torch.arange(0, self.B * n + 1, n, dtype=torch.int64) for n in sz]
+        self.k_h = [torch.full((self.B,), n, dtype=torch.int64) for n in self.LEVELS]
+        # features of the points each level's KNN searches (levels 0, 1, 2)
+        self.feat_h = [synthetic.c3_level_features(self.B * sz[l], self.CH[l], seed + 1 + l) for l in range(3)]
+        g = torch.Generator().manual_seed(seed + 7)
+        self.gout_h = [torch.randn(self.B * self.LEVELS[l], self.CH[l], generator=g) for l in range(3)]
+        if pin:
+            self.pos_h = self.pos_h.pin_memory()
+            self.feat_h = [f.pin_memory() for f in self.feat_h]
+
+    def __init__(self, dev, seed):
+        self.dev = dev
+        self._host_init(seed)
+        L = self.L = nat.load()
+        sz = self._sizes()
+        self.pos = self.pos_h.to(dev)
+        self.lptr = [t.to(dev) for t in self.lptr_h]
+        self.k = [t.to(dev) for t in self.k_h]
+        self.feat = [t.to(dev) for t in self.feat_h]
+        self.gout = [t.to(dev) for t in self.gout_h]
+        nq = [self.B * n for n in self.LEVELS]
+        self.nq = nq
+        self.idx = [torch.empty(n, dtype=torch.int64, device=dev) for n in nq]
+        self.cent = [torch.empty(n, 3, device=dev) for n in nq]
+        self.nidx = [torch.empty(n, self.KNN, dtype=torch.int64, device=dev) for n in nq]
+        self.ndist = [torch.empty(n, self.KNN, device=dev) for n in nq]
+        self.csr = [_csr_uniform(n, self.KNN, dev) for n in nq]
+        self.msg = [torch.empty(nq[l] * self.KNN, self.CH[l], dtype=torch.bfloat16, device=dev) for l in range(3)]
+        self.gmsg = [torch.empty_like(m) for m in self.msg]
+        self.out = [torch.empty(nq[l], self.CH[l], device=dev) for l in range(3)]
+        self.arg = [torch.empty(nq[l], self.CH[l], dtype=torch.int32, device=dev) for l in range(3)]
+        self.ws_fps = [nat.workspace(L.gdl_fps_workspace_size(self.B * sz[l], sz[l]), dev) for l in range(3)]
+        self.ws_knn = [nat.workspace(L.gdl_knn_workspace_size(nq[l], self.B, self.KNN, sz[l]), dev) for l in range(3)]
+        self.ws_seg = [nat.workspace(L.gdl_segment_reduce_workspace_size(nq[l] * self.KNN, nq[l]), dev)
+                       for l in range(3)]
+
+    def _s(self):
+        return torch.cuda.current_stream(self.dev).cuda_stream
+
+    def _src(self, l):
+        return self.pos if l == 0 else self.cent[l - 1]
+
+    def stage_fps(self):
+        sz = self._sizes()
+        for l in range(3):
+            ws = self.ws_fps[l]
+            nat.check(self.L.gdl_fps(self._src(l).data_ptr(), self.lptr[l].data_ptr(), self.k[l].data_ptr(), self.B,
+                                     self.B * sz[l], sz[l], 0, self.idx[l].data_ptr(), self.cent[l].data_ptr(),
+                                     ws.data_ptr(), ws.numel(), self._s()), "fps")
+
+    def stage_knn(self):
+        sz = self._sizes()
+        for l in range(3):
+            ws = self.ws_knn[l]
+            nat.check(self.L.gdl_knn(self.cent[l].data_ptr(), self._src(l).data_ptr(), self.lptr[l + 1].data_ptr(),
+                                     self.lptr[l].data_ptr(), self.B, self.nq[l], self.KNN, sz[l],
+                                     self.nidx[l].data_ptr(), self.ndist[l].data_ptr(), ws.data_ptr(), ws.numel(),
+                                     self._s()), "knn")
+
+    def stage_gather(self):  # msg = feats[knn_idx], materialised
+        for l in range(3):
+            f = self.feat[l]
+            nat.check(self.L.gdl_gather_rows(f.data_ptr(), f.shape[0], f.shape[1] * 2, self.nidx[l].data_ptr(),
+                                             self.msg[l].shape[0], self.msg[l].data_ptr(), self._s()), "gather")
+
+    def stage_seg_fwd(self):
+        for l in range(3):
+            ns, ne = self.csr[l]
+            ws = self.ws_seg[l]
+            nat.check(self.L.gdl_segment_reduce(self.msg[l].data_ptr(), 1, self.msg[l].shape[0], self.CH[l], None,
+                                                ns.data_ptr(), ne.data_ptr(), self.nq[l], 2, self.out[l].data_ptr(),
+                                                self.arg[l].data_ptr(), ws.data_ptr(), ws.numel(), self._s()),
+                      "segment max")
+
+    def stage_seg_bwd(self):
+        for l in range(3):
+            ns, ne = self.csr[l]
+            ws = self.ws_seg[l]
+            nat.check(self.L.gdl_segment_reduce_backward(self.gout[l].data_ptr(), self.msg[l].data_ptr(), 1,
+                                                         self.out[l].data_ptr(), self.arg[l].data_ptr(),
+                                                         self.msg[l].shape[0], self.CH[l], None, ns.data_ptr(),
+                                                         ne.data_ptr(), self.nq[l], 2, self.gmsg[l].data_ptr(),
+                                                         ws.data_ptr(), ws.numel(), self._s()), "segment max bwd")
+
+    def stage_list(self):
+        return [("fps_chain", self.stage_fps), ("knn", self.stage_knn), ("gather", self.stage_gather),
+                ("segment_max_fwd", self.stage_seg_fwd), ("segment_max_bwd", self.stage_seg_bwd)]
+
+    def step(self):
+        for _, fn in self.stage_list():
+            fn()
+
+    def edges(self):
+        return sum(n * self.KNN for n in self.nq)
+
+    def stage_bytes(self, E):
+        sz, K = self._sizes(), self.KNN
+        nsrc = [self.B * n for n in sz]
+        return {
+            "fps_chain": sum(12 * nsrc[l] + 20 * self.nq[l] for l in range(3)),
+            "knn": sum(12 * (self.nq[l] + nsrc[l]) + 12 * self.nq[l] * K for l in range(3)),
+            "gather": sum(4 * self.nq[l] * K * self.CH[l] + 8 * self.nq[l] * K for l in range(3)),
+            # bf16 messages in; fp32 max + int32 arg out; 8 bytes of offsets per segment
+            "segment_max_fwd": sum(2 * self.nq[l] * K * self.CH[l] + 8 * self.nq[l] * (self.CH[l] + 1)
+                                   for l in range(3)),
+            # fp32 grad_out + int32 arg in; bf16 grad for every message slot out
+            "segment_max_bwd": sum(8 * self.nq[l] * (self.CH[l] + 1) + 2 * self.nq[l] * K * self.CH[l]
+                                   for l in range(3)),
+        }
+
+    def e2e_step(self):
+        pos = self.pos_h.to(self.dev, non_blocking=True)
+        feats = [f.to(self.dev, non_blocking=True) for f in self.feat_h]
+        src, outs = pos, []
+        for l in range(3):
+            _, cent = csrc.fps_cuda(src, self.lptr_h[l], self.k_h[l], return_pos=True)
+            nidx, _ = csrc.knn_cuda(cent, src, self.lptr_h[l + 1], self.lptr_h[l], self.KNN)
+            msg = csrc.gather_rows(feats[l], nidx)
+            ns, ne = self.csr[l]
+            out, arg = csrc.segment_reduce_cuda(msg, None, ns, ne, self.nq[l], "max", with_arg=True)
+            csrc.segment_reduce_backward_cuda(self.gout[l], msg, out, arg, None, ns, ne, self.nq[l], "max",
+                                              grad_msg=self.gmsg[l])
+            outs.append(out.to("cpu", non_blocking=True))
+            src = cent
+        torch.cuda.current_stream(self.dev).synchronize()
+        return outs
+
+    e2e_h2d = property(lambda self: self.pos_h.numel() * 4 + sum(f.numel() * 2 for f in self.feat_h))
+    e2e_d2h = property(lambda self: sum(self.nq[l] * self.CH[l] * 4 for l in range(3)))
+
+    cpu_clouds = 1
+    cpu_fraction = 1 / 32
+    cpu_sample = "1 of 32 clouds (FPS chain, KNN per level, bf16 segment max fwd+bwd) per sample, scaled x32"
+
+    def cpu_step(self, O):
+        sz = self._sizes()
+        src = self.pos_h.numpy()[: self.N]
+        for l in range(3):
+            n, m = sz[l], self.LEVELS[l]
+            idx = O.fps(src, [0, n], [m], dist=O.DIST_CUDA)
+            cent = src[idx]
+            nidx, _ = O.knn(cent, src, [0, m], [0, n], self.KNN, dist=O.DIST_CUDA)
+            bits = self.feat_h[l][:n].view(torch.int16).numpy().view(np.uint16)
+            msg = bits[nidx.reshape(-1)]
+            ns = (np.arange(m) * self.KNN).astype(np.int32)
+            out = O.segment_reduce(msg, None, ns, ns + self.KNN, m, "max")
+            O.segment_reduce_backward(self.gout_h[l][:m].numpy(), msg, out, None, ns, ns + self.KNN, m, "max")
+            src = cent
+
+
 class C4:
     """64 source/target pairs x 16384 points: KNN k=1 target->source, 6-channel residual
     features, segment sum per cloud (64 segments x 16384 rows)."""
@@ -481,7 +658,7 @@ class C5:
         O.fps(pos, [0, self.N], [self.cpu_picks], dist=O.DIST_CUDA)
 
 
-CONFIGS = {"c1": C1, "c2": C2, "c4": C4, "c5": C5}
+CONFIGS = {"c1": C1, "c2": C2, "c3": C3, "c4": C4, "c5": C5}
 
 
 

@@ -39,6 +39,7 @@ PROTOTYPES = {
     "gdl_segment_reduce_noalloc": (ctypes.c_int, [_P, _I32, _I64, _I64, _P, _P, _P, _I64, _I32, _P, _P, _P]),
     "gdl_segment_reduce_backward": (ctypes.c_int,
                                     [_P, _P, _I32, _P, _P, _I64, _I64, _P, _P, _P, _I64, _I32, _P, _P, _SZ, _P]),
+    "gdl_gather_rows": (ctypes.c_int, [_P, _I64, _I64, _P, _I64, _P, _P]),
 }
 
 TIE = {"reference": 0, "lowest_index": 1}

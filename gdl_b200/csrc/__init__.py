@@ -18,11 +18,13 @@ from __future__ import annotations
 
 from typing import Optional, Tuple
 
+import numpy as np
 import torch
 
 from .. import _native as nat
 
 __all__ = [
+    "gather_rows",
     "get_radius_graph_backend", "radius_graph_cuda", "radius_graph_csr",
     "segment_reduce_available", "sort_and_build_csr_cuda", "segment_reduce_sum_cuda", "segment_reduce_cuda",
     "segment_reduce_backward_cuda", "knn_available", "knn_cuda", "knn_self_cuda", "fps_available", "fps_cuda",
@@ -99,6 +101,7 @@ def knn_cuda(query: torch.Tensor, source: torch.Tensor, ptr_q: torch.Tensor, ptr
     dev = nat.require_cuda(query, source, what="knn_cuda")
     query = query.contiguous().float()
     source = source.contiguous().float()
+    ptr_s_host = ptr_s.to(torch.int64) if not ptr_s.is_cuda else None
     ptr_q = ptr_q.to(device=dev, dtype=torch.int64).contiguous()
     ptr_s = ptr_s.to(device=dev, dtype=torch.int64).contiguous()
     K = int(k)
@@ -111,7 +114,12 @@ def knn_cuda(query: torch.Tensor, source: torch.Tensor, ptr_q: torch.Tensor, ptr
     idx = torch.empty(nq, K, dtype=torch.int64, device=dev)
     dist = torch.empty(nq, K, dtype=torch.float32, device=dev)
     L = nat.load()
-    max_src = source.shape[0]
+    # largest cloud: exact when ptr_s lives on the host, else the mean (it only sizes the
+    # split of each cloud's scan over CTAs; any value is correct)
+    if ptr_s_host is not None and B > 0:
+        max_src = int((ptr_s_host[1:] - ptr_s_host[:-1]).max())
+    else:
+        max_src = -(-source.shape[0] // max(B, 1))
     ws = nat.workspace(L.gdl_knn_workspace_size(nq, B, K, max_src), dev)
     nat.check(L.gdl_knn(query.data_ptr(), source.data_ptr() if source.numel() else None, ptr_q.data_ptr(),
                         ptr_s.data_ptr(), B, nq, K, max_src, idx.data_ptr(), dist.data_ptr(), ws.data_ptr(),
@@ -266,3 +274,22 @@ def segment_reduce_backward_cuda(grad_out: torch.Tensor, msg: torch.Tensor, out:
                                             nat.REDUCE[reduce], grad_msg.data_ptr(), ws.data_ptr(), ws.numel(),
                                             nat.stream(dev)), "gdl_segment_reduce_backward")
     return grad_msg
+
+
+def gather_rows(src: torch.Tensor, idx: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """out[i] = src[idx[i]] for a 2-D tensor of any dtype (rows of a multiple of 4 bytes);
+    indices outside [0, src.shape[0]) give zero rows. The msg = feats[knn_idx] step of the
+    reference's pooling layer (nn/modules/equivariant_pool.py:277-300)."""
+    dev = nat.require_cuda(src, idx, what="gather_rows")
+    src = src.contiguous()
+    idx = idx.reshape(-1).to(torch.int64).contiguous()
+    shape = (idx.numel(),) + tuple(src.shape[1:])
+    if out is None:
+        out = torch.empty(shape, dtype=src.dtype, device=dev)
+    elif tuple(out.shape) != shape or out.dtype != src.dtype or not out.is_contiguous():
+        raise nat.GdlError("gather_rows: out must be a contiguous tensor of shape [len(idx), *src.shape[1:]]")
+    row_bytes = src[0].numel() * src.element_size() if src.shape[0] else int(np.prod(shape[1:])) * src.element_size()
+    nat.check(nat.load().gdl_gather_rows(src.data_ptr() if src.numel() else None, src.shape[0], row_bytes,
+                                         idx.data_ptr(), idx.numel(), out.data_ptr(), nat.stream(dev)),
+              "gdl_gather_rows")
+    return out

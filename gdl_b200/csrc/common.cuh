@@ -57,6 +57,29 @@ __device__ __forceinline__ float dist2(float ax, float ay, float az, float bx, f
     return fma_ftz(dz, dz, fma_ftz(dx, dx, mul_ftz(dy, dy)));
 }
 
+// ---------------------------------------------------------------- packed fp32x2 arithmetic
+// sm_100a executes two fp32 lanes per instruction with the same IEEE rounding as the scalar
+// forms (.rn, flush-to-zero), so the packed distance below is bit-identical to dist2().
+__device__ __forceinline__ uint64_t pack2(float lo, float hi) {
+    uint64_t r;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+    return r;
+}
+__device__ __forceinline__ void unpack2(uint64_t v, float &lo, float &hi) {
+    asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+}
+__device__ __forceinline__ uint64_t dist2_x2(uint64_t qx, uint64_t qy, uint64_t qz, uint64_t sx, uint64_t sy,
+                                             uint64_t sz) {
+    uint64_t dx, dy, dz, r;
+    asm("sub.rn.ftz.f32x2 %0, %1, %2;" : "=l"(dx) : "l"(qx), "l"(sx));
+    asm("sub.rn.ftz.f32x2 %0, %1, %2;" : "=l"(dy) : "l"(qy), "l"(sy));
+    asm("sub.rn.ftz.f32x2 %0, %1, %2;" : "=l"(dz) : "l"(qz), "l"(sz));
+    asm("mul.rn.ftz.f32x2 %0, %1, %1;" : "=l"(r) : "l"(dy));
+    asm("fma.rn.ftz.f32x2 %0, %1, %1, %2;" : "=l"(r) : "l"(dx), "l"(r));
+    asm("fma.rn.ftz.f32x2 %0, %1, %1, %2;" : "=l"(r) : "l"(dz), "l"(r));
+    return r;
+}
+
 // ---------------------------------------------------------------- warp helpers
 __device__ __forceinline__ unsigned lane_id() { return threadIdx.x & 31u; }
 

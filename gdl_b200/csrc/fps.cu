@@ -97,11 +97,14 @@ __device__ __forceinline__ void pad_outputs(int64_t *__restrict__ out, float *__
 // Per-thread register state: P points i = base + threadIdx.x + j * THREADS.
 template <int THREADS, int P>
 struct PointRegs {
-    float x[P], y[P], z[P], md[P];
+    static_assert(P % 2 == 0, "points are held in pairs");
+    uint64_t xp[P / 2], yp[P / 2], zp[P / 2];  // coordinates of points (2h, 2h+1), packed fp32x2
+    float md[P];
     uint32_t np[P];  // ~priority; 0 marks a padding slot (never wins)
 
     __device__ __forceinline__ void load(const float *__restrict__ pos, int64_t start, int n, int base, int tie,
                                          float4 *__restrict__ sxyz) {
+        float x[P], y[P], z[P];
 #pragma unroll
         for (int j = 0; j < P; ++j) {
             const int i = base + (int)threadIdx.x + j * THREADS;
@@ -119,16 +122,27 @@ struct PointRegs {
                 np[j] = 0u;
             }
         }
+#pragma unroll
+        for (int h = 0; h < P / 2; ++h) {
+            xp[h] = pack2(x[2 * h], x[2 * h + 1]);
+            yp[h] = pack2(y[2 * h], y[2 * h + 1]);
+            zp[h] = pack2(z[2 * h], z[2 * h + 1]);
+        }
     }
 
     // update the minima against (sx, sy, sz); this thread's best key (tree max over P)
     __device__ __forceinline__ uint64_t step(float sx, float sy, float sz) {
+        const uint64_t SX = pack2(sx, sx), SY = pack2(sy, sy), SZ = pack2(sz, sz);
         uint64_t k[P];
 #pragma unroll
-        for (int j = 0; j < P; ++j) {
-            const float m = fminf(dist2(x[j], y[j], z[j], sx, sy, sz), md[j]);
-            md[j] = m;
-            k[j] = np[j] ? make_key(m, np[j]) : 0ull;
+        for (int h = 0; h < P / 2; ++h) {
+            float d0, d1;  // dist2(point, s) for both points of the pair, bit-identical to dist2()
+            unpack2(dist2_x2(xp[h], yp[h], zp[h], SX, SY, SZ), d0, d1);
+            const float m0 = fminf(d0, md[2 * h]), m1 = fminf(d1, md[2 * h + 1]);
+            md[2 * h] = m0;
+            md[2 * h + 1] = m1;
+            k[2 * h] = np[2 * h] ? make_key(m0, np[2 * h]) : 0ull;
+            k[2 * h + 1] = np[2 * h + 1] ? make_key(m1, np[2 * h + 1]) : 0ull;
         }
 #pragma unroll
         for (int w = 1; w < P; w <<= 1)
@@ -368,7 +382,7 @@ extern "C" int gdl_fps(const float *pos, const int64_t *ptr, const int64_t *k_pe
     else if (m <= 1024) e = launch_cta<256, 4>(num_clouds, pos, ptr, k_per_cloud, tie_break, out_idx, out_pos, st);
     else if (m <= 2048) e = launch_cta<256, 8>(num_clouds, pos, ptr, k_per_cloud, tie_break, out_idx, out_pos, st);
     else if (m <= 4096) e = launch_cta<256, 16>(num_clouds, pos, ptr, k_per_cloud, tie_break, out_idx, out_pos, st);
-    else if (m <= kCtaCapacity) e = launch_cta<kClusterThreads, kClusterP>(num_clouds, pos, ptr, k_per_cloud, tie_break, out_idx, out_pos, st);
+    else if (m <= kCtaCapacity) e = launch_cta<256, 32>(num_clouds, pos, ptr, k_per_cloud, tie_break, out_idx, out_pos, st);
     else {
         const int cs = (int)((m + kCtaCapacity - 1) / kCtaCapacity);
         e = cudaErrorInvalidConfiguration;

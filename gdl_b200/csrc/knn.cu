@@ -49,62 +49,59 @@ __global__ void __launch_bounds__(kScanThreads) knn_tiles_kernel(const int64_t *
 // each of them touches.
 constexpr int kKnnGroup = 8;  // sources per distance group (one vote, one group minimum)
 constexpr int kKnnBuf = 16;   // buffered candidates per thread; a flush starts at > kKnnBuf - kKnnGroup
+constexpr int kS = kKnnThreads;  // stride between the slots of one thread's list
 
-__device__ __forceinline__ void sheap_sift_down(float *d, int *id, int n, int at) {
-    for (;;) {
-        const int l = 2 * at + 1, r = l + 1;
-        int g = at;
-        float gd = d[at * kKnnThreads];
-        if (l < n) {
-            const float ld = d[l * kKnnThreads];
-            if (ld > gd) { g = l; gd = ld; }
+// Entries are (distance, index bits) pairs. kheap_* is a max-heap of L entries over distance
+// (filled unsorted, heapified when full, root replaced by strictly smaller distances); `thr`
+// mirrors the root once full (+inf before). Sinks x from slot `at`.
+template <int L>
+__device__ __forceinline__ void kheap_sink(float2 *h, int at, float2 x) {
+#pragma unroll
+    for (int lvl = 0; lvl < 7; ++lvl) {  // 7 levels hold 127 >= L entries
+        const int l = 2 * at + 1;
+        if (l >= L) break;
+        float2 c = h[l * kS];
+        int g = l;
+        if (l + 1 < L) {
+            const float2 r = h[(l + 1) * kS];
+            if (r.x > c.x) {
+                c = r;
+                g = l + 1;
+            }
         }
-        if (r < n) {
-            const float rd = d[r * kKnnThreads];
-            if (rd > gd) { g = r; gd = rd; }
-        }
-        if (g == at) return;
-        const float td = d[at * kKnnThreads];
-        const int ti = id[at * kKnnThreads];
-        d[at * kKnnThreads] = gd;
-        id[at * kKnnThreads] = id[g * kKnnThreads];
-        d[g * kKnnThreads] = td;
-        id[g * kKnnThreads] = ti;
+        if (!(c.x > x.x)) break;
+        h[at * kS] = c;
         at = g;
     }
+    h[at * kS] = x;
 }
 
-// Max-heap of the L smallest distances seen (filled unsorted, heapified when full, root
-// replaced by strictly smaller distances). `thr` mirrors the root once full (+inf before).
-__device__ __forceinline__ void sheap_add(float *d, int *id, int &cnt, int L, float &thr, float dist, int idx) {
+template <int L>
+__device__ __forceinline__ void kheap_add(float2 *h, int &cnt, float &thr, float2 x) {
     if (cnt < L) {
-        d[cnt * kKnnThreads] = dist;
-        id[cnt * kKnnThreads] = idx;
+        h[cnt * kS] = x;
         if (++cnt == L) {
-            for (int j = L / 2 - 1; j >= 0; --j) sheap_sift_down(d, id, L, j);
-            thr = d[0];
+            for (int j = L / 2 - 1; j >= 0; --j) kheap_sink<L>(h, j, h[j * kS]);
+            thr = h[0].x;
         }
     } else {
-        d[0] = dist;
-        id[0] = idx;
-        sheap_sift_down(d, id, L, 0);
-        thr = d[0];
+        kheap_sink<L>(h, 0, x);
+        thr = h[0].x;
     }
 }
 
-// ascending by distance, into thread-local arrays
-__device__ __forceinline__ void sheap_sorted(const float *d, const int *id, int cnt, float *od, int *oi) {
+// the heap's entries, ascending by distance, into thread-local arrays
+__device__ __forceinline__ void kheap_sorted(const float2 *h, int cnt, float *od, int *oi) {
     for (int a = 0; a < cnt; ++a) {
-        const float kd = d[a * kKnnThreads];
-        const int ki = id[a * kKnnThreads];
+        const float2 x = h[a * kS];
         int b = a - 1;
-        while (b >= 0 && od[b] > kd) {
+        while (b >= 0 && od[b] > x.x) {
             od[b + 1] = od[b];
             oi[b + 1] = oi[b];
             --b;
         }
-        od[b + 1] = kd;
-        oi[b + 1] = ki;
+        od[b + 1] = x.x;
+        oi[b + 1] = __float_as_int(x.y);
     }
 }
 
@@ -127,54 +124,31 @@ __device__ __forceinline__ void write_row(int64_t *__restrict__ oi, float *__res
     }
 }
 
-// ---------------------------------------------------------------- packed fp32x2 arithmetic
-// sm_100a executes two fp32 lanes per instruction with the same IEEE rounding as the scalar
-// forms (.rn, flush-to-zero), so the packed distance below is bit-identical to dist2().
-__device__ __forceinline__ uint64_t pack2(float lo, float hi) {
-    uint64_t r;
-    asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
-    return r;
-}
-__device__ __forceinline__ void unpack2(uint64_t v, float &lo, float &hi) {
-    asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
-}
-__device__ __forceinline__ uint64_t dist2_x2(uint64_t qx, uint64_t qy, uint64_t qz, uint64_t sx, uint64_t sy,
-                                             uint64_t sz) {
-    uint64_t dx, dy, dz, r;
-    asm("sub.rn.ftz.f32x2 %0, %1, %2;" : "=l"(dx) : "l"(qx), "l"(sx));
-    asm("sub.rn.ftz.f32x2 %0, %1, %2;" : "=l"(dy) : "l"(qy), "l"(sy));
-    asm("sub.rn.ftz.f32x2 %0, %1, %2;" : "=l"(dz) : "l"(qz), "l"(sz));
-    asm("mul.rn.ftz.f32x2 %0, %1, %1;" : "=l"(r) : "l"(dy));
-    asm("fma.rn.ftz.f32x2 %0, %1, %1, %2;" : "=l"(r) : "l"(dx), "l"(r));
-    asm("fma.rn.ftz.f32x2 %0, %1, %1, %2;" : "=l"(r) : "l"(dz), "l"(r));
-    return r;
-}
-
 // ---------------------------------------------------------------- fast path
-template <int KB>
+template <int L>
 struct KnnSmem {
     float sx[kKnnChunk], sy[kKnnChunk], sz[kKnnChunk];  // staged sources, SoA
-    float hd[(KB + 1) * kKnnThreads];                    // heap of the k_eff + 1 best
-    int hi[(KB + 1) * kKnnThreads];
-    float bd[kKnnBuf * kKnnThreads];  // candidates that beat the threshold, not yet in the heap
-    int bi[kKnnBuf * kKnnThreads];
-    int nonfinite;                    // a staged source has a NaN/inf coordinate
+    float2 heap[L * kKnnThreads];                        // the L best per thread
+    float2 buf[kKnnBuf * kKnnThreads];  // candidates that beat the threshold, not yet in the heap
+    int nonfinite;                      // a staged source has a NaN/inf coordinate
 };
 
-template <int KB>
+template <int L>
 constexpr size_t knn_smem_bytes() {
-    return sizeof(KnnSmem<KB>);
+    return sizeof(KnnSmem<L>);
 }
 
 // Fast path: kKnnThreads queries of one cloud per CTA (one per thread, coordinates in
 // registers); the cloud's sources (or this CTA's share of them, `split` > 1) are staged in
 // shared memory in kKnnChunk-point chunks and read by broadcast, eight at a time. A thread
-// keeps its k_eff + 1 best in a shared-memory max-heap; distances below the heap root go
+// keeps its L best (L = KB + 1, KB = the reference's heap size >= k; L = 2 for k = 1) in a
+// shared-memory max-heap, of which the first k_eff + 1 decide the output; distances below the
+// heap root go
 // to a per-thread buffer first, and the warp drains all its buffers together once a vote
 // finds one nearly full -- so heap work is paid per lane, not per union of lanes. Queries
-// whose final list holds equal distances, or that met a non-finite coordinate, are handed
-// to knn_exact_kernel.
-template <int KB>
+// whose final list holds equal distances, that met a non-finite coordinate or whose
+// distances overflowed are handed to knn_exact_kernel.
+template <int KB, int L>
 __global__ void __launch_bounds__(kKnnThreads) knn_fast_kernel(
     const float *__restrict__ query, const float *__restrict__ source, const int64_t *__restrict__ ptr_q,
     const int64_t *__restrict__ ptr_s, int32_t B, int k, int split, const int32_t *__restrict__ tile_base,
@@ -182,7 +156,7 @@ __global__ void __launch_bounds__(kKnnThreads) knn_fast_kernel(
     int32_t *__restrict__ part_i, int32_t *__restrict__ part_cnt, int32_t *__restrict__ flag_list,
     int32_t *__restrict__ flag_count) {
     extern __shared__ __align__(16) unsigned char knn_smem_raw[];
-    KnnSmem<KB> &S = *reinterpret_cast<KnnSmem<KB> *>(knn_smem_raw);
+    KnnSmem<L> &S = *reinterpret_cast<KnnSmem<L> *>(knn_smem_raw);
     const int t = blockIdx.x;
     const int qt = t / split, sp = t - (t / split) * split;
     if (qt >= tile_base[B]) return;  // uniform over the CTA
@@ -193,7 +167,6 @@ __global__ void __launch_bounds__(kKnnThreads) knn_fast_kernel(
     const int64_t s0 = ptr_s[b], len = ptr_s[b + 1] - ptr_s[b];
     const int64_t ss = s0 + len * sp / split, se = s0 + len * (sp + 1) / split;
     const int ke = k < 64 ? k : 64;
-    const int L = ke + 1;
     float qx = 0.0f, qy = 0.0f, qz = 0.0f;
     bool nonfinite = false;
     if (valid) {
@@ -204,10 +177,8 @@ __global__ void __launch_bounds__(kKnnThreads) knn_fast_kernel(
     }
     if (tid == 0) S.nonfinite = 0;
     const uint64_t QX = pack2(qx, qx), QY = pack2(qy, qy), QZ = pack2(qz, qz);
-    float *hd = S.hd + tid;
-    int *hi = S.hi + tid;
-    float *bd = S.bd + tid;
-    int *bi = S.bi + tid;
+    float2 *heap = S.heap + tid;
+    float2 *buf = S.buf + tid;
     int cnt = 0, nb = 0;
     // invalid threads run the loop (they vote) but never accept a candidate
     float thr = valid ? __int_as_float(0x7f800000) : -__int_as_float(0x7f800000);
@@ -235,8 +206,8 @@ __global__ void __launch_bounds__(kKnnThreads) knn_fast_kernel(
         for (int j = 0; j < mg; j += kKnnGroup) {
             if (__any_sync(0xffffffffu, nb > kKnnBuf - kKnnGroup)) {
                 for (int e = 0; e < nb; ++e) {
-                    const float d = bd[e * kKnnThreads];
-                    if (d < thr) sheap_add(hd, hi, cnt, L, thr, d, bi[e * kKnnThreads]);
+                    const float2 x = buf[e * kS];
+                    if (x.x < thr) kheap_add<L>(heap, cnt, thr, x);
                 }
                 nb = 0;
             }
@@ -253,28 +224,31 @@ __global__ void __launch_bounds__(kKnnThreads) knn_fast_kernel(
             unpack2(dist2_x2(QX, QY, QZ, pack2(x1.z, x1.w), pack2(y1.z, y1.w), pack2(z1.z, z1.w)), d[6], d[7]);
             const float mn = fminf(fminf(fminf(d[0], d[1]), fminf(d[2], d[3])), fminf(fminf(d[4], d[5]), fminf(d[6], d[7])));
             if (mn < thr) {
+                // branch-free append: every candidate is written at slot nb, which advances only
+                // when it is kept (nb <= kKnnBuf - kKnnGroup here, so slot nb stays in range)
                 const int base = (int)(c0 + j);  // global index of d[0]
 #pragma unroll
                 for (int e = 0; e < kKnnGroup; ++e) {
-                    if (d[e] < thr) {
-                        bd[nb * kKnnThreads] = d[e];
-                        bi[nb * kKnnThreads] = base + e;
-                        ++nb;
-                    }
+                    buf[nb * kS] = make_float2(d[e], __int_as_float(base + e));
+                    nb += d[e] < thr ? 1 : 0;
                 }
             }
         }
     }
     for (int e = 0; e < nb; ++e) {
-        const float d = bd[e * kKnnThreads];
-        if (d < thr) sheap_add(hd, hi, cnt, L, thr, d, bi[e * kKnnThreads]);
+        const float2 x = buf[e * kS];
+        if (x.x < thr) kheap_add<L>(heap, cnt, thr, x);
     }
     __syncthreads();  // S.nonfinite is complete
     nonfinite |= S.nonfinite != 0;
     if (!valid) return;
     float td[KB + 1];
     int ti[KB + 1];
-    sheap_sorted(hd, hi, cnt, td, ti);
+    // Every finite distance enters a heap that is not full, so a short list means distances
+    // that overflowed to +inf (or NaN): the reference's heap keeps those while it fills.
+    nonfinite |= (int64_t)cnt < (se - ss < L ? se - ss : (int64_t)L);
+    kheap_sorted(heap, cnt, td, ti);
+    if (cnt > ke + 1) cnt = ke + 1;  // only the first k_eff + 1 decide the output
     if (split == 1) {
         if (nonfinite || top_has_tie(td, cnt)) {
             flag_list[atomicAdd(flag_count, 1)] = (int32_t)q;
@@ -293,53 +267,72 @@ __global__ void __launch_bounds__(kKnnThreads) knn_fast_kernel(
     }
 }
 
-// Merges the `split` ascending partial lists of a query (two-pointer merges, first L kept).
-template <int KB>
+// Merges the `split` ascending partial lists of a query (at most k_eff + 1 entries each):
+// one warp per query stages the lists in shared memory, lane s walks list s, and each step
+// takes the smallest head (lowest list on equal heads) by a warp min-reduction.
+constexpr int kMergeWarps = kKnnThreads / 32;
+
+static size_t knn_merge_smem(int split, int k) {
+    const int lm = (k < 64 ? k : 64) + 1;
+    return sizeof(float2) * (size_t)kMergeWarps * (size_t)(split + 1) * lm;
+}
+
 __global__ void __launch_bounds__(kKnnThreads) knn_merge_kernel(
-    const int64_t *__restrict__ ptr_q, int32_t B, int k, int split, const float *__restrict__ part_d,
+    const int64_t *__restrict__ ptr_q, int32_t B, int k, int split, int part_stride, const float *__restrict__ part_d,
     const int32_t *__restrict__ part_i, const int32_t *__restrict__ part_cnt, int64_t *__restrict__ out_idx,
     float *__restrict__ out_dist, int32_t *__restrict__ flag_list, int32_t *__restrict__ flag_count) {
-    const int64_t q = ptr_q[0] + (int64_t)blockIdx.x * kKnnThreads + threadIdx.x;
-    if (q >= ptr_q[B]) return;
+    extern __shared__ float2 merge_smem[];
+    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+    const int64_t q = ptr_q[0] + (int64_t)blockIdx.x * kMergeWarps + w;
+    if (q >= ptr_q[B]) return;  // uniform over the warp
     const int ke = k < 64 ? k : 64;
-    const int L = ke + 1;
-    float ad[KB + 1], bdv[KB + 1];
-    int ai[KB + 1], biv[KB + 1];
-    float *cd = ad, *nd = bdv;
-    int *ci = ai, *ni = biv;
-    int cnt = 0;
+    const int lm = ke + 1;
+    float2 *stage = merge_smem + (size_t)w * (split + 1) * lm;
+    float2 *out = stage + (size_t)split * lm;
     const int64_t base = (q - ptr_q[0]) * split;
-    for (int sp = 0; sp < split; ++sp) {
-        const int c = part_cnt[base + sp];
-        if (c < 0) {  // a partial scan met a non-finite coordinate
-            flag_list[atomicAdd(flag_count, 1)] = (int32_t)q;
-            return;
-        }
-        const float *pd = part_d + (base + sp) * (KB + 1);
-        const int32_t *pi = part_i + (base + sp) * (KB + 1);
-        int a = 0, bb = 0, o = 0;
-        while (o < L && (a < cnt || bb < c)) {
-            const bool take_b = bb < c && (a >= cnt || pd[bb] < cd[a]);
-            if (take_b) {
-                nd[o] = pd[bb];
-                ni[o] = pi[bb];
-                ++bb;
-            } else {
-                nd[o] = cd[a];
-                ni[o] = ci[a];
-                ++a;
-            }
-            ++o;
-        }
-        cnt = o;
-        float *tdp = cd; cd = nd; nd = tdp;
-        int *tip = ci; ci = ni; ni = tip;
-    }
-    if (top_has_tie(cd, cnt)) {
-        flag_list[atomicAdd(flag_count, 1)] = (int32_t)q;
+    int c = lane < split ? part_cnt[base + lane] : 0;
+    if (__any_sync(0xffffffffu, c < 0)) {  // a partial scan met a non-finite coordinate
+        if (lane == 0) flag_list[atomicAdd(flag_count, 1)] = (int32_t)q;
         return;
     }
-    write_row(out_idx + q * k, out_dist + q * k, k, cnt < ke ? cnt : ke, cd, ci);
+    if (c > lm) c = lm;
+    for (int sp = 0; sp < split; ++sp) {
+        const int cs = __shfl_sync(0xffffffffu, c, sp);
+        const float *pd = part_d + (base + sp) * part_stride;
+        const int32_t *pi = part_i + (base + sp) * part_stride;
+        for (int j = lane; j < cs; j += 32) stage[sp * lm + j] = make_float2(pd[j], __int_as_float(pi[j]));
+    }
+    __syncwarp();
+    int p = 0;
+    unsigned key = c > 0 ? __float_as_uint(stage[lane * lm].x) : 0xffffffffu;  // distances are >= 0
+    int cnt = 0;
+    for (; cnt < lm; ++cnt) {
+        const unsigned m = __reduce_min_sync(0xffffffffu, key);
+        if (m == 0xffffffffu) break;
+        const int win = __ffs(__ballot_sync(0xffffffffu, key == m)) - 1;
+        if (lane == win) {
+            out[cnt] = stage[lane * lm + p];
+            ++p;
+            key = p < c ? __float_as_uint(stage[lane * lm + p].x) : 0xffffffffu;
+        }
+    }
+    __syncwarp();
+    bool tie = false;
+    for (int j = 1 + lane; j < cnt; j += 32) tie |= out[j].x == out[j - 1].x;
+    if (__any_sync(0xffffffffu, tie)) {
+        if (lane == 0) flag_list[atomicAdd(flag_count, 1)] = (int32_t)q;
+        return;
+    }
+    const int valid = cnt < ke ? cnt : ke;
+    for (int j = lane; j < k; j += 32) {
+        if (j < valid) {
+            out_idx[q * k + j] = __float_as_int(out[j].y);
+            out_dist[q * k + j] = out[j].x;
+        } else {
+            out_idx[q * k + j] = -1;
+            out_dist[q * k + j] = 1e30f;
+        }
+    }
 }
 
 __device__ __forceinline__ int find_cloud(const int64_t *__restrict__ ptr, int B, int64_t q) {
@@ -354,9 +347,10 @@ __device__ __forceinline__ int find_cloud(const int64_t *__restrict__ ptr, int B
 
 // The reference kernel's heap, replayed exactly for flagged queries: one warp per query.
 // The lanes compute 32 distances at a time; a candidate the heap would reject at the start
-// of the batch (full and d >= root -- the root never grows) is rejected at its turn too, so
-// only the ballot of the others is walked, in source order, and every lane applies the
-// same MinKHeap::add to its own copy of the heap.
+// of the batch (full and d >= root -- the root never grows while distances are ordered) is
+// rejected at its turn too, so only the ballot of the others is walked, in source order,
+// and every lane applies the same MinKHeap::add to its own copy of the heap. A batch with a
+// NaN distance (or a NaN root) walks every candidate.
 __global__ void __launch_bounds__(kKnnThreads) knn_exact_kernel(
     const float *__restrict__ query, const float *__restrict__ source, const int64_t *__restrict__ ptr_q,
     const int64_t *__restrict__ ptr_s, int32_t B, int k, const int32_t *__restrict__ flag_list,
@@ -370,17 +364,32 @@ __global__ void __launch_bounds__(kKnnThreads) knn_exact_kernel(
         const float qx = query[3 * q], qy = query[3 * q + 1], qz = query[3 * q + 2];
         MinKHeap h;
         h.init(knn_bucket(k));
-        for (int64_t c0 = ptr_s[b]; c0 < ptr_s[b + 1]; c0 += 32) {
-            const int64_t s = c0 + lane;
-            const bool in = s < ptr_s[b + 1];
-            float d = 0.0f;
-            if (in) d = dist2(qx, qy, qz, source[3 * s], source[3 * s + 1], source[3 * s + 2]);
-            const bool full = h.count >= h.cap;
-            unsigned live = __ballot_sync(0xffffffffu, in && !(full && d >= h.d[0]));
-            while (live) {
-                const int l = __ffs(live) - 1;
-                live &= live - 1;
-                h.add(__shfl_sync(0xffffffffu, d, l), (int)(c0 + l));
+        const int64_t se = ptr_s[b + 1];
+        for (int64_t c0 = ptr_s[b]; c0 < se; c0 += 128) {
+            float px[4], py[4], pz[4];
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {  // loads of four rounds in flight together
+                const int64_t s = c0 + 32 * u + lane;
+                px[u] = py[u] = pz[u] = 0.0f;
+                if (s < se) {
+                    px[u] = source[3 * s];
+                    py[u] = source[3 * s + 1];
+                    pz[u] = source[3 * s + 2];
+                }
+            }
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                const bool in = c0 + 32 * u + lane < se;
+                const float d = dist2(qx, qy, qz, px[u], py[u], pz[u]);
+                const bool full = h.count >= h.cap;
+                // a NaN distance or root is unordered: then every candidate goes through add()
+                const bool unordered = __any_sync(0xffffffffu, in && d != d) || (full && h.d[0] != h.d[0]);
+                unsigned live = __ballot_sync(0xffffffffu, in && (unordered || !(full && d >= h.d[0])));
+                while (live) {
+                    const int l = __ffs(live) - 1;
+                    live &= live - 1;
+                    h.add(__shfl_sync(0xffffffffu, d, l), (int)(c0 + 32 * u + l));
+                }
             }
         }
         h.sort_ascending();
@@ -442,14 +451,25 @@ static void knn_launch(const float *query, const float *source, const int64_t *p
                        int32_t B, int64_t n_q, int k, int split, const KnnWs &w, int64_t *oi, float *od,
                        cudaStream_t st) {
     const int64_t grid = (n_q / kKnnThreads + B) * split;
-    const size_t smem = knn_smem_bytes<KB>();
-    cudaFuncSetAttribute(knn_fast_kernel<KB>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    knn_fast_kernel<KB><<<(unsigned)grid, kKnnThreads, smem, st>>>(query, source, ptr_q, ptr_s, B, k, split,
-                                                               w.tile_base, oi, od, w.part_d, w.part_i, w.part_cnt,
-                                                               w.flag_list, w.flag_count);
-    if (split > 1)
-        knn_merge_kernel<KB><<<(unsigned)((n_q + kKnnThreads - 1) / kKnnThreads), kKnnThreads, 0, st>>>(
-            ptr_q, B, k, split, w.part_d, w.part_i, w.part_cnt, oi, od, w.flag_list, w.flag_count);
+    if (KB == 4 && k == 1) {  // nearest neighbour: a list of two decides it
+        const size_t smem = knn_smem_bytes<2>();
+        cudaFuncSetAttribute(knn_fast_kernel<KB, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        knn_fast_kernel<KB, 2><<<(unsigned)grid, kKnnThreads, smem, st>>>(
+            query, source, ptr_q, ptr_s, B, k, split, w.tile_base, oi, od, w.part_d, w.part_i, w.part_cnt,
+            w.flag_list, w.flag_count);
+    } else {
+        const size_t smem = knn_smem_bytes<KB + 1>();
+        cudaFuncSetAttribute(knn_fast_kernel<KB, KB + 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        knn_fast_kernel<KB, KB + 1><<<(unsigned)grid, kKnnThreads, smem, st>>>(
+            query, source, ptr_q, ptr_s, B, k, split, w.tile_base, oi, od, w.part_d, w.part_i, w.part_cnt,
+            w.flag_list, w.flag_count);
+    }
+    if (split > 1) {
+        const size_t msm = knn_merge_smem(split, k);
+        cudaFuncSetAttribute(knn_merge_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)msm);
+        knn_merge_kernel<<<(unsigned)((n_q + kMergeWarps - 1) / kMergeWarps), kKnnThreads, msm, st>>>(
+            ptr_q, B, k, split, KB + 1, w.part_d, w.part_i, w.part_cnt, oi, od, w.flag_list, w.flag_count);
+    }
 }
 
 }  // namespace gdl

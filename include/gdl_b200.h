@@ -182,6 +182,18 @@ int gdl_segment_reduce_noalloc(const void *msg, int32_t dtype, int64_t num_rows,
                                const int32_t *node_start, const int32_t *node_end, int64_t num_nodes, int32_t reduce,
                                float *out, int32_t *arg_out, void *stream);
 
+/* ------------------------------------------------------------------------ row gather
+ * out[i, :] = src[idx[i], :] -- the msg = feats[knn_idx] materialisation of the reference's
+ * pooling layer (geoembodied/nn/modules/equivariant_pool.py:277-300, torch indexing there;
+ * no counterpart in geoembodied/csrc).
+ *
+ * src        [n_src, row_bytes] any element type; row_bytes a multiple of 4
+ * idx        [n_idx] i64; an index outside [0, n_src) yields a zero row
+ * out        [n_idx, row_bytes]
+ */
+int gdl_gather_rows(const void *src, int64_t n_src, int64_t row_bytes, const int64_t *idx, int64_t n_idx, void *out,
+                    void *stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -41,6 +41,12 @@ def _clouds(seed, sizes, kind="uniform", scale=1.0):
         x = base[torch.randint(0, base.shape[0], (n,), generator=g)]
     else:
         x = (torch.rand(n, 3, generator=g) * 2 - 1) * scale
+    if kind in ("nonfinite", "huge"):  # infinite coordinates; distances that overflow to inf
+        # No NaN distance can arise (sources may be infinite, queries only huge): the reference
+        # is built with fast math, which leaves its comparisons with NaN compiler-defined.
+        pick = torch.randint(0, n, (max(n // 50, 3),), generator=g)
+        vals = torch.tensor([float("inf"), -float("inf"), 1e20, -3e19] if kind == "nonfinite" else [1e20, -3e19])
+        x[pick, torch.randint(0, 3, (pick.numel(),), generator=g)] = vals[torch.arange(pick.numel()) % vals.numel()]
     ptr = torch.tensor(np.concatenate([[0], np.cumsum(sizes)]), dtype=torch.int64)
     return x.contiguous(), ptr
 
@@ -80,13 +86,13 @@ def test_fps_vs_reference_kernel(ref, kind, tie):
         assert torch.equal(got, want), f"{kind} seed {seed}: first diff at {(got != want).nonzero()[:3]}"
 
 
-@pytest.mark.parametrize("kind", ["uniform", "lattice", "dup"])
+@pytest.mark.parametrize("kind", ["uniform", "lattice", "dup", "nonfinite"])
 @pytest.mark.parametrize("k", [1, 4, 7, 16, 32, 64, 80])
 def test_knn_vs_reference_kernel(ref, kind, k):
     from gdl_b200 import csrc
 
     x, ptr = _clouds(11, [1500, 40, 3000], kind)
-    q, pq = _clouds(12, [300, 10, 700], kind)
+    q, pq = _clouds(12, [300, 10, 700], "huge" if kind == "nonfinite" else kind)
     wi, wd = ref["knn"].knn_cuda(q.to(DEV), x.to(DEV), pq.to(DEV), ptr.to(DEV), k)
     gi, gd = csrc.knn_cuda(q.to(DEV), x.to(DEV), pq.to(DEV), ptr.to(DEV), k)
     assert torch.equal(gi.cpu(), wi.cpu())
