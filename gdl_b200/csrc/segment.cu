@@ -27,41 +27,69 @@ namespace gdl {
 
 constexpr int kLongSegment = 4096;
 constexpr int kSegThreads = 256;
-constexpr int kUnroll = 4;
+constexpr int kUnroll = 4;       // rows in flight per lane, long segments
+// rows in flight per lane, short segments: 64 bytes at 16-byte vectors, 8 rows below that
+template <int VEC>
+struct ShortUnroll {
+    static constexpr int value = VEC >= 8 ? 4 : 8;
+};
 
 // ----------------------------------------------------------------- vector loads as f32
+// VecIO<T, VEC>: VEC consecutive elements of type T. `load_raw` issues one vector load
+// (kept raw so that many rows can be in flight in few registers), `cvt` widens it to f32;
+// `store` narrows f32 values back to T; `store_raw` writes VEC elements already in T.
 template <typename T, int VEC>
 struct VecIO;
 
 template <>
-struct VecIO<float, 4> {
-    static __device__ __forceinline__ void load(const float *p, float *v) {
-        float4 t = __ldg(reinterpret_cast<const float4 *>(p));
-        v[0] = t.x; v[1] = t.y; v[2] = t.z; v[3] = t.w;
+struct VecIO<float, 8> {
+    struct Raw { float4 a, b; };
+    static __device__ __forceinline__ Raw load_raw(const float *p) {
+        return {__ldg(reinterpret_cast<const float4 *>(p)), __ldg(reinterpret_cast<const float4 *>(p) + 1)};
     }
+    static __device__ __forceinline__ void cvt(const Raw &r, float *v) {
+        v[0] = r.a.x; v[1] = r.a.y; v[2] = r.a.z; v[3] = r.a.w;
+        v[4] = r.b.x; v[5] = r.b.y; v[6] = r.b.z; v[7] = r.b.w;
+    }
+    static __device__ __forceinline__ void store(float *p, const float *v) {
+        reinterpret_cast<float4 *>(p)[0] = make_float4(v[0], v[1], v[2], v[3]);
+        reinterpret_cast<float4 *>(p)[1] = make_float4(v[4], v[5], v[6], v[7]);
+    }
+    static __device__ __forceinline__ void store_raw(float *p, const float *v) { store(p, v); }
+};
+template <>
+struct VecIO<float, 4> {
+    using Raw = float4;
+    static __device__ __forceinline__ Raw load_raw(const float *p) { return __ldg(reinterpret_cast<const float4 *>(p)); }
+    static __device__ __forceinline__ void cvt(const Raw &t, float *v) { v[0] = t.x; v[1] = t.y; v[2] = t.z; v[3] = t.w; }
     static __device__ __forceinline__ void store(float *p, const float *v) {
         *reinterpret_cast<float4 *>(p) = make_float4(v[0], v[1], v[2], v[3]);
     }
+    static __device__ __forceinline__ void store_raw(float *p, const float *v) { store(p, v); }
 };
 template <>
 struct VecIO<float, 2> {
-    static __device__ __forceinline__ void load(const float *p, float *v) {
-        float2 t = __ldg(reinterpret_cast<const float2 *>(p));
-        v[0] = t.x; v[1] = t.y;
-    }
+    using Raw = float2;
+    static __device__ __forceinline__ Raw load_raw(const float *p) { return __ldg(reinterpret_cast<const float2 *>(p)); }
+    static __device__ __forceinline__ void cvt(const Raw &t, float *v) { v[0] = t.x; v[1] = t.y; }
     static __device__ __forceinline__ void store(float *p, const float *v) {
         *reinterpret_cast<float2 *>(p) = make_float2(v[0], v[1]);
     }
+    static __device__ __forceinline__ void store_raw(float *p, const float *v) { store(p, v); }
 };
 template <>
 struct VecIO<float, 1> {
-    static __device__ __forceinline__ void load(const float *p, float *v) { v[0] = __ldg(p); }
+    using Raw = float;
+    static __device__ __forceinline__ Raw load_raw(const float *p) { return __ldg(p); }
+    static __device__ __forceinline__ void cvt(const Raw &t, float *v) { v[0] = t; }
     static __device__ __forceinline__ void store(float *p, const float *v) { *p = v[0]; }
+    static __device__ __forceinline__ void store_raw(float *p, const float *v) { *p = v[0]; }
 };
 template <>
 struct VecIO<uint16_t, 8> {
-    static __device__ __forceinline__ void load(const uint16_t *p, float *v) {
-        uint4 t = __ldg(reinterpret_cast<const uint4 *>(p));
+    using Raw = uint4;
+    static __device__ __forceinline__ Raw load_raw(const uint16_t *p) { return __ldg(reinterpret_cast<const uint4 *>(p)); }
+    static __device__ __forceinline__ void cvt(const Raw &t, float *v) {
         const uint32_t w[4] = {t.x, t.y, t.z, t.w};
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
@@ -69,65 +97,100 @@ struct VecIO<uint16_t, 8> {
             v[2 * i + 1] = __uint_as_float(w[i] & 0xffff0000u);
         }
     }
-    static __device__ __forceinline__ void store(uint16_t *p, const float *v) {
-        uint32_t w[4];
-#pragma unroll
-        for (int i = 0; i < 4; ++i)
-            w[i] = (uint32_t)f32_to_bf16_bits(v[2 * i]) | ((uint32_t)f32_to_bf16_bits(v[2 * i + 1]) << 16);
-        *reinterpret_cast<uint4 *>(p) = make_uint4(w[0], w[1], w[2], w[3]);
+    static __device__ __forceinline__ void store_raw(uint16_t *p, const uint16_t *v) {
+        *reinterpret_cast<uint4 *>(p) = make_uint4((uint32_t)v[0] | ((uint32_t)v[1] << 16), (uint32_t)v[2] | ((uint32_t)v[3] << 16),
+                                                   (uint32_t)v[4] | ((uint32_t)v[5] << 16), (uint32_t)v[6] | ((uint32_t)v[7] << 16));
     }
 };
 template <>
 struct VecIO<uint16_t, 4> {
-    static __device__ __forceinline__ void load(const uint16_t *p, float *v) {
-        uint2 t = __ldg(reinterpret_cast<const uint2 *>(p));
+    using Raw = uint2;
+    static __device__ __forceinline__ Raw load_raw(const uint16_t *p) { return __ldg(reinterpret_cast<const uint2 *>(p)); }
+    static __device__ __forceinline__ void cvt(const Raw &t, float *v) {
         v[0] = __uint_as_float(t.x << 16); v[1] = __uint_as_float(t.x & 0xffff0000u);
         v[2] = __uint_as_float(t.y << 16); v[3] = __uint_as_float(t.y & 0xffff0000u);
     }
-    static __device__ __forceinline__ void store(uint16_t *p, const float *v) {
-        uint2 t;
-        t.x = (uint32_t)f32_to_bf16_bits(v[0]) | ((uint32_t)f32_to_bf16_bits(v[1]) << 16);
-        t.y = (uint32_t)f32_to_bf16_bits(v[2]) | ((uint32_t)f32_to_bf16_bits(v[3]) << 16);
-        *reinterpret_cast<uint2 *>(p) = t;
+    static __device__ __forceinline__ void store_raw(uint16_t *p, const uint16_t *v) {
+        *reinterpret_cast<uint2 *>(p) = make_uint2((uint32_t)v[0] | ((uint32_t)v[1] << 16), (uint32_t)v[2] | ((uint32_t)v[3] << 16));
     }
 };
 template <>
 struct VecIO<uint16_t, 2> {
-    static __device__ __forceinline__ void load(const uint16_t *p, float *v) {
-        uint32_t t = __ldg(reinterpret_cast<const unsigned int *>(p));
+    using Raw = uint32_t;
+    static __device__ __forceinline__ Raw load_raw(const uint16_t *p) { return __ldg(reinterpret_cast<const unsigned int *>(p)); }
+    static __device__ __forceinline__ void cvt(const Raw &t, float *v) {
         v[0] = __uint_as_float(t << 16); v[1] = __uint_as_float(t & 0xffff0000u);
     }
-    static __device__ __forceinline__ void store(uint16_t *p, const float *v) {
-        *reinterpret_cast<uint32_t *>(p) = (uint32_t)f32_to_bf16_bits(v[0]) | ((uint32_t)f32_to_bf16_bits(v[1]) << 16);
+    static __device__ __forceinline__ void store_raw(uint16_t *p, const uint16_t *v) {
+        *reinterpret_cast<uint32_t *>(p) = (uint32_t)v[0] | ((uint32_t)v[1] << 16);
     }
 };
 template <>
 struct VecIO<uint16_t, 1> {
-    static __device__ __forceinline__ void load(const uint16_t *p, float *v) { v[0] = bf16_bits_to_f32(__ldg(p)); }
-    static __device__ __forceinline__ void store(uint16_t *p, const float *v) { *p = f32_to_bf16_bits(v[0]); }
+    using Raw = uint16_t;
+    static __device__ __forceinline__ Raw load_raw(const uint16_t *p) { return __ldg(p); }
+    static __device__ __forceinline__ void cvt(const Raw &t, float *v) { v[0] = bf16_bits_to_f32(t); }
+    static __device__ __forceinline__ void store_raw(uint16_t *p, const uint16_t *v) { *p = v[0]; }
 };
 
+template <typename T, int VEC>
+__device__ __forceinline__ void vec_load(const T *p, float *v) {
+    VecIO<T, VEC>::cvt(VecIO<T, VEC>::load_raw(p), v);
+}
+
+// f32 value -> element of type T (bf16 rounds to nearest even)
+template <typename T>
+__device__ __forceinline__ T to_elem(float f);
+template <>
+__device__ __forceinline__ float to_elem<float>(float f) { return f; }
+template <>
+__device__ __forceinline__ uint16_t to_elem<uint16_t>(float f) { return f32_to_bf16_bits(f); }
+
 // ----------------------------------------------------------------- reduction state
-// max keeps (best, slot of first best, #values equal to best (saturating), NaN seen)
+// max keeps (best, slot of the first best, "another value equals best", NaN seen), branch-free;
+// the first value pushed starts it (arg < 0 marks "no value yet"). NaN is tracked by a
+// NaN-propagating max (max.NaN), so a NaN anywhere makes the result NaN.
+__device__ __forceinline__ float max_nan(float a, float b) {
+    float r;
+    asm("max.NaN.f32 %0, %1, %2;" : "=f"(r) : "f"(a), "f"(b));
+    return r;
+}
+
 struct MaxState {
-    float best;
-    int arg;
-    int cnt;
-    bool nan;
-    __device__ __forceinline__ void init() { best = __int_as_float(0xff800000); arg = -1; cnt = 0; nan = false; }
+    float best, nanacc;
+    int arg;  // -1: no value yet
+    bool tie;
+    __device__ __forceinline__ void init() {
+        best = nanacc = __int_as_float(0xff800000);
+        arg = -1;
+        tie = false;
+    }
     __device__ __forceinline__ void push(float v, int slot) {
-        if (v != v) { nan = true; return; }
-        if (cnt == 0 || v > best) { best = v; arg = slot; cnt = 1; }
-        else if (v == best) { cnt = cnt < 2 ? cnt + 1 : 2; }
+        const bool gt = v > best || arg < 0;  // the first value always starts the maximum
+        const bool eq = v == best;
+        tie = !gt && (tie || eq);
+        best = gt ? v : best;
+        arg = gt ? slot : arg;
+        nanacc = max_nan(nanacc, v);
     }
     __device__ __forceinline__ void merge(const MaxState &o) {  // o covers later slots
-        nan = nan || o.nan;
-        if (o.cnt == 0) return;
-        if (cnt == 0 || o.best > best) { best = o.best; arg = o.arg; cnt = o.cnt; }
-        else if (o.best == best) { cnt = (cnt + o.cnt) < 2 ? cnt + o.cnt : 2; }
+        if (o.arg < 0) return;
+        if (arg < 0) {
+            *this = o;
+            return;
+        }
+        nanacc = max_nan(nanacc, o.nanacc);
+        if (o.best > best) {
+            best = o.best;
+            arg = o.arg;
+            tie = o.tie;
+        } else if (o.best == best) {
+            tie = true;
+        }
     }
-    __device__ __forceinline__ float value() const { return nan ? __int_as_float(0x7fc00000) : (cnt == 0 ? 0.0f : best); }
-    __device__ __forceinline__ int arg_out() const { return (nan || cnt != 1) ? -1 : arg; }
+    __device__ __forceinline__ bool nan() const { return nanacc != nanacc; }
+    __device__ __forceinline__ float value() const { return nan() ? __int_as_float(0x7fc00000) : (arg < 0 ? 0.0f : best); }
+    __device__ __forceinline__ int arg_out() const { return (nan() || tie) ? -1 : arg; }
 };
 
 // Queue segment n for the one-CTA-per-segment kernel; true if it was queued. A full queue
@@ -158,6 +221,7 @@ __global__ void __launch_bounds__(kSegThreads) seg_fwd_short_kernel(
     if (n >= N) return;
     const int s = ns[n], e = ne[n];
     if (e - s > kLongSegment && queue_long<G>(n, lig, long_list, long_count, max_long)) return;
+    using IO = VecIO<T, VEC>;
     for (int64_t c0 = 0; c0 < C; c0 += (int64_t)G * VEC) {
         const int64_t c = c0 + (int64_t)lig * VEC;
         if (c >= C) continue;
@@ -168,26 +232,31 @@ __global__ void __launch_bounds__(kSegThreads) seg_fwd_short_kernel(
             acc[v] = 0.0f;
             if (RED == GDL_REDUCE_MAX) mx[v].init();
         }
+        // batches of U rows with their loads issued together: deg / U memory latencies
+        constexpr int U = ShortUnroll<VEC>::value;
         int j = s;
-        for (; j + kUnroll <= e; j += kUnroll) {
-            float x[kUnroll][VEC];
+        for (; j + U <= e; j += U) {
+            typename IO::Raw r[U];
 #pragma unroll
-            for (int u = 0; u < kUnroll; ++u) {
+            for (int u = 0; u < U; ++u) {
                 const int64_t row = perm ? (int64_t)__ldg(perm + j + u) : (int64_t)(j + u);
-                VecIO<T, VEC>::load(msg + row * C + c, x[u]);
+                r[u] = IO::load_raw(msg + row * C + c);
             }
 #pragma unroll
-            for (int u = 0; u < kUnroll; ++u)
+            for (int u = 0; u < U; ++u) {
+                float x[VEC];
+                IO::cvt(r[u], x);
 #pragma unroll
                 for (int v = 0; v < VEC; ++v) {
-                    if (RED == GDL_REDUCE_MAX) mx[v].push(x[u][v], j + u);
-                    else acc[v] = add_ftz(acc[v], x[u][v]);
+                    if (RED == GDL_REDUCE_MAX) mx[v].push(x[v], j + u);
+                    else acc[v] = add_ftz(acc[v], x[v]);
                 }
+            }
         }
         for (; j < e; ++j) {
             float x[VEC];
             const int64_t row = perm ? (int64_t)__ldg(perm + j) : (int64_t)j;
-            VecIO<T, VEC>::load(msg + row * C + c, x);
+            vec_load<T, VEC>(msg + row * C + c, x);
 #pragma unroll
             for (int v = 0; v < VEC; ++v) {
                 if (RED == GDL_REDUCE_MAX) mx[v].push(x[v], j);
@@ -220,8 +289,8 @@ __global__ void __launch_bounds__(kSegThreads) seg_fwd_long_kernel(
     constexpr int kRG = kSegThreads / G;
     __shared__ float part[kRG][G * VEC];
     __shared__ int part_arg[RED == GDL_REDUCE_MAX ? kRG : 1][RED == GDL_REDUCE_MAX ? G * VEC : 1];
-    __shared__ int part_cnt[RED == GDL_REDUCE_MAX ? kRG : 1][RED == GDL_REDUCE_MAX ? G * VEC : 1];
-    __shared__ unsigned char part_nan[RED == GDL_REDUCE_MAX ? kRG : 1][RED == GDL_REDUCE_MAX ? G * VEC : 1];
+    __shared__ unsigned char part_tie[RED == GDL_REDUCE_MAX ? kRG : 1][RED == GDL_REDUCE_MAX ? G * VEC : 1];
+    __shared__ float part_nan[RED == GDL_REDUCE_MAX ? kRG : 1][RED == GDL_REDUCE_MAX ? G * VEC : 1];
     if ((int)blockIdx.x >= *long_count) return;
     const int64_t n = long_list[blockIdx.x];
     const int s = ns[n], e = ne[n];
@@ -247,7 +316,7 @@ __global__ void __launch_bounds__(kSegThreads) seg_fwd_long_kernel(
 #pragma unroll
                 for (int u = 0; u < kUnroll; ++u) {
                     const int64_t row = perm ? (int64_t)__ldg(perm + j + u) : (int64_t)(j + u);
-                    VecIO<T, VEC>::load(msg + row * C + c, x[u]);
+                    vec_load<T, VEC>(msg + row * C + c, x[u]);
                 }
 #pragma unroll
                 for (int u = 0; u < kUnroll; ++u)
@@ -260,7 +329,7 @@ __global__ void __launch_bounds__(kSegThreads) seg_fwd_long_kernel(
             for (; j < j1; ++j) {
                 float x[VEC];
                 const int64_t row = perm ? (int64_t)__ldg(perm + j) : (int64_t)j;
-                VecIO<T, VEC>::load(msg + row * C + c, x);
+                vec_load<T, VEC>(msg + row * C + c, x);
 #pragma unroll
                 for (int v = 0; v < VEC; ++v) {
                     if (RED == GDL_REDUCE_MAX) mx[v].push(x[v], j);
@@ -274,8 +343,8 @@ __global__ void __launch_bounds__(kSegThreads) seg_fwd_long_kernel(
             if (RED == GDL_REDUCE_MAX) {
                 part[rg][k] = mx[v].best;
                 part_arg[rg][k] = mx[v].arg;
-                part_cnt[rg][k] = mx[v].cnt;
-                part_nan[rg][k] = mx[v].nan;
+                part_tie[rg][k] = mx[v].tie;
+                part_nan[rg][k] = mx[v].nanacc;
             } else {
                 part[rg][k] = acc[v];
             }
@@ -289,7 +358,7 @@ __global__ void __launch_bounds__(kSegThreads) seg_fwd_long_kernel(
                     m.init();
                     for (int r = 0; r < kRG; ++r) {
                         MaxState o;
-                        o.best = part[r][k]; o.arg = part_arg[r][k]; o.cnt = part_cnt[r][k]; o.nan = part_nan[r][k];
+                        o.best = part[r][k]; o.arg = part_arg[r][k]; o.tie = part_tie[r][k] != 0; o.nanacc = part_nan[r][k];
                         m.merge(o);
                     }
                     out[n * C + ch] = m.value();
@@ -305,57 +374,93 @@ __global__ void __launch_bounds__(kSegThreads) seg_fwd_long_kernel(
     }
 }
 
-// gradient of one (segment, VEC channels) for slots [j0, j1) of segment n
+// gradient of one (segment, VEC channels) for slots [j0, j1) of segment n. The values a slot
+// can receive are fixed per segment (sum: g; mean: g / deg; max: g / #maxima where the slot
+// holds the maximum, 0 * that share elsewhere -- torch's mask * share, signed zeros included),
+// so they are converted to T once and each slot only selects and stores.
 template <typename T, int VEC, int RED>
 __device__ __forceinline__ void seg_bwd_range(const float *__restrict__ grad_out, const T *__restrict__ msg,
                                               const float *__restrict__ out, const int32_t *__restrict__ arg,
                                               int64_t C, const int32_t *__restrict__ perm, int64_t n, int s, int e,
                                               int j0, int j1, int64_t c, T *__restrict__ grad_msg) {
-    float g[VEC], base[VEC];
-    VecIO<float, VEC>::load(grad_out + n * C + c, g);
+    float g[VEC];
+    vec_load<float, VEC>(grad_out + n * C + c, g);
+    T hit_v[VEC], miss_v[VEC];
     int a[VEC];
     float mx[VEC];
+    bool need = false;  // some channel has a tied (or NaN) maximum: compare values per slot
+    if (RED == GDL_REDUCE_MAX) {
 #pragma unroll
-    for (int v = 0; v < VEC; ++v) {
-        if (RED == GDL_REDUCE_SUM) {
-            base[v] = g[v];
-        } else if (RED == GDL_REDUCE_MEAN) {
-            base[v] = __fdiv_rn(g[v], (float)(e - s));
-        } else {
+        for (int v = 0; v < VEC; ++v) {
             a[v] = arg ? arg[n * C + c + v] : -1;
             mx[v] = out[n * C + c + v];
-            base[v] = g[v];
-            if (a[v] < 0) {  // tied (or NaN) maximum: share among every slot equal to it
-                int t = 0;
-                for (int k = s; k < e; ++k) {
-                    float x;
-                    const int64_t rk = perm ? (int64_t)__ldg(perm + k) : (int64_t)k;
-                    VecIO<T, 1>::load(msg + rk * C + c + v, &x);
-                    t += (x == mx[v]);
+            need |= a[v] < 0;
+        }
+    }
+    int t[VEC];  // slots equal to the maximum, per tied channel
+#pragma unroll
+    for (int v = 0; v < VEC; ++v) t[v] = 0;
+    if (RED == GDL_REDUCE_MAX && need) {
+        using IO = VecIO<T, VEC>;
+        constexpr int U = 4;  // tied channels only: few registers beat deep batches here
+        for (int k = s; k < e; k += U) {
+            typename IO::Raw r[U];
+#pragma unroll
+            for (int u = 0; u < U; ++u)
+                if (k + u < e) r[u] = IO::load_raw(msg + (perm ? (int64_t)__ldg(perm + k + u) : (int64_t)(k + u)) * C + c);
+#pragma unroll
+            for (int u = 0; u < U; ++u) {
+                if (k + u < e) {
+                    float x[VEC];
+                    IO::cvt(r[u], x);
+#pragma unroll
+                    for (int v = 0; v < VEC; ++v) t[v] += x[v] == mx[v];
                 }
-                base[v] = __fdiv_rn(g[v], (float)t);
             }
         }
     }
-    for (int j = j0; j < j1; ++j) {
-        const int64_t row = perm ? (int64_t)__ldg(perm + j) : (int64_t)j;
-        float val[VEC];
-        if (RED == GDL_REDUCE_MAX) {
-            float x[VEC];
-            bool need = false;
 #pragma unroll
-            for (int v = 0; v < VEC; ++v) need |= a[v] < 0;
-            if (need) VecIO<T, VEC>::load(msg + row * C + c, x);
+    for (int v = 0; v < VEC; ++v) {
+        float base;
+        if (RED == GDL_REDUCE_SUM) base = g[v];
+        else if (RED == GDL_REDUCE_MEAN) base = __fdiv_rn(g[v], (float)(e - s));
+        else base = a[v] < 0 ? __fdiv_rn(g[v], (float)t[v]) : g[v];  // tied: share among the maxima
+        hit_v[v] = to_elem<T>(1.0f * base);
+        miss_v[v] = to_elem<T>(0.0f * base);
+    }
+    if constexpr (RED == GDL_REDUCE_MAX) {
+        // one loop for every lane: only lanes with a tied channel load the values (batched)
+        using IO = VecIO<T, VEC>;
+        constexpr int U = 4;
+        for (int j = j0; j < j1; j += U) {
+            typename IO::Raw r[U];
+            if (need) {
 #pragma unroll
-            for (int v = 0; v < VEC; ++v) {
-                const bool hit = a[v] >= 0 ? (a[v] == j) : (x[v] == mx[v]);
-                val[v] = (hit ? 1.0f : 0.0f) * base[v];  // torch: mask * share
+                for (int u = 0; u < U; ++u)
+                    if (j + u < j1)
+                        r[u] = IO::load_raw(msg + (perm ? (int64_t)__ldg(perm + j + u) : (int64_t)(j + u)) * C + c);
             }
-        } else {
 #pragma unroll
-            for (int v = 0; v < VEC; ++v) val[v] = base[v];
+            for (int u = 0; u < U; ++u) {
+                if (j + u < j1) {
+                    float x[VEC];
+                    if (need) IO::cvt(r[u], x);
+                    T val[VEC];
+#pragma unroll
+                    for (int v = 0; v < VEC; ++v) {
+                        const bool hit = a[v] >= 0 ? (a[v] == j + u) : (x[v] == mx[v]);
+                        val[v] = hit ? hit_v[v] : miss_v[v];
+                    }
+                    const int64_t row = perm ? (int64_t)__ldg(perm + j + u) : (int64_t)(j + u);
+                    VecIO<T, VEC>::store_raw(grad_msg + row * C + c, val);
+                }
+            }
         }
-        VecIO<T, VEC>::store(grad_msg + row * C + c, val);
+    } else {
+        for (int j = j0; j < j1; ++j) {  // a pure store stream
+            const int64_t row = perm ? (int64_t)__ldg(perm + j) : (int64_t)j;
+            VecIO<T, VEC>::store_raw(grad_msg + row * C + c, hit_v);
+        }
     }
 }
 
@@ -430,8 +535,7 @@ static SegShape seg_shape(int64_t C, uintptr_t align_bits) {
     for (int v = maxv; v >= 1; v >>= 1) {
         if (C % v == 0 && (align_bits % (v * sizeof(T))) == 0) { vec = v; break; }
     }
-    // prefer filling a warp over the widest vector when a row is narrower than 32 vectors
-    while (vec > 1 && (C / vec) < 32 && (C / (vec / 2)) <= 32 && (sizeof(T) * vec / 2) >= 4) vec >>= 1;
+    // the widest vector: 16-byte accesses keep the most bytes in flight per lane
     int64_t lanes = C / vec;
     int g = 1;
     while (g < lanes && g < 32) g <<= 1;
@@ -440,7 +544,8 @@ static SegShape seg_shape(int64_t C, uintptr_t align_bits) {
 
 // narrow a shape until its VEC-wide f32 accesses (out / grad_out rows) are aligned too
 static SegShape fit_f32_side(SegShape sh, int64_t C, uintptr_t alf) {
-    while (sh.vec > 1 && (sh.vec > 4 || alf % (uintptr_t)(sh.vec * 4) != 0)) sh.vec >>= 1;
+    // f32 rows take VEC = 8 as two 16-byte accesses
+    while (sh.vec > 1 && alf % (uintptr_t)(sh.vec * 4 < 16 ? sh.vec * 4 : 16) != 0) sh.vec >>= 1;
     int64_t lanes = C / sh.vec;
     int g = 1;
     while (g < lanes && g < 32) g <<= 1;
@@ -490,6 +595,7 @@ static void launch_fwd_v(SegShape sh, const void *msg, int64_t C, const int32_t 
                          const int32_t *ne, int64_t N, float *out, int32_t *arg, int32_t *ll, int32_t *lc,
                          int64_t ml, cudaStream_t st) {
     switch (sh.vec) {
+    case 8: launch_fwd_g<T, 8, RED>(sh.group, msg, C, perm, ns, ne, N, out, arg, ll, lc, ml, st); break;
     case 4: launch_fwd_g<T, 4, RED>(sh.group, msg, C, perm, ns, ne, N, out, arg, ll, lc, ml, st); break;
     case 2: launch_fwd_g<T, 2, RED>(sh.group, msg, C, perm, ns, ne, N, out, arg, ll, lc, ml, st); break;
     default: launch_fwd_g<T, 1, RED>(sh.group, msg, C, perm, ns, ne, N, out, arg, ll, lc, ml, st); break;
@@ -528,6 +634,7 @@ static void launch_bwd_v(SegShape sh, const float *go, const void *msg, const fl
                          int64_t C, const int32_t *perm, const int32_t *ns, const int32_t *ne, int64_t N, void *gm,
                          int32_t *ll, int32_t *lc, int64_t ml, cudaStream_t st) {
     switch (sh.vec) {
+    case 8: launch_bwd_g<T, 8, RED>(sh.group, go, msg, out, arg, C, perm, ns, ne, N, gm, ll, lc, ml, st); break;
     case 4: launch_bwd_g<T, 4, RED>(sh.group, go, msg, out, arg, C, perm, ns, ne, N, gm, ll, lc, ml, st); break;
     case 2: launch_bwd_g<T, 2, RED>(sh.group, go, msg, out, arg, C, perm, ns, ne, N, gm, ll, lc, ml, st); break;
     default: launch_bwd_g<T, 1, RED>(sh.group, go, msg, out, arg, C, perm, ns, ne, N, gm, ll, lc, ml, st); break;
