@@ -15,6 +15,7 @@ inputs with the shapes of the reference's use cases; see gdl_b200/synthetic.py):
   c4            64 source/target pairs x 16384 points: KNN k=1, residual segment sum.
   c5            8 clouds x 131072 LiDAR points: FPS -> 16384, radius graph (r = 1 m, 64),
                 segment sum of 64-channel features.
+  c5g           (auxiliary) c5's clouds: radius graph r = 1 m, 64 over all points, segment sum.
 
 value : input points per second with inputs resident in HBM, timed with CUDA events on the
         launching stream, L2 flushed (256 MiB write) between steps, max over ranks.
@@ -658,7 +659,78 @@ class C5:
         O.fps(pos, [0, self.N], [self.cpu_picks], dist=O.DIST_CUDA)
 
 
-CONFIGS = {"c1": C1, "c2": C2, "c3": C3, "c4": C4, "c5": C5}
+class C5G(C5):
+    """Auxiliary LiDAR graph-build workload (not one of the reference's configurations): config 5's
+    clouds, radius graph r = 1 m, 64 neighbours over ALL 131072 points of each cloud, segment sum of
+    64-channel point features over it. In config 5 proper the graph is built over the 16384 FPS
+    centroids, which FPS leaves >= 1.75 m apart, so r = 1 m gives no edge there."""
+    name = "c5g"
+    metric = "points/sec (radius graph r=1 k=64 over all points + segment sum C=64), config 5 clouds"
+    launches_per_step = 25 + 2
+
+    def _host_init(self, seed, pin=True):
+        pos, ptr = synthetic.c5_points(seed=seed, B=self.B, N=self.N)
+        self.n_points = pos.shape[0]
+        self.nc = self.n_points
+        self.pos_h = torch.from_numpy(pos)
+        self.ptr_h = torch.from_numpy(ptr)
+        g = torch.Generator().manual_seed(seed + 1)
+        self.feat_h = torch.randn(self.n_points, self.C, generator=g)
+        if pin:
+            self.pos_h, self.feat_h = self.pos_h.pin_memory(), self.feat_h.pin_memory()
+
+    def __init__(self, dev, seed):
+        self.dev = dev
+        self._host_init(seed)
+        self.pos, self.ptr = self.pos_h.to(dev), self.ptr_h.to(dev)
+        self.feat = self.feat_h.to(dev)
+        self.cap = self.nc * self.NN
+        L = self.L = nat.load()
+        self.row_ptr = torch.empty(self.nc + 1, dtype=torch.int64, device=dev)
+        self.src = torch.zeros(self.cap, dtype=torch.int64, device=dev)
+        self.row_ptr32 = torch.zeros(self.nc + 1, dtype=torch.int32, device=dev)
+        self.ns, self.ne = self.row_ptr32[:-1], self.row_ptr32[1:]
+        self.src32 = torch.zeros(self.cap, dtype=torch.int32, device=dev)
+        self.out = torch.empty(self.nc, self.C, device=dev)
+        self.ws_rad = nat.workspace(L.gdl_radius_graph_workspace_size(self.nc, self.B, self.NN), dev)
+        self.ws_seg = nat.workspace(L.gdl_segment_reduce_workspace_size(self.cap, self.nc), dev)
+
+    def stage_radius(self):
+        nat.check(self.L.gdl_radius_graph(self.pos.data_ptr(), self.ptr.data_ptr(), self.B, self.nc, self.N, self.R,
+                                          self.NN, 0, None, self.row_ptr.data_ptr(), self.src.data_ptr(), None,
+                                          self.row_ptr32.data_ptr(), self.src32.data_ptr(), self.ws_rad.data_ptr(),
+                                          self.ws_rad.numel(), self._s()), "radius")
+
+    def stage_list(self):
+        return [("radius_graph", self.stage_radius), ("segment_sum", self.stage_seg)]
+
+    def stage_bytes(self, E):
+        nc, C = self.nc, self.C
+        return {"radius_graph": 12 * nc + 12 * E + 12 * (nc + 1),
+                "segment_sum": 4 * E * C + 4 * nc * C + 4 * (E + 2 * nc)}
+
+    def e2e_step(self):
+        pos = self.pos_h.to(self.dev, non_blocking=True)
+        feat = self.feat_h.to(self.dev, non_blocking=True)
+        row_ptr, src, _, rp32, src32 = csrc.radius_graph_csr(pos, self.R, self.ptr_h, max_num_neighbors=self.NN,
+                                                             int32_csr=True)
+        out = csrc.segment_reduce_cuda(feat, src32, rp32[:-1], rp32[1:], self.nc, "sum")
+        host = out.to("cpu", non_blocking=True)
+        torch.cuda.current_stream(self.dev).synchronize()
+        return host
+
+    e2e_d2h = property(lambda self: self.nc * self.C * 4)
+    cpu_fraction = 1 / 8
+    cpu_sample = "radius graph + segment sum of 1 of 8 clouds per sample, scaled x8"
+
+    def cpu_step(self, O):
+        pos = self.pos_h.numpy()[:self.N]
+        rp, src = O.radius_graph(pos, np.array([0, self.N]), self.R, self.NN, dist=O.DIST_CUDA)
+        O.segment_reduce(self.feat_h.numpy()[:self.N], src.astype(np.int32), rp[:-1].astype(np.int32),
+                         rp[1:].astype(np.int32), self.N, "sum")
+
+
+CONFIGS = {"c1": C1, "c2": C2, "c3": C3, "c4": C4, "c5": C5, "c5g": C5G}
 
 
 
@@ -711,6 +783,16 @@ class ClockSampler:
                 "reasons": sorted(self.reasons), "samples": len(self.sm)}
 
 
+ROOFLINE_NOTES = {
+    "fps": "FPS is one argmax per pick over the whole cloud, a serial latency chain on one CTA (or "
+           "cluster) per cloud; its HBM fraction is tiny by nature -- the kernel reads the points once. "
+           "Its bound is issue and latency per pick (ncu: profiles/fps_cta_kernel_c2.md).",
+    "fps_chain": "see fps",
+    "knn": "brute-force KNN is bound by the fp32 pipe (8 flops per pair), not by HBM; the pair rate is "
+           "reported in profiles/knn_fast_kernel_c3_c4.md.",
+}
+
+
 def measured_peak():
     p = ROOT / "MEASURED_PEAKS.json"
     if p.exists():
@@ -719,12 +801,12 @@ def measured_peak():
     return 6650.0, "fallback"
 
 
-def ncu_traffic(kernel_stage):
+def ncu_traffic(config, stage):
+    """DRAM bytes per launch of `stage` measured by ncu for `config` (profiles/ncu_traffic.json)."""
     p = ROOT / "profiles" / "ncu_traffic.json"
     if not p.exists():
         return None
-    d = json.loads(p.read_text())
-    return d.get(kernel_stage)
+    return json.loads(p.read_text()).get(config, {}).get(stage)
 
 
 def dist_env():
@@ -876,10 +958,11 @@ def run_ours(args, cfg_cls):
                        "parallelism": f"clouds sharded over {ws} GPU(s), no collective in a step"},
             "stage_ms": stage_ms,
             "roofline": {"kernel": dom, "bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
-                         "frac": achieved / peak, "traffic": ncu_traffic(dom),
+                         "frac": achieved / peak, "traffic": ncu_traffic(cfg.name, dom),
                          "peak_source": (f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured"
                                          else "fallback 6.65 TB/s"),
-                         "algorithmic_bytes_per_launch": algo},
+                         "algorithmic_bytes_per_launch": algo,
+                         "note": ROOFLINE_NOTES.get(dom, "")},
             "gpu_launches": cfg.launches_per_step * args.steps,
             "clocks": clk.summary(),
         }

@@ -125,8 +125,8 @@ __global__ void rg_gather_kernel(const float *__restrict__ x, const int64_t *__r
                                  const int32_t *__restrict__ sorted_idx, float4 *__restrict__ sorted_pts) {
     const int64_t j = ptr[0] + (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
     if (j >= ptr[B]) return;
-    const int64_t o = sorted_idx[j];
-    sorted_pts[j] = make_float4(x[3 * o], x[3 * o + 1], x[3 * o + 2], 0.0f);
+    const int64_t o = sorted_idx[j];  // .w carries the point's global index
+    sorted_pts[j] = make_float4(x[3 * o], x[3 * o + 1], x[3 * o + 2], __int_as_float((int32_t)o));
 }
 
 __device__ __forceinline__ int64_t lower_bound_u32(const uint32_t *__restrict__ a, int64_t lo, int64_t hi, uint32_t v) {
@@ -136,79 +136,6 @@ __device__ __forceinline__ int64_t lower_bound_u32(const uint32_t *__restrict__ 
         else hi = m;
     }
     return lo;
-}
-
-constexpr int kQueryThreads = 128;
-
-__global__ void __launch_bounds__(kQueryThreads) rg_query_kernel(
-    const float *__restrict__ x, const int64_t *__restrict__ ptr, int32_t B, int64_t n, const uint8_t *__restrict__ mask,
-    float r_sq, float inv, int loop, int cap, const GridParams *__restrict__ gp,
-    const uint32_t *__restrict__ sorted_keys, const int32_t *__restrict__ sorted_idx,
-    const float4 *__restrict__ sorted_pts, int32_t *__restrict__ counts, int32_t *__restrict__ padded) {
-    const int64_t q = (int64_t)blockIdx.x * kQueryThreads + threadIdx.x;
-    if (q >= n) return;
-    if (q < ptr[0] || q >= ptr[B] || (mask && !mask[q])) {
-        counts[q] = 0;
-        return;
-    }
-    const int b = find_cloud_i(ptr, B, q);
-    const GridParams g = gp[b];
-    if (!g.ok) {
-        counts[q] = 0;
-        return;
-    }
-    const int64_t cs0 = ptr[b], cs1 = ptr[b + 1];
-    const float qx = x[3 * q], qy = x[3 * q + 1], qz = x[3 * q + 2];
-    const int qc[3] = {cell_coord(qx, g.mn[0], inv), cell_coord(qy, g.mn[1], inv), cell_coord(qz, g.mn[2], inv)};
-    const int zlo = qc[2] - 1 < 0 ? 0 : qc[2] - 1;
-    const int zhi = qc[2] + 1 > g.res[2] - 1 ? g.res[2] - 1 : qc[2] + 1;
-    float hd[64];
-    int hid[64];
-    int cnt = 0;
-    if (zlo <= zhi) {
-        for (int dx = -1; dx <= 1; ++dx) {
-            const int cx = qc[0] + dx;
-            if (cx < 0 || cx >= g.res[0]) continue;
-            for (int dy = -1; dy <= 1; ++dy) {
-                const int cy = qc[1] + dy;
-                if (cy < 0 || cy >= g.res[1]) continue;
-                const uint32_t col = (uint32_t)((cx * g.res[1] + cy) * g.res[2]);
-                const int64_t j0 = lower_bound_u32(sorted_keys, cs0, cs1, col + (uint32_t)zlo);
-                const int64_t j1 = lower_bound_u32(sorted_keys, j0, cs1, col + (uint32_t)zhi + 1u);
-                for (int64_t j = j0; j < j1; ++j) {
-                    const int o = sorted_idx[j];
-                    if (!loop && o == (int)q) continue;
-                    const float4 s = sorted_pts[j];
-                    const float d = dist2(qx, qy, qz, s.x, s.y, s.z);
-                    if (d < r_sq) heap_add(hd, hid, cnt, cap, d, o);
-                }
-            }
-        }
-    }
-    sort_ints(hid, cnt);  // kept set, ascending source index
-    int32_t *dst = padded + q * cap;
-    for (int a = 0; a < cnt; ++a) dst[a] = hid[a];
-    counts[q] = cnt;
-}
-
-__global__ void rg_compact_kernel(const int32_t *__restrict__ counts, const int32_t *__restrict__ padded, int64_t n,
-                                  int cap, const int64_t *__restrict__ row_ptr, int64_t *__restrict__ src,
-                                  int64_t *__restrict__ dst, int32_t *__restrict__ row_ptr32,
-                                  int32_t *__restrict__ src32) {
-    // one warp per query row: lanes copy the row's entries
-    const int64_t q = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
-    const int lane = threadIdx.x & 31;
-    if (q > n) return;
-    if (row_ptr32 && lane == 0) row_ptr32[q] = (int32_t)row_ptr[q];
-    if (q == n) return;
-    const int c = counts[q];
-    const int64_t o = row_ptr[q];
-    for (int a = lane; a < c; a += 32) {
-        const int32_t v = padded[q * cap + a];
-        src[o + a] = v;
-        if (src32) src32[o + a] = v;
-        if (dst) dst[o + a] = q;
-    }
 }
 
 // ------------------------------------------------------------------ small clouds, fused
@@ -658,12 +585,309 @@ __global__ void __launch_bounds__(kSmallThreads) rg_small_compact_kernel(
         }
 }
 
+
+// ------------------------------------------------------------------ any cloud size
+// Dense cell table: cell_start[kCellBudget * ptr[b] + c] = first sorted position of cloud b with
+// key >= c (c = 0..ncells), built when the grid has at most kCellBudget * n_b - 1 cells; a
+// (dx, dy) column's z-cells zlo..zhi are then [cell_start[col + zlo], cell_start[col + zhi + 1]).
+// Clouds with larger grids binary-search the sorted keys instead.
+constexpr int kCellBudget = 16;
+
+__device__ __forceinline__ bool dense_cells(const GridParams &g, int64_t n_b) {
+    return (int64_t)g.ncells + 1 <= kCellBudget * n_b;
+}
+
+__global__ void rg_cells_kernel(const int64_t *__restrict__ ptr, int32_t B, const GridParams *__restrict__ gp,
+                                const uint32_t *__restrict__ sorted_keys, int32_t *__restrict__ cell_start) {
+    const int64_t t = kCellBudget * ptr[0] + (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (t >= kCellBudget * ptr[B]) return;
+    int lo = 0, hi = B - 1;  // cloud whose table holds entry t
+    while (lo < hi) {
+        const int mid = (lo + hi + 1) >> 1;
+        if (kCellBudget * ptr[mid] <= t) lo = mid;
+        else hi = mid - 1;
+    }
+    const int b = lo;
+    const GridParams g = gp[b];
+    const int64_t s0 = ptr[b], s1 = ptr[b + 1];
+    const int64_t c = t - kCellBudget * s0;
+    if (!dense_cells(g, s1 - s0) || c > g.ncells) return;
+    cell_start[t] = (int32_t)lower_bound_u32(sorted_keys, s0, s1, (uint32_t)c);
+}
+
+// One warp per query. Lanes 0-8 find the sorted ranges of the 9 z-columns of the 27-cell
+// neighbourhood in the reference's (dx, dy) order; a warp scan turns them into one candidate
+// list that the lanes test 32 at a time, and ballot/popc append the sources in range to the
+// query's padded row in scan order (rows are sorted at compaction). The reference keeps them
+// all when at most `cap` are in range. Otherwise its heap keeps the `cap` smallest distances
+// whenever the cap-th and the next are different; the warp finds the cap-th distance by a
+// coarse histogram (one rescan), a compaction of the candidates below the cutoff into shared
+// memory (one rescan) and a radix select there, and writes the sources at or below it. A tie
+// at the cut (or a cutoff that leaves too many candidates) replays the reference heap on lane 0.
+constexpr int kQueryWarps = 8;
+constexpr int kScanDepth = 4;  // candidate batches of 32 in flight per warp
+constexpr int kOvfCap = 1024;  // candidates a warp can hold for the selection
+constexpr int kHistBins = 256;
+
+struct QueryWarpSmem {
+    float2 buf[kOvfCap];  // (distance, global index bits)
+    int hist[kHistBins];
+};
+
+__global__ void __launch_bounds__(kQueryWarps * 32) rg_query_warp_kernel(
+    const float *__restrict__ x, const int64_t *__restrict__ ptr, int32_t B, int64_t n, const uint8_t *__restrict__ mask,
+    float r_sq, float inv, int loop, int cap, const GridParams *__restrict__ gp,
+    const uint32_t *__restrict__ sorted_keys, const int32_t *__restrict__ cell_start,
+    const float4 *__restrict__ sorted_pts, int32_t *__restrict__ counts, int32_t *__restrict__ padded) {
+    // sorted_pts spans every cloud: a point's sorted position lies in its own cloud's range
+    extern __shared__ __align__(16) unsigned char query_smem[];  // kQueryWarps x QueryWarpSmem
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    QueryWarpSmem &W = reinterpret_cast<QueryWarpSmem *>(query_smem)[warp];
+    const unsigned lt_mask = (1u << lane) - 1u;
+    const int64_t nwarps = (int64_t)gridDim.x * kQueryWarps;
+    const int64_t p0 = ptr[0], p1 = ptr[B];
+    const int64_t gw = (int64_t)blockIdx.x * kQueryWarps + warp;
+    for (int64_t q = gw * 32 + lane; q < n; q += nwarps * 32)  // points outside every cloud
+        if (q < p0 || q >= p1) counts[q] = 0;
+    // queries in cell order (position j of the sorted points): warps running together share
+    // most of their candidate columns in L1
+    for (int64_t j = p0 + gw; j < p1; j += nwarps) {
+        int kept = 0;
+        const int64_t q = __float_as_int(sorted_pts[j].w);
+        const bool live = !(mask && !mask[q]);
+        const int b = find_cloud_i(ptr, B, j);
+        const GridParams g = gp[b];
+        if (live && g.ok) {  // uniform over the warp
+            const int64_t s0 = ptr[b], s1 = ptr[b + 1];
+            const float qx = x[3 * q], qy = x[3 * q + 1], qz = x[3 * q + 2];
+            const int qc0 = cell_coord(qx, g.mn[0], inv), qc1 = cell_coord(qy, g.mn[1], inv),
+                      qc2 = cell_coord(qz, g.mn[2], inv);
+            const int zlo = qc2 - 1 < 0 ? 0 : qc2 - 1;
+            const int zhi = qc2 + 1 > g.res[2] - 1 ? g.res[2] - 1 : qc2 + 1;
+            int64_t j0 = 0;
+            int len = 0;
+            if (lane < 9) {
+                const int cx = qc0 + lane / 3 - 1, cy = qc1 + lane % 3 - 1;
+                if (zlo <= zhi && cx >= 0 && cx < g.res[0] && cy >= 0 && cy < g.res[1]) {
+                    const int colc = (cx * g.res[1] + cy) * g.res[2];
+                    int64_t e;
+                    if (dense_cells(g, s1 - s0)) {
+                        const int32_t *cs = cell_start + kCellBudget * s0;
+                        j0 = cs[colc + zlo];
+                        e = cs[colc + zhi + 1];
+                    } else {
+                        j0 = lower_bound_u32(sorted_keys, s0, s1, (uint32_t)(colc + zlo));
+                        e = lower_bound_u32(sorted_keys, j0, s1, (uint32_t)(colc + zhi) + 1u);
+                    }
+                    len = (int)(e - j0);
+                }
+            }
+            int clen[9];
+            int64_t cbeg[9];
+#pragma unroll
+            for (int c = 0; c < 9; ++c) {  // every lane takes the 9 (start, length) pairs
+                clen[c] = __shfl_sync(0xffffffffu, len, c);
+                cbeg[c] = __shfl_sync(0xffffffffu, j0, c);
+            }
+            // the candidates in scan order, column by column, 32 at a time; body(ok, d, o) runs
+            // on every lane for every batch (ok: the lane holds a source in range)
+            // (loads of kScanDepth batches are issued before the first is tested)
+            auto scan = [&](auto &&body) {
+#pragma unroll
+                for (int c = 0; c < 9; ++c) {
+                    for (int k0 = 0; k0 < clen[c]; k0 += 32 * kScanDepth) {
+                        float4 sp[kScanDepth];
+#pragma unroll
+                        for (int u = 0; u < kScanDepth; ++u) {
+                            const int k = k0 + 32 * u + lane;
+                            if (k < clen[c]) sp[u] = sorted_pts[cbeg[c] + k];
+                        }
+#pragma unroll
+                        for (int u = 0; u < kScanDepth; ++u) {
+                            if (k0 + 32 * u >= clen[c]) break;  // uniform over the warp
+                            const int k = k0 + 32 * u + lane;
+                            bool ok = false;
+                            float d = 0.0f;
+                            int o = 0;
+                            if (k < clen[c]) {
+                                o = __float_as_int(sp[u].w);
+                                d = dist2(qx, qy, qz, sp[u].x, sp[u].y, sp[u].z);
+                                ok = (loop || (int64_t)o != q) && d < r_sq;
+                            }
+                            body(ok, d, o);
+                        }
+                    }
+                }
+            };
+            int32_t *row = padded + q * cap;
+            // pass 1: sources in range in scan order, the first `cap` into the row and the first
+            // kOvfCap (distance, source) pairs into shared memory
+            scan([&](bool ok, float d, int o) {
+                const unsigned hits = __ballot_sync(0xffffffffu, ok);
+                const int pos = kept + __popc(hits & lt_mask);
+                if (ok) {
+                    if (pos < cap) row[pos] = o;
+                    if (pos < kOvfCap) W.buf[pos] = make_float2(d, __int_as_float(o));
+                }
+                kept += __popc(hits);
+            });
+            if (kept > cap) {
+                int m = kept;  // candidates in the buffer
+                bool replay = false;
+                if (kept > kOvfCap) {
+                    // cutoff: the smallest histogram bin edge with at least cap + 1 candidates
+                    // below it; the buffer is refilled with the candidates under it
+                    const float scale = (float)kHistBins / r_sq;
+                    __syncwarp();
+                    for (int h = lane; h < kHistBins; h += 32) W.hist[h] = 0;
+                    __syncwarp();
+                    scan([&](bool ok, float d, int o) {
+                        if (ok) atomicAdd(&W.hist[min((int)(d * scale), kHistBins - 1)], 1);
+                    });
+                    __syncwarp();
+                    int v[kHistBins / 32], sum = 0;  // 8 consecutive bins per lane, warp scan
+#pragma unroll
+                    for (int i = 0; i < kHistBins / 32; ++i) {
+                        v[i] = W.hist[lane * (kHistBins / 32) + i];
+                        sum += v[i];
+                    }
+                    int pre = sum;
+                    for (int o = 1; o < 32; o <<= 1) {
+                        const int y = __shfl_up_sync(0xffffffffu, pre, o);
+                        if (lane >= o) pre += y;
+                    }
+                    int run = pre - sum, found = kHistBins, upto = 0;
+#pragma unroll
+                    for (int i = 0; i < kHistBins / 32; ++i) {
+                        run += v[i];
+                        if (found == kHistBins && run >= cap + 1) {
+                            found = lane * (kHistBins / 32) + i;
+                            upto = run;
+                        }
+                    }
+                    const unsigned have = __ballot_sync(0xffffffffu, found < kHistBins);
+                    const int srcl = __ffs(have) - 1;  // lowest lane: the first bin reaching cap + 1
+                    const int cut_bin = __shfl_sync(0xffffffffu, found, srcl);
+                    const int nbuf = __shfl_sync(0xffffffffu, upto, srcl);
+                    __syncwarp();
+                    replay = nbuf > kOvfCap;
+                    if (!replay) {
+                        m = 0;
+                        scan([&](bool ok, float d, int o) {
+                            ok = ok && min((int)(d * scale), kHistBins - 1) <= cut_bin;
+                            const unsigned hits = __ballot_sync(0xffffffffu, ok);
+                            const int pos = m + __popc(hits & lt_mask);
+                            if (ok && pos < kOvfCap) W.buf[pos] = make_float2(d, __int_as_float(o));
+                            m += __popc(hits);
+                        });
+                        if (m > kOvfCap) m = kOvfCap;  // cannot happen: the histogram counted these
+                    }
+                }
+                __syncwarp();
+                if (!replay) {
+                    // radix select of the cap-th smallest distance (rank cap, 1-based), 8 bits a pass
+                    uint32_t prefix = 0, pmask = 0;
+                    int rank = cap;  // rank within the candidates matching the prefix
+                    for (int shift = 24; shift >= 0; shift -= 8) {
+                        for (int h = lane; h < kHistBins; h += 32) W.hist[h] = 0;
+                        __syncwarp();
+                        for (int i = lane; i < m; i += 32) {
+                            const uint32_t u = __float_as_uint(W.buf[i].x);
+                            if ((u & pmask) == prefix) atomicAdd(&W.hist[(u >> shift) & 255u], 1);
+                        }
+                        __syncwarp();
+                        int v[kHistBins / 32], sum = 0;
+#pragma unroll
+                        for (int i = 0; i < kHistBins / 32; ++i) {
+                            v[i] = W.hist[lane * (kHistBins / 32) + i];
+                            sum += v[i];
+                        }
+                        int pre = sum;
+                        for (int o = 1; o < 32; o <<= 1) {
+                            const int y = __shfl_up_sync(0xffffffffu, pre, o);
+                            if (lane >= o) pre += y;
+                        }
+                        int run = pre - sum, found = -1, before = 0;
+#pragma unroll
+                        for (int i = 0; i < kHistBins / 32; ++i) {
+                            if (found < 0 && run + v[i] >= rank) {
+                                found = lane * (kHistBins / 32) + i;
+                                before = run;
+                            }
+                            run += v[i];
+                        }
+                        const unsigned have = __ballot_sync(0xffffffffu, found >= 0);
+                        const int srcl = __ffs(have) - 1;
+                        const int digit = __shfl_sync(0xffffffffu, found, srcl);
+                        rank -= __shfl_sync(0xffffffffu, before, srcl);
+                        prefix |= (uint32_t)digit << shift;
+                        pmask |= 255u << shift;
+                        __syncwarp();
+                    }
+                    const float vcap = __uint_as_float(prefix);  // the cap-th smallest distance
+                    // the kept set is {d <= vcap} when exactly cap candidates qualify
+                    int le = 0;
+                    for (int i = lane; i < m; i += 32) le += W.buf[i].x <= vcap;
+                    for (int o = 16; o > 0; o >>= 1) le += __shfl_xor_sync(0xffffffffu, le, o);
+                    if (le != cap) {
+                        replay = true;  // tie at the cut: the scan order decides
+                    } else {
+                        int w = 0;
+                        for (int base = 0; base < m; base += 32) {
+                            const int i = base + lane;
+                            const bool ok = i < m && W.buf[i].x <= vcap;
+                            const unsigned hits = __ballot_sync(0xffffffffu, ok);
+                            if (ok) row[w + __popc(hits & lt_mask)] = __float_as_int(W.buf[i].y);
+                            w += __popc(hits);
+                        }
+                    }
+                    __syncwarp();
+                }
+                if (replay) {  // the reference heap, fed in scan order, on lane 0
+                    if (lane == 0) {
+                        float hd[64];
+                        int hid[64];
+                        int hc = 0;
+#pragma unroll
+                        for (int c = 0; c < 9; ++c)
+                            for (int k = 0; k < clen[c]; ++k) {
+                                const float4 sp = sorted_pts[cbeg[c] + k];
+                                const int o = __float_as_int(sp.w);
+                                if (!loop && (int64_t)o == q) continue;
+                                const float d = dist2(qx, qy, qz, sp.x, sp.y, sp.z);
+                                if (d < r_sq) heap_add(hd, hid, hc, cap, d, o);
+                            }
+                        for (int a2 = 0; a2 < hc; ++a2) row[a2] = hid[a2];
+                    }
+                    __syncwarp();
+                }
+                kept = cap;
+            }
+        }
+        if (lane == 0) counts[q] = kept;
+    }
+}
+
+// row_ptr from the exclusive scan of counts; one warp sorts each row ascending and writes it
+__global__ void rg_compact_sort_kernel(const int32_t *__restrict__ counts, const int32_t *__restrict__ padded,
+                                       int64_t n, int cap, const int64_t *__restrict__ row_ptr,
+                                       int64_t *__restrict__ src, int64_t *__restrict__ dst,
+                                       int32_t *__restrict__ row_ptr32, int32_t *__restrict__ src32) {
+    const int64_t q = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    const int lane = threadIdx.x & 31;
+    if (q > n) return;  // uniform over the warp
+    if (row_ptr32 && lane == 0) row_ptr32[q] = (int32_t)row_ptr[q];
+    if (q == n) return;
+    warp_sort_emit(padded + q * cap, 1, counts[q], row_ptr[q], q, src, dst, src32);
+}
+
 struct RadiusWs {
     GridParams *gp;
     int32_t *key_bits;
     uint32_t *keys, *sorted_keys;
     int32_t *sorted_idx, *counts, *padded;
     float4 *sorted_pts;
+    int32_t *cell_start;
     int64_t *scan_scratch;
     int32_t *cloud_tot;
     RadixScratch rs;
@@ -686,6 +910,7 @@ static size_t radius_ws(int64_t n, int32_t B, int cap, char *base, RadiusWs *w) 
     t.counts = (int32_t *)take(sizeof(int32_t) * nn);
     t.padded = (int32_t *)take(sizeof(int32_t) * nn * cap);
     t.sorted_pts = (float4 *)take(sizeof(float4) * nn);
+    t.cell_start = (int32_t *)take(sizeof(int32_t) * kCellBudget * nn);
     t.scan_scratch = (int64_t *)take(sizeof(int64_t) * (scan_blocks(nn) + 1));
     t.cloud_tot = (int32_t *)take(sizeof(int32_t) * (B > 0 ? B : 1));
     const size_t rbytes = radix_scratch_bytes(nn, B > 0 ? B : 1);
@@ -748,12 +973,18 @@ extern "C" int gdl_radius_graph(const float *x, const int64_t *ptr, int32_t num_
     GDL_CUDA_TRY(radix_sort_pairs(w.keys, nullptr, w.sorted_keys, w.sorted_idx, n_points, ptr, num_clouds, 4,
                                   w.key_bits, w.rs, st));
     rg_gather_kernel<<<g256, 256, 0, st>>>(x, ptr, num_clouds, w.sorted_idx, w.sorted_pts);
-    rg_query_kernel<<<(unsigned)((n_points + kQueryThreads - 1) / kQueryThreads), kQueryThreads, 0, st>>>(
-        x, ptr, num_clouds, n_points, mask, r_sq, inv, loop, cap, w.gp, w.sorted_keys, w.sorted_idx, w.sorted_pts,
-        w.counts, w.padded);
+    rg_cells_kernel<<<(unsigned)((kCellBudget * n_points + 255) / 256), 256, 0, st>>>(ptr, num_clouds, w.gp,
+                                                                                    w.sorted_keys, w.cell_start);
+    const int64_t qblocks = (n_points + kQueryWarps - 1) / kQueryWarps;
+    const unsigned qgrid = (unsigned)(qblocks < 32 * kSmCount ? qblocks : 32 * kSmCount);
+    const size_t qsmem = sizeof(QueryWarpSmem) * kQueryWarps;
+    GDL_CUDA_TRY(cudaFuncSetAttribute(rg_query_warp_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)qsmem));
+    rg_query_warp_kernel<<<qgrid, kQueryWarps * 32, qsmem, st>>>(x, ptr, num_clouds, n_points, mask, r_sq, inv, loop, cap,
+                                                             w.gp, w.sorted_keys, w.cell_start, w.sorted_pts,
+                                                             w.counts, w.padded);
     GDL_CUDA_TRY((exclusive_scan<int32_t, int64_t>(w.counts, out_row_ptr, n_points, w.scan_scratch,
                                                    out_row_ptr + n_points, st)));
-    rg_compact_kernel<<<(unsigned)(((n_points + 1) * 32 + 255) / 256), 256, 0, st>>>(
+    rg_compact_sort_kernel<<<(unsigned)(((n_points + 1) * 32 + 255) / 256), 256, 0, st>>>(
         w.counts, w.padded, n_points, cap, out_row_ptr, out_src, out_dst, out_row_ptr32, out_src32);
     GDL_CUDA_TRY(cudaGetLastError());
     return GDL_OK;
