@@ -18,6 +18,7 @@
 // Small query sets split each cloud's sources over `split` CTAs; knn_merge_kernel merges
 // their sorted partial lists.
 #include "common.cuh"
+#include "knn_grid.cuh"
 #include "radix.cuh"
 
 namespace gdl {
@@ -422,7 +423,14 @@ static int knn_split(int64_t n_q, int32_t B, int64_t max_src) {
 struct KnnWs {
     int32_t *tile_base, *flag_count, *flag_list, *part_i, *part_cnt;
     float *part_d;
+    bool grid;  // clouds large enough for the grid path (knn_grid.cu)
+    KgWs kg;
 };
+
+// The grid path needs local source indices below 2^31.
+static bool knn_use_grid(int32_t B, int64_t max_src) {
+    return max_src >= kKgMinSources && (int64_t)B * max_src < ((int64_t)1 << 31) - 1;
+}
 
 static size_t knn_ws(int64_t n_q, int32_t B, int32_t k, int64_t max_src, char *base, KnnWs *w) {
     const int split = knn_split(n_q, B, max_src);
@@ -442,6 +450,12 @@ static size_t knn_ws(int64_t n_q, int32_t B, int32_t k, int64_t max_src, char *b
     t.part_cnt = (int32_t *)take(sizeof(int32_t) * np);
     t.part_d = (float *)take(sizeof(float) * np * (kb + 1));
     t.part_i = (int32_t *)take(sizeof(int32_t) * np * (kb + 1));
+    t.grid = knn_use_grid(B, max_src);
+    if (t.grid) {
+        const size_t gbytes = knn_grid_ws((int64_t)B * max_src, B, nullptr, nullptr);
+        char *gb = take(gbytes);
+        if (base) knn_grid_ws((int64_t)B * max_src, B, gb, &t.kg);
+    }
     if (w) *w = t;
     return off;
 }
@@ -502,6 +516,14 @@ extern "C" int gdl_knn(const float *query, const float *source, const int64_t *p
     GDL_CUDA_TRY(cudaMemsetAsync(w.flag_count, 0, sizeof(int32_t), st));
     knn_tiles_kernel<<<1, kScanThreads, 0, st>>>(ptr_q, num_clouds, w.tile_base);
     knn_pad_kernel<<<padg, 256, 0, st>>>(ptr_q, num_clouds, n_query, k, out_idx, out_dist);
+    if (w.grid) {  // large clouds: exact search over a grid of each cloud's sources
+        GDL_CUDA_TRY(knn_grid_run(query, source, ptr_q, ptr_s, num_clouds, n_query, k, max_cloud_sources, w.kg,
+                                  out_idx, out_dist, w.flag_list, w.flag_count, st));
+        knn_exact_kernel<<<kSmCount, kKnnThreads, 0, st>>>(query, source, ptr_q, ptr_s, num_clouds, k, w.flag_list,
+                                                           w.flag_count, out_idx, out_dist);
+        GDL_CUDA_TRY(cudaGetLastError());
+        return GDL_OK;
+    }
     const int split = knn_split(n_query, num_clouds, max_cloud_sources);
     switch (knn_bucket(k)) {
     case 4: knn_launch<4>(query, source, ptr_q, ptr_s, num_clouds, n_query, k, split, w, out_idx, out_dist, st); break;

@@ -1,0 +1,47 @@
+// knn_grid.cuh -- exact KNN over a uniform grid of each cloud's sources (large clouds).
+#pragma once
+
+#include "common.cuh"
+#include "radix.cuh"
+
+namespace gdl {
+
+// The grid path serves calls whose largest cloud has at least this many sources. Below it the
+// brute-force scan wins: it is fp32-bound at ~3 T pairs/s, while a uniform grid cannot fit both
+// clustered sources and queries that sit away from them (measured on configurations 3 and 4:
+// 1.28 ms vs 1.2 ms and 37.9 ms vs 4.8 ms), and the quadratic cost only bites for larger clouds.
+constexpr int64_t kKgMinSources = 32768;
+constexpr int kKgCellBudget = 16;  // grid cells per source point at most (dense cell table)
+
+struct KGrid {
+    float mn[3];
+    float h, inv;
+    float delta;  // coordinate slack of the pruning bound (rounding of cell assignment)
+    int res[3];
+    int ok;       // 1 grid built; 0 cloud without sources; -1 non-finite coordinates
+};
+
+struct KgWs {
+    int64_t *lptr;      // [B + 1] source offsets relative to ptr_s[0]
+    int32_t *invalid;   // [1] the sources exceed the capacity the workspace was sized for
+    KGrid *grid;        // [B]
+    int32_t *key_bits;  // [1]
+    uint32_t *keys, *sorted_keys;
+    int32_t *sorted_idx;
+    float4 *pts;   // sorted sources, .w = local source index
+    int2 *cells;   // [kKgCellBudget * nmax] (first, one-past-last) sorted position per cell
+    RadixScratch rs;
+};
+
+// bytes of the grid path's workspace for at most `nmax` sources in `B` clouds (base == nullptr:
+// size only); carves `w` from `base` otherwise
+size_t knn_grid_ws(int64_t nmax, int32_t B, char *base, KgWs *w);
+
+// Builds the grids and answers every query of [ptr_q[0], ptr_q[B]): rows are written, or the
+// query is appended to flag_list for the exact heap replay (equal distances among its k+1
+// nearest, non-finite coordinates, or a search that ran out of room).
+cudaError_t knn_grid_run(const float *query, const float *source, const int64_t *ptr_q, const int64_t *ptr_s,
+                         int32_t B, int64_t n_q, int k, int64_t max_src, const KgWs &w, int64_t *out_idx,
+                         float *out_dist, int32_t *flag_list, int32_t *flag_count, cudaStream_t st);
+
+}  // namespace gdl

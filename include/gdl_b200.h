@@ -84,7 +84,10 @@ int gdl_fps(const float *pos, const int64_t *ptr, const int64_t *k_per_cloud, in
  * squared distances, 1e30 padded. At most min(k, 64) neighbours per query (the reference's
  * MinK<64> bucket), ascending distance; equal distances are ordered exactly as the
  * reference's heap orders them. Queries outside every [ptr_q[b], ptr_q[b+1]) keep padding.
- * max_cloud_sources: host-side upper bound of max_b (ptr_s[b+1] - ptr_s[b]).
+ * max_cloud_sources: host-side bound of the sources per cloud, max_b (ptr_s[b+1] - ptr_s[b]),
+ * or any value with num_clouds * max_cloud_sources >= ptr_s[num_clouds] - ptr_s[0] (e.g. the mean
+ * rounded up). Calls with max_cloud_sources >= 32768 search a grid of each cloud's sources (exact;
+ * knn_grid.cu); if the bound is violated there, every query falls back to the exact heap replay.
  */
 size_t gdl_knn_workspace_size(int64_t n_query, int32_t num_clouds, int32_t k, int64_t max_cloud_sources);
 int gdl_knn(const float *query, const float *source, const int64_t *ptr_q, const int64_t *ptr_s,

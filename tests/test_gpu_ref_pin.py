@@ -34,7 +34,11 @@ def ref():
 def _clouds(seed, sizes, kind="uniform", scale=1.0):
     g = torch.Generator().manual_seed(seed)
     n = int(sum(sizes))
-    if kind == "lattice":  # exact ties everywhere
+    if kind == "gmm":  # clustered: 8 tight blobs in the unit cube
+        centres = torch.rand(8, 3, generator=g)
+        comp = torch.randint(0, 8, (n,), generator=g)
+        x = (centres[comp] + 0.03 * torch.randn(n, 3, generator=g)) * scale
+    elif kind == "lattice":  # exact ties everywhere
         x = torch.randint(0, 6, (n, 3), generator=g).float() * 0.25 * scale
     elif kind == "dup":  # many duplicated points
         base = torch.rand(max(n // 8, 1), 3, generator=g) * scale
@@ -93,6 +97,23 @@ def test_knn_vs_reference_kernel(ref, kind, k):
 
     x, ptr = _clouds(11, [1500, 40, 3000], kind)
     q, pq = _clouds(12, [300, 10, 700], "huge" if kind == "nonfinite" else kind)
+    wi, wd = ref["knn"].knn_cuda(q.to(DEV), x.to(DEV), pq.to(DEV), ptr.to(DEV), k)
+    gi, gd = csrc.knn_cuda(q.to(DEV), x.to(DEV), pq.to(DEV), ptr.to(DEV), k)
+    assert torch.equal(gi.cpu(), wi.cpu())
+    assert torch.equal(gd.cpu().view(torch.int32), wd.cpu().view(torch.int32))
+
+
+@pytest.mark.parametrize("kind", ["uniform", "gmm", "lattice", "dup", "nonfinite", "far"])
+@pytest.mark.parametrize("k", [1, 4, 16, 32, 64, 80])
+def test_knn_grid_path_vs_reference_kernel(ref, kind, k):
+    """Clouds of >= 32768 sources take the grid search (knn_grid.cu); a small cloud rides along."""
+    from gdl_b200 import csrc
+
+    skind = "uniform" if kind == "far" else kind
+    x, ptr = _clouds(21, [40000, 60, 33000, 36000], skind)
+    q, pq = _clouds(22, [700, 15, 900, 300], "huge" if kind == "nonfinite" else skind)
+    if kind == "far":  # queries far outside the sources' box: long shell searches
+        q = q * 50.0
     wi, wd = ref["knn"].knn_cuda(q.to(DEV), x.to(DEV), pq.to(DEV), ptr.to(DEV), k)
     gi, gd = csrc.knn_cuda(q.to(DEV), x.to(DEV), pq.to(DEV), ptr.to(DEV), k)
     assert torch.equal(gi.cpu(), wi.cpu())
