@@ -18,6 +18,7 @@
 // 142-158), VEC channels per lane. Max uses the forward's arg and re-reads msg only for
 // tied maxima, whose gradient is shared evenly (torch's amax rule).
 #include <initializer_list>
+#include <type_traits>
 #include <mutex>
 
 #include "common.cuh"
@@ -210,6 +211,133 @@ __device__ __forceinline__ bool queue_long(int64_t n, int lig, int32_t *long_lis
     return __shfl_sync(gmask, queued, leader) != 0;
 }
 
+// ---------------------------------------------------------------- packed bf16 max
+// Two bf16 channels per 32-bit word. Per channel: the maximum (max.NaN: a NaN anywhere makes it
+// NaN), the largest of the other values (`second`, starts as NaN, which max ignores) and the slot
+// of the first maximum (updated on strictly greater values). The maximum is tied exactly when
+// second == best at the end. Three packed operations and two selects per pair of values.
+struct MaxBf16x2 {
+    uint32_t best, second;
+    int arg_lo, arg_hi;
+    __device__ __forceinline__ void first(uint32_t w, int slot) {
+        best = w;
+        second = 0x7fc07fc0u;  // NaN: no second value yet
+        arg_lo = arg_hi = slot;
+    }
+    __device__ __forceinline__ void push(uint32_t w, int slot) {
+        asm("{\n\t.reg .pred gl, gh;\n\t.reg .b32 lo;\n\t"
+            "setp.gt.bf16x2 gl|gh, %4, %0;\n\t"
+            "selp.b32 %2, %5, %2, gl;\n\t"
+            "selp.b32 %3, %5, %3, gh;\n\t"
+            "min.bf16x2 lo, %0, %4;\n\t"
+            "max.bf16x2 %1, %1, lo;\n\t"
+            "max.NaN.bf16x2 %0, %0, %4;\n\t}"
+            : "+r"(best), "+r"(second), "+r"(arg_lo), "+r"(arg_hi)
+            : "r"(w), "r"(slot));
+    }
+};
+
+template <int W, typename Raw>
+__device__ __forceinline__ void raw_words(const Raw &r, uint32_t (&w)[W]);
+template <>
+__device__ __forceinline__ void raw_words<4, uint4>(const uint4 &r, uint32_t (&w)[4]) {
+    w[0] = r.x; w[1] = r.y; w[2] = r.z; w[3] = r.w;
+}
+template <>
+__device__ __forceinline__ void raw_words<2, uint2>(const uint2 &r, uint32_t (&w)[2]) {
+    w[0] = r.x; w[1] = r.y;
+}
+template <>
+__device__ __forceinline__ void raw_words<1, uint32_t>(const uint32_t &r, uint32_t (&w)[1]) {
+    w[0] = r;
+}
+
+// one channel of segment n by the scalar rules (value, first slot, tie): used when the maximum
+// is a zero, whose sign the packed max may not keep from the first occurrence
+template <typename T>
+__device__ __noinline__ void seg_max_exact(const T *__restrict__ msg, int64_t C, const int32_t *__restrict__ perm,
+                                           int s, int e, int64_t ch, float &val, int &argo) {
+    MaxState m;
+    m.init();
+    for (int j = s; j < e; ++j) {
+        float x;
+        vec_load<T, 1>(msg + (perm ? (int64_t)__ldg(perm + j) : (int64_t)j) * C + ch, &x);
+        m.push(x, j);
+    }
+    val = m.value();
+    argo = m.arg_out();
+}
+
+// bf16 max of short segments, packed: VEC channels per lane (VEC even)
+template <int VEC>
+__device__ __forceinline__ void seg_fwd_bf16_max(const uint16_t *__restrict__ msg, int64_t C,
+                                                 const int32_t *__restrict__ perm, int s, int e, int64_t n,
+                                                 int64_t c, float *__restrict__ out, int32_t *__restrict__ arg) {
+    using IO = VecIO<uint16_t, VEC>;
+    constexpr int W = VEC / 2;
+    constexpr int U = ShortUnroll<VEC>::value;
+    MaxBf16x2 mx[W];
+    float o[VEC];
+    if (e <= s) {
+#pragma unroll
+        for (int v = 0; v < VEC; ++v) {
+            o[v] = 0.0f;
+            if (arg) arg[n * C + c + v] = -1;
+        }
+        VecIO<float, VEC>::store(out + n * C + c, o);
+        return;
+    }
+    {  // the first row starts every channel
+        uint32_t w[W];
+        raw_words<W>(IO::load_raw(msg + (perm ? (int64_t)__ldg(perm + s) : (int64_t)s) * C + c), w);
+#pragma unroll
+        for (int i = 0; i < W; ++i) mx[i].first(w[i], s);
+    }
+    int j = s + 1;
+    for (; j + U <= e; j += U) {
+        typename IO::Raw r[U];
+#pragma unroll
+        for (int u = 0; u < U; ++u) r[u] = IO::load_raw(msg + (perm ? (int64_t)__ldg(perm + j + u) : (int64_t)(j + u)) * C + c);
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+            uint32_t w[W];
+            raw_words<W>(r[u], w);
+#pragma unroll
+            for (int i = 0; i < W; ++i) mx[i].push(w[i], j + u);
+        }
+    }
+    for (; j < e; ++j) {
+        uint32_t w[W];
+        raw_words<W>(IO::load_raw(msg + (perm ? (int64_t)__ldg(perm + j) : (int64_t)j) * C + c), w);
+#pragma unroll
+        for (int i = 0; i < W; ++i) mx[i].push(w[i], j);
+    }
+#pragma unroll
+    for (int i = 0; i < W; ++i) {
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+            const int v = 2 * i + h;
+            const uint32_t bb = h ? (mx[i].best & 0xffff0000u) : (mx[i].best << 16);
+            const uint32_t sb = h ? (mx[i].second & 0xffff0000u) : (mx[i].second << 16);
+            const float best = __uint_as_float(bb), second = __uint_as_float(sb);
+            int a = h ? mx[i].arg_hi : mx[i].arg_lo;
+            float val;
+            if (best != best) {  // a NaN in the segment
+                val = __int_as_float(0x7fc00000);
+                a = -1;
+            } else if (best == 0.0f) {  // keep the first zero's sign, as the scalar rule does
+                seg_max_exact<uint16_t>(msg, C, perm, s, e, c + v, val, a);
+            } else {
+                val = best;
+                if (second == best) a = -1;  // tied maximum
+            }
+            o[v] = val;
+            if (arg) arg[n * C + c + v] = a;
+        }
+    }
+    VecIO<float, VEC>::store(out + n * C + c, o);
+}
+
 template <typename T, int VEC, int G, int RED>
 __global__ void __launch_bounds__(kSegThreads) seg_fwd_short_kernel(
     const T *__restrict__ msg, int64_t C, const int32_t *__restrict__ perm, const int32_t *__restrict__ ns,
@@ -222,60 +350,67 @@ __global__ void __launch_bounds__(kSegThreads) seg_fwd_short_kernel(
     const int s = ns[n], e = ne[n];
     if (e - s > kLongSegment && queue_long<G>(n, lig, long_list, long_count, max_long)) return;
     using IO = VecIO<T, VEC>;
-    for (int64_t c0 = 0; c0 < C; c0 += (int64_t)G * VEC) {
-        const int64_t c = c0 + (int64_t)lig * VEC;
-        if (c >= C) continue;
-        float acc[VEC];
-        MaxState mx[RED == GDL_REDUCE_MAX ? VEC : 1];
-#pragma unroll
-        for (int v = 0; v < VEC; ++v) {
-            acc[v] = 0.0f;
-            if (RED == GDL_REDUCE_MAX) mx[v].init();
+    if constexpr (std::is_same<T, uint16_t>::value && RED == GDL_REDUCE_MAX && VEC % 2 == 0) {
+        for (int64_t c0 = 0; c0 < C; c0 += (int64_t)G * VEC) {
+            const int64_t c = c0 + (int64_t)lig * VEC;
+            if (c < C) seg_fwd_bf16_max<VEC>(msg, C, perm, s, e, n, c, out, arg);
         }
-        // batches of U rows with their loads issued together: deg / U memory latencies
-        constexpr int U = ShortUnroll<VEC>::value;
-        int j = s;
-        for (; j + U <= e; j += U) {
-            typename IO::Raw r[U];
-#pragma unroll
-            for (int u = 0; u < U; ++u) {
-                const int64_t row = perm ? (int64_t)__ldg(perm + j + u) : (int64_t)(j + u);
-                r[u] = IO::load_raw(msg + row * C + c);
+    } else {
+        for (int64_t c0 = 0; c0 < C; c0 += (int64_t)G * VEC) {
+            const int64_t c = c0 + (int64_t)lig * VEC;
+            if (c >= C) continue;
+            float acc[VEC];
+            MaxState mx[RED == GDL_REDUCE_MAX ? VEC : 1];
+    #pragma unroll
+            for (int v = 0; v < VEC; ++v) {
+                acc[v] = 0.0f;
+                if (RED == GDL_REDUCE_MAX) mx[v].init();
             }
-#pragma unroll
-            for (int u = 0; u < U; ++u) {
+            // batches of U rows with their loads issued together: deg / U memory latencies
+            constexpr int U = ShortUnroll<VEC>::value;
+            int j = s;
+            for (; j + U <= e; j += U) {
+                typename IO::Raw r[U];
+    #pragma unroll
+                for (int u = 0; u < U; ++u) {
+                    const int64_t row = perm ? (int64_t)__ldg(perm + j + u) : (int64_t)(j + u);
+                    r[u] = IO::load_raw(msg + row * C + c);
+                }
+    #pragma unroll
+                for (int u = 0; u < U; ++u) {
+                    float x[VEC];
+                    IO::cvt(r[u], x);
+    #pragma unroll
+                    for (int v = 0; v < VEC; ++v) {
+                        if (RED == GDL_REDUCE_MAX) mx[v].push(x[v], j + u);
+                        else acc[v] = add_ftz(acc[v], x[v]);
+                    }
+                }
+            }
+            for (; j < e; ++j) {
                 float x[VEC];
-                IO::cvt(r[u], x);
-#pragma unroll
+                const int64_t row = perm ? (int64_t)__ldg(perm + j) : (int64_t)j;
+                vec_load<T, VEC>(msg + row * C + c, x);
+    #pragma unroll
                 for (int v = 0; v < VEC; ++v) {
-                    if (RED == GDL_REDUCE_MAX) mx[v].push(x[v], j + u);
+                    if (RED == GDL_REDUCE_MAX) mx[v].push(x[v], j);
                     else acc[v] = add_ftz(acc[v], x[v]);
                 }
             }
-        }
-        for (; j < e; ++j) {
-            float x[VEC];
-            const int64_t row = perm ? (int64_t)__ldg(perm + j) : (int64_t)j;
-            vec_load<T, VEC>(msg + row * C + c, x);
-#pragma unroll
+            float o[VEC];
+    #pragma unroll
             for (int v = 0; v < VEC; ++v) {
-                if (RED == GDL_REDUCE_MAX) mx[v].push(x[v], j);
-                else acc[v] = add_ftz(acc[v], x[v]);
+                if (RED == GDL_REDUCE_MAX) {
+                    o[v] = mx[v].value();
+                    if (arg) arg[n * C + c + v] = mx[v].arg_out();
+                } else if (RED == GDL_REDUCE_MEAN) {
+                    o[v] = (e > s) ? __fdiv_rn(acc[v], (float)(e - s)) : 0.0f;
+                } else {
+                    o[v] = acc[v];
+                }
             }
+            VecIO<float, VEC>::store(out + n * C + c, o);
         }
-        float o[VEC];
-#pragma unroll
-        for (int v = 0; v < VEC; ++v) {
-            if (RED == GDL_REDUCE_MAX) {
-                o[v] = mx[v].value();
-                if (arg) arg[n * C + c + v] = mx[v].arg_out();
-            } else if (RED == GDL_REDUCE_MEAN) {
-                o[v] = (e > s) ? __fdiv_rn(acc[v], (float)(e - s)) : 0.0f;
-            } else {
-                o[v] = acc[v];
-            }
-        }
-        VecIO<float, VEC>::store(out + n * C + c, o);
     }
 }
 
@@ -375,92 +510,88 @@ __global__ void __launch_bounds__(kSegThreads) seg_fwd_long_kernel(
 }
 
 // gradient of one (segment, VEC channels) for slots [j0, j1) of segment n. The values a slot
-// can receive are fixed per segment (sum: g; mean: g / deg; max: g / #maxima where the slot
-// holds the maximum, 0 * that share elsewhere -- torch's mask * share, signed zeros included),
-// so they are converted to T once and each slot only selects and stores.
+// can receive are fixed per segment (sum: g; mean: g / deg; max: g where the slot holds the
+// maximum, 0 * g elsewhere -- torch's mask * share, signed zeros included), so they are converted
+// to T once and the slots are a pure store stream. A max channel without a unique maximum (arg
+// -1: tied or NaN) gets its values from seg_bwd_max_fix_kernel afterwards.
 template <typename T, int VEC, int RED>
 __device__ __forceinline__ void seg_bwd_range(const float *__restrict__ grad_out, const T *__restrict__ msg,
                                               const float *__restrict__ out, const int32_t *__restrict__ arg,
                                               int64_t C, const int32_t *__restrict__ perm, int64_t n, int s, int e,
                                               int j0, int j1, int64_t c, T *__restrict__ grad_msg) {
+    (void)msg;
+    (void)out;
     float g[VEC];
     vec_load<float, VEC>(grad_out + n * C + c, g);
     T hit_v[VEC], miss_v[VEC];
-    int a[VEC];
-    float mx[VEC];
-    bool need = false;  // some channel has a tied (or NaN) maximum: compare values per slot
-    if (RED == GDL_REDUCE_MAX) {
-#pragma unroll
-        for (int v = 0; v < VEC; ++v) {
-            a[v] = arg ? arg[n * C + c + v] : -1;
-            mx[v] = out[n * C + c + v];
-            need |= a[v] < 0;
-        }
-    }
-    int t[VEC];  // slots equal to the maximum, per tied channel
-#pragma unroll
-    for (int v = 0; v < VEC; ++v) t[v] = 0;
-    if (RED == GDL_REDUCE_MAX && need) {
-        using IO = VecIO<T, VEC>;
-        constexpr int U = 4;  // tied channels only: few registers beat deep batches here
-        for (int k = s; k < e; k += U) {
-            typename IO::Raw r[U];
-#pragma unroll
-            for (int u = 0; u < U; ++u)
-                if (k + u < e) r[u] = IO::load_raw(msg + (perm ? (int64_t)__ldg(perm + k + u) : (int64_t)(k + u)) * C + c);
-#pragma unroll
-            for (int u = 0; u < U; ++u) {
-                if (k + u < e) {
-                    float x[VEC];
-                    IO::cvt(r[u], x);
-#pragma unroll
-                    for (int v = 0; v < VEC; ++v) t[v] += x[v] == mx[v];
-                }
-            }
-        }
-    }
 #pragma unroll
     for (int v = 0; v < VEC; ++v) {
-        float base;
-        if (RED == GDL_REDUCE_SUM) base = g[v];
-        else if (RED == GDL_REDUCE_MEAN) base = __fdiv_rn(g[v], (float)(e - s));
-        else base = a[v] < 0 ? __fdiv_rn(g[v], (float)t[v]) : g[v];  // tied: share among the maxima
+        const float base = RED == GDL_REDUCE_MEAN ? __fdiv_rn(g[v], (float)(e - s)) : g[v];
         hit_v[v] = to_elem<T>(1.0f * base);
         miss_v[v] = to_elem<T>(0.0f * base);
     }
-    if constexpr (RED == GDL_REDUCE_MAX) {
-        // one loop for every lane: only lanes with a tied channel load the values (batched)
-        using IO = VecIO<T, VEC>;
-        constexpr int U = 4;
-        for (int j = j0; j < j1; j += U) {
-            typename IO::Raw r[U];
-            if (need) {
+    if constexpr (RED == GDL_REDUCE_MAX && sizeof(T) == 4) {
+        // f32: select per slot and channel (a tied channel gets misses; the fix-up rewrites it)
+        int a[VEC];
 #pragma unroll
-                for (int u = 0; u < U; ++u)
-                    if (j + u < j1)
-                        r[u] = IO::load_raw(msg + (perm ? (int64_t)__ldg(perm + j + u) : (int64_t)(j + u)) * C + c);
-            }
-#pragma unroll
-            for (int u = 0; u < U; ++u) {
-                if (j + u < j1) {
-                    float x[VEC];
-                    if (need) IO::cvt(r[u], x);
-                    T val[VEC];
-#pragma unroll
-                    for (int v = 0; v < VEC; ++v) {
-                        const bool hit = a[v] >= 0 ? (a[v] == j + u) : (x[v] == mx[v]);
-                        val[v] = hit ? hit_v[v] : miss_v[v];
-                    }
-                    const int64_t row = perm ? (int64_t)__ldg(perm + j + u) : (int64_t)(j + u);
-                    VecIO<T, VEC>::store_raw(grad_msg + row * C + c, val);
-                }
-            }
-        }
-    } else {
-        for (int j = j0; j < j1; ++j) {  // a pure store stream
+        for (int v = 0; v < VEC; ++v) a[v] = arg ? arg[n * C + c + v] : -1;
+        for (int j = j0; j < j1; ++j) {
             const int64_t row = perm ? (int64_t)__ldg(perm + j) : (int64_t)j;
-            VecIO<T, VEC>::store_raw(grad_msg + row * C + c, hit_v);
+            T val[VEC];
+#pragma unroll
+            for (int v = 0; v < VEC; ++v) val[v] = a[v] == j ? hit_v[v] : miss_v[v];
+            VecIO<T, VEC>::store_raw(grad_msg + row * C + c, val);
         }
+        return;
+    }
+    // bf16 max (and sum / mean): one constant row for every slot -- for max the miss row, then
+    // each channel's unique maximum written over it, which costs no per-value work per slot
+    const T *row_v = RED == GDL_REDUCE_MAX ? miss_v : hit_v;
+    for (int j = j0; j < j1; ++j) {
+        const int64_t row = perm ? (int64_t)__ldg(perm + j) : (int64_t)j;
+        VecIO<T, VEC>::store_raw(grad_msg + row * C + c, row_v);
+    }
+    if constexpr (RED == GDL_REDUCE_MAX) {
+        if (!arg) return;  // every channel is fixed up afterwards
+#pragma unroll
+        for (int v = 0; v < VEC; ++v) {  // the unique maximum's slot, after its miss row (same thread)
+            const int av = arg[n * C + c + v];
+            if (av >= j0 && av < j1) {
+                const int64_t row = perm ? (int64_t)__ldg(perm + av) : (int64_t)av;
+                grad_msg[row * C + c + v] = hit_v[v];
+            }
+        }
+    }
+}
+
+// Max channels without a unique maximum (arg -1, or no arg at all): the gradient is shared evenly
+// among the slots equal to the maximum (torch's amax rule); a NaN maximum equals no slot, so
+// every slot gets 0 * (g / 0). One thread per (segment, channel); all other threads leave at once.
+template <typename T>
+__global__ void __launch_bounds__(256) seg_bwd_max_fix_kernel(
+    const float *__restrict__ grad_out, const T *__restrict__ msg, const float *__restrict__ out,
+    const int32_t *__restrict__ arg, int64_t C, const int32_t *__restrict__ perm, const int32_t *__restrict__ ns,
+    const int32_t *__restrict__ ne, int64_t N, T *__restrict__ grad_msg) {
+    const int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (t >= N * C) return;
+    if (arg && arg[t] >= 0) return;
+    const int64_t n = t / C, ch = t - n * C;
+    const int s = ns[n], e = ne[n];
+    if (e <= s) return;
+    const float mx = out[t];
+    int cnt = 0;
+    for (int j = s; j < e; ++j) {
+        float x;
+        vec_load<T, 1>(msg + (perm ? (int64_t)__ldg(perm + j) : (int64_t)j) * C + ch, &x);
+        cnt += x == mx;
+    }
+    const float base = __fdiv_rn(grad_out[t], (float)cnt);
+    const T hit = to_elem<T>(1.0f * base), miss = to_elem<T>(0.0f * base);
+    for (int j = s; j < e; ++j) {
+        const int64_t row = perm ? (int64_t)__ldg(perm + j) : (int64_t)j;
+        float x;
+        vec_load<T, 1>(msg + row * C + ch, &x);
+        grad_msg[row * C + ch] = x == mx ? hit : miss;
     }
 }
 
@@ -613,6 +744,9 @@ static void launch_bwd(const float *go, const void *msg, const float *out, const
     if (ml > 0)
         seg_bwd_long_kernel<T, VEC, G, RED><<<(unsigned)ml, kSegThreads, 0, st>>>(go, (const T *)msg, out, arg, C, perm,
                                                                                  ns, ne, (T *)gm, ll, lc);
+    if (RED == GDL_REDUCE_MAX)
+        seg_bwd_max_fix_kernel<T><<<(unsigned)((N * C + 255) / 256), 256, 0, st>>>(go, (const T *)msg, out, arg, C,
+                                                                                   perm, ns, ne, N, (T *)gm);
 }
 
 template <typename T, int VEC, int RED>
