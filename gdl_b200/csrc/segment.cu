@@ -565,33 +565,53 @@ __device__ __forceinline__ void seg_bwd_range(const float *__restrict__ grad_out
 }
 
 // Max channels without a unique maximum (arg -1, or no arg at all): the gradient is shared evenly
-// among the slots equal to the maximum (torch's amax rule); a NaN maximum equals no slot, so
-// every slot gets 0 * (g / 0). One thread per (segment, channel); all other threads leave at once.
+// among the slots equal to the maximum (torch's amax rule); a NaN maximum equals no slot, so every
+// slot gets 0 * (g / 0). One warp per segment: the lanes read the segment's arg row, and for each
+// channel to fix, every lane loads the value of one slot, a ballot counts the maxima, and the
+// lanes write the shares (segments longer than 32 slots take their slots 32 at a time).
+constexpr int kFixWarps = 8;
+
 template <typename T>
-__global__ void __launch_bounds__(256) seg_bwd_max_fix_kernel(
+__global__ void __launch_bounds__(kFixWarps * 32) seg_bwd_max_fix_kernel(
     const float *__restrict__ grad_out, const T *__restrict__ msg, const float *__restrict__ out,
     const int32_t *__restrict__ arg, int64_t C, const int32_t *__restrict__ perm, const int32_t *__restrict__ ns,
     const int32_t *__restrict__ ne, int64_t N, T *__restrict__ grad_msg) {
-    const int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-    if (t >= N * C) return;
-    if (arg && arg[t] >= 0) return;
-    const int64_t n = t / C, ch = t - n * C;
-    const int s = ns[n], e = ne[n];
-    if (e <= s) return;
-    const float mx = out[t];
-    int cnt = 0;
-    for (int j = s; j < e; ++j) {
-        float x;
-        vec_load<T, 1>(msg + (perm ? (int64_t)__ldg(perm + j) : (int64_t)j) * C + ch, &x);
-        cnt += x == mx;
-    }
-    const float base = __fdiv_rn(grad_out[t], (float)cnt);
-    const T hit = to_elem<T>(1.0f * base), miss = to_elem<T>(0.0f * base);
-    for (int j = s; j < e; ++j) {
-        const int64_t row = perm ? (int64_t)__ldg(perm + j) : (int64_t)j;
-        float x;
-        vec_load<T, 1>(msg + row * C + ch, &x);
-        grad_msg[row * C + ch] = x == mx ? hit : miss;
+    const int lane = threadIdx.x & 31;
+    const int64_t nw = (int64_t)gridDim.x * kFixWarps;
+    for (int64_t n = (int64_t)blockIdx.x * kFixWarps + (threadIdx.x >> 5); n < N; n += nw) {
+        const int s = ns[n], e = ne[n];
+        if (e <= s) continue;  // uniform over the warp
+        for (int64_t c0 = 0; c0 < C; c0 += 32) {
+            const int64_t cl = c0 + lane;
+            unsigned todo = __ballot_sync(0xffffffffu, cl < C && (!arg || arg[n * C + cl] < 0));
+            while (todo) {
+                const int64_t ch = c0 + __ffs(todo) - 1;
+                todo &= todo - 1;
+                const float mx = out[n * C + ch];
+                int cnt = 0;
+                for (int j0 = s; j0 < e; j0 += 32) {
+                    const int j = j0 + lane;
+                    bool eq = false;
+                    if (j < e) {
+                        float x;
+                        vec_load<T, 1>(msg + (perm ? (int64_t)__ldg(perm + j) : (int64_t)j) * C + ch, &x);
+                        eq = x == mx;
+                    }
+                    cnt += __popc(__ballot_sync(0xffffffffu, eq));
+                }
+                const float base = __fdiv_rn(grad_out[n * C + ch], (float)cnt);
+                const T hit = to_elem<T>(1.0f * base), miss = to_elem<T>(0.0f * base);
+                for (int j0 = s; j0 < e; j0 += 32) {
+                    const int j = j0 + lane;
+                    if (j < e) {
+                        const int64_t row = perm ? (int64_t)__ldg(perm + j) : (int64_t)j;
+                        float x;
+                        vec_load<T, 1>(msg + row * C + ch, &x);
+                        grad_msg[row * C + ch] = x == mx ? hit : miss;
+                    }
+                }
+            }
+        }
     }
 }
 
@@ -744,9 +764,11 @@ static void launch_bwd(const float *go, const void *msg, const float *out, const
     if (ml > 0)
         seg_bwd_long_kernel<T, VEC, G, RED><<<(unsigned)ml, kSegThreads, 0, st>>>(go, (const T *)msg, out, arg, C, perm,
                                                                                  ns, ne, (T *)gm, ll, lc);
-    if (RED == GDL_REDUCE_MAX)
-        seg_bwd_max_fix_kernel<T><<<(unsigned)((N * C + 255) / 256), 256, 0, st>>>(go, (const T *)msg, out, arg, C,
-                                                                                   perm, ns, ne, N, (T *)gm);
+    if (RED == GDL_REDUCE_MAX) {
+        const int64_t fb = (N + kFixWarps - 1) / kFixWarps;
+        seg_bwd_max_fix_kernel<T><<<(unsigned)(fb < 16 * kSmCount ? fb : 16 * kSmCount), kFixWarps * 32, 0, st>>>(
+            go, (const T *)msg, out, arg, C, perm, ns, ne, N, (T *)gm);
+    }
 }
 
 template <typename T, int VEC, int RED>
