@@ -29,14 +29,14 @@ constexpr int kKnnMaxSplit = 32;
 
 // query tiles per cloud -> exclusive prefix (one block)
 __global__ void __launch_bounds__(kScanThreads) knn_tiles_kernel(const int64_t *__restrict__ ptr_q, int32_t B,
-                                                                 int32_t *__restrict__ tile_base) {
+                                                                 int32_t tile, int32_t *__restrict__ tile_base) {
     __shared__ int32_t warp_sums[32];
     __shared__ int32_t total;
     int32_t carry = 0;
     for (int32_t b0 = 0; b0 < B; b0 += kScanThreads) {
         const int32_t b = b0 + threadIdx.x;
         int32_t t = 0;
-        if (b < B) t = (int32_t)((ptr_q[b + 1] - ptr_q[b] + kKnnThreads - 1) / kKnnThreads);
+        if (b < B) t = (int32_t)((ptr_q[b + 1] - ptr_q[b] + tile - 1) / tile);
         int32_t off = block_exclusive_scan<int32_t>(t, warp_sums, &total) + carry;
         if (b < B) tile_base[b] = off;
         carry += total;
@@ -336,6 +336,157 @@ __global__ void __launch_bounds__(kKnnThreads) knn_merge_kernel(
     }
 }
 
+// ---------------------------------------------------------------- one warp per query (k >= 8, small clouds)
+// For larger k the per-thread heaps above spend their time in lock-step sift-downs. Here a warp
+// owns a query: its lanes test 32 sources at a time against the threshold (the (k_eff+1)-th best
+// so far), and each accepted candidate is inserted into the warp's sorted list of the L = k_eff+1
+// best, held as entry lane + 32 r in register set r of every lane: the insert position is one
+// ballot/popc, the shift one shuffle. The CTA's 8 queries (warps) of one cloud share the sources
+// staged in shared memory. Ties, non-finite coordinates and overflowed distances go to
+// knn_exact_kernel as in the per-thread path.
+constexpr int kWarpMinK = 8;
+// Measured: faster than the per-thread heaps for k = 16 over 2048 sources (57 vs 73 us), slower
+// for k = 32 over 8192 sources (1.59 vs 1.2 ms), where the serial insert chain dominates.
+constexpr int64_t kWarpMaxSources = 4096;
+constexpr int kWarpQ = 8;         // queries (warps) per CTA
+constexpr int kWarpChunk = 2048;  // sources staged per pass
+
+template <int NR>
+__device__ __forceinline__ void warp_list_insert(float (&ed)[NR], int (&ei)[NR], float dd, int ii, int lane) {
+    int pos = 0;
+#pragma unroll
+    for (int r = 0; r < NR; ++r) pos += __popc(__ballot_sync(0xffffffffu, ed[r] < dd));
+    float ud[NR], xd[NR];
+    int ui[NR], xi[NR];
+#pragma unroll
+    for (int r = 0; r < NR; ++r) {  // entry (lane + 32 r - 1), read before any entry changes
+        ud[r] = __shfl_up_sync(0xffffffffu, ed[r], 1);
+        ui[r] = __shfl_up_sync(0xffffffffu, ei[r], 1);
+        xd[r] = r > 0 ? __shfl_sync(0xffffffffu, ed[r > 0 ? r - 1 : 0], 31) : 0.0f;
+        xi[r] = r > 0 ? __shfl_sync(0xffffffffu, ei[r > 0 ? r - 1 : 0], 31) : 0;
+    }
+#pragma unroll
+    for (int r = 0; r < NR; ++r) {
+        const int i = lane + 32 * r;
+        if (i > pos) {
+            ed[r] = lane == 0 ? xd[r] : ud[r];
+            ei[r] = lane == 0 ? xi[r] : ui[r];
+        } else if (i == pos) {
+            ed[r] = dd;
+            ei[r] = ii;
+        }
+    }
+}
+
+template <int NR>
+__global__ void __launch_bounds__(kWarpQ * 32) knn_warp_kernel(
+    const float *__restrict__ query, const float *__restrict__ source, const int64_t *__restrict__ ptr_q,
+    const int64_t *__restrict__ ptr_s, int32_t B, int k, const int32_t *__restrict__ tile_base,
+    int64_t *__restrict__ out_idx, float *__restrict__ out_dist, int32_t *__restrict__ flag_list,
+    int32_t *__restrict__ flag_count) {
+    __shared__ float4 sh[kWarpChunk];
+    __shared__ int bad_s;
+    const int t = blockIdx.x;
+    if (t >= tile_base[B]) return;  // uniform over the CTA
+    const int b = find_segment(tile_base, B, t);
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int64_t q = ptr_q[b] + (int64_t)(t - tile_base[b]) * kWarpQ + warp;
+    const bool valid = q < ptr_q[b + 1];  // uniform over the warp
+    const int64_t s0 = ptr_s[b], s1 = ptr_s[b + 1];
+    const int ke = k < 64 ? k : 64;
+    const int L = ke + 1;
+    float qx = 0.0f, qy = 0.0f, qz = 0.0f;
+    bool nonfinite = false;
+    if (valid) {
+        qx = query[3 * q];
+        qy = query[3 * q + 1];
+        qz = query[3 * q + 2];
+        nonfinite = !(isfinite(qx) && isfinite(qy) && isfinite(qz));
+    }
+    const float kInf = __int_as_float(0x7f800000);
+    float ed[NR];
+    int ei[NR];
+#pragma unroll
+    for (int r = 0; r < NR; ++r) {
+        ed[r] = kInf;
+        ei[r] = -1;
+    }
+    float thr = kInf;
+    int cnt = 0;
+    if (threadIdx.x == 0) bad_s = 0;
+    for (int64_t c0 = s0; c0 < s1; c0 += kWarpChunk) {
+        const int m = (int)(s1 - c0 < kWarpChunk ? s1 - c0 : kWarpChunk);
+        __syncthreads();
+        bool bad = false;
+        for (int j = threadIdx.x; j < m; j += kWarpQ * 32) {
+            const float *p = source + 3 * (c0 + j);
+            const float x = p[0], y = p[1], z = p[2];
+            bad |= !(isfinite(x) && isfinite(y) && isfinite(z));
+            sh[j] = make_float4(x, y, z, 0.0f);
+        }
+        if (bad) bad_s = 1;
+        __syncthreads();
+        if (!valid) continue;  // uniform over the warp; the next pass's barrier is still reached
+        for (int j0 = 0; j0 < m; j0 += 32) {
+            const int j = j0 + lane;
+            float d = kInf;
+            if (j < m) {
+                const float4 sp = sh[j];
+                d = dist2(qx, qy, qz, sp.x, sp.y, sp.z);
+            }
+            unsigned acc = __ballot_sync(0xffffffffu, d < thr);
+            while (acc) {
+                const int l = __ffs(acc) - 1;
+                acc &= acc - 1;
+                const float dd = __shfl_sync(0xffffffffu, d, l);
+                if (!(dd < thr)) continue;  // the threshold tightened since the ballot (uniform)
+                warp_list_insert<NR>(ed, ei, dd, (int)(c0 + j0 + l), lane);
+                ++cnt;
+#pragma unroll
+                for (int r = 0; r < NR; ++r)  // threshold = entry L - 1 (register set, lane uniform)
+                    if ((L - 1) / 32 == r) thr = __shfl_sync(0xffffffffu, ed[r], (L - 1) & 31);
+            }
+        }
+    }
+    __syncthreads();  // bad_s is complete
+    nonfinite |= bad_s != 0;
+    if (!valid) return;
+    const int have = cnt < L ? cnt : L;
+    // every finite distance enters a list that is not full: a short list means overflowed distances
+    bool flag = nonfinite || (int64_t)have < (s1 - s0 < L ? s1 - s0 : (int64_t)L);
+    if (!flag) {
+        bool tie = false;
+#pragma unroll
+        for (int r = 0; r < NR; ++r) {
+            const float up = __shfl_up_sync(0xffffffffu, ed[r], 1);
+            const float cross = r > 0 ? __shfl_sync(0xffffffffu, ed[r > 0 ? r - 1 : 0], 31) : 0.0f;
+            const int i = lane + 32 * r;
+            const float prev = lane > 0 ? up : cross;
+            if (i >= 1 && i < have && prev == ed[r]) tie = true;
+        }
+        flag = __any_sync(0xffffffffu, tie);
+    }
+    if (flag) {
+        if (lane == 0) flag_list[atomicAdd(flag_count, 1)] = (int32_t)q;
+        return;
+    }
+    const int nv = have < ke ? have : ke;
+    int64_t *oi = out_idx + q * k;
+    float *od = out_dist + q * k;
+#pragma unroll
+    for (int r = 0; r < NR; ++r) {
+        const int i = lane + 32 * r;
+        if (i < k) {
+            oi[i] = i < nv ? (int64_t)ei[r] : -1;
+            od[i] = i < nv ? ed[r] : 1e30f;
+        }
+    }
+    for (int i = 32 * NR + lane; i < k; i += 32) {
+        oi[i] = -1;
+        od[i] = 1e30f;
+    }
+}
+
 __device__ __forceinline__ int find_cloud(const int64_t *__restrict__ ptr, int B, int64_t q) {
     int lo = 0, hi = B - 1;
     while (lo < hi) {
@@ -514,11 +665,29 @@ extern "C" int gdl_knn(const float *query, const float *source, const int64_t *p
         return cudaGetLastError() == cudaSuccess ? GDL_OK : GDL_ERR_CUDA;
     }
     GDL_CUDA_TRY(cudaMemsetAsync(w.flag_count, 0, sizeof(int32_t), st));
-    knn_tiles_kernel<<<1, kScanThreads, 0, st>>>(ptr_q, num_clouds, w.tile_base);
+    const bool warp_path = k >= kWarpMinK && max_cloud_sources <= kWarpMaxSources;
+    knn_tiles_kernel<<<1, kScanThreads, 0, st>>>(ptr_q, num_clouds, warp_path ? kWarpQ : kKnnThreads, w.tile_base);
     knn_pad_kernel<<<padg, 256, 0, st>>>(ptr_q, num_clouds, n_query, k, out_idx, out_dist);
     if (w.grid) {  // large clouds: exact search over a grid of each cloud's sources
         GDL_CUDA_TRY(knn_grid_run(query, source, ptr_q, ptr_s, num_clouds, n_query, k, max_cloud_sources, w.kg,
                                   out_idx, out_dist, w.flag_list, w.flag_count, st));
+        knn_exact_kernel<<<kSmCount, kKnnThreads, 0, st>>>(query, source, ptr_q, ptr_s, num_clouds, k, w.flag_list,
+                                                           w.flag_count, out_idx, out_dist);
+        GDL_CUDA_TRY(cudaGetLastError());
+        return GDL_OK;
+    }
+    if (warp_path) {
+        const unsigned grid = (unsigned)(n_query / kWarpQ + num_clouds);
+        const int L = (k < 64 ? k : 64) + 1;
+        if (L <= 32)
+            knn_warp_kernel<1><<<grid, kWarpQ * 32, 0, st>>>(query, source, ptr_q, ptr_s, num_clouds, k, w.tile_base,
+                                                             out_idx, out_dist, w.flag_list, w.flag_count);
+        else if (L <= 64)
+            knn_warp_kernel<2><<<grid, kWarpQ * 32, 0, st>>>(query, source, ptr_q, ptr_s, num_clouds, k, w.tile_base,
+                                                             out_idx, out_dist, w.flag_list, w.flag_count);
+        else
+            knn_warp_kernel<3><<<grid, kWarpQ * 32, 0, st>>>(query, source, ptr_q, ptr_s, num_clouds, k, w.tile_base,
+                                                             out_idx, out_dist, w.flag_list, w.flag_count);
         knn_exact_kernel<<<kSmCount, kKnnThreads, 0, st>>>(query, source, ptr_q, ptr_s, num_clouds, k, w.flag_list,
                                                            w.flag_count, out_idx, out_dist);
         GDL_CUDA_TRY(cudaGetLastError());
