@@ -352,33 +352,6 @@ constexpr int kWarpQ = 8;         // queries (warps) per CTA
 constexpr int kWarpChunk = 2048;  // sources staged per pass
 
 template <int NR>
-__device__ __forceinline__ void warp_list_insert(float (&ed)[NR], int (&ei)[NR], float dd, int ii, int lane) {
-    int pos = 0;
-#pragma unroll
-    for (int r = 0; r < NR; ++r) pos += __popc(__ballot_sync(0xffffffffu, ed[r] < dd));
-    float ud[NR], xd[NR];
-    int ui[NR], xi[NR];
-#pragma unroll
-    for (int r = 0; r < NR; ++r) {  // entry (lane + 32 r - 1), read before any entry changes
-        ud[r] = __shfl_up_sync(0xffffffffu, ed[r], 1);
-        ui[r] = __shfl_up_sync(0xffffffffu, ei[r], 1);
-        xd[r] = r > 0 ? __shfl_sync(0xffffffffu, ed[r > 0 ? r - 1 : 0], 31) : 0.0f;
-        xi[r] = r > 0 ? __shfl_sync(0xffffffffu, ei[r > 0 ? r - 1 : 0], 31) : 0;
-    }
-#pragma unroll
-    for (int r = 0; r < NR; ++r) {
-        const int i = lane + 32 * r;
-        if (i > pos) {
-            ed[r] = lane == 0 ? xd[r] : ud[r];
-            ei[r] = lane == 0 ? xi[r] : ui[r];
-        } else if (i == pos) {
-            ed[r] = dd;
-            ei[r] = ii;
-        }
-    }
-}
-
-template <int NR>
 __global__ void __launch_bounds__(kWarpQ * 32) knn_warp_kernel(
     const float *__restrict__ query, const float *__restrict__ source, const int64_t *__restrict__ ptr_q,
     const int64_t *__restrict__ ptr_s, int32_t B, int k, const int32_t *__restrict__ tile_base,

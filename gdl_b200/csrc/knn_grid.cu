@@ -17,25 +17,18 @@
 //
 // Query (one warp): shell s = 1 is the 3x3x3 block around the query's (clamped) cell; shell
 // s > 1 adds the cells at Chebyshev distance s. A cell column's z-run is one contiguous sorted
-// range. Candidates at or below the current (k_eff+1)-th distance T are appended to a shared
-// buffer; when it fills, a radix select finds T and the buffer keeps d <= T. After each shell,
-// the search stops once T (1 + 1e-5) < (b - delta)^2, b = the distance from the query to the
-// nearest face of the examined block that is not the grid's edge, delta = the coordinate slack of
-// cell assignment. The k_eff + 1 nearest are then sorted by a warp bitonic sort.
+// range. Candidates below the current (k_eff+1)-th distance T enter the warp's sorted list of the
+// k_eff + 1 nearest (one ballot/popc and one shuffle per insert). After each shell the search
+// stops once T (1 + 1e-5) < (b - delta)^2, b = the distance from the query to the nearest face of
+// the examined block that is not the grid's edge, delta = the coordinate slack of cell assignment.
 #include "knn_grid.cuh"
 
 namespace gdl {
 
 constexpr int kKgGridThreads = 1024;
 constexpr int kKgWarps = 8;
-constexpr int kKgBuf = 1024;
-constexpr int kKgBins = 256;
 constexpr int kKgMaxShell = 12;  // farther than this: the query goes to the exact replay
-
-struct KgWarpSmem {
-    float2 buf[kKgBuf];  // (distance, local source index bits)
-    int hist[kKgBins];
-};
+constexpr int kKgDepth = 4;      // candidate batches of 32 in flight per warp
 
 static __device__ __forceinline__ int kg_find(const int64_t *__restrict__ p, int B, int64_t j) {
     int lo = 0, hi = B - 1;
@@ -186,7 +179,10 @@ static __global__ void __launch_bounds__(kKgGridThreads) kg_grid_kernel(
         const float t = fmaxf(4.0f, 0.5f * (float)(ke + 1));
         KGrid gf = g;
         float h = g.h;
-        if (occ > t) {  // clustered: shrink the cells toward t points seen per point
+        // clustered clouds: shrink the cells toward t points seen per point -- for k >= 8, whose
+        // answers lie within a few points; for smaller k the density cell stays, so that queries
+        // off the sources' clusters still end their search in the first shells
+        if (occ > t && ke >= 8) {
             float eff[3], maxe = 0.0f;
             for (int a = 0; a < 3; ++a) maxe = fmaxf(maxe, (float)g.res[a] * g.h);
             for (int a = 0; a < 3; ++a) eff[a] = fmaxf((float)g.res[a] * g.h, 1e-3f * maxe);
@@ -245,111 +241,13 @@ static __global__ void kg_cells_kernel(const int64_t *__restrict__ lptr, int32_t
     if (j == c1 - 1 || skeys[j + 1] != key) tab[key].y = (int)(j - c0) + 1;
 }
 
-// rank-th smallest (1-based) of buf[0, m).x; the values are >= 0 or +inf, so their bit patterns
-// order like the values. Radix select, 8 bits a pass, histogram in shared memory.
-static __device__ float kg_kth(const float2 *buf, int m, int rank, int *hist, int lane) {
-    uint32_t prefix = 0, pmask = 0;
-    for (int shift = 24; shift >= 0; shift -= 8) {
-        for (int h = lane; h < kKgBins; h += 32) hist[h] = 0;
-        __syncwarp();
-        for (int i = lane; i < m; i += 32) {
-            const uint32_t u = __float_as_uint(buf[i].x);
-            if ((u & pmask) == prefix) atomicAdd(&hist[(u >> shift) & 255u], 1);
-        }
-        __syncwarp();
-        int v[kKgBins / 32], sum = 0;
-#pragma unroll
-        for (int i = 0; i < kKgBins / 32; ++i) {
-            v[i] = hist[lane * (kKgBins / 32) + i];
-            sum += v[i];
-        }
-        int pre = sum;
-        for (int o = 1; o < 32; o <<= 1) {
-            const int y = __shfl_up_sync(0xffffffffu, pre, o);
-            if (lane >= o) pre += y;
-        }
-        int run = pre - sum, found = -1, before = 0;
-#pragma unroll
-        for (int i = 0; i < kKgBins / 32; ++i) {
-            if (found < 0 && run + v[i] >= rank) {
-                found = lane * (kKgBins / 32) + i;
-                before = run;
-            }
-            run += v[i];
-        }
-        const unsigned have = __ballot_sync(0xffffffffu, found >= 0);
-        const int srcl = have ? __ffs(have) - 1 : 0;
-        const int digit = __shfl_sync(0xffffffffu, found, srcl);
-        rank -= __shfl_sync(0xffffffffu, before, srcl);
-        prefix |= (uint32_t)(digit & 255) << shift;
-        pmask |= 255u << shift;
-        __syncwarp();
-    }
-    return __uint_as_float(prefix);
-}
-
-// keep buf entries with distance <= v, in place (every lane reads before any lane writes)
-static __device__ int kg_compact(float2 *buf, int m, float v, int lane) {
-    const unsigned lt = (1u << lane) - 1u;
-    int w = 0;
-    for (int base = 0; base < m; base += 32) {
-        const int i = base + lane;
-        float2 e = make_float2(0.0f, 0.0f);
-        bool keep = false;
-        if (i < m) {
-            e = buf[i];
-            keep = e.x <= v;
-        }
-        __syncwarp();
-        const unsigned hb = __ballot_sync(0xffffffffu, keep);
-        if (keep) buf[w + __popc(hb & lt)] = e;
-        w += __popc(hb);
-        __syncwarp();
-    }
-    return w;
-}
-
-// ascending bitonic sort of 128 keys, element r * 32 + lane in a[r]
-static __device__ __forceinline__ void kg_sort128(uint64_t (&a)[4], int lane) {
-#pragma unroll
-    for (int size = 2; size <= 128; size <<= 1) {
-#pragma unroll
-        for (int stride = size >> 1; stride > 0; stride >>= 1) {
-            if (stride >= 32) {
-                const int rs = stride >> 5;
-#pragma unroll
-                for (int r = 0; r < 4; ++r) {
-                    const int pr = r ^ rs;
-                    if (pr > r) {
-                        const bool up = ((r * 32 + lane) & size) == 0;
-                        const uint64_t x = a[r], y = a[pr];
-                        const uint64_t mn = x < y ? x : y, mx = x < y ? y : x;
-                        a[r] = up ? mn : mx;
-                        a[pr] = up ? mx : mn;
-                    }
-                }
-            } else {
-#pragma unroll
-                for (int r = 0; r < 4; ++r) {
-                    const int e = r * 32 + lane;
-                    const uint64_t p = __shfl_xor_sync(0xffffffffu, a[r], stride);
-                    const bool up = (e & size) == 0, lower = (e & stride) == 0;
-                    a[r] = (lower == up) ? (a[r] < p ? a[r] : p) : (a[r] < p ? p : a[r]);
-                }
-            }
-        }
-    }
-}
-
+template <int NR>
 static __global__ void __launch_bounds__(kKgWarps * 32) kg_query_kernel(
     const float *__restrict__ query, const int64_t *__restrict__ ptr_q, int32_t B, const int64_t *__restrict__ ptr_s,
     const int64_t *__restrict__ lptr, const KGrid *__restrict__ grids, const float4 *__restrict__ pts,
     const int2 *__restrict__ cells, int k, const int32_t *__restrict__ invalid, int64_t *__restrict__ out_idx,
     float *__restrict__ out_dist, int32_t *__restrict__ flag_list, int32_t *__restrict__ flag_count) {
-    extern __shared__ __align__(16) unsigned char kg_smem[];
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    KgWarpSmem &W = reinterpret_cast<KgWarpSmem *>(kg_smem)[warp];
-    const unsigned lt = (1u << lane) - 1u;
     const int ke = k < 64 ? k : 64;
     const int64_t q0 = ptr_q[0], q1 = ptr_q[B], sbase = ptr_s[0];
     const int64_t nw = (int64_t)gridDim.x * kKgWarps;
@@ -374,8 +272,16 @@ static __global__ void __launch_bounds__(kKgWarps * 32) kg_query_kernel(
         const float qp[3] = {query[3 * q], query[3 * q + 1], query[3 * q + 2]};
         bool flag = g.ok != 1 || !(isfinite(qp[0]) && isfinite(qp[1]) && isfinite(qp[2]));
         const int K1 = (int)(ke + 1 < nb ? ke + 1 : nb);
-        int m = 0;
-        float T = kInf;
+        // the warp's sorted list of the K1 nearest so far; thr = its K1-th entry (+inf until full)
+        float ed[NR];
+        int ei[NR];
+#pragma unroll
+        for (int r = 0; r < NR; ++r) {
+            ed[r] = kInf;
+            ei[r] = -1;
+        }
+        float thr = kInf;
+        int cnt = 0;
         if (!flag) {
             int qc[3];
             for (int a = 0; a < 3; ++a) qc[a] = kg_cell(qp[a], g.mn[a], g.inv, g.res[a]);
@@ -387,9 +293,9 @@ static __global__ void __launch_bounds__(kKgWarps * 32) kg_query_kernel(
                     break;
                 }
                 const int side = 2 * s + 1, npairs = side * side;
-                for (int p0 = 0; p0 < npairs && !flag; p0 += 32) {
+                for (int p0 = 0; p0 < npairs; p0 += 32) {
                     const int p = p0 + lane;
-                    int ra0 = 0, re0 = 0, ra1 = 0, re1 = 0;  // two sorted ranges [ra, re)
+                    int ra0 = 0, re0 = 0, ra1 = 0, re1 = 0;  // two sorted ranges [ra, re) of the cloud
                     if (p < npairs) {
                         const int dx = p / side - s, dy = p % side - s;
                         const int cx = qc[0] + dx, cy = qc[1] + dy;
@@ -418,42 +324,46 @@ static __global__ void __launch_bounds__(kKgWarps * 32) kg_query_kernel(
                     // candidates of every non-empty range, 32 at a time
                     auto take = [&](int ra, int re) {
                         unsigned busy = __ballot_sync(0xffffffffu, re > ra);
-                        while (busy && !flag) {
+                        while (busy) {
                             const int l = __ffs(busy) - 1;
                             busy &= busy - 1;
                             const int a = __shfl_sync(0xffffffffu, ra, l), e = __shfl_sync(0xffffffffu, re, l);
-                            for (int j0 = a; j0 < e; j0 += 32) {
+                            for (int jb = a; jb < e; jb += 32 * kKgDepth) {
+                              float4 sp[kKgDepth];  // loads of kKgDepth batches issued together
+#pragma unroll
+                              for (int u = 0; u < kKgDepth; ++u)
+                                  if (jb + 32 * u + lane < e) sp[u] = pts[s0 + jb + 32 * u + lane];
+#pragma unroll
+                              for (int u = 0; u < kKgDepth; ++u) {
+                                const int j0 = jb + 32 * u;
+                                if (j0 >= e) break;  // uniform over the warp
                                 const int j = j0 + lane;
-                                bool acc = false;
-                                float d = 0.0f;
+                                float d = kInf;
                                 int o = 0;
                                 if (j < e) {
-                                    const float4 sp = pts[s0 + j];
-                                    o = __float_as_int(sp.w);
-                                    d = dist2(qp[0], qp[1], qp[2], sp.x, sp.y, sp.z);
-                                    acc = d <= T;
+                                    o = __float_as_int(sp[u].w);
+                                    d = dist2(qp[0], qp[1], qp[2], sp[u].x, sp[u].y, sp[u].z);
                                 }
-                                const unsigned hb = __ballot_sync(0xffffffffu, acc);
-                                if (acc) W.buf[m + __popc(hb & lt)] = make_float2(d, __int_as_float(o));
-                                m += __popc(hb);
-                                if (m > kKgBuf - 32) {  // keep the K1 nearest (and their ties)
-                                    __syncwarp();
-                                    T = kg_kth(W.buf, m, K1, W.hist, lane);
-                                    m = kg_compact(W.buf, m, T, lane);
-                                    if (m > kKgBuf - 64) {  // a mass of equal distances: give up
-                                        flag = true;
-                                        break;
-                                    }
+                                unsigned acc = __ballot_sync(0xffffffffu, d < thr);
+                                while (acc) {
+                                    const int l2 = __ffs(acc) - 1;
+                                    acc &= acc - 1;
+                                    const float dd = __shfl_sync(0xffffffffu, d, l2);
+                                    const int oo = __shfl_sync(0xffffffffu, o, l2);
+                                    if (!(dd < thr)) continue;  // tightened since the ballot (uniform)
+                                    warp_list_insert<NR>(ed, ei, dd, oo, lane);
+                                    ++cnt;
+#pragma unroll
+                                    for (int r = 0; r < NR; ++r)
+                                        if ((K1 - 1) / 32 == r) thr = __shfl_sync(0xffffffffu, ed[r], (K1 - 1) & 31);
                                 }
+                              }
                             }
                         }
                     };
                     take(ra0, re0);
-                    if (!flag) take(ra1, re1);
+                    take(ra1, re1);
                 }
-                if (flag) break;
-                __syncwarp();
-                if (m >= K1) T = kg_kth(W.buf, m, K1, W.hist, lane);
                 // pruning bound: distance to the nearest face of the examined block that is not
                 // the grid's edge (points lie inside the grid, the edge cells are open-ended)
                 float bound = kInf;
@@ -470,59 +380,44 @@ static __global__ void __launch_bounds__(kKgWarps * 32) kg_query_kernel(
                 }
                 if (covered) {
                     done = true;
-                } else if (m >= K1) {
+                } else if (cnt >= K1) {
                     const float bb = bound - g.delta;
-                    done = bb > 0.0f && T * 1.00001f < bb * bb;
+                    done = bb > 0.0f && thr * 1.00001f < bb * bb;
                 }
             }
         }
-        if (!flag) {
-            // the K1 nearest: entries at or below the K1-th distance, sorted
-            __syncwarp();
-            const float v = m > K1 ? kg_kth(W.buf, m, K1, W.hist, lane) : kInf;
-            m = kg_compact(W.buf, m, v, lane);
-            if (m > 128) flag = true;  // more than 128 at or below the K1-th: equal distances
-        }
-        if (!flag) {
-            uint64_t key[4];
-#pragma unroll
-            for (int r = 0; r < 4; ++r) {
-                const int i = r * 32 + lane;
-                key[r] = ~0ull;
-                if (i < m) {
-                    const float2 e = W.buf[i];
-                    key[r] = ((uint64_t)__float_as_uint(e.x) << 32) | (uint32_t)__float_as_int(e.y);
-                }
-            }
-            kg_sort128(key, lane);
-            // equal distances among the first K1 -> the reference heap decides their order
+        const int have = cnt < K1 ? cnt : K1;
+        // every finite distance enters a list that is not full: a short list means overflowed distances
+        if (!flag && have < K1) flag = true;
+        if (!flag) {  // equal distances among the K1 nearest: the reference heap decides their order
             bool tie = false;
 #pragma unroll
-            for (int r = 0; r < 4; ++r) {
-                const uint64_t up = __shfl_up_sync(0xffffffffu, key[r], 1);
-                const uint64_t prev_last = r > 0 ? __shfl_sync(0xffffffffu, key[r - 1], 31) : 0ull;
-                const int e = r * 32 + lane;
-                const uint64_t prev = lane > 0 ? up : prev_last;
-                if (e >= 1 && e < K1 && (prev >> 32) == (key[r] >> 32)) tie = true;
+            for (int r = 0; r < NR; ++r) {
+                const float up = __shfl_up_sync(0xffffffffu, ed[r], 1);
+                const float cross = r > 0 ? __shfl_sync(0xffffffffu, ed[r > 0 ? r - 1 : 0], 31) : 0.0f;
+                const int i = lane + 32 * r;
+                const float prev = lane > 0 ? up : cross;
+                if (i >= 1 && i < K1 && prev == ed[r]) tie = true;
             }
             flag = __any_sync(0xffffffffu, tie);
-            if (!flag) {
-                const int valid = K1 < ke ? K1 : ke;
+        }
+        if (!flag) {
+            const int nv = K1 < ke ? K1 : ke;
 #pragma unroll
-                for (int r = 0; r < 4; ++r) {
-                    const int e = r * 32 + lane;
-                    if (e < valid) {
-                        oi[e] = sbase + (int64_t)(uint32_t)key[r];
-                        od[e] = __uint_as_float((uint32_t)(key[r] >> 32));
-                    }
-                }
-                for (int j = valid + lane; j < k; j += 32) {
-                    oi[j] = -1;
-                    od[j] = 1e30f;
+            for (int r = 0; r < NR; ++r) {
+                const int i = lane + 32 * r;
+                if (i < k) {
+                    oi[i] = i < nv ? sbase + (int64_t)ei[r] : -1;
+                    od[i] = i < nv ? ed[r] : 1e30f;
                 }
             }
+            for (int i = 32 * NR + lane; i < k; i += 32) {
+                oi[i] = -1;
+                od[i] = 1e30f;
+            }
+        } else if (lane == 0) {
+            flag_list[atomicAdd(flag_count, 1)] = (int32_t)q;
         }
-        if (flag && lane == 0) flag_list[atomicAdd(flag_count, 1)] = (int32_t)q;
         __syncwarp();
     }
 }
@@ -569,13 +464,18 @@ cudaError_t knn_grid_run(const float *query, const float *source, const int64_t 
     e = cudaMemsetAsync(w.cells, 0, sizeof(int2) * kKgCellBudget * nmax, st);
     if (e != cudaSuccess) return e;
     kg_cells_kernel<<<g256, 256, 0, st>>>(w.lptr, B, w.grid, w.sorted_keys, w.cells);
-    const size_t smem = sizeof(KgWarpSmem) * kKgWarps;
-    e = cudaFuncSetAttribute(kg_query_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    if (e != cudaSuccess) return e;
     const int64_t blocks = (n_q + kKgWarps - 1) / kKgWarps;
     const unsigned grid = (unsigned)(blocks < 24 * kSmCount ? (blocks > 0 ? blocks : 1) : 24 * kSmCount);
-    kg_query_kernel<<<grid, kKgWarps * 32, smem, st>>>(query, ptr_q, B, ptr_s, w.lptr, w.grid, w.pts, w.cells, k,
-                                                        w.invalid, out_idx, out_dist, flag_list, flag_count);
+    const int K1 = (k < 64 ? k : 64) + 1;
+    if (K1 <= 32)
+        kg_query_kernel<1><<<grid, kKgWarps * 32, 0, st>>>(query, ptr_q, B, ptr_s, w.lptr, w.grid, w.pts, w.cells, k,
+                                                          w.invalid, out_idx, out_dist, flag_list, flag_count);
+    else if (K1 <= 64)
+        kg_query_kernel<2><<<grid, kKgWarps * 32, 0, st>>>(query, ptr_q, B, ptr_s, w.lptr, w.grid, w.pts, w.cells, k,
+                                                          w.invalid, out_idx, out_dist, flag_list, flag_count);
+    else
+        kg_query_kernel<3><<<grid, kKgWarps * 32, 0, st>>>(query, ptr_q, B, ptr_s, w.lptr, w.grid, w.pts, w.cells, k,
+                                                          w.invalid, out_idx, out_dist, flag_list, flag_count);
     return cudaGetLastError();
 }
 

@@ -7,11 +7,41 @@
 namespace gdl {
 
 // The grid path serves calls whose largest cloud has at least this many sources. Below it the
-// brute-force scan wins: it is fp32-bound at ~3 T pairs/s, while a uniform grid cannot fit both
-// clustered sources and queries that sit away from them (measured on configurations 3 and 4:
-// 1.28 ms vs 1.2 ms and 37.9 ms vs 4.8 ms), and the quadratic cost only bites for larger clouds.
+// brute-force scan wins: it is fp32-bound at ~3.6 T pairs/s, while one uniform cell size cannot fit
+// both clustered sources and queries that sit away from them (measured on configurations 3 and 4:
+// 1.44 ms vs 1.2 ms and 5.5 ms vs 4.8 ms), and the quadratic cost only bites for larger clouds.
 constexpr int64_t kKgMinSources = 32768;
 constexpr int kKgCellBudget = 16;  // grid cells per source point at most (dense cell table)
+
+// Warp-distributed sorted list of the best (distance, index) pairs: entry lane + 32 r lives in
+// register set r of every lane, ascending, +inf padded. Inserts (dd, ii) after the entries smaller
+// than dd: the position is one ballot/popc per set, the shift one shuffle. All lanes call it.
+template <int NR>
+__device__ __forceinline__ void warp_list_insert(float (&ed)[NR], int (&ei)[NR], float dd, int ii, int lane) {
+    int pos = 0;
+#pragma unroll
+    for (int r = 0; r < NR; ++r) pos += __popc(__ballot_sync(0xffffffffu, ed[r] < dd));
+    float ud[NR], xd[NR];
+    int ui[NR], xi[NR];
+#pragma unroll
+    for (int r = 0; r < NR; ++r) {  // entry (lane + 32 r - 1), read before any entry changes
+        ud[r] = __shfl_up_sync(0xffffffffu, ed[r], 1);
+        ui[r] = __shfl_up_sync(0xffffffffu, ei[r], 1);
+        xd[r] = r > 0 ? __shfl_sync(0xffffffffu, ed[r > 0 ? r - 1 : 0], 31) : 0.0f;
+        xi[r] = r > 0 ? __shfl_sync(0xffffffffu, ei[r > 0 ? r - 1 : 0], 31) : 0;
+    }
+#pragma unroll
+    for (int r = 0; r < NR; ++r) {
+        const int i = lane + 32 * r;
+        if (i > pos) {
+            ed[r] = lane == 0 ? xd[r] : ud[r];
+            ei[r] = lane == 0 ? xi[r] : ui[r];
+        } else if (i == pos) {
+            ed[r] = dd;
+            ei[r] = ii;
+        }
+    }
+}
 
 struct KGrid {
     float mn[3];
