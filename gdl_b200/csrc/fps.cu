@@ -193,10 +193,28 @@ __global__ void __launch_bounds__(THREADS) fps_cta_kernel(const float *__restric
 }
 
 // ------------------------------------------------------------------ cluster per cloud
-struct Rec {  // one CTA's best point
+// Per pick, warp 0 of every CTA sends its winner record to every CTA of the cluster with
+// st.async stores into distributed shared memory, each completing 24 bytes of a transaction on
+// the receiving CTA's mbarrier; a CTA then waits on its own mbarrier only (no cluster-wide
+// barrier per pick: 1.18 vs 1.63 us per pick at 16 CTAs). Two record buffers and two mbarriers
+// alternate between picks: a CTA's record for pick k+2 can only be sent after the CTA received
+// this CTA's record for pick k+1, which is sent after this CTA finished reading pick k's.
+// Every wait is bounded; a CTA that gives up stops, and rank 0 then marks the cloud's remaining
+// picks with -2 (never observed; a broken cluster exchange would show up there, not as a hang).
+struct __align__(32) Rec {  // one CTA's best point
     unsigned long long key;
     float x, y, z, pad;
 };
+
+__device__ __forceinline__ uint32_t smem_u32(const void *p) { return (uint32_t)__cvta_generic_to_shared(p); }
+
+__device__ __forceinline__ uint32_t mapa_u32(uint32_t a, int rank) {
+    uint32_t r;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(rank));
+    return r;
+}
+
+constexpr int kClusterWaitLimit = 1 << 20;  // mbarrier polls before a CTA gives up
 
 template <int THREADS, int P>
 __global__ void __launch_bounds__(THREADS) fps_cluster_kernel(const float *__restrict__ pos,
@@ -208,6 +226,7 @@ __global__ void __launch_bounds__(THREADS) fps_cluster_kernel(const float *__res
     extern __shared__ float4 sxyz[];  // this CTA's THREADS * P points
     __shared__ unsigned long long slots[2][NW];
     __shared__ Rec recs[2][kMaxCluster];
+    __shared__ __align__(8) unsigned long long mbar[2];
     __shared__ int64_t red[NW];
     cg::cluster_group cluster = cg::this_cluster();
     const int cs = (int)cluster.num_blocks();
@@ -229,29 +248,57 @@ __global__ void __launch_bounds__(THREADS) fps_cluster_kernel(const float *__res
         sz = pos[3 * start + 2];
         if (rank == 0 && threadIdx.x == 0) emit(out, out_pos, o0, start, 0, sx, sy, sz);
     }
+    if (threadIdx.x == 0) {
+        for (int p = 0; p < 2; ++p) asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(smem_u32(&mbar[p])));
+        asm volatile("fence.mbarrier_init.release.cluster;");
+    }
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    cluster.sync();  // every CTA resident and initialised before remote writes
-    for (int64_t k = 1; k < actual; ++k) {
+    uint32_t phase[2] = {0u, 0u};
+    cluster.sync();  // every CTA resident, its barriers initialised, before any remote store
+    int64_t k = 1;
+    for (; k < actual; ++k) {
         const uint64_t wk = warp_max_key(pr.step(sx, sy, sz));
         const int par = (int)(k & 1);
         if (lane == 0) slots[par][warp] = wk;
         __syncthreads();
-        if (warp == 0) {  // this CTA's winner, published into every CTA's record slot [rank]
+        if (warp == 0) {  // this CTA's winner, sent into every CTA's record slot [rank]
             const unsigned long long key = warp_max_key(lane < NW ? slots[par][lane] : 0ull);
-            Rec r;
-            r.key = key;
+            float rx = 0.0f, ry = 0.0f, rz = 0.0f;
             if (key != 0ull) {
                 const float4 c = sxyz[fps_index(~(uint32_t)key, tie) - base];
-                r.x = c.x;
-                r.y = c.y;
-                r.z = c.z;
-            } else {
-                r.x = r.y = r.z = 0.0f;
+                rx = c.x;
+                ry = c.y;
+                rz = c.z;
             }
-            r.pad = 0.0f;
-            if (lane < cs) *cluster.map_shared_rank(&recs[par][rank], lane) = r;
+            if (lane == 0)  // this CTA expects one 24-byte record from each CTA for this pick
+                asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(&mbar[par])),
+                             "r"(cs * 24)
+                             : "memory");
+            if (lane < cs) {
+                const uint32_t dst = mapa_u32(smem_u32(&recs[par][rank]), lane);
+                const uint32_t bar = mapa_u32(smem_u32(&mbar[par]), lane);
+                asm volatile(
+                    "st.async.shared::cluster.mbarrier::complete_tx::bytes.v4.b32 [%0], {%1, %2, %3, %4}, [%5];" ::"r"(
+                        dst),
+                    "r"((uint32_t)key), "r"((uint32_t)(key >> 32)), "r"(__float_as_uint(rx)), "r"(__float_as_uint(ry)),
+                    "r"(bar)
+                    : "memory");
+                asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.v2.b32 [%0], {%1, %2}, [%3];" ::"r"(
+                                 dst + 16),
+                             "r"(__float_as_uint(rz)), "r"(0u), "r"(bar)
+                             : "memory");
+            }
         }
-        cluster.sync();
+        uint32_t done = 0;
+        for (int it = 0; it < kClusterWaitLimit && !done; ++it)
+            asm volatile(
+                "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\tselp.u32 %0, 1, 0, "
+                "p;\n\t}"
+                : "=r"(done)
+                : "r"(smem_u32(&mbar[par])), "r"(phase[par])
+                : "memory");
+        phase[par] ^= 1u;
+        if (!__syncthreads_and(done)) break;  // the whole CTA stops if any thread gave up
         const unsigned long long mine = lane < cs ? recs[par][lane].key : 0ull;
         const uint64_t best = warp_max_key(mine);
         const int src = __ffs(__ballot_sync(0xffffffffu, lane < cs && mine == best)) - 1;
@@ -261,6 +308,8 @@ __global__ void __launch_bounds__(THREADS) fps_cluster_kernel(const float *__res
         sz = w.z;
         if (rank == 0 && threadIdx.x == 0) emit(out, out_pos, o0 + k, start, fps_index(~(uint32_t)best, tie), sx, sy, sz);
     }
+    if (k < actual && rank == 0)  // a wait gave up: mark the picks this cloud did not make
+        for (int64_t j = k + threadIdx.x; j < actual; j += THREADS) out[o0 + j] = -2;
     cluster.sync();  // no CTA leaves while a peer may still write into it
 }
 
