@@ -16,6 +16,9 @@ inputs with the shapes of the reference's use cases; see gdl_b200/synthetic.py):
   c5            8 clouds x 131072 LiDAR points: FPS -> 16384, radius graph (r = 1 m, 64),
                 segment sum of 64-channel features.
   c5g           (auxiliary) c5's clouds: radius graph r = 1 m, 64 over all points, segment sum.
+  c5s           (auxiliary) c5's clouds: SpatialGraph.build -- radius graph r = 1 m, 64 over all
+                points with each edge's distance, direction and l <= 2 spherical harmonics, the
+                CSR fields and the per-cloud average degree.
 
 value : input points per second with inputs resident in HBM, timed with CUDA events on the
         launching stream, L2 flushed (256 MiB write) between steps, max over ranks.
@@ -29,6 +32,7 @@ in oracle/, all host threads) on the same configuration.
 from __future__ import annotations
 
 import argparse
+import ctypes
 import json
 import os
 import statistics
@@ -46,6 +50,7 @@ sys.path.insert(0, str(ROOT))
 from gdl_b200 import _native as nat  # noqa: E402
 from gdl_b200 import csrc, synthetic  # noqa: E402
 from gdl_b200 import functional as F  # noqa: E402
+from gdl_b200.spatial_graph import SpatialGraph  # noqa: E402
 
 L2_FLUSH_BYTES = 256 << 20
 
@@ -730,7 +735,83 @@ class C5G(C5):
                          rp[1:].astype(np.int32), self.N, "sum")
 
 
-CONFIGS = {"c1": C1, "c2": C2, "c3": C3, "c4": C4, "c5": C5, "c5g": C5G}
+class C5S(C5G):
+    """Auxiliary graph-geometry workload (the reference's SpatialGraph.build, nn/modules/
+    spatial_graph.py:88-167, on config 5's clouds): radius graph r = 1 m, 64 neighbours over all
+    131072 points of each cloud with every edge's distance, direction and l <= 2 spherical
+    harmonics written by the emission kernel, then the sort-free CSR fields and each cloud's
+    average degree."""
+    name = "c5s"
+    metric = ("points/sec (SpatialGraph.build: radius graph r=1 k=64 + edge dist/direction/spherical "
+              "harmonics l<=2 + CSR + avg degree), config 5 clouds")
+    launches_per_step = 25 + 1
+    MAX_L = 2
+
+    def __init__(self, dev, seed):
+        super().__init__(dev, seed)
+        f = dict(dtype=torch.float32, device=dev)
+        self.dst = torch.zeros(self.cap, dtype=torch.int64, device=dev)
+        self.dist = torch.empty(self.cap, **f)
+        self.direction = torch.empty(self.cap, 3, **f)
+        self.sph = torch.empty(self.cap, (self.MAX_L + 1) ** 2, **f)
+        self.geom = nat.EdgeGeometry(None, self.dist.data_ptr(), self.direction.data_ptr(), self.sph.data_ptr(),
+                                     self.MAX_L)
+        i32 = dict(dtype=torch.int32, device=dev)
+        self.col_sorted, self.perm = torch.empty(self.cap, **i32), torch.empty(self.cap, **i32)
+        self.node_start, self.node_end = torch.empty(self.nc, **i32), torch.empty(self.nc, **i32)
+        self.avg = torch.empty(self.nc, **f)
+        self.batch_h = torch.arange(self.B).repeat_interleave(self.N)
+        self.feat_h = torch.empty(0)  # no features in this workload
+
+    def stage_radius_geometry(self):
+        nat.check(self.L.gdl_radius_graph_geometry(self.pos.data_ptr(), self.ptr.data_ptr(), self.B, self.nc, self.N,
+                                                   self.R, self.NN, 0, None, self.row_ptr.data_ptr(),
+                                                   self.src.data_ptr(), self.dst.data_ptr(),
+                                                   self.row_ptr32.data_ptr(), self.src32.data_ptr(),
+                                                   ctypes.byref(self.geom), self.ws_rad.data_ptr(),
+                                                   self.ws_rad.numel(), self._s()), "radius geometry")
+
+    def stage_finish(self):
+        nat.check(self.L.gdl_radius_csr_finish(self.row_ptr.data_ptr(), self.dst.data_ptr(), self.nc, self.cap,
+                                               self.ptr.data_ptr(), self.B, self.col_sorted.data_ptr(),
+                                               self.perm.data_ptr(), self.node_start.data_ptr(),
+                                               self.node_end.data_ptr(), self.avg.data_ptr(), self._s()),
+                  "csr finish")
+
+    def stage_list(self):
+        return [("radius_geometry", self.stage_radius_geometry), ("csr_finish", self.stage_finish)]
+
+    def stage_bytes(self, E):
+        nc = self.nc
+        # points in; per edge src/dst i64 + src32 + dist + direction + 9 harmonics out; row pointers
+        geo = 12 * nc + E * (8 + 8 + 4 + 4 + 12 + 4 * (self.MAX_L + 1) ** 2) + 12 * (nc + 1)
+        # row_ptr + dst in; col_sorted + perm out; node_start/end + avg degree out
+        return {"radius_geometry": geo, "csr_finish": 8 * (nc + 1) + 8 * E + 8 * E + 12 * nc}
+
+    def e2e_step(self):
+        pos = self.pos_h.to(self.dev, non_blocking=True)
+        batch = self.batch_h.to(self.dev, non_blocking=True)
+        g = SpatialGraph.build(pos, self.R, max_num_neighbors=self.NN, batch=batch, max_l=self.MAX_L,
+                               num_batch_elements=self.B)
+        host = g.avg_degree.to("cpu", non_blocking=True)
+        torch.cuda.current_stream(self.dev).synchronize()
+        return host
+
+    e2e_h2d = property(lambda self: self.pos_h.numel() * 4 + self.batch_h.numel() * 8)
+    e2e_d2h = property(lambda self: self.nc * 4 + 8 * (self.B + 1) + 8)  # avg degree + cloud sizes + edge count
+    cpu_fraction = 1 / 8
+    cpu_sample = "radius graph + edge geometry + CSR + avg degree of 1 of 8 clouds per sample, scaled x8"
+
+    def cpu_step(self, O):
+        pos = self.pos_h.numpy()[:self.N]
+        rp, src = O.radius_graph(pos, np.array([0, self.N]), self.R, self.NN, dist=O.DIST_CUDA)
+        row, col = O.csr_to_coo(rp, src)
+        O.edge_geometry(pos, row, col, max_l=self.MAX_L)
+        _, _, ns, ne = O.sort_and_build_csr(col, self.N)
+        O.cloud_avg_degree(ns, ne)
+
+
+CONFIGS = {"c1": C1, "c2": C2, "c3": C3, "c4": C4, "c5": C5, "c5g": C5G, "c5s": C5S}
 
 
 

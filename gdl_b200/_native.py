@@ -20,6 +20,14 @@ _P = ctypes.c_void_p
 _I32 = ctypes.c_int32
 _I64 = ctypes.c_int64
 _SZ = ctypes.c_size_t
+
+
+class EdgeGeometry(ctypes.Structure):
+    """gdl_edge_geometry: nullable device pointers of the per-edge outputs."""
+    _fields_ = [("diff", _P), ("dist", _P), ("direction", _P), ("sph", _P), ("sph_max_l", _I32)]
+
+
+_PG = ctypes.POINTER(EdgeGeometry)
 PROTOTYPES = {
     "gdl_version": (ctypes.c_int, []),
     "gdl_status_string": (ctypes.c_char_p, [ctypes.c_int]),
@@ -32,6 +40,13 @@ PROTOTYPES = {
     "gdl_radius_graph": (ctypes.c_int,
                          [_P, _P, _I32, _I64, _I64, ctypes.c_double, _I32, _I32, _P, _P, _P, _P, _P, _P, _P, _SZ,
                           _P]),
+    "gdl_radius_graph_geometry": (ctypes.c_int,
+                                  [_P, _P, _I32, _I64, _I64, ctypes.c_double, _I32, _I32, _P, _P, _P, _P, _P, _P,
+                                   _PG, _P, _SZ, _P]),
+    "gdl_edge_geometry_coo": (ctypes.c_int, [_P, _I64, _P, _P, _I64, _PG, _P]),
+    "gdl_cloud_avg_degree_workspace_size": (_SZ, [_I32]),
+    "gdl_cloud_avg_degree": (ctypes.c_int, [_P, _P, _I64, _P, _P, _I32, _P, _P, _SZ, _P]),
+    "gdl_radius_csr_finish": (ctypes.c_int, [_P, _P, _I64, _I64, _P, _I32, _P, _P, _P, _P, _P, _P]),
     "gdl_sort_and_build_csr_workspace_size": (_SZ, [_I64, _I64]),
     "gdl_sort_and_build_csr": (ctypes.c_int, [_P, _I64, _I64, _P, _P, _P, _P, _P, _SZ, _P]),
     "gdl_segment_reduce_workspace_size": (_SZ, [_I64, _I64]),

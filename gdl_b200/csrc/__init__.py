@@ -16,6 +16,7 @@ libgdl_b200.so on the current CUDA stream. Differences, all deliberate:
 
 from __future__ import annotations
 
+import ctypes
 from typing import Optional, Tuple
 
 import numpy as np
@@ -133,6 +134,38 @@ def knn_self_cuda(points: torch.Tensor, ptr: torch.Tensor, k: int) -> Tuple[torc
 
 
 # --------------------------------------------------------------------------- radius graph
+def _radius_call(x, r, ptr, max_num_neighbors, loop, mask, with_dst, max_cloud_points, int32_csr, geom):
+    dev = nat.require_cuda(x, what="radius_graph")
+    x = x.contiguous().float()
+    N = x.shape[0]
+    if max_cloud_points is None:
+        max_cloud_points = int((ptr[1:] - ptr[:-1]).max()) if (not ptr.is_cuda and ptr.numel() > 1) else 0
+    ptr = ptr.to(device=dev, dtype=torch.int64).contiguous()
+    B = ptr.numel() - 1
+    cap_k = 16 if max_num_neighbors <= 16 else 32 if max_num_neighbors <= 32 else 64
+    cap = max(N * cap_k, 1)
+    row_ptr = torch.empty(N + 1, dtype=torch.int64, device=dev)
+    src = torch.empty(cap, dtype=torch.int64, device=dev)
+    dst = torch.empty_like(src) if with_dst else None
+    rp32 = torch.empty(N + 1, dtype=torch.int32, device=dev) if int32_csr else None
+    src32 = torch.empty(cap, dtype=torch.int32, device=dev) if int32_csr else None
+    m = None
+    if mask is not None and mask.numel() > 0:
+        m = mask.to(device=dev).contiguous()
+        m = m.view(torch.uint8) if m.dtype == torch.bool else m.to(torch.uint8)
+    L = nat.load()
+    ws = nat.workspace(L.gdl_radius_graph_workspace_size(N, B, int(max_num_neighbors)), dev)
+    args = (x.data_ptr() if N else None, ptr.data_ptr(), B, N, int(max_cloud_points), float(r), int(max_num_neighbors),
+            int(bool(loop)), nat.ptr(m), row_ptr.data_ptr(), src.data_ptr(), nat.ptr(dst), nat.ptr(rp32),
+            nat.ptr(src32))
+    if geom is None:
+        nat.check(L.gdl_radius_graph(*args, ws.data_ptr(), ws.numel(), nat.stream(dev)), "gdl_radius_graph")
+    else:
+        nat.check(L.gdl_radius_graph_geometry(*args, geom(cap, dev), ws.data_ptr(), ws.numel(), nat.stream(dev)),
+                  "gdl_radius_graph_geometry")
+    return row_ptr, src, dst, rp32, src32, ptr
+
+
 def radius_graph_csr(x: torch.Tensor, r: float, ptr: torch.Tensor, *, max_num_neighbors: int = 32,
                      loop: bool = False, mask: Optional[torch.Tensor] = None, with_dst: bool = True,
                      max_cloud_points: Optional[int] = None, int32_csr: bool = False):
@@ -145,31 +178,110 @@ def radius_graph_csr(x: torch.Tensor, r: float, ptr: torch.Tensor, *, max_num_ne
     4096 points use the fused one-CTA-per-cloud kernels. ``int32_csr`` appends
     (row_ptr32 [N+1], src32 [cap]) int32 copies, the layout segment_reduce_cuda consumes.
     """
-    dev = nat.require_cuda(x, what="radius_graph")
-    x = x.contiguous().float()
-    N = x.shape[0]
-    if max_cloud_points is None:
-        max_cloud_points = int((ptr[1:] - ptr[:-1]).max()) if (not ptr.is_cuda and ptr.numel() > 1) else 0
-    ptr = ptr.to(device=dev, dtype=torch.int64).contiguous()
-    B = ptr.numel() - 1
-    cap_k = 16 if max_num_neighbors <= 16 else 32 if max_num_neighbors <= 32 else 64
-    row_ptr = torch.empty(N + 1, dtype=torch.int64, device=dev)
-    src = torch.empty(max(N * cap_k, 1), dtype=torch.int64, device=dev)
-    dst = torch.empty_like(src) if with_dst else None
-    rp32 = torch.empty(N + 1, dtype=torch.int32, device=dev) if int32_csr else None
-    src32 = torch.empty(src.numel(), dtype=torch.int32, device=dev) if int32_csr else None
-    m = None
-    if mask is not None and mask.numel() > 0:
-        m = mask.to(device=dev).contiguous()
-        m = m.view(torch.uint8) if m.dtype == torch.bool else m.to(torch.uint8)
-    L = nat.load()
-    ws = nat.workspace(L.gdl_radius_graph_workspace_size(N, B, int(max_num_neighbors)), dev)
-    nat.check(L.gdl_radius_graph(x.data_ptr() if N else None, ptr.data_ptr(), B, N, int(max_cloud_points), float(r),
-                                 int(max_num_neighbors),
-                                 int(bool(loop)), nat.ptr(m), row_ptr.data_ptr(), src.data_ptr(), nat.ptr(dst),
-                                 nat.ptr(rp32), nat.ptr(src32), ws.data_ptr(), ws.numel(), nat.stream(dev)),
-              "gdl_radius_graph")
+    row_ptr, src, dst, rp32, src32, _ = _radius_call(x, r, ptr, max_num_neighbors, loop, mask, with_dst,
+                                                     max_cloud_points, int32_csr, None)
     return (row_ptr, src, dst, rp32, src32) if int32_csr else (row_ptr, src, dst)
+
+
+class _GeomOut:
+    """Per-edge output buffers of the geometry entry points (gdl_edge_geometry)."""
+
+    def __init__(self, max_l: Optional[int], with_diff: bool, with_dist: bool = True, with_dir: bool = True):
+        if max_l is not None and max_l not in (0, 1, 2):
+            raise ValueError(f"max_l must be 0, 1 or 2, got {max_l}")
+        self.max_l, self.with_diff, self.with_dist, self.with_dir = max_l, with_diff, with_dist, with_dir
+        self.diff = self.dist = self.direction = self.sph = None
+        self._struct = None
+
+    def __call__(self, cap: int, dev):
+        f = dict(dtype=torch.float32, device=dev)
+        self.diff = torch.empty(cap, 3, **f) if self.with_diff else None
+        self.dist = torch.empty(cap, **f) if self.with_dist else None
+        self.direction = torch.empty(cap, 3, **f) if self.with_dir else None
+        self.sph = torch.empty(cap, (self.max_l + 1) ** 2, **f) if self.max_l is not None else None
+        self._struct = nat.EdgeGeometry(nat.ptr(self.diff), nat.ptr(self.dist), nat.ptr(self.direction),
+                                        nat.ptr(self.sph), int(self.max_l or 0))
+        return ctypes.byref(self._struct)
+
+
+def radius_graph_geometry_csr(x: torch.Tensor, r: float, ptr: torch.Tensor, *, max_num_neighbors: int = 32,
+                              loop: bool = False, mask: Optional[torch.Tensor] = None, max_l: Optional[int] = 2,
+                              with_diff: bool = False, max_cloud_points: Optional[int] = None) -> dict:
+    """radius_graph_csr plus each edge's geometry, written by the kernel that emits the edge.
+
+    Returns a dict of device tensors, edge slots [0, row_ptr[N]) valid: ``row_ptr`` [N+1],
+    ``src``/``dst`` [cap] int64, ``row_ptr32`` [N+1] / ``src32`` [cap] int32, ``dist`` [cap],
+    ``direction`` [cap, 3], ``sph`` [cap, (max_l+1)^2] (None when max_l is None), ``diff``
+    [cap, 3] (None unless with_diff), and ``ptr`` (int64 on the device). Values follow
+    compute_edge_vectors (x[dst] - x[src]) and spherical_harmonics(normalize=False) of the
+    reference (functional/radius_graph.py:338-358, kernels/triton_sph_harm.py:200-240)."""
+    g = _GeomOut(max_l, with_diff)
+    row_ptr, src, dst, rp32, src32, ptr_d = _radius_call(x, r, ptr, max_num_neighbors, loop, mask, True,
+                                                         max_cloud_points, True, g)
+    return dict(row_ptr=row_ptr, src=src, dst=dst, row_ptr32=rp32, src32=src32, dist=g.dist,
+                direction=g.direction, sph=g.sph, diff=g.diff, ptr=ptr_d)
+
+
+def radius_csr_finish(row_ptr: torch.Tensor, dst: torch.Tensor, N: int, *, ptr: Optional[torch.Tensor] = None,
+                      avg_degree: bool = True):
+    """SpatialGraph's CSR fields of a destination-grouped radius graph without a sort:
+    (col_sorted [cap] i32, perm [cap] i32, node_start [N] i32, node_end [N] i32, avg_degree [N]
+    f32 or None); the first row_ptr[N] slots of col_sorted / perm are valid. ``ptr`` (device
+    int64) gives the clouds of the average degree, None one cloud."""
+    dev = nat.require_cuda(row_ptr, dst, what="radius_csr_finish")
+    cap = dst.numel()
+    i32 = dict(dtype=torch.int32, device=dev)
+    cs, pm = torch.empty(cap, **i32), torch.empty(cap, **i32)
+    ns, ne = torch.empty(N, **i32), torch.empty(N, **i32)
+    avg = torch.empty(N, dtype=torch.float32, device=dev) if avg_degree else None
+    B = 0 if ptr is None else ptr.numel() - 1
+    L = nat.load()
+    nat.check(L.gdl_radius_csr_finish(row_ptr.data_ptr(), dst.data_ptr(), int(N), cap, nat.ptr(ptr), B,
+                                      nat.ptr(cs) if cap else None, nat.ptr(pm) if cap else None,
+                                      nat.ptr(ns) if N else None, nat.ptr(ne) if N else None,
+                                      nat.ptr(avg) if N else None, nat.stream(dev)), "gdl_radius_csr_finish")
+    return cs, pm, ns, ne, avg
+
+
+def edge_geometry_cuda(x: torch.Tensor, row: torch.Tensor, col: torch.Tensor, *, max_l: Optional[int] = None,
+                       with_diff: bool = True, with_dist: bool = True, with_dir: bool = True):
+    """(diff, dist, direction, sph) of COO edges row=src -> col=dst (compute_edge_vectors +
+    spherical_harmonics(normalize=False) of the reference); entries not requested are None."""
+    dev = nat.require_cuda(x, row, col, what="edge_geometry_cuda")
+    x = x.contiguous().float()
+    row = row.to(torch.int64).contiguous()
+    col = col.to(torch.int64).contiguous()
+    E = row.numel()
+    g = _GeomOut(max_l, with_diff, with_dist, with_dir)
+    st = g(E, dev)
+    nat.check(nat.load().gdl_edge_geometry_coo(x.data_ptr() if x.numel() else None, x.shape[0],
+                                               row.data_ptr() if E else None, col.data_ptr() if E else None, E, st,
+                                               nat.stream(dev)), "gdl_edge_geometry_coo")
+    return g.diff, g.dist, g.direction, g.sph
+
+
+def cloud_avg_degree_cuda(node_start: torch.Tensor, node_end: torch.Tensor, *, batch: Optional[torch.Tensor] = None,
+                          ptr: Optional[torch.Tensor] = None, num_clouds: Optional[int] = None) -> torch.Tensor:
+    """avg_degree [N] of SpatialGraph (nn/modules/spatial_graph.py:131-153): the average degree
+    of each node's cloud (clouds from ``batch``, else ``ptr``, else one), clamped at 1."""
+    dev = nat.require_cuda(node_start, node_end, what="cloud_avg_degree_cuda")
+    N = node_start.numel()
+    out = torch.empty(N, dtype=torch.float32, device=dev)
+    b = p = None
+    B = 0
+    if batch is not None:
+        b = batch.to(device=dev, dtype=torch.int64).contiguous()
+        B = int(num_clouds) if num_clouds is not None else (int(b.max().item()) + 1 if N else 1)
+    elif ptr is not None:
+        p = ptr.to(device=dev, dtype=torch.int64).contiguous()
+        B = p.numel() - 1
+    L = nat.load()
+    ws = nat.workspace(L.gdl_cloud_avg_degree_workspace_size(max(B, 1)), dev)
+    nat.check(L.gdl_cloud_avg_degree(node_start.contiguous().data_ptr() if N else None,
+                                     node_end.contiguous().data_ptr() if N else None, N, nat.ptr(b), nat.ptr(p), B,
+                                     out.data_ptr() if N else None, ws.data_ptr(), ws.numel(), nat.stream(dev)),
+              "gdl_cloud_avg_degree")
+    return out
 
 
 def radius_graph_cuda(x: torch.Tensor, r: float, *, max_num_neighbors: int = 32, loop: bool = False,

@@ -18,6 +18,7 @@
 // B200 layout: all clouds in one launch per stage (no host loop, no host syncs), sorted
 // coordinates gathered once as float4 for 16-byte loads in the candidate loop.
 #include "common.cuh"
+#include "geom.cuh"
 #include "radix.cuh"
 
 namespace gdl {
@@ -484,10 +485,10 @@ __global__ void __launch_bounds__(kSmallThreads) rg_small_kernel(
 }
 
 // Sort one query's kept sources (count <= 64, in padded[0, c)) ascending with a warp bitonic
-// sort (two keys per lane) and write them at o.
+// sort (two keys per lane) and write them at o, with their geometry when g.x is set.
 __device__ __forceinline__ void warp_sort_emit(const int32_t *__restrict__ col, int64_t stride, int c, int64_t o,
                                                int64_t q, int64_t *__restrict__ src, int64_t *__restrict__ dstv,
-                                               int32_t *__restrict__ src32) {
+                                               int32_t *__restrict__ src32, const EdgeGeom &g) {
     const int lane = threadIdx.x & 31;
     int a = lane < c ? col[lane * stride] : 0x7fffffff;
     int b = lane + 32 < c ? col[(lane + 32) * stride] : 0x7fffffff;
@@ -534,6 +535,15 @@ __device__ __forceinline__ void warp_sort_emit(const int32_t *__restrict__ col, 
         if (src32) src32[o + lane + 32] = b;
         if (dstv) dstv[o + lane + 32] = q;
     }
+    if (g.x && c > 0) {
+        const float qx = g.x[3 * q], qy = g.x[3 * q + 1], qz = g.x[3 * q + 2];
+        if (lane < c)
+            edge_geom_store(g, o + lane, qx, qy, qz, g.x[3 * (int64_t)a], g.x[3 * (int64_t)a + 1],
+                            g.x[3 * (int64_t)a + 2]);
+        if (lane + 32 < c)
+            edge_geom_store(g, o + lane + 32, qx, qy, qz, g.x[3 * (int64_t)b], g.x[3 * (int64_t)b + 1],
+                            g.x[3 * (int64_t)b + 2]);
+    }
 }
 
 // grid = num_clouds * split. Every CTA of cloud b takes the cloud's global edge offset (sum of the
@@ -543,7 +553,7 @@ __global__ void __launch_bounds__(kSmallThreads) rg_small_compact_kernel(
     const int64_t *__restrict__ ptr, int32_t B, int split, int64_t n_all, int cap, const int32_t *__restrict__ counts,
     const int32_t *__restrict__ padded, const int32_t *__restrict__ cloud_tot, int64_t *__restrict__ row_ptr,
     int64_t *__restrict__ src, int64_t *__restrict__ dstv, int32_t *__restrict__ row_ptr32,
-    int32_t *__restrict__ src32) {
+    int32_t *__restrict__ src32, const EdgeGeom geom) {
     __shared__ int64_t warp_sums[32];
     __shared__ int64_t total;
     __shared__ int64_t offs[kSmallMax];
@@ -572,7 +582,7 @@ __global__ void __launch_bounds__(kSmallThreads) rg_small_compact_kernel(
         if (row_ptr32) row_ptr32[gq] = (int32_t)offs[q];
     }
     for (int q = qb + warp; q < qe; q += kSmallWarps)  // one warp sorts and writes a row
-        warp_sort_emit(padded + (s0 + q) * cap, 1, counts[s0 + q], offs[q], s0 + q, src, dstv, src32);
+        warp_sort_emit(padded + (s0 + q) * cap, 1, counts[s0 + q], offs[q], s0 + q, src, dstv, src32, geom);
     if (b == 0 && part == 0)  // points before the first cloud have no edges
         for (int64_t q = tid; q < ptr[0]; q += kSmallThreads) {
             row_ptr[q] = 0;
@@ -872,13 +882,14 @@ __global__ void __launch_bounds__(kQueryWarps * 32) rg_query_warp_kernel(
 __global__ void rg_compact_sort_kernel(const int32_t *__restrict__ counts, const int32_t *__restrict__ padded,
                                        int64_t n, int cap, const int64_t *__restrict__ row_ptr,
                                        int64_t *__restrict__ src, int64_t *__restrict__ dst,
-                                       int32_t *__restrict__ row_ptr32, int32_t *__restrict__ src32) {
+                                       int32_t *__restrict__ row_ptr32, int32_t *__restrict__ src32,
+                                       const EdgeGeom geom) {
     const int64_t q = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
     const int lane = threadIdx.x & 31;
     if (q > n) return;  // uniform over the warp
     if (row_ptr32 && lane == 0) row_ptr32[q] = (int32_t)row_ptr[q];
     if (q == n) return;
-    warp_sort_emit(padded + q * cap, 1, counts[q], row_ptr[q], q, src, dst, src32);
+    warp_sort_emit(padded + q * cap, 1, counts[q], row_ptr[q], q, src, dst, src32, geom);
 }
 
 struct RadiusWs {
@@ -928,14 +939,17 @@ extern "C" size_t gdl_radius_graph_workspace_size(int64_t n_points, int32_t num_
     return radius_ws(n_points, num_clouds, radius_bucket(max_num_neighbors), nullptr, nullptr);
 }
 
-extern "C" int gdl_radius_graph(const float *x, const int64_t *ptr, int32_t num_clouds, int64_t n_points,
-                                int64_t max_cloud_points, double radius, int32_t max_num_neighbors, int32_t loop,
-                                const uint8_t *mask, int64_t *out_row_ptr, int64_t *out_src, int64_t *out_dst,
-                                int32_t *out_row_ptr32, int32_t *out_src32, void *workspace, size_t workspace_bytes,
-                                void *stream) {
+extern "C" int gdl_radius_graph_geometry(const float *x, const int64_t *ptr, int32_t num_clouds, int64_t n_points,
+                                         int64_t max_cloud_points, double radius, int32_t max_num_neighbors,
+                                         int32_t loop, const uint8_t *mask, int64_t *out_row_ptr, int64_t *out_src,
+                                         int64_t *out_dst, int32_t *out_row_ptr32, int32_t *out_src32,
+                                         const gdl_edge_geometry *geometry, void *workspace, size_t workspace_bytes,
+                                         void *stream) {
     cudaStream_t st = (cudaStream_t)stream;
     GDL_RETURN_IF(num_clouds < 0 || n_points < 0, GDL_ERR_INVALID);
     GDL_RETURN_IF(!out_row_ptr, GDL_ERR_INVALID);
+    GDL_RETURN_IF(!edge_geom_valid(geometry), GDL_ERR_INVALID);
+    const EdgeGeom geom = edge_geom_from(x, geometry);
     GDL_RETURN_IF(n_points >= INT32_MAX / 64, GDL_ERR_OVERFLOW);
     const float r = (float)radius;  // radius_graph_kernel.cu:266
     if (n_points == 0 || num_clouds == 0 || !(r > 0.0f)) {
@@ -962,7 +976,7 @@ extern "C" int gdl_radius_graph(const float *x, const int64_t *ptr, int32_t num_
                                                                          n_points, w.counts, w.padded, w.cloud_tot);
         rg_small_compact_kernel<<<num_clouds * split, kSmallThreads, 0, st>>>(
             ptr, num_clouds, split, n_points, cap, w.counts, w.padded, w.cloud_tot, out_row_ptr, out_src, out_dst,
-            out_row_ptr32, out_src32);
+            out_row_ptr32, out_src32, geom);
         GDL_CUDA_TRY(cudaGetLastError());
         return GDL_OK;
     }
@@ -985,7 +999,17 @@ extern "C" int gdl_radius_graph(const float *x, const int64_t *ptr, int32_t num_
     GDL_CUDA_TRY((exclusive_scan<int32_t, int64_t>(w.counts, out_row_ptr, n_points, w.scan_scratch,
                                                    out_row_ptr + n_points, st)));
     rg_compact_sort_kernel<<<(unsigned)(((n_points + 1) * 32 + 255) / 256), 256, 0, st>>>(
-        w.counts, w.padded, n_points, cap, out_row_ptr, out_src, out_dst, out_row_ptr32, out_src32);
+        w.counts, w.padded, n_points, cap, out_row_ptr, out_src, out_dst, out_row_ptr32, out_src32, geom);
     GDL_CUDA_TRY(cudaGetLastError());
     return GDL_OK;
+}
+
+extern "C" int gdl_radius_graph(const float *x, const int64_t *ptr, int32_t num_clouds, int64_t n_points,
+                                int64_t max_cloud_points, double radius, int32_t max_num_neighbors, int32_t loop,
+                                const uint8_t *mask, int64_t *out_row_ptr, int64_t *out_src, int64_t *out_dst,
+                                int32_t *out_row_ptr32, int32_t *out_src32, void *workspace, size_t workspace_bytes,
+                                void *stream) {
+    return gdl_radius_graph_geometry(x, ptr, num_clouds, n_points, max_cloud_points, radius, max_num_neighbors, loop,
+                                     mask, out_row_ptr, out_src, out_dst, out_row_ptr32, out_src32, nullptr,
+                                     workspace, workspace_bytes, stream);
 }

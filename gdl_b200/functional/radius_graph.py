@@ -8,6 +8,7 @@ from typing import Optional, Tuple
 import torch
 from torch import Tensor
 
+from .. import _native as nat
 from .. import csrc
 
 
@@ -60,8 +61,12 @@ def radius_graph(x: Tensor, r: float, *, max_num_neighbors: int = 32, batch: Opt
 
 
 def compute_edge_vectors(x: Tensor, row: Tensor, col: Tensor) -> Tuple[Tensor, Tensor, Tensor]:
-    """(diff = x[col] - x[row], |diff| clamped at 1e-8, diff / |diff|) -- the reference's
-    formula (radius_graph.py:338-358), evaluated with torch ops."""
-    diff = x[col] - x[row]
-    dist = diff.norm(dim=-1, keepdim=True).clamp(min=1e-8)
-    return diff, dist.squeeze(-1), diff / dist
+    """(diff = x[col] - x[row], |diff| clamped at 1e-8, diff / |diff|) of the reference
+    (radius_graph.py:338-358), one CUDA kernel over the edges with the reference's CPU
+    rounding (gdl_edge_geometry_coo). Positions are constants here: ``x`` that requires grad
+    raises (the reference differentiates through torch ops; this build does not)."""
+    if x.requires_grad and torch.is_grad_enabled():
+        raise nat.GdlError("compute_edge_vectors: positions that require grad are not supported; "
+                           "pass x.detach()")
+    diff, dist, direction, _ = csrc.edge_geometry_cuda(x, row, col)
+    return diff, dist, direction

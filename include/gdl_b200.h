@@ -121,6 +121,66 @@ int gdl_radius_graph(const float *x, const int64_t *ptr, int32_t num_clouds, int
                      int32_t *out_row_ptr32, int32_t *out_src32, void *workspace, size_t workspace_bytes,
                      void *stream);
 
+/* ------------------------------------------------------------------------ edge geometry
+ * Replaces compute_edge_vectors(x, row, col) -- geoembodied/functional/radius_graph.py:338-358 --
+ * and spherical_harmonics(direction, max_l, normalize=False) -- kernels/triton_sph_harm.py:
+ * 200-240, 322-369 -- as SpatialGraph.build / from_edge_index call them
+ * (nn/modules/spatial_graph.py:126-129, 222-223). Per edge (src -> dst):
+ *   diff      [E, 3] x[dst] - x[src]
+ *   dist      [E]    |diff| clamped below at 1e-8
+ *   direction [E, 3] diff / dist
+ *   sph       [E, (sph_max_l + 1)^2] real spherical harmonics of direction, l <= sph_max_l,
+ *             channels [Y00 | Y1-1 Y10 Y11 | Y2-2 Y2-1 Y20 Y21 Y22]
+ * Every pointer is nullable (nothing written). Rounding: IEEE single precision as the
+ * reference's torch CPU evaluation of the same formulas.
+ */
+typedef struct gdl_edge_geometry {
+    float *diff;
+    float *dist;
+    float *direction;
+    float *sph;
+    int32_t sph_max_l; /* 0, 1 or 2 when sph is set */
+} gdl_edge_geometry;
+
+/* The radius graph of gdl_radius_graph with the geometry of each edge written by the kernel
+ * that emits the edge (edge slot j of out_src gets slot j of every geometry array; capacity
+ * as for out_src). Same workspace as gdl_radius_graph. No counterpart kernel in the reference,
+ * whose radius graph and geometry are separate passes. */
+int gdl_radius_graph_geometry(const float *x, const int64_t *ptr, int32_t num_clouds, int64_t n_points,
+                              int64_t max_cloud_points, double radius, int32_t max_num_neighbors, int32_t loop,
+                              const uint8_t *mask, int64_t *out_row_ptr, int64_t *out_src, int64_t *out_dst,
+                              int32_t *out_row_ptr32, int32_t *out_src32, const gdl_edge_geometry *geometry,
+                              void *workspace, size_t workspace_bytes, void *stream);
+
+/* Geometry of COO edges (row = src, col = dst, int64, any order) over x [n_points, 3].
+ * An edge with an index outside [0, n_points) gets NaN in every output. */
+int gdl_edge_geometry_coo(const float *x, int64_t n_points, const int64_t *row, const int64_t *col,
+                          int64_t n_edges, const gdl_edge_geometry *geometry, void *stream);
+
+/* Per-node average degree of the node's cloud, clamped below at 1 -- the avg_degree of
+ * SpatialGraph.build / from_edge_index (nn/modules/spatial_graph.py:131-153, 225-239):
+ * degree[n] = node_end[n] - node_start[n]; the cloud of node n is batch[n] (batch given, any
+ * order, values in [0, num_clouds)), else the b with ptr[b] <= n < ptr[b+1] (ptr given), else
+ * one cloud of all nodes. out[n] = float(sum of the cloud's degrees) / float(max(nodes, 1)),
+ * then max(., 1). Nodes outside every cloud get 1. Sums are exact (integer atomics). */
+size_t gdl_cloud_avg_degree_workspace_size(int32_t num_clouds);
+int gdl_cloud_avg_degree(const int32_t *node_start, const int32_t *node_end, int64_t n_nodes, const int64_t *batch,
+                         const int64_t *ptr, int32_t num_clouds, float *out, void *workspace, size_t workspace_bytes,
+                         void *stream);
+
+/* SpatialGraph's CSR fields for a radius graph from gdl_radius_graph(_geometry), without a sort:
+ * its edges already come grouped by ascending destination, so sort_and_build_csr(col, N)
+ * (segment_reduce_kernel.cu:100-169) of them is the identity permutation. With
+ * E = row_ptr[n_points] (read on the device, E <= capacity):
+ *   col_sorted [capacity] i32: first E = dst;  perm [capacity] i32: first E = 0 .. E-1
+ *   node_start / node_end [n_points] i32 (0 / 0 for nodes without edges, as the reference)
+ *   avg_degree [n_points] f32: edges of the node's cloud / its nodes, clamped below at 1,
+ *              clouds from ptr [num_clouds + 1] (nullable: one cloud of all n_points nodes)
+ * Every output is nullable. No counterpart kernel in the reference. */
+int gdl_radius_csr_finish(const int64_t *row_ptr, const int64_t *dst, int64_t n_points, int64_t capacity,
+                          const int64_t *ptr, int32_t num_clouds, int32_t *col_sorted, int32_t *perm,
+                          int32_t *node_start, int32_t *node_end, float *avg_degree, void *stream);
+
 /* -------------------------------------------------------------------------- CSR build
  * Replaces sort_and_build_csr(col, N) -- geoembodied/csrc/segment_reduce_kernel.cu:100-169.
  * col [num_edges] i64 in [0, num_nodes). Stable sort by destination:

@@ -581,3 +581,84 @@ int gdl_oracle_segment_reduce_backward(const float *grad_out, const void *msg, i
     free(g);
     return 0;
 }
+
+/* ---------------------------------------------------------------- edge geometry
+ * compute_edge_vectors (functional/radius_graph.py:338-358) and spherical_harmonics
+ * (kernels/triton_sph_harm.py:200-240, normalize=False) as the reference's torch CPU path
+ * rounds them: diff = x[col] - x[row]; |diff| = sqrtf(fmaf(dz, dz, fmaf(dy, dy, dx * dx)))
+ * (torch's 2-norm accumulation over a row of three, pinned against torch 2.11 on the CPU);
+ * dist = clamp(|diff|, min=1e-8) keeping NaN; dir = diff / dist; harmonics with one rounding
+ * per torch op, constants (double) rounded to float first. Any output may be NULL. An edge
+ * with an index outside [0, n) gets NaN everywhere.
+ */
+static void sph_row(float *o, int dim, float x, float y, float z) {
+    const float c0 = (float)0.28209479177387814, c1 = (float)0.4886025119029199;
+    const float c20 = (float)0.31539156525252005, c21 = (float)1.0925484305920792;
+    const float c22 = (float)0.5462742152960396;
+    o[0] = c0 * 1.0f;
+    if (dim == 1) return;
+    o[1] = c1 * y; o[2] = c1 * z; o[3] = c1 * x;
+    if (dim == 4) return;
+    o[4] = (c21 * x) * y;
+    o[5] = (c21 * y) * z;
+    o[6] = c20 * ((3.0f * z) * z - 1.0f);
+    o[7] = (c21 * x) * z;
+    o[8] = c22 * (x * x - y * y);
+}
+
+int gdl_oracle_edge_geometry(const float *x, int64_t n, const int64_t *row, const int64_t *col, int64_t E,
+                             float *diff, float *dist, float *dir, float *sph, int max_l) {
+    const int dim = (max_l + 1) * (max_l + 1);
+    for (int64_t e = 0; e < E; ++e) {
+        const int64_t s = row[e], q = col[e];
+        float dx, dy, dz;
+        if (s >= 0 && s < n && q >= 0 && q < n) {
+            dx = x[3 * q] - x[3 * s]; dy = x[3 * q + 1] - x[3 * s + 1]; dz = x[3 * q + 2] - x[3 * s + 2];
+        } else {
+            dx = dy = dz = NAN;
+        }
+        const float nrm = sqrtf(fmaf(dz, dz, fmaf(dy, dy, dx * dx)));
+        const float d = nrm < 1e-8f ? 1e-8f : nrm;
+        if (diff) { diff[3 * e] = dx; diff[3 * e + 1] = dy; diff[3 * e + 2] = dz; }
+        if (dist) dist[e] = d;
+        const float ux = dx / d, uy = dy / d, uz = dz / d;
+        if (dir) { dir[3 * e] = ux; dir[3 * e + 1] = uy; dir[3 * e + 2] = uz; }
+        if (sph) sph_row(sph + e * dim, dim, ux, uy, uz);
+    }
+    return 0;
+}
+
+/* Per-node average degree of its cloud, clamped below at 1 (nn/modules/spatial_graph.py:
+ * 131-153): cloud_sum / max(cloud_cnt, 1) over degree = node_end - node_start, clouds from
+ * batch (if given), else ptr (if given), else one cloud; sums in exact integers, converted to
+ * float once (equal to the reference's float scatter_add while sums stay below 2^24). Nodes
+ * outside every cloud get 1. */
+int gdl_oracle_cloud_avg_degree(const int32_t *ns, const int32_t *ne, int64_t n, const int64_t *batch,
+                                const int64_t *ptr, int B, float *out) {
+    if (!batch && !ptr) B = 1;
+    int64_t *sum = (int64_t *)calloc((size_t)(B > 0 ? B : 1), sizeof(int64_t));
+    int64_t *cnt = (int64_t *)calloc((size_t)(B > 0 ? B : 1), sizeof(int64_t));
+    int *cl = (int *)malloc(sizeof(int) * (size_t)(n > 0 ? n : 1));
+    for (int64_t i = 0; i < n; ++i) {
+        int b = 0;
+        if (batch) b = (batch[i] >= 0 && batch[i] < B) ? (int)batch[i] : -1;
+        else if (ptr) {
+            b = -1;
+            for (int c = 0; c < B; ++c)
+                if (ptr[c] <= i && i < ptr[c + 1]) { b = c; break; }
+        }
+        cl[i] = b;
+        if (b >= 0) { sum[b] += (int64_t)ne[i] - ns[i]; cnt[b] += 1; }
+    }
+    for (int64_t i = 0; i < n; ++i) {
+        const int b = cl[i];
+        float a = 1.0f;
+        if (b >= 0) {
+            a = (float)sum[b] / (float)(cnt[b] > 1 ? cnt[b] : 1);
+            if (a < 1.0f) a = 1.0f;
+        }
+        out[i] = a;
+    }
+    free(sum); free(cnt); free(cl);
+    return 0;
+}

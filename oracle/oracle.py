@@ -75,6 +75,8 @@ def lib() -> ctypes.CDLL:
         L.gdl_oracle_num_threads.restype = i32
         L.gdl_oracle_set_num_threads.argtypes = [i32]
         L.gdl_oracle_radius_grid.argtypes = [P, i64, ctypes.c_float, P, P]
+        L.gdl_oracle_edge_geometry.argtypes = [P, i64, P, P, i64, P, P, P, P, i32]
+        L.gdl_oracle_cloud_avg_degree.argtypes = [P, P, i64, P, P, i32, P]
         _lib = L
     return _lib
 
@@ -203,6 +205,39 @@ def segment_reduce_backward(grad_out, msg, out, perm, node_start, node_end, N: i
                                              _p(_c(node_start, np.int32)), _p(_c(node_end, np.int32)), N, C, E,
                                              REDUCE[reduce], _p(gm))
     return gm
+
+
+def edge_geometry(x, row, col, max_l=2):
+    """(diff [E,3], dist [E], direction [E,3], sph [E,(max_l+1)^2]) of COO edges row -> col."""
+    x = _c(x, np.float32)
+    row = _c(row, np.int64)
+    col = _c(col, np.int64)
+    E = row.shape[0]
+    diff = np.zeros((E, 3), np.float32)
+    dist = np.zeros(E, np.float32)
+    dire = np.zeros((E, 3), np.float32)
+    sph = np.zeros((E, (max_l + 1) ** 2), np.float32)
+    lib().gdl_oracle_edge_geometry(_p(x), x.shape[0], _p(row), _p(col), E, _p(diff), _p(dist), _p(dire), _p(sph),
+                                   int(max_l))
+    return diff, dist, dire, sph
+
+
+def cloud_avg_degree(node_start, node_end, batch=None, ptr=None, num_clouds=None) -> np.ndarray:
+    ns = _c(node_start, np.int32)
+    ne = _c(node_end, np.int32)
+    n = ns.shape[0]
+    b = None if batch is None else _c(batch, np.int64)
+    p = None if ptr is None else _c(ptr, np.int64)
+    if b is not None:
+        B = int(num_clouds) if num_clouds is not None else (int(b.max()) + 1 if n else 1)
+    elif p is not None:
+        B = p.shape[0] - 1
+    else:
+        B = 1
+    out = np.zeros(n, np.float32)
+    lib().gdl_oracle_cloud_avg_degree(_p(ns), _p(ne), n, None if b is None else _p(b), None if p is None else _p(p),
+                                      B, _p(out))
+    return out
 
 
 def bf16_bits(x: np.ndarray) -> np.ndarray:

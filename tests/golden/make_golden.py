@@ -13,6 +13,9 @@ inputs, what the reference's public entry points return on the CPU:
 * ``functional.segment_reduce.sort_and_build_csr`` / ``segment_reduce`` (+ autograd)
 * ``torch.scatter_reduce(include_self=False)`` mean/amax (+ autograd), the semantics
   the reference's callers use for segment mean/max.
+* ``nn.modules.spatial_graph.SpatialGraph.build`` / ``from_edge_index`` and
+  ``functional.radius_graph.compute_edge_vectors`` + the spherical harmonics' torch path
+  (``kernels.triton_sph_harm._spherical_harmonics_pytorch``) -> ``golden_graph.npz``.
 
 Inputs that would make the CPU path and the CUDA kernels disagree for reasons the
 reference itself documents (exact distance ties, pairs at the radius boundary where
@@ -225,6 +228,81 @@ def gen_segment(S, out, knn_idx):
             out[tag + "_grad"] = m.grad.float().numpy()
 
 
+def _ref_spatial_graph(root: str):
+    """The reference's SpatialGraph, loaded from its file: ``geoembodied.nn`` as a package
+    imports modules (``geoembodied.data``) that the reference tree does not ship."""
+    import importlib.util
+
+    path = Path(root) / "geoembodied" / "nn" / "modules" / "spatial_graph.py"
+    spec = importlib.util.spec_from_file_location("ref_spatial_graph", path)
+    mod = importlib.util.module_from_spec(spec)
+    sys.modules["ref_spatial_graph"] = mod
+    spec.loader.exec_module(mod)
+    return mod.SpatialGraph
+
+
+def gen_graph(root: str, R, out):
+    """SpatialGraph.build / from_edge_index (nn/modules/spatial_graph.py:88-246) and the
+    geometry of hand-made edges (compute_edge_vectors + spherical harmonics, l <= 0, 1, 2)."""
+    import importlib
+
+    SG = _ref_spatial_graph(root)
+    sph = importlib.import_module("geoembodied.kernels.triton_sph_harm")._spherical_harmonics_pytorch
+    for seed in range(500, 600):
+        g = torch.Generator().manual_seed(seed)
+        B, n, r, K = 3, 300, 0.2, 32
+        x = torch.rand(B * n, 3, generator=g).numpy().astype(np.float32)
+        if _radius_safe(x, B, r, K) and _radius_safe(x[:n], 1, r, K):
+            break
+    else:
+        raise RuntimeError("no graph fixture without boundary pairs found")
+    out["graph_x"] = x
+    out["graph_meta"] = np.array([B, n, K, seed], np.int64)
+    out["graph_r"] = np.array([r], np.float64)
+    batch = torch.arange(B).repeat_interleave(n)
+    # unequal clouds (300, 250, 280 points) in shuffled order: without num_batch_elements the
+    # reference takes its per-cloud loop, which honours the batch labels (radius_graph.py:
+    # 181-198; equal-size batches are cut into consecutive blocks whatever the labels say)
+    sel = torch.cat([torch.arange(0, 300), torch.arange(300, 550), torch.arange(600, 880)])
+    perm = torch.randperm(sel.numel(), generator=torch.Generator().manual_seed(seed + 1))
+    out["graph_sel"] = sel.numpy()
+    out["graph_perm"] = perm.numpy()
+    cases = {
+        "batch": (torch.from_numpy(x), dict(batch=batch, num_batch_elements=B)),
+        "single": (torch.from_numpy(x[:n]), {}),
+        "shuffled": (torch.from_numpy(x)[sel][perm], dict(batch=batch[sel][perm])),
+    }
+    for tag, (pos, kw) in cases.items():
+        gr = SG.build(pos, r, max_num_neighbors=K, **kw)
+        for f in ("row", "col", "dist", "direction", "Y", "node_start", "node_end", "avg_degree"):
+            out[f"graph_{tag}_{f}"] = getattr(gr, f).numpy()
+    # from_edge_index on the batch graph's edges (same values, CSR re-derived)
+    gb = SG.from_edge_index(torch.from_numpy(out["graph_batch_row"]), torch.from_numpy(out["graph_batch_col"]),
+                            torch.from_numpy(x), B * n, max_l=1, batch=batch, num_batch_elements=B)
+    for f in ("col_sorted", "perm", "node_start", "node_end", "avg_degree", "Y"):
+        out[f"graph_fei_{f}"] = getattr(gb, f).numpy()
+
+    # hand-made edges: ordinary, self edge (zero vector), a vector shorter than the 1e-8 clamp,
+    # axis-aligned, huge coordinates (|diff|^2 overflows), non-finite coordinates
+    pts = np.array([[0.1, -0.2, 0.3], [0.7, 0.25, -0.4], [0.1, -0.2, 0.3 + 4e-9], [1e20, 0, 0], [-1e20, 0, 0],
+                    [np.inf, 0, 0], [np.nan, 1, 2], [0, 0, 0], [0, 0, 1.5], [3e-39, 0, 0]], np.float32)
+    pairs = np.array([[0, 1], [1, 0], [0, 0], [0, 2], [2, 0], [3, 4], [4, 3], [5, 0], [6, 1], [7, 8], [8, 7],
+                      [9, 7], [7, 9], [1, 8]], np.int64)
+    g = torch.Generator().manual_seed(11)
+    rnd = (torch.randn(600, 3, generator=g) * torch.tensor([1e-3, 1.0, 30.0])).numpy().astype(np.float32)
+    xg = np.concatenate([pts, rnd]).astype(np.float32)
+    ng = xg.shape[0]
+    rr = torch.randint(0, ng, (4000,), generator=g).numpy()
+    cc = torch.randint(0, ng, (4000,), generator=g).numpy()
+    row = np.concatenate([pairs[:, 0], rr]).astype(np.int64)
+    col = np.concatenate([pairs[:, 1], cc]).astype(np.int64)
+    out["geo_x"], out["geo_row"], out["geo_col"] = xg, row, col
+    diff, dist, direction = R.compute_edge_vectors(torch.from_numpy(xg), torch.from_numpy(row), torch.from_numpy(col))
+    out["geo_diff"], out["geo_dist"], out["geo_dir"] = diff.numpy(), dist.numpy(), direction.numpy()
+    for lmax in (0, 1, 2):
+        out[f"geo_Y{lmax}"] = sph(direction, lmax).numpy()
+
+
 def main():
     root = sys.argv[1] if len(sys.argv) > 1 else "/root/reference"
     F, K, R, S = _ref(root)
@@ -236,6 +314,10 @@ def main():
     gen_segment(S, out, out["knn_c1_idx"])
     np.savez_compressed(HERE / "golden_cpu.npz", **out)
     print("wrote", HERE / "golden_cpu.npz", sum(v.nbytes for v in out.values()) / 1e6, "MB raw")
+    graph = {}
+    gen_graph(root, R, graph)
+    np.savez_compressed(HERE / "golden_graph.npz", **graph)
+    print("wrote", HERE / "golden_graph.npz", sum(v.nbytes for v in graph.values()) / 1e6, "MB raw")
 
 
 if __name__ == "__main__":

@@ -55,6 +55,11 @@ def test_argument_validation_without_gpu(lib):
     assert lib.gdl_fps(None, None, None, 1, 10, 10, 7, None, None, None, 0, None) == 1
     assert lib.gdl_segment_reduce(None, 5, 1, 1, None, None, None, 1, 0, None, None, None, 0, None) == 1
     assert lib.gdl_knn(None, None, None, None, 1, 10, 4, 10, None, None, None, 0, None) == 1
+    bad = nat.EdgeGeometry(None, None, None, 1, 3)  # harmonics of degree 3 are not provided
+    assert lib.gdl_edge_geometry_coo(None, 4, None, None, 2, bad, None) == 1
+    assert lib.gdl_cloud_avg_degree(None, None, 3, None, None, 0, None, None, 0, None) == 1
+    assert lib.gdl_radius_csr_finish(None, None, 3, 3, None, 0, None, None, None, None, None, None) == 1
+    assert lib.gdl_cloud_avg_degree_workspace_size(8) >= 128
 
 
 def test_cpu_tensors_raise():
@@ -67,3 +72,12 @@ def test_cpu_tensors_raise():
         csrc.radius_graph_csr(x, 0.5, torch.tensor([0, 4]))
     with pytest.raises(nat.GdlError):
         csrc.segment_reduce_cuda(x, None, torch.zeros(1, dtype=torch.int32), torch.ones(1, dtype=torch.int32), 1)
+    e = torch.zeros(2, dtype=torch.int64)
+    with pytest.raises(nat.GdlError):
+        csrc.edge_geometry_cuda(x, e, e)
+    from gdl_b200.spatial_graph import SpatialGraph
+
+    with pytest.raises(nat.GdlError):
+        SpatialGraph.build(x, 0.5)
+    with pytest.raises(nat.GdlError):  # positions that require grad are refused before any device check
+        SpatialGraph.build(x.requires_grad_(True), 0.5)
