@@ -10,16 +10,27 @@
 
 namespace gdl {
 
-__global__ void __launch_bounds__(256) edge_geom_coo_kernel(const float *__restrict__ x, int64_t n, const int64_t *__restrict__ row,
+// One warp per 32 consecutive edges; outputs staged per warp (warp_geom_emit).
+__global__ void __launch_bounds__(256) edge_geom_coo_kernel(const float *__restrict__ x, int64_t n,
+                                                            const int64_t *__restrict__ row,
                                                             const int64_t *__restrict__ col, int64_t E, EdgeGeom g) {
-    for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < E; e += (int64_t)gridDim.x * blockDim.x) {
-        const int64_t s = row[e], q = col[e];
-        if (s >= 0 && s < n && q >= 0 && q < n) {
-            edge_geom_store(g, e, x[3 * q], x[3 * q + 1], x[3 * q + 2], x[3 * s], x[3 * s + 1], x[3 * s + 2]);
-        } else {
-            const float nan = __int_as_float(0x7fc00000);
-            edge_geom_store(g, e, nan, nan, nan, nan, nan, nan);
+    __shared__ float stage[8 * kGeomStageFloats];
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    float *st = stage + warp * kGeomStageFloats;
+    const int64_t nwarps = (int64_t)gridDim.x * 8;
+    for (int64_t e0 = ((int64_t)blockIdx.x * 8 + warp) * 32; e0 < E; e0 += nwarps * 32) {
+        const int cnt = (int)(E - e0 < 32 ? E - e0 : 32);
+        float q3[3], s3[3];
+        const float nan = __int_as_float(0x7fc00000);
+        q3[0] = q3[1] = q3[2] = s3[0] = s3[1] = s3[2] = nan;
+        if (lane < cnt) {
+            const int64_t s = row[e0 + lane], q = col[e0 + lane];
+            if (s >= 0 && s < n && q >= 0 && q < n) {
+                q3[0] = x[3 * q], q3[1] = x[3 * q + 1], q3[2] = x[3 * q + 2];
+                s3[0] = x[3 * s], s3[1] = x[3 * s + 1], s3[2] = x[3 * s + 2];
+            }
         }
+        warp_geom_emit(g, st, e0, cnt, lane, q3[0], q3[1], q3[2], s3[0], s3[1], s3[2]);
     }
 }
 

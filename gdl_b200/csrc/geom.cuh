@@ -48,27 +48,43 @@ __device__ __forceinline__ void sph_store(float *__restrict__ o, int dim, float 
     o[8] = __fmul_rn(kShC22, __fsub_rn(__fmul_rn(x, x), __fmul_rn(y, y)));
 }
 
-// Writes edge e's geometry from the destination position (qx, qy, qz) and the source's.
-__device__ __forceinline__ void edge_geom_store(const EdgeGeom &g, int64_t e, float qx, float qy, float qz, float sx,
-                                                float sy, float sz) {
-    const float dx = __fsub_rn(qx, sx), dy = __fsub_rn(qy, sy), dz = __fsub_rn(qz, sz);
-    const float n = __fsqrt_rn(__fmaf_rn(dz, dz, __fmaf_rn(dy, dy, __fmul_rn(dx, dx))));
-    const float d = n < 1e-8f ? 1e-8f : n;  // clamp(min=1e-8); NaN stays NaN
-    if (g.diff) {
-        g.diff[3 * e] = dx;
-        g.diff[3 * e + 1] = dy;
-        g.diff[3 * e + 2] = dz;
-    }
-    if (g.dist) g.dist[e] = d;
-    if (g.dir || g.sph) {
+// Per-warp staging for warp_geom_emit: dist [32] | direction [32 x 3] | diff [32 x 3] |
+// harmonics [32 x 9] floats.
+constexpr int kGeomStageFloats = 32 + 96 + 96 + 288;
+
+// Geometry of `cnt` <= 32 consecutive edge slots e0 .. e0 + cnt - 1, lane i holding slot e0 + i
+// (destination q, source s). The values go through the warp's staging area `st` so that every
+// output array is written by consecutive lanes at consecutive addresses: the rows of the [E, 3]
+// and [E, 9] arrays are 12 and 36 bytes long, and lane-per-row stores would touch up to eight
+// times the 32-byte sectors they fill. All lanes call it (warp-uniform e0, cnt).
+__device__ __forceinline__ void warp_geom_emit(const EdgeGeom &g, float *__restrict__ st, int64_t e0, int cnt,
+                                               int lane, float qx, float qy, float qz, float sx, float sy,
+                                               float sz) {
+    float *s_dist = st, *s_dir = st + 32, *s_diff = st + 128, *s_sph = st + 224;
+    if (lane < cnt) {
+        const float dx = __fsub_rn(qx, sx), dy = __fsub_rn(qy, sy), dz = __fsub_rn(qz, sz);
+        const float n = __fsqrt_rn(__fmaf_rn(dz, dz, __fmaf_rn(dy, dy, __fmul_rn(dx, dx))));
+        const float d = n < 1e-8f ? 1e-8f : n;  // clamp(min=1e-8); NaN stays NaN
         const float ux = __fdiv_rn(dx, d), uy = __fdiv_rn(dy, d), uz = __fdiv_rn(dz, d);
-        if (g.dir) {
-            g.dir[3 * e] = ux;
-            g.dir[3 * e + 1] = uy;
-            g.dir[3 * e + 2] = uz;
-        }
-        if (g.sph) sph_store(g.sph + e * g.sph_dim, g.sph_dim, ux, uy, uz);
+        s_dist[lane] = d;
+        s_dir[3 * lane] = ux;
+        s_dir[3 * lane + 1] = uy;
+        s_dir[3 * lane + 2] = uz;
+        s_diff[3 * lane] = dx;
+        s_diff[3 * lane + 1] = dy;
+        s_diff[3 * lane + 2] = dz;
+        if (g.sph) sph_store(s_sph + g.sph_dim * lane, g.sph_dim, ux, uy, uz);
     }
+    __syncwarp();
+    if (g.dist)
+        for (int f = lane; f < cnt; f += 32) g.dist[e0 + f] = s_dist[f];
+    if (g.dir)
+        for (int f = lane; f < 3 * cnt; f += 32) g.dir[3 * e0 + f] = s_dir[f];
+    if (g.diff)
+        for (int f = lane; f < 3 * cnt; f += 32) g.diff[3 * e0 + f] = s_diff[f];
+    if (g.sph)
+        for (int f = lane; f < g.sph_dim * cnt; f += 32) g.sph[g.sph_dim * e0 + f] = s_sph[f];
+    __syncwarp();
 }
 
 // Builds the device-side descriptor from the C-ABI one (nullptr: no geometry).

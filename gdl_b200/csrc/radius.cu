@@ -485,10 +485,12 @@ __global__ void __launch_bounds__(kSmallThreads) rg_small_kernel(
 }
 
 // Sort one query's kept sources (count <= 64, in padded[0, c)) ascending with a warp bitonic
-// sort (two keys per lane) and write them at o, with their geometry when g.x is set.
+// sort (two keys per lane) and write them at o, with their geometry when g.x is set (staged in
+// the warp's kGeomStageFloats floats at geo_st).
 __device__ __forceinline__ void warp_sort_emit(const int32_t *__restrict__ col, int64_t stride, int c, int64_t o,
                                                int64_t q, int64_t *__restrict__ src, int64_t *__restrict__ dstv,
-                                               int32_t *__restrict__ src32, const EdgeGeom &g) {
+                                               int32_t *__restrict__ src32, const EdgeGeom &g,
+                                               float *__restrict__ geo_st) {
     const int lane = threadIdx.x & 31;
     int a = lane < c ? col[lane * stride] : 0x7fffffff;
     int b = lane + 32 < c ? col[(lane + 32) * stride] : 0x7fffffff;
@@ -535,14 +537,14 @@ __device__ __forceinline__ void warp_sort_emit(const int32_t *__restrict__ col, 
         if (src32) src32[o + lane + 32] = b;
         if (dstv) dstv[o + lane + 32] = q;
     }
-    if (g.x && c > 0) {
+    if (g.x && c > 0) {  // c is warp-uniform
         const float qx = g.x[3 * q], qy = g.x[3 * q + 1], qz = g.x[3 * q + 2];
-        if (lane < c)
-            edge_geom_store(g, o + lane, qx, qy, qz, g.x[3 * (int64_t)a], g.x[3 * (int64_t)a + 1],
-                            g.x[3 * (int64_t)a + 2]);
-        if (lane + 32 < c)
-            edge_geom_store(g, o + lane + 32, qx, qy, qz, g.x[3 * (int64_t)b], g.x[3 * (int64_t)b + 1],
-                            g.x[3 * (int64_t)b + 2]);
+        const int64_t sa = lane < c ? a : q, sb = lane + 32 < c ? b : q;
+        warp_geom_emit(g, geo_st, o, c < 32 ? c : 32, lane, qx, qy, qz, g.x[3 * sa], g.x[3 * sa + 1],
+                       g.x[3 * sa + 2]);
+        if (c > 32)
+            warp_geom_emit(g, geo_st, o + 32, c - 32, lane, qx, qy, qz, g.x[3 * sb], g.x[3 * sb + 1],
+                           g.x[3 * sb + 2]);
     }
 }
 
@@ -557,6 +559,7 @@ __global__ void __launch_bounds__(kSmallThreads) rg_small_compact_kernel(
     __shared__ int64_t warp_sums[32];
     __shared__ int64_t total;
     __shared__ int64_t offs[kSmallMax];
+    extern __shared__ float geo_stage[];  // kSmallWarps * kGeomStageFloats when geometry is written
     const int b = blockIdx.x / split, part = blockIdx.x % split;
     const int tid = threadIdx.x, warp = tid >> 5;
     int64_t base = 0;
@@ -582,7 +585,8 @@ __global__ void __launch_bounds__(kSmallThreads) rg_small_compact_kernel(
         if (row_ptr32) row_ptr32[gq] = (int32_t)offs[q];
     }
     for (int q = qb + warp; q < qe; q += kSmallWarps)  // one warp sorts and writes a row
-        warp_sort_emit(padded + (s0 + q) * cap, 1, counts[s0 + q], offs[q], s0 + q, src, dstv, src32, geom);
+        warp_sort_emit(padded + (s0 + q) * cap, 1, counts[s0 + q], offs[q], s0 + q, src, dstv, src32, geom,
+                       geo_stage + warp * kGeomStageFloats);
     if (b == 0 && part == 0)  // points before the first cloud have no edges
         for (int64_t q = tid; q < ptr[0]; q += kSmallThreads) {
             row_ptr[q] = 0;
@@ -884,12 +888,14 @@ __global__ void rg_compact_sort_kernel(const int32_t *__restrict__ counts, const
                                        int64_t *__restrict__ src, int64_t *__restrict__ dst,
                                        int32_t *__restrict__ row_ptr32, int32_t *__restrict__ src32,
                                        const EdgeGeom geom) {
+    extern __shared__ float geo_stage[];  // (blockDim.x / 32) * kGeomStageFloats when geometry is written
     const int64_t q = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
     const int lane = threadIdx.x & 31;
     if (q > n) return;  // uniform over the warp
     if (row_ptr32 && lane == 0) row_ptr32[q] = (int32_t)row_ptr[q];
     if (q == n) return;
-    warp_sort_emit(padded + q * cap, 1, counts[q], row_ptr[q], q, src, dst, src32, geom);
+    warp_sort_emit(padded + q * cap, 1, counts[q], row_ptr[q], q, src, dst, src32, geom,
+                   geo_stage + (threadIdx.x >> 5) * kGeomStageFloats);
 }
 
 struct RadiusWs {
@@ -974,7 +980,11 @@ extern "C" int gdl_radius_graph_geometry(const float *x, const int64_t *ptr, int
         GDL_CUDA_TRY(cudaMemsetAsync(w.cloud_tot, 0, sizeof(int32_t) * num_clouds, st));
         rg_small_kernel<<<num_clouds * split, kSmallThreads, smem, st>>>(x, ptr, mask, r_sq, inv, loop, cap, split,
                                                                          n_points, w.counts, w.padded, w.cloud_tot);
-        rg_small_compact_kernel<<<num_clouds * split, kSmallThreads, 0, st>>>(
+        const size_t geo_smem = geom.x ? sizeof(float) * kGeomStageFloats * kSmallWarps : 0;
+        if (geo_smem)
+            GDL_CUDA_TRY(cudaFuncSetAttribute(rg_small_compact_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                              (int)geo_smem));
+        rg_small_compact_kernel<<<num_clouds * split, kSmallThreads, geo_smem, st>>>(
             ptr, num_clouds, split, n_points, cap, w.counts, w.padded, w.cloud_tot, out_row_ptr, out_src, out_dst,
             out_row_ptr32, out_src32, geom);
         GDL_CUDA_TRY(cudaGetLastError());
@@ -998,7 +1008,8 @@ extern "C" int gdl_radius_graph_geometry(const float *x, const int64_t *ptr, int
                                                              w.counts, w.padded);
     GDL_CUDA_TRY((exclusive_scan<int32_t, int64_t>(w.counts, out_row_ptr, n_points, w.scan_scratch,
                                                    out_row_ptr + n_points, st)));
-    rg_compact_sort_kernel<<<(unsigned)(((n_points + 1) * 32 + 255) / 256), 256, 0, st>>>(
+    const size_t geo_smem = geom.x ? sizeof(float) * kGeomStageFloats * (256 / 32) : 0;
+    rg_compact_sort_kernel<<<(unsigned)(((n_points + 1) * 32 + 255) / 256), 256, geo_smem, st>>>(
         w.counts, w.padded, n_points, cap, out_row_ptr, out_src, out_dst, out_row_ptr32, out_src32, geom);
     GDL_CUDA_TRY(cudaGetLastError());
     return GDL_OK;
