@@ -12,6 +12,8 @@ inputs with the shapes of the reference's use cases; see gdl_b200/synthetic.py):
                 (64 channels).
   c3            32 GMM clouds x 8192 points: FPS chain 8192 -> 2048 -> 512 -> 128, KNN k=32
                 per level, segment max over gathered bf16 features, forward and backward.
+  c3i           (auxiliary) c3's clouds: the decoder's KNN k=3 inverse-distance interpolation
+                128 -> 512 -> 2048 -> 8192 of scalar + vector features, forward and backward.
   c4            64 source/target pairs x 16384 points: KNN k=1, residual segment sum.
   c5            8 clouds x 131072 LiDAR points: FPS -> 16384, radius graph (r = 1 m, 64),
                 segment sum of 64-channel features.
@@ -472,6 +474,178 @@ class C3:
             src = cent
 
 
+class C3I:
+    """Auxiliary KNN-aggregation workload (the reference's EquivariantInterpolate decoder pass,
+    nn/modules/equivariant_interp.py:58-139, on config 3's clouds): the FPS hierarchy
+    8192 -> 2048 -> 512 -> 128 of 32 GMM clouds is built once; a step upsamples 128 -> 512 ->
+    2048 -> 8192 per cloud: KNN k = 3 of the dense points among the coarse ones, inverse-distance
+    weights, weighted sums of C scalar and C/4 x 3 vector channels (C = 256 / 128 / 64), and the
+    backward to the coarse features."""
+    name = "c3i"
+    metric = ("points/sec (KNN k=3 + inverse-distance interpolation of scalar+vector features, fwd+bwd, "
+              "128->512->2048->8192), config 3 clouds")
+    B, N, KNN = 32, 8192, 3
+    SIZES = (8192, 2048, 512, 128)
+    CH = (64, 128, 256)  # channels of the coarse level of each step (dense level l <- coarse l + 1)
+    # per step l: knn 5; idw 1 + two weighted sums; backward: keys 1 + radix + offsets 1 + 2 tables
+    points_per_step = property(lambda self: self.B * self.N)
+    cpu_fraction = 1 / 32
+    cpu_sample = "the three interpolation steps (KNN, weights, sums, backward) of 1 of 32 clouds, scaled x32"
+
+    @staticmethod
+    def _radix_launches(n_src):
+        bits = 1
+        while bits < 32 and (1 << bits) <= n_src:
+            bits += 1
+        return 1 + 4 * ((bits + 7) // 8)
+
+    @property
+    def launches_per_step(self):
+        n = 0
+        for l in range(3):
+            n += 5 + 3 + 1 + self._radix_launches(self.B * self.SIZES[l + 1]) + 1 + 2
+        return n
+
+    def _host_init(self, seed, pin=True):
+        pos, ptr = synthetic.c3_points(seed=seed, B=self.B, N=self.N)
+        self.pos_h = torch.from_numpy(pos)
+        self.lptr_h = [torch.arange(0, self.B * n + 1, n, dtype=torch.int64) for n in self.SIZES]
+        g = torch.Generator().manual_seed(seed + 3)
+        self.s_h = [torch.randn(self.B * self.SIZES[l + 1], self.CH[l], generator=g) for l in range(3)]
+        self.v_h = [torch.randn(self.B * self.SIZES[l + 1], self.CH[l] // 4, 3, generator=g) for l in range(3)]
+        self.gs_h = [torch.randn(self.B * self.SIZES[l], self.CH[l], generator=g) for l in range(3)]
+        self.gv_h = [torch.randn(self.B * self.SIZES[l], self.CH[l] // 4, 3, generator=g) for l in range(3)]
+        if pin:
+            self.pos_h = self.pos_h.pin_memory()
+
+    def _levels(self, dev):
+        """positions of every level: FPS chain on the device (setup, untimed)."""
+        lv = [self.pos_h.to(dev)]
+        for l in range(3):
+            idx, cent = csrc.fps_cuda(lv[-1], self.lptr_h[l], torch.full((self.B,), self.SIZES[l + 1]),
+                                      return_pos=True)
+            lv.append(cent)
+        return lv
+
+    def __init__(self, dev, seed):
+        self.dev = dev
+        self._host_init(seed)
+        L = self.L = nat.load()
+        self.lv = self._levels(dev)
+        self.lptr = [t.to(dev) for t in self.lptr_h]
+        self.s = [t.to(dev) for t in self.s_h]
+        self.v = [t.to(dev) for t in self.v_h]
+        self.gs = [t.to(dev) for t in self.gs_h]
+        self.gv = [t.to(dev) for t in self.gv_h]
+        nq = [self.B * self.SIZES[l] for l in range(3)]
+        self.nq = nq
+        self.idx = [torch.empty(n, self.KNN, dtype=torch.int64, device=dev) for n in nq]
+        self.dist = [torch.empty(n, self.KNN, device=dev) for n in nq]
+        self.w = [torch.empty(n, self.KNN, device=dev) for n in nq]
+        self.so = [torch.empty(nq[l], self.CH[l], device=dev) for l in range(3)]
+        self.vo = [torch.empty(nq[l], self.CH[l] // 4, 3, device=dev) for l in range(3)]
+        self.gsrc_s = [torch.empty_like(t) for t in self.s]
+        self.gsrc_v = [torch.empty_like(t) for t in self.v]
+        self.ws_knn = [nat.workspace(L.gdl_knn_workspace_size(nq[l], self.B, self.KNN, self.SIZES[l + 1]), dev)
+                       for l in range(3)]
+        self.ws_bwd = [nat.workspace(L.gdl_knn_weighted_sum_backward_workspace_size(nq[l], self.KNN,
+                                                                                   self.B * self.SIZES[l + 1]), dev)
+                       for l in range(3)]
+        self._ptrs = []
+        for l in range(3):
+            go = (ctypes.c_void_p * 2)(self.gs[l].data_ptr(), self.gv[l].data_ptr())
+            gsrc = (ctypes.c_void_p * 2)(self.gsrc_s[l].data_ptr(), self.gsrc_v[l].data_ptr())
+            dims = (ctypes.c_int64 * 2)(self.CH[l], 3 * (self.CH[l] // 4))
+            self._ptrs.append((go, gsrc, dims))
+
+    def _s(self):
+        return torch.cuda.current_stream(self.dev).cuda_stream
+
+    def stage_knn(self):
+        for l in range(3):
+            ws = self.ws_knn[l]
+            nat.check(self.L.gdl_knn(self.lv[l].data_ptr(), self.lv[l + 1].data_ptr(), self.lptr[l].data_ptr(),
+                                     self.lptr[l + 1].data_ptr(), self.B, self.nq[l], self.KNN, self.SIZES[l + 1],
+                                     self.idx[l].data_ptr(), self.dist[l].data_ptr(), ws.data_ptr(), ws.numel(),
+                                     self._s()), "knn")
+
+    def stage_fwd(self):
+        for l in range(3):
+            n, k = self.nq[l], self.KNN
+            nat.check(self.L.gdl_knn_idw_weights(self.idx[l].data_ptr(), self.dist[l].data_ptr(), n, k,
+                                                 self.w[l].data_ptr(), self._s()), "idw")
+            for src, out, dim in ((self.s[l], self.so[l], self.CH[l]), (self.v[l], self.vo[l], 3 * (self.CH[l] // 4))):
+                nat.check(self.L.gdl_knn_weighted_sum(src.data_ptr(), src.shape[0], dim, self.idx[l].data_ptr(),
+                                                      self.w[l].data_ptr(), n, k, out.data_ptr(), self._s()), "wsum")
+
+    def stage_bwd(self):
+        for l in range(3):
+            go, gsrc, dims = self._ptrs[l]
+            ws = self.ws_bwd[l]
+            nat.check(self.L.gdl_knn_weighted_sum_backward(go, gsrc, dims, 2, self.idx[l].data_ptr(),
+                                                           self.w[l].data_ptr(), self.nq[l], self.KNN,
+                                                           self.s[l].shape[0], ws.data_ptr(), ws.numel(), self._s()),
+                      "wsum bwd")
+
+    def stage_list(self):
+        return [("knn", self.stage_knn), ("interp_fwd", self.stage_fwd), ("interp_bwd", self.stage_bwd)]
+
+    def step(self):
+        for _, fn in self.stage_list():
+            fn()
+
+    def edges(self):
+        return sum(n * self.KNN for n in self.nq)
+
+    def stage_bytes(self, E):
+        k = self.KNN
+        b = {"knn": 0, "interp_fwd": 0, "interp_bwd": 0}
+        for l in range(3):
+            nq, nc, D = self.nq[l], self.B * self.SIZES[l + 1], self.CH[l] + 3 * (self.CH[l] // 4)
+            b["knn"] += 12 * (nq + nc) + 12 * nq * k
+            # idx + dist in, weights out; per table idx + weights in, coarse rows once, output rows
+            b["interp_fwd"] += 12 * nq * k + 4 * nq * k + 2 * 12 * nq * k + 4 * nc * D + 4 * nq * D
+            # idx in, sorted pairs (keys + positions), per table grad rows in once, grad_src out
+            b["interp_bwd"] += 8 * nq * k + 16 * nq * k + 4 * nq * D + 4 * nc * D
+        return b
+
+    def e2e_step(self):
+        pos = self.pos_h.to(self.dev, non_blocking=True)
+        lv = [pos] + self.lv[1:]  # coarse levels come from the encoder; dense points are this step's input
+        outs = []
+        for l in range(3):
+            s = self.s[l].detach().requires_grad_(True)
+            v = self.v[l].detach().requires_grad_(True)
+            so, vo = F.knn_interpolate(lv[l], lv[l + 1], s, v, self.lptr[l], self.lptr[l + 1], self.KNN)
+            torch.autograd.backward([so, vo], [self.gs[l], self.gv[l]])
+            outs.append(so)
+        host = outs[-1].to("cpu", non_blocking=True)
+        torch.cuda.current_stream(self.dev).synchronize()
+        return host
+
+    e2e_h2d = property(lambda self: self.pos_h.numel() * 4)
+    e2e_d2h = property(lambda self: self.nq[2] * self.CH[2] * 4)
+
+    def cpu_step(self, O):
+        if not hasattr(self, "_cpu_levels"):
+            pos = self.pos_h.numpy()[:self.N]
+            lv = [pos]
+            for l in range(3):
+                idx = O.fps(lv[-1], [0, lv[-1].shape[0]], [self.SIZES[l + 1]], dist=O.DIST_CUDA)
+                lv.append(lv[-1][idx])
+            self._cpu_levels = lv
+        lv = self._cpu_levels
+        for l in range(3):
+            nd, nc = self.SIZES[l], self.SIZES[l + 1]
+            idx, dist = O.knn(lv[l], lv[l + 1], [0, nd], [0, nc], self.KNN, dist=O.DIST_CUDA)
+            w = O.knn_idw_weights(idx, dist)
+            s, v = self.s_h[l].numpy()[:nc], self.v_h[l].numpy()[:nc]
+            O.knn_weighted_sum(s, idx, w)
+            O.knn_weighted_sum(v, idx, w)
+            O.knn_weighted_sum_backward(self.gs_h[l].numpy()[:nd], idx, w, nc)
+            O.knn_weighted_sum_backward(self.gv_h[l].numpy()[:nd], idx, w, nc)
+
+
 class C4:
     """64 source/target pairs x 16384 points: KNN k=1 target->source, 6-channel residual
     features, segment sum per cloud (64 segments x 16384 rows)."""
@@ -811,7 +985,7 @@ class C5S(C5G):
         O.cloud_avg_degree(ns, ne)
 
 
-CONFIGS = {"c1": C1, "c2": C2, "c3": C3, "c4": C4, "c5": C5, "c5g": C5G, "c5s": C5S}
+CONFIGS = {"c1": C1, "c2": C2, "c3": C3, "c3i": C3I, "c4": C4, "c5": C5, "c5g": C5G, "c5s": C5S}
 
 
 

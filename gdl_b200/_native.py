@@ -47,6 +47,11 @@ PROTOTYPES = {
     "gdl_cloud_avg_degree_workspace_size": (_SZ, [_I32]),
     "gdl_cloud_avg_degree": (ctypes.c_int, [_P, _P, _I64, _P, _P, _I32, _P, _P, _SZ, _P]),
     "gdl_radius_csr_finish": (ctypes.c_int, [_P, _P, _I64, _I64, _P, _I32, _P, _P, _P, _P, _P, _P]),
+    "gdl_knn_idw_weights": (ctypes.c_int, [_P, _P, _I64, _I32, _P, _P]),
+    "gdl_knn_weighted_sum": (ctypes.c_int, [_P, _I64, _I64, _P, _P, _I64, _I32, _P, _P]),
+    "gdl_knn_weighted_sum_backward_workspace_size": (_SZ, [_I64, _I32, _I64]),
+    "gdl_knn_weighted_sum_backward": (ctypes.c_int, [_P, _P, _P, _I32, _P, _P, _I64, _I32, _I64, _P, _SZ, _P]),
+    "gdl_knn_weighted_sum_weight_grad": (ctypes.c_int, [_P, _P, _I64, _I64, _P, _I64, _I32, _I32, _P, _P]),
     "gdl_sort_and_build_csr_workspace_size": (_SZ, [_I64, _I64]),
     "gdl_sort_and_build_csr": (ctypes.c_int, [_P, _I64, _I64, _P, _P, _P, _P, _P, _SZ, _P]),
     "gdl_segment_reduce_workspace_size": (_SZ, [_I64, _I64]),

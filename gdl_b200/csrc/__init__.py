@@ -405,3 +405,85 @@ def gather_rows(src: torch.Tensor, idx: torch.Tensor, out: Optional[torch.Tensor
                                          idx.data_ptr(), idx.numel(), out.data_ptr(), nat.stream(dev)),
               "gdl_gather_rows")
     return out
+
+
+# --------------------------------------------------------------------------- KNN aggregation
+def _rows(t: torch.Tensor) -> torch.Tensor:
+    """[n, ...] float32 contiguous viewed as [n, dim]."""
+    t = t.contiguous()
+    if t.dtype != torch.float32:
+        t = t.float()
+    return t.reshape(t.shape[0], -1)
+
+
+def knn_idw_weights_cuda(idx: torch.Tensor, dist: torch.Tensor) -> torch.Tensor:
+    """Inverse-distance weights of EquivariantInterpolate (nn/modules/equivariant_interp.py:92-96)
+    from KNN output: w = inv / max(sum inv, 1e-8), inv = 1/sqrt(max(dist, 1e-4)), 0 for padding."""
+    dev = nat.require_cuda(idx, dist, what="knn_idw_weights_cuda")
+    idx = idx.to(torch.int64).contiguous()
+    dist = dist.contiguous().float()
+    n, k = idx.shape
+    w = torch.empty(n, k, dtype=torch.float32, device=dev)
+    nat.check(nat.load().gdl_knn_idw_weights(nat.ptr(idx) if w.numel() else None, nat.ptr(dist) if w.numel() else None,
+                                             n, k, nat.ptr(w) if w.numel() else None, nat.stream(dev)),
+              "gdl_knn_idw_weights")
+    return w
+
+
+def knn_weighted_sum_cuda(src: torch.Tensor, idx: torch.Tensor, weight: torch.Tensor) -> torch.Tensor:
+    """out[q] = sum_j weight[q, j] * src[idx[q, j]] over valid neighbours, shape [n_query, *src.shape[1:]]
+    (one pass, no [n_query, k, ...] gather)."""
+    dev = nat.require_cuda(src, idx, weight, what="knn_weighted_sum_cuda")
+    s2 = _rows(src)
+    idx = idx.to(torch.int64).contiguous()
+    weight = weight.contiguous().float()
+    n, k = idx.shape
+    out = torch.empty(n, *src.shape[1:], dtype=torch.float32, device=dev)
+    dim = s2.shape[1]
+    nat.check(nat.load().gdl_knn_weighted_sum(nat.ptr(s2) if s2.numel() else None, s2.shape[0], dim,
+                                              nat.ptr(idx) if idx.numel() else None,
+                                              nat.ptr(weight) if weight.numel() else None, n, k,
+                                              nat.ptr(out) if out.numel() else None, nat.stream(dev)),
+              "gdl_knn_weighted_sum")
+    return out
+
+
+def knn_weighted_sum_backward_cuda(grad_outs, idx: torch.Tensor, weight: torch.Tensor, src_shapes):
+    """Gradients w.r.t. the source tables of knn_weighted_sum_cuda: one transposed (sorted) pair
+    list shared by all tables, deterministic fp32 folds. ``src_shapes``: shapes of the sources."""
+    dev = nat.require_cuda(idx, weight, what="knn_weighted_sum_backward_cuda")
+    idx = idx.to(torch.int64).contiguous()
+    weight = weight.contiguous().float()
+    n, k = idx.shape
+    n_src = int(src_shapes[0][0]) if src_shapes else 0
+    gos = [_rows(g) for g in grad_outs]
+    outs = [torch.empty(*shp, dtype=torch.float32, device=dev) for shp in src_shapes]
+    o2 = [o.reshape(o.shape[0], -1) for o in outs]
+    T = len(gos)
+    gop = (ctypes.c_void_p * max(T, 1))(*[g.data_ptr() for g in gos])
+    osp = (ctypes.c_void_p * max(T, 1))(*[o.data_ptr() for o in o2])
+    dims = (ctypes.c_int64 * max(T, 1))(*[o.shape[1] for o in o2])
+    L = nat.load()
+    ws = nat.workspace(L.gdl_knn_weighted_sum_backward_workspace_size(n, k, n_src), dev)
+    nat.check(L.gdl_knn_weighted_sum_backward(gop, osp, dims, T, nat.ptr(idx) if idx.numel() else None,
+                                              nat.ptr(weight) if weight.numel() else None, n, k, n_src,
+                                              ws.data_ptr(), ws.numel(), nat.stream(dev)),
+              "gdl_knn_weighted_sum_backward")
+    return outs
+
+
+def knn_weighted_sum_weight_grad_cuda(grad_outs, srcs, idx: torch.Tensor) -> torch.Tensor:
+    """grad_weight[q, j] = sum over tables of sum_c grad_out[q, c] * src[idx[q, j], c]."""
+    dev = nat.require_cuda(idx, what="knn_weighted_sum_weight_grad_cuda")
+    idx = idx.to(torch.int64).contiguous()
+    n, k = idx.shape
+    gw = torch.zeros(n, k, dtype=torch.float32, device=dev)
+    L = nat.load()
+    for t, (g, s) in enumerate(zip(grad_outs, srcs)):
+        g2, s2 = _rows(g), _rows(s)
+        nat.check(L.gdl_knn_weighted_sum_weight_grad(nat.ptr(g2) if g2.numel() else None,
+                                                     nat.ptr(s2) if s2.numel() else None, s2.shape[0], s2.shape[1],
+                                                     nat.ptr(idx) if idx.numel() else None, n, k, int(t > 0),
+                                                     nat.ptr(gw) if gw.numel() else None, nat.stream(dev)),
+                  "gdl_knn_weighted_sum_weight_grad")
+    return gw

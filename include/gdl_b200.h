@@ -181,6 +181,38 @@ int gdl_radius_csr_finish(const int64_t *row_ptr, const int64_t *dst, int64_t n_
                           const int64_t *ptr, int32_t num_clouds, int32_t *col_sorted, int32_t *perm,
                           int32_t *node_start, int32_t *node_end, float *avg_degree, void *stream);
 
+/* -------------------------------------------------------------------- KNN aggregation
+ * Replaces the weighted neighbour sums of the reference's KNN consumers, which gather
+ * [n_query, k, dim] rows with torch indexing and reduce them over k:
+ *   EquivariantPool         s_out = (w[..., None] * scalars[idx]).sum(1), v_out likewise
+ *                           (nn/modules/equivariant_pool.py:395-420)
+ *   EquivariantInterpolate  inverse-distance weights + the same sums for s, v, t2
+ *                           (nn/modules/equivariant_interp.py:91-125)
+ * idx [n_query, k] i64 (KNN output; entries < 0 or >= n_src are skipped), rows f32.
+ *
+ * gdl_knn_idw_weights: out_weight[q, j] = inv_j / max(sum_j inv_j, 1e-8) with
+ *   inv_j = 1 / sqrt(max(dist[q, j], 1e-4)), 0 where idx[q, j] < 0 (dist = squared distances).
+ * gdl_knn_weighted_sum: out[q, :] = sum_j weight[q, j] * src[idx[q, j], :], src [n_src, dim],
+ *   out [n_query, dim]; an fp32 fold in j order from 0, products rounded first.
+ * gdl_knn_weighted_sum_backward: grad_src[t][s, :] = sum over the (q, j) with idx[q, j] = s, in
+ *   (q, j) order, of weight[q, j] * grad_out[t][q, :], for n_tables tables sharing idx/weight
+ *   (host arrays of device pointers and dims). Deterministic (sorted pairs, no atomics).
+ * gdl_knn_weighted_sum_weight_grad: grad_weight[q, j] (+= if accumulate) sum_c grad_out[q, c] *
+ *   src[idx[q, j], c]; 0 for skipped pairs.
+ * No counterpart kernels in the reference (torch indexing, mul and sum there).
+ */
+int gdl_knn_idw_weights(const int64_t *idx, const float *dist, int64_t n_query, int32_t k, float *out_weight,
+                        void *stream);
+int gdl_knn_weighted_sum(const float *src, int64_t n_src, int64_t dim, const int64_t *idx, const float *weight,
+                         int64_t n_query, int32_t k, float *out, void *stream);
+size_t gdl_knn_weighted_sum_backward_workspace_size(int64_t n_query, int32_t k, int64_t n_src);
+int gdl_knn_weighted_sum_backward(const float *const *grad_out, float *const *grad_src, const int64_t *dims,
+                                  int32_t n_tables, const int64_t *idx, const float *weight, int64_t n_query,
+                                  int32_t k, int64_t n_src, void *workspace, size_t workspace_bytes, void *stream);
+int gdl_knn_weighted_sum_weight_grad(const float *grad_out, const float *src, int64_t n_src, int64_t dim,
+                                     const int64_t *idx, int64_t n_query, int32_t k, int32_t accumulate,
+                                     float *grad_weight, void *stream);
+
 /* -------------------------------------------------------------------------- CSR build
  * Replaces sort_and_build_csr(col, N) -- geoembodied/csrc/segment_reduce_kernel.cu:100-169.
  * col [num_edges] i64 in [0, num_nodes). Stable sort by destination:

@@ -662,3 +662,80 @@ int gdl_oracle_cloud_avg_degree(const int32_t *ns, const int32_t *ne, int64_t n,
     free(sum); free(cnt); free(cl);
     return 0;
 }
+
+/* ---------------------------------------------------------------- KNN aggregation
+ * EquivariantInterpolate (nn/modules/equivariant_interp.py:91-125) and the weighted sums of
+ * EquivariantPool (nn/modules/equivariant_pool.py:395-420):
+ *   idw:  inv_j = 1 / sqrtf(max(dist, 1e-4)) (0 where idx < 0), s = sum_j inv_j in j order,
+ *         w_j = inv_j / max(s, 1e-8)
+ *   sum:  out[q] = sum_j w[q,j] * src[idx[q,j]] in j order from 0, product rounded first;
+ *         neighbours outside [0, n_src) are skipped
+ *   bwd:  grad_src[s] = sum over (q, j) ascending with idx = s of w[q,j] * grad_out[q]
+ *   wgrad: per (q, j), 32 lane-strided partial sums over c then a xor butterfly (16, 8, 4, 2, 1)
+ *         -- the fixed order the GPU kernel uses (the reference's order is torch's).
+ */
+int gdl_oracle_knn_idw_weights(const int64_t *idx, const float *dist, int64_t n_q, int K, float *w) {
+    for (int64_t q = 0; q < n_q; ++q) {
+        float s = 0.0f;
+        for (int k = 0; k < K; ++k) {
+            float v = 0.0f;
+            if (idx[q * K + k] >= 0) {
+                float d = dist[q * K + k];
+                d = d < 1e-4f ? 1e-4f : d;
+                v = 1.0f / sqrtf(d);
+            }
+            s = s + v;
+            w[q * K + k] = v;
+        }
+        s = s < 1e-8f ? 1e-8f : s;
+        for (int k = 0; k < K; ++k) w[q * K + k] = w[q * K + k] / s;
+    }
+    return 0;
+}
+
+int gdl_oracle_knn_weighted_sum(const float *src, int64_t n_src, int64_t dim, const int64_t *idx, const float *w,
+                                int64_t n_q, int K, float *out) {
+    for (int64_t q = 0; q < n_q; ++q)
+        for (int64_t c = 0; c < dim; ++c) {
+            float acc = 0.0f;
+            for (int k = 0; k < K; ++k) {
+                const int64_t s = idx[q * K + k];
+                if (s >= 0 && s < n_src) acc = acc + w[q * K + k] * src[s * dim + c];
+            }
+            out[q * dim + c] = acc;
+        }
+    return 0;
+}
+
+int gdl_oracle_knn_weighted_sum_backward(const float *gout, int64_t dim, const int64_t *idx, const float *w,
+                                         int64_t n_q, int K, int64_t n_src, float *gsrc) {
+    for (int64_t i = 0; i < n_src * dim; ++i) gsrc[i] = 0.0f;
+    for (int64_t q = 0; q < n_q; ++q)
+        for (int k = 0; k < K; ++k) {
+            const int64_t s = idx[q * K + k];
+            if (s < 0 || s >= n_src) continue;
+            for (int64_t c = 0; c < dim; ++c) gsrc[s * dim + c] = gsrc[s * dim + c] + w[q * K + k] * gout[q * dim + c];
+        }
+    return 0;
+}
+
+int gdl_oracle_knn_weighted_sum_weight_grad(const float *gout, const float *src, int64_t n_src, int64_t dim,
+                                            const int64_t *idx, int64_t n_q, int K, int accumulate, float *gw) {
+    for (int64_t p = 0; p < n_q * K; ++p) {
+        float lanes[32];
+        const int64_t s = idx[p];
+        for (int l = 0; l < 32; ++l) {
+            float a = 0.0f;
+            if (s >= 0 && s < n_src)
+                for (int64_t c = l; c < dim; c += 32) a = a + gout[(p / K) * dim + c] * src[s * dim + c];
+            lanes[l] = a;
+        }
+        for (int off = 16; off > 0; off >>= 1) {
+            float nxt[32];
+            for (int l = 0; l < 32; ++l) nxt[l] = lanes[l] + lanes[l ^ off];
+            for (int l = 0; l < 32; ++l) lanes[l] = nxt[l];
+        }
+        gw[p] = accumulate ? gw[p] + lanes[0] : lanes[0];
+    }
+    return 0;
+}

@@ -77,6 +77,10 @@ def lib() -> ctypes.CDLL:
         L.gdl_oracle_radius_grid.argtypes = [P, i64, ctypes.c_float, P, P]
         L.gdl_oracle_edge_geometry.argtypes = [P, i64, P, P, i64, P, P, P, P, i32]
         L.gdl_oracle_cloud_avg_degree.argtypes = [P, P, i64, P, P, i32, P]
+        L.gdl_oracle_knn_idw_weights.argtypes = [P, P, i64, i32, P]
+        L.gdl_oracle_knn_weighted_sum.argtypes = [P, i64, i64, P, P, i64, i32, P]
+        L.gdl_oracle_knn_weighted_sum_backward.argtypes = [P, i64, P, P, i64, i32, i64, P]
+        L.gdl_oracle_knn_weighted_sum_weight_grad.argtypes = [P, P, i64, i64, P, i64, i32, i32, P]
         _lib = L
     return _lib
 
@@ -238,6 +242,52 @@ def cloud_avg_degree(node_start, node_end, batch=None, ptr=None, num_clouds=None
     lib().gdl_oracle_cloud_avg_degree(_p(ns), _p(ne), n, None if b is None else _p(b), None if p is None else _p(p),
                                       B, _p(out))
     return out
+
+
+def knn_idw_weights(idx, dist) -> np.ndarray:
+    idx = _c(idx, np.int64)
+    dist = _c(dist, np.float32)
+    n, k = idx.shape
+    w = np.zeros((n, k), np.float32)
+    lib().gdl_oracle_knn_idw_weights(_p(idx), _p(dist), n, k, _p(w))
+    return w
+
+
+def knn_weighted_sum(src, idx, w) -> np.ndarray:
+    src = _c(src, np.float32)
+    shape = src.shape
+    s2 = src.reshape(shape[0], -1)
+    idx = _c(idx, np.int64)
+    w = _c(w, np.float32)
+    n, k = idx.shape
+    out = np.zeros((n, s2.shape[1]), np.float32)
+    lib().gdl_oracle_knn_weighted_sum(_p(s2), s2.shape[0], s2.shape[1], _p(idx), _p(w), n, k, _p(out))
+    return out.reshape((n,) + shape[1:])
+
+
+def knn_weighted_sum_backward(grad_out, idx, w, n_src: int) -> np.ndarray:
+    g = _c(grad_out, np.float32)
+    shape = g.shape
+    g2 = g.reshape(shape[0], -1)
+    idx = _c(idx, np.int64)
+    w = _c(w, np.float32)
+    n, k = idx.shape
+    out = np.zeros((n_src, g2.shape[1]), np.float32)
+    lib().gdl_oracle_knn_weighted_sum_backward(_p(g2), g2.shape[1], _p(idx), _p(w), n, k, n_src, _p(out))
+    return out.reshape((n_src,) + shape[1:])
+
+
+def knn_weighted_sum_weight_grad(grad_outs, srcs, idx) -> np.ndarray:
+    idx = _c(idx, np.int64)
+    n, k = idx.shape
+    gw = np.zeros((n, k), np.float32)
+    for t, (g, s) in enumerate(zip(grad_outs, srcs)):
+        g2 = _c(g, np.float32).reshape(n, -1)
+        s2 = _c(s, np.float32)
+        s2 = s2.reshape(s2.shape[0], -1)
+        lib().gdl_oracle_knn_weighted_sum_weight_grad(_p(g2), _p(s2), s2.shape[0], s2.shape[1], _p(idx), n, k,
+                                                      int(t > 0), _p(gw))
+    return gw
 
 
 def bf16_bits(x: np.ndarray) -> np.ndarray:

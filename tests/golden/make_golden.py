@@ -16,6 +16,8 @@ inputs, what the reference's public entry points return on the CPU:
 * ``nn.modules.spatial_graph.SpatialGraph.build`` / ``from_edge_index`` and
   ``functional.radius_graph.compute_edge_vectors`` + the spherical harmonics' torch path
   (``kernels.triton_sph_harm._spherical_harmonics_pytorch``) -> ``golden_graph.npz``.
+* ``nn.modules.equivariant_interp.EquivariantInterpolate`` forward/backward and the weighted-sum
+  lines of ``EquivariantPool`` -> ``golden_aggregate.npz``.
 
 Inputs that would make the CPU path and the CUDA kernels disagree for reasons the
 reference itself documents (exact distance ties, pairs at the radius boundary where
@@ -303,6 +305,70 @@ def gen_graph(root: str, R, out):
         out[f"geo_Y{lmax}"] = sph(direction, lmax).numpy()
 
 
+def _ref_module_file(root: str, rel: str, name: str):
+    import importlib.util
+
+    spec = importlib.util.spec_from_file_location(name, Path(root) / rel)
+    mod = importlib.util.module_from_spec(spec)
+    sys.modules[name] = mod
+    spec.loader.exec_module(mod)
+    return mod
+
+
+def gen_aggregate(root: str, out):
+    """EquivariantInterpolate.forward + backward (nn/modules/equivariant_interp.py:58-139) and the
+    weighted-sum block of EquivariantPool (nn/modules/equivariant_pool.py:395-420, its three
+    formula lines evaluated on the same gathers) + backward, on the CPU."""
+    EI = _ref_module_file(root, "geoembodied/nn/modules/equivariant_interp.py", "ref_equivariant_interp")
+    g = torch.Generator().manual_seed(21)
+    nd, nc = [500, 37, 420], [120, 2, 90]  # a coarse cloud of 2 points pads KNN k=3
+    dense = torch.rand(sum(nd), 3, generator=g)
+    coarse = torch.rand(sum(nc), 3, generator=g)
+    ptr_d = torch.tensor([0] + list(np.cumsum(nd)), dtype=torch.int64)
+    ptr_c = torch.tensor([0] + list(np.cumsum(nc)), dtype=torch.int64)
+    s = torch.randn(sum(nc), 16, generator=g, requires_grad=True)
+    v = torch.randn(sum(nc), 8, 3, generator=g, requires_grad=True)
+    t2 = torch.randn(sum(nc), 4, 5, generator=g, requires_grad=True)
+    s_skip = torch.randn(sum(nd), 6, generator=g)
+    v_skip = torch.randn(sum(nd), 2, 3, generator=g)
+    so, vo, to = EI.EquivariantInterpolate(3)(dense, coarse, s, v, ptr_d, ptr_c, s_skip, v_skip, t2, None)
+    gs, gv, gt = (torch.randn(t.shape, generator=g) for t in (so, vo, to))
+    torch.autograd.backward([so, vo, to], [gs, gv, gt])
+    for k, t in dict(dense=dense, coarse=coarse, ptr_d=ptr_d, ptr_c=ptr_c, s=s, v=v, t2=t2, s_skip=s_skip,
+                     v_skip=v_skip, s_out=so, v_out=vo, t2_out=to, g_s=gs, g_v=gv, g_t2=gt, grad_s=s.grad,
+                     grad_v=v.grad, grad_t2=t2.grad).items():
+        out["interp_" + k] = t.detach().numpy()
+
+    # pool block: KNN k=16 of 64 seeds per cloud into clouds of 200 / 9 / 150 points (padding in the
+    # 9-point cloud), attention-like weights from a masked softmax
+    knn = importlib_module("geoembodied.functional.knn").knn
+    npts, nseed = [200, 9, 150], [64, 5, 64]
+    pos = torch.rand(sum(npts), 3, generator=g)
+    ptr = torch.tensor([0] + list(np.cumsum(npts)), dtype=torch.int64)
+    seeds = torch.cat([pos[int(ptr[b]):int(ptr[b]) + nseed[b]] for b in range(3)])
+    ptr_s = torch.tensor([0] + list(np.cumsum(nseed)), dtype=torch.int64)
+    knn_idx, _ = knn(seeds, pos, ptr_s, ptr, 16)
+    valid = knn_idx >= 0
+    logits = torch.randn(knn_idx.shape, generator=g).masked_fill(~valid, float("-inf"))
+    w = torch.softmax(logits, dim=-1).requires_grad_(True)
+    scalars = torch.randn(sum(npts), 32, generator=g, requires_grad=True)
+    vectors = torch.randn(sum(npts), 4, 3, generator=g, requires_grad=True)
+    safe_idx = knn_idx.clamp(min=0)
+    s_out = (w.unsqueeze(-1) * scalars[safe_idx]).sum(dim=1)
+    v_out = (w.unsqueeze(-1).unsqueeze(-1) * vectors[safe_idx]).sum(dim=1)
+    gs2, gv2 = torch.randn(s_out.shape, generator=g), torch.randn(v_out.shape, generator=g)
+    torch.autograd.backward([s_out, v_out], [gs2, gv2])
+    for k, t in dict(idx=knn_idx, w=w, scalars=scalars, vectors=vectors, s_out=s_out, v_out=v_out, g_s=gs2,
+                     g_v=gv2, grad_s=scalars.grad, grad_v=vectors.grad, grad_w=w.grad).items():
+        out["pool_" + k] = t.detach().numpy()
+
+
+def importlib_module(name: str):
+    import importlib
+
+    return importlib.import_module(name)
+
+
 def main():
     root = sys.argv[1] if len(sys.argv) > 1 else "/root/reference"
     F, K, R, S = _ref(root)
@@ -318,6 +384,10 @@ def main():
     gen_graph(root, R, graph)
     np.savez_compressed(HERE / "golden_graph.npz", **graph)
     print("wrote", HERE / "golden_graph.npz", sum(v.nbytes for v in graph.values()) / 1e6, "MB raw")
+    agg = {}
+    gen_aggregate(root, agg)
+    np.savez_compressed(HERE / "golden_aggregate.npz", **agg)
+    print("wrote", HERE / "golden_aggregate.npz", sum(v.nbytes for v in agg.values()) / 1e6, "MB raw")
 
 
 if __name__ == "__main__":
