@@ -199,3 +199,8 @@ def test_spatial_graph_full_size_lidar_geometry(oracle):
     assert bits_equal(out["direction"][:E].cpu().numpy()[pick], direction)
     assert bits_equal(out["sph"][:E].cpu().numpy()[pick], sph)
     assert float(out["dist"][:E].max()) < 1.0
+    # the COO entry point over the same edges writes the same bits on every edge
+    _, d2, u2, y2 = csrc.edge_geometry_cuda(xd, out["src"][:E], out["dst"][:E], max_l=2, with_diff=False)
+    assert torch.equal(d2.view(torch.int32), out["dist"][:E].view(torch.int32))
+    assert torch.equal(u2.view(torch.int32), out["direction"][:E].view(torch.int32))
+    assert torch.equal(y2.view(torch.int32), out["sph"][:E].view(torch.int32))
