@@ -18,6 +18,8 @@ inputs with the shapes of the reference's use cases; see gdl_b200/synthetic.py):
   c5            8 clouds x 131072 LiDAR points: FPS -> 16384, radius graph (r = 1 m, 64),
                 segment sum of 64-channel features.
   c5g           (auxiliary) c5's clouds: radius graph r = 1 m, 64 over all points, segment sum.
+  c5h           (auxiliary) c5 with the reference encoder's hybrid graph (radius graph + symmetric
+                KNN-3 fallback, deduplicated, with edge geometry) over the FPS centroids.
   c5s           (auxiliary) c5's clouds: SpatialGraph.build -- radius graph r = 1 m, 64 over all
                 points with each edge's distance, direction and l <= 2 spherical harmonics, the
                 CSR fields and the per-cloud average degree.
@@ -909,6 +911,124 @@ class C5G(C5):
                          rp[1:].astype(np.int32), self.N, "sum")
 
 
+class C5H(C5):
+    """Config 5 with the reference encoder's hybrid graph in place of the plain radius graph
+    (_EncoderStage._build_hybrid_graph, nn/modules/multi_scale_se3_net.py:126-219): FPS 16384 per
+    LiDAR cloud, radius graph r = 1 m / 64 over the centroids (empty: FPS leaves them >= 1.75 m
+    apart), self-KNN k = 4, both directions of the 3 nearest for every node with fewer than 3
+    radius in-edges, deduplicated in (row, col) order with its CSR and each edge's distance,
+    direction and l <= 2 harmonics, the per-node average degree, and the segment sum of
+    64-channel features over the resulting graph."""
+    name = "c5h"
+    metric = ("points/sec (FPS 16384 + hybrid radius r=1 k=64 / KNN-3 fallback graph with edge geometry + "
+              "segment sum C=64), config 5")
+    KF = 3
+    MAX_L = 2
+
+    @property
+    def launches_per_step(self):
+        bits = 1
+        while bits < 32 and (1 << bits) <= self.nc:
+            bits += 1
+        radix = 1 + 4 * ((bits + 7) // 8)
+        # fps 1; radius (general path) 25 - 2 segment launches of C5's count; knn 5; hybrid: count,
+        # scan 3, fill, unique, scan 3, emit, radix, order; avg degree 2; segment 2
+        return 1 + 23 + 5 + (1 + 3 + 1 + 1 + 3 + 1 + radix + 1) + 2 + 2
+
+    def __init__(self, dev, seed):
+        super().__init__(dev, seed)
+        L = self.L
+        nc = self.nc
+        self.cap_h = int(L.gdl_hybrid_graph_capacity(nc, self.NN, self.KF))
+        i64, i32 = dict(dtype=torch.int64, device=dev), dict(dtype=torch.int32, device=dev)
+        f = dict(dtype=torch.float32, device=dev)
+        self.knn_idx = torch.empty(nc, self.KF + 1, **i64)
+        self.knn_d = torch.empty(nc, self.KF + 1, **f)
+        self.h_rp = torch.empty(nc + 1, **i64)
+        self.h_row, self.h_col = torch.empty(self.cap_h, **i64), torch.empty(self.cap_h, **i64)
+        self.h_cs, self.h_perm = torch.empty(self.cap_h, **i32), torch.empty(self.cap_h, **i32)
+        self.h_src = torch.empty(self.cap_h, **i32)
+        self.h_ns, self.h_ne = torch.empty(nc, **i32), torch.empty(nc, **i32)
+        self.dist = torch.empty(self.cap_h, **f)
+        self.direction = torch.empty(self.cap_h, 3, **f)
+        self.sph = torch.empty(self.cap_h, (self.MAX_L + 1) ** 2, **f)
+        self.avg = torch.empty(nc, **f)
+        self.geom = nat.EdgeGeometry(None, self.dist.data_ptr(), self.direction.data_ptr(), self.sph.data_ptr(),
+                                     self.MAX_L)
+        self.ws_knn = nat.workspace(L.gdl_knn_workspace_size(nc, self.B, self.KF + 1, self.K), dev)
+        self.ws_h = nat.workspace(L.gdl_hybrid_graph_workspace_size(nc, self.NN, self.KF), dev)
+        self.ws_avg = nat.workspace(L.gdl_cloud_avg_degree_workspace_size(self.B), dev)
+        self.ws_seg_h = nat.workspace(L.gdl_segment_reduce_workspace_size(self.cap_h, nc), dev)
+
+    def stage_knn(self):
+        nat.check(self.L.gdl_knn(self.cent.data_ptr(), self.cent.data_ptr(), self.cptr.data_ptr(), self.cptr.data_ptr(),
+                                 self.B, self.nc, self.KF + 1, self.K, self.knn_idx.data_ptr(), self.knn_d.data_ptr(),
+                                 self.ws_knn.data_ptr(), self.ws_knn.numel(), self._s()), "knn")
+
+    def stage_hybrid(self):
+        nat.check(self.L.gdl_hybrid_graph(self.cent.data_ptr(), self.row_ptr.data_ptr(), self.src.data_ptr(),
+                                          self.knn_idx.data_ptr(), self.nc, self.NN, self.KF, self.h_rp.data_ptr(),
+                                          self.h_row.data_ptr(), self.h_col.data_ptr(), self.h_cs.data_ptr(),
+                                          self.h_perm.data_ptr(), self.h_src.data_ptr(), self.h_ns.data_ptr(),
+                                          self.h_ne.data_ptr(), ctypes.byref(self.geom), self.ws_h.data_ptr(),
+                                          self.ws_h.numel(), self._s()), "hybrid")
+        nat.check(self.L.gdl_cloud_avg_degree(self.h_ns.data_ptr(), self.h_ne.data_ptr(), self.nc, None,
+                                              self.cptr.data_ptr(), self.B, self.avg.data_ptr(),
+                                              self.ws_avg.data_ptr(), self.ws_avg.numel(), self._s()), "avg degree")
+
+    def stage_seg(self):
+        nat.check(self.L.gdl_segment_reduce(self.feat.data_ptr(), 0, self.nc, self.C, self.h_src.data_ptr(),
+                                            self.h_ns.data_ptr(), self.h_ne.data_ptr(), self.nc, 0, self.out.data_ptr(),
+                                            None, self.ws_seg_h.data_ptr(), self.ws_seg_h.numel(), self._s()),
+                  "segment")
+
+    def stage_list(self):
+        return [("fps", self.stage_fps), ("radius_graph", self.stage_radius), ("knn", self.stage_knn),
+                ("hybrid_graph", self.stage_hybrid), ("segment_sum", self.stage_seg)]
+
+    def edges(self):
+        return int(self.h_rp[-1].item())
+
+    def stage_bytes(self, E):
+        nc, C = self.nc, self.C
+        b = super().stage_bytes(E)
+        k = self.KF + 1
+        b["knn"] = 12 * 2 * nc + 12 * nc * k
+        # radius CSR + knn in; per edge (row, col) i64 + col_sorted, perm, src_sorted i32 + dist,
+        # direction, 9 harmonics out; node start/end + average degree
+        b["hybrid_graph"] = 8 * (nc + 1) + 8 * nc * k + E * (16 + 12 + 52) + 20 * nc
+        b["segment_sum"] = 4 * E * C + 4 * nc * C + 4 * (E + 2 * nc)
+        return b
+
+    def e2e_step(self):
+        from gdl_b200.hybrid_graph import build_hybrid_graph
+        pos = self.pos_h.to(self.dev, non_blocking=True)
+        feat = self.feat_h.to(self.dev, non_blocking=True)
+        idx, cent = csrc.fps_cuda(pos, self.ptr_h, self.k_h, return_pos=True)
+        g = build_hybrid_graph(cent, self.R, self.cptr_h, max_num_neighbors=self.NN, knn_fallback_k=self.KF)
+        src_of_slot = g.row[g.perm.long()].to(torch.int32)
+        out = csrc.segment_reduce_cuda(feat, src_of_slot, g.node_start, g.node_end, self.nc, "sum")
+        host = out.to("cpu", non_blocking=True)
+        torch.cuda.current_stream(self.dev).synchronize()
+        return host
+
+    cpu_clouds = 1
+    cpu_fraction = (2048 / 16384) / 8
+    cpu_sample = ("FPS of 2048 of 16384 picks on 1 of 8 clouds per sample, scaled x64 (FPS dominates this step; "
+                  "the hybrid graph of those centroids runs in the same sample)")
+
+    def cpu_step(self, O):
+        pos = self.pos_h.numpy()[:self.N]
+        idx = O.fps(pos, [0, self.N], [self.cpu_picks], dist=O.DIST_CUDA)
+        cent = pos[idx]
+        n = cent.shape[0]
+        rp, src = O.radius_graph(cent, np.array([0, n]), self.R, self.NN, dist=O.DIST_CUDA)
+        knn_idx, _ = O.knn(cent, cent, [0, n], [0, n], self.KF + 1, dist=O.DIST_CUDA)
+        row, col = O.hybrid_graph(rp, src, knn_idx, self.KF)
+        O.edge_geometry(cent, row, col, max_l=self.MAX_L)
+        O.sort_and_build_csr(col, n)
+
+
 class C5S(C5G):
     """Auxiliary graph-geometry workload (the reference's SpatialGraph.build, nn/modules/
     spatial_graph.py:88-167, on config 5's clouds): radius graph r = 1 m, 64 neighbours over all
@@ -985,7 +1105,7 @@ class C5S(C5G):
         O.cloud_avg_degree(ns, ne)
 
 
-CONFIGS = {"c1": C1, "c2": C2, "c3": C3, "c3i": C3I, "c4": C4, "c5": C5, "c5g": C5G, "c5s": C5S}
+CONFIGS = {"c1": C1, "c2": C2, "c3": C3, "c3i": C3I, "c4": C4, "c5": C5, "c5g": C5G, "c5h": C5H, "c5s": C5S}
 
 
 

@@ -47,6 +47,10 @@ PROTOTYPES = {
     "gdl_cloud_avg_degree_workspace_size": (_SZ, [_I32]),
     "gdl_cloud_avg_degree": (ctypes.c_int, [_P, _P, _I64, _P, _P, _I32, _P, _P, _SZ, _P]),
     "gdl_radius_csr_finish": (ctypes.c_int, [_P, _P, _I64, _I64, _P, _I32, _P, _P, _P, _P, _P, _P]),
+    "gdl_hybrid_graph_capacity": (_I64, [_I64, _I32, _I32]),
+    "gdl_hybrid_graph_workspace_size": (_SZ, [_I64, _I32, _I32]),
+    "gdl_hybrid_graph": (ctypes.c_int,
+                         [_P, _P, _P, _P, _I64, _I32, _I32, _P, _P, _P, _P, _P, _P, _P, _P, _PG, _P, _SZ, _P]),
     "gdl_knn_idw_weights": (ctypes.c_int, [_P, _P, _I64, _I32, _P, _P]),
     "gdl_knn_weighted_sum": (ctypes.c_int, [_P, _I64, _I64, _P, _P, _I64, _I32, _P, _P]),
     "gdl_knn_weighted_sum_backward_workspace_size": (_SZ, [_I64, _I32, _I64]),

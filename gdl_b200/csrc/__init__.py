@@ -487,3 +487,43 @@ def knn_weighted_sum_weight_grad_cuda(grad_outs, srcs, idx: torch.Tensor) -> tor
                                                      nat.ptr(gw) if gw.numel() else None, nat.stream(dev)),
                   "gdl_knn_weighted_sum_weight_grad")
     return gw
+
+
+# --------------------------------------------------------------------------- hybrid graph
+def hybrid_graph_cuda(radius_row_ptr: torch.Tensor, radius_src: torch.Tensor, knn_idx: Optional[torch.Tensor],
+                      N: int, max_num_neighbors: int, knn_fallback_k: int, x: Optional[torch.Tensor] = None,
+                      max_l: Optional[int] = None) -> dict:
+    """Radius edges + symmetric KNN fallback edges for nodes with fewer than knn_fallback_k
+    radius in-edges, deduplicated in (row, col) order (multi_scale_se3_net.py:126-219), with
+    the CSR of sort_and_build_csr(col) and, when ``x`` is given, each edge's distance and
+    direction (+ harmonics up to ``max_l``). Returns device tensors: ``row_ptr`` [N+1] (E at
+    [N]), ``row`` / ``col`` [cap] int64, ``col_sorted`` / ``perm`` / ``src_sorted`` [cap] int32,
+    ``node_start`` / ``node_end`` [N] int32, ``dist`` / ``direction`` / ``sph`` (or None); the
+    first E slots of the edge arrays are valid."""
+    dev = nat.require_cuda(radius_row_ptr, radius_src, what="hybrid_graph_cuda")
+    L = nat.load()
+    kf = int(knn_fallback_k)
+    cap = max(int(L.gdl_hybrid_graph_capacity(N, int(max_num_neighbors), kf)), 1)
+    knn_idx = None if (knn_idx is None or kf == 0) else knn_idx.to(torch.int64).contiguous()
+    i64 = dict(dtype=torch.int64, device=dev)
+    i32 = dict(dtype=torch.int32, device=dev)
+    out = dict(row_ptr=torch.empty(N + 1, **i64), row=torch.empty(cap, **i64), col=torch.empty(cap, **i64),
+               col_sorted=torch.empty(cap, **i32), perm=torch.empty(cap, **i32), src_sorted=torch.empty(cap, **i32),
+               node_start=torch.empty(max(N, 1), **i32), node_end=torch.empty(max(N, 1), **i32))
+    g = None
+    if x is not None:
+        x = x.contiguous().float()
+        g = _GeomOut(max_l, False)
+        gp = g(cap, dev)
+    ws = nat.workspace(L.gdl_hybrid_graph_workspace_size(N, int(max_num_neighbors), kf), dev)
+    nat.check(L.gdl_hybrid_graph(nat.ptr(x) if (x is not None and N) else None, radius_row_ptr.data_ptr(),
+                                 radius_src.data_ptr(), nat.ptr(knn_idx), N, int(max_num_neighbors), kf,
+                                 out["row_ptr"].data_ptr(), out["row"].data_ptr(), out["col"].data_ptr(),
+                                 out["col_sorted"].data_ptr(), out["perm"].data_ptr(), out["src_sorted"].data_ptr(),
+                                 out["node_start"].data_ptr(), out["node_end"].data_ptr(), gp if g else None,
+                                 ws.data_ptr(), ws.numel(), nat.stream(dev)), "gdl_hybrid_graph")
+    out["node_start"], out["node_end"] = out["node_start"][:N], out["node_end"][:N]
+    out["dist"] = g.dist if g else None
+    out["direction"] = g.direction if g else None
+    out["sph"] = g.sph if g else None
+    return out

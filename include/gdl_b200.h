@@ -181,6 +181,33 @@ int gdl_radius_csr_finish(const int64_t *row_ptr, const int64_t *dst, int64_t n_
                           const int64_t *ptr, int32_t num_clouds, int32_t *col_sorted, int32_t *perm,
                           int32_t *node_start, int32_t *node_end, float *avg_degree, void *stream);
 
+/* ------------------------------------------------------------------------ hybrid graph
+ * Replaces _EncoderStage._build_hybrid_graph (geoembodied/nn/modules/multi_scale_se3_net.py:
+ * 126-219) up to its SpatialGraph: radius edges, plus both directions of (q, m) for every node
+ * q with fewer than knn_fallback_k radius in-edges and each valid m of knn_idx[q, 1 ..
+ * knn_fallback_k] (knn_self with k = knn_fallback_k + 1, column 0 dropped), deduplicated and --
+ * like the reference's hash unique() -- ordered by (row, col); then from_edge_index's geometry
+ * and sort_and_build_csr(col) (segment_reduce_kernel.cu:100-169) without a second sort.
+ *   x              [n_points, 3] f32 (read only for the geometry)
+ *   radius_row_ptr / radius_src: gdl_radius_graph's destination CSR, built with the same
+ *                  max_num_neighbors (it sizes the buffers here)
+ *   knn_idx        [n_points, knn_fallback_k + 1] i64 (gdl_knn of the points against themselves)
+ * Outputs (capacity = gdl_hybrid_graph_capacity(...) slots; the edge count E is written at
+ * out_row_ptr[n_points], on the device):
+ *   out_row / out_col [capacity] i64: the edges in (row, col) order (first E valid)
+ *   out_row_ptr [n_points + 1] i64: destination CSR of the same edges
+ *   col_sorted / perm [capacity] i32, node_start / node_end [n_points] i32: the segment-reduce CSR
+ *   src_sorted [capacity] i32 (nullable): the source of each col-sorted slot, row[perm[j]]
+ *   geometry (nullable): per edge in (row, col) order, as gdl_edge_geometry_coo
+ * No counterpart kernel in the reference. */
+int64_t gdl_hybrid_graph_capacity(int64_t n_points, int32_t max_num_neighbors, int32_t knn_fallback_k);
+size_t gdl_hybrid_graph_workspace_size(int64_t n_points, int32_t max_num_neighbors, int32_t knn_fallback_k);
+int gdl_hybrid_graph(const float *x, const int64_t *radius_row_ptr, const int64_t *radius_src, const int64_t *knn_idx,
+                     int64_t n_points, int32_t max_num_neighbors, int32_t knn_fallback_k, int64_t *out_row_ptr,
+                     int64_t *out_row, int64_t *out_col, int32_t *col_sorted, int32_t *perm, int32_t *src_sorted,
+                     int32_t *node_start, int32_t *node_end, const gdl_edge_geometry *geometry, void *workspace,
+                     size_t workspace_bytes, void *stream);
+
 /* -------------------------------------------------------------------- KNN aggregation
  * Replaces the weighted neighbour sums of the reference's KNN consumers, which gather
  * [n_query, k, dim] rows with torch indexing and reduce them over k:

@@ -739,3 +739,43 @@ int gdl_oracle_knn_weighted_sum_weight_grad(const float *gout, const float *src,
     }
     return 0;
 }
+
+/* ---------------------------------------------------------------- hybrid graph
+ * _EncoderStage._build_hybrid_graph (nn/modules/multi_scale_se3_net.py:126-219): the radius
+ * edges (src -> q) plus, for every q with fewer than kf radius in-edges, (q -> m) and (m -> q)
+ * for each valid m of knn[q, 1..kf]; deduplicated and ordered by row * n + col, as the
+ * reference's `unique()` of the edge hashes returns them. Returns E; out_row / out_col need
+ * room for the radius edges + 2 n kf.
+ */
+static int cmp_i64(const void *a, const void *b) {
+    const int64_t x = *(const int64_t *)a, y = *(const int64_t *)b;
+    return (x > y) - (x < y);
+}
+
+int64_t gdl_oracle_hybrid_graph(const int64_t *row_ptr, const int64_t *src, const int64_t *knn, int64_t n, int kf,
+                                int64_t *out_row, int64_t *out_col) {
+    const int64_t er = row_ptr[n] - row_ptr[0];
+    int64_t *h = (int64_t *)malloc(sizeof(int64_t) * (size_t)(er + 2 * n * kf + 1));
+    int64_t m = 0;
+    for (int64_t q = 0; q < n; ++q)
+        for (int64_t j = row_ptr[q]; j < row_ptr[q + 1]; ++j) h[m++] = src[j] * n + q;
+    for (int64_t q = 0; q < n; ++q) {
+        if (row_ptr[q + 1] - row_ptr[q] >= kf) continue;
+        for (int j = 1; j <= kf; ++j) {
+            const int64_t v = knn[q * (kf + 1) + j];
+            if (v < 0 || v >= n) continue;
+            h[m++] = q * n + v;
+            h[m++] = v * n + q;
+        }
+    }
+    qsort(h, (size_t)m, sizeof(int64_t), cmp_i64);
+    int64_t E = 0;
+    for (int64_t i = 0; i < m; ++i) {
+        if (i > 0 && h[i] == h[i - 1]) continue;
+        out_row[E] = h[i] / n;
+        out_col[E] = h[i] % n;
+        ++E;
+    }
+    free(h);
+    return E;
+}

@@ -78,6 +78,8 @@ def lib() -> ctypes.CDLL:
         L.gdl_oracle_edge_geometry.argtypes = [P, i64, P, P, i64, P, P, P, P, i32]
         L.gdl_oracle_cloud_avg_degree.argtypes = [P, P, i64, P, P, i32, P]
         L.gdl_oracle_knn_idw_weights.argtypes = [P, P, i64, i32, P]
+        L.gdl_oracle_hybrid_graph.argtypes = [P, P, P, i64, i32, P, P]
+        L.gdl_oracle_hybrid_graph.restype = i64
         L.gdl_oracle_knn_weighted_sum.argtypes = [P, i64, i64, P, P, i64, i32, P]
         L.gdl_oracle_knn_weighted_sum_backward.argtypes = [P, i64, P, P, i64, i32, i64, P]
         L.gdl_oracle_knn_weighted_sum_weight_grad.argtypes = [P, P, i64, i64, P, i64, i32, i32, P]
@@ -242,6 +244,19 @@ def cloud_avg_degree(node_start, node_end, batch=None, ptr=None, num_clouds=None
     lib().gdl_oracle_cloud_avg_degree(_p(ns), _p(ne), n, None if b is None else _p(b), None if p is None else _p(p),
                                       B, _p(out))
     return out
+
+
+def hybrid_graph(row_ptr, src, knn_idx, kf: int):
+    """(row, col) int64 of the radius + KNN-fallback union, ordered by (row, col)."""
+    rp = _c(row_ptr, np.int64)
+    src = _c(src, np.int64)
+    n = rp.shape[0] - 1
+    knn = _c(knn_idx, np.int64) if kf > 0 else np.zeros((max(n, 1), 1), np.int64)
+    cap = int(rp[-1] - rp[0]) + 2 * n * kf + 1
+    row = np.zeros(cap, np.int64)
+    col = np.zeros(cap, np.int64)
+    E = lib().gdl_oracle_hybrid_graph(_p(rp), _p(src) if src.size else None, _p(knn), n, kf, _p(row), _p(col))
+    return row[:E], col[:E]
 
 
 def knn_idw_weights(idx, dist) -> np.ndarray:

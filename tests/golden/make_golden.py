@@ -16,6 +16,8 @@ inputs, what the reference's public entry points return on the CPU:
 * ``nn.modules.spatial_graph.SpatialGraph.build`` / ``from_edge_index`` and
   ``functional.radius_graph.compute_edge_vectors`` + the spherical harmonics' torch path
   (``kernels.triton_sph_harm._spherical_harmonics_pytorch``) -> ``golden_graph.npz``.
+* ``nn.modules.multi_scale_se3_net._EncoderStage._build_hybrid_graph`` / ``_estimate_adaptive_radius``
+  -> ``golden_graph.npz`` (``hyb_*``).
 * ``nn.modules.equivariant_interp.EquivariantInterpolate`` forward/backward and the weighted-sum
   lines of ``EquivariantPool`` -> ``golden_aggregate.npz``.
 
@@ -363,6 +365,68 @@ def gen_aggregate(root: str, out):
         out["pool_" + k] = t.detach().numpy()
 
 
+def _stub_data_package():
+    """geoembodied.nn's package import reaches geoembodied.data, which the reference tree does not
+    ship; two empty stand-in modules let the encoder stage's file import (nothing of them runs)."""
+    import types
+
+    if "geoembodied.data" in sys.modules:
+        return
+    d = types.ModuleType("geoembodied.data")
+    b = types.ModuleType("geoembodied.data.batch")
+    b.PointCloudBatch = object
+    b.to_dense_batch = None
+    d.batch = b
+    sys.modules["geoembodied.data"] = d
+    sys.modules["geoembodied.data.batch"] = b
+
+
+def _knn_gaps_ok(x: np.ndarray, sizes, k: int) -> bool:
+    """the k + 1 nearest of every point (self included) have distinct distances with a relative
+    gap above 1e-5, so CPU and GPU distance rounding select and order the same neighbours"""
+    o = 0
+    for n in sizes:
+        p = x[o:o + n].astype(np.float64)
+        o += n
+        d = np.sort(((p[:, None, :] - p[None, :, :]) ** 2).sum(-1), axis=1)[:, :k + 2]
+        if np.any(np.diff(d[:, 1:], axis=1) <= 1e-5 * d[:, 2:]):
+            return False
+    return True
+
+
+def gen_hybrid(root: str, out):
+    """_EncoderStage._estimate_adaptive_radius / _build_hybrid_graph (nn/modules/
+    multi_scale_se3_net.py:99-219) on the CPU, called on a stand-in stage object."""
+    import types
+
+    _stub_data_package()
+    ms = importlib_module("geoembodied.nn.modules.multi_scale_se3_net")
+    stage = types.SimpleNamespace(max_num_neighbors=64, knn_fallback_k=3, radius_multiplier=4.0)
+    r, K, kf = 0.1, 64, 3
+    for seed in range(700, 800):
+        g = torch.Generator().manual_seed(seed)
+        clouds = []
+        for b in range(3):
+            centres = torch.rand(3, 3, generator=g) * 1.5
+            cl = centres.repeat_interleave(30, 0) + torch.randn(90, 3, generator=g) * 0.03
+            clouds.append(torch.cat([cl, torch.rand(110, 3, generator=g) * 1.5]))
+        x = torch.cat(clouds).numpy().astype(np.float32)
+        if _radius_safe(x, 3, r, K) and _knn_gaps_ok(x, [200] * 3, kf + 1):
+            break
+    else:
+        raise RuntimeError("no hybrid fixture found")
+    pos = torch.from_numpy(x)
+    ptr = torch.tensor([0, 200, 400, 600], dtype=torch.int64)
+    out["hyb_x"] = x
+    out["hyb_meta"] = np.array([K, kf, seed], np.int64)
+    out["hyb_r"] = np.array([r], np.float64)
+    out["hyb_adaptive_radius"] = np.array([ms._EncoderStage._estimate_adaptive_radius(stage, pos, ptr)], np.float64)
+    for tag, batch in (("nobatch", None), ("batch", torch.arange(3).repeat_interleave(200))):
+        gr = ms._EncoderStage._build_hybrid_graph(stage, pos, r, ptr, batch)
+        for f in ("row", "col", "dist", "col_sorted", "perm", "node_start", "node_end", "avg_degree"):
+            out[f"hyb_{tag}_{f}"] = getattr(gr, f).numpy()
+
+
 def importlib_module(name: str):
     import importlib
 
@@ -382,6 +446,7 @@ def main():
     print("wrote", HERE / "golden_cpu.npz", sum(v.nbytes for v in out.values()) / 1e6, "MB raw")
     graph = {}
     gen_graph(root, R, graph)
+    gen_hybrid(root, graph)
     np.savez_compressed(HERE / "golden_graph.npz", **graph)
     print("wrote", HERE / "golden_graph.npz", sum(v.nbytes for v in graph.values()) / 1e6, "MB raw")
     agg = {}

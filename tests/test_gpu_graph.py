@@ -204,3 +204,77 @@ def test_spatial_graph_full_size_lidar_geometry(oracle):
     assert torch.equal(d2.view(torch.int32), out["dist"][:E].view(torch.int32))
     assert torch.equal(u2.view(torch.int32), out["direction"][:E].view(torch.int32))
     assert torch.equal(y2.view(torch.int32), out["sph"][:E].view(torch.int32))
+
+
+# ------------------------------------------------------------------------- hybrid graph
+from gdl_b200.hybrid_graph import HybridGraphBuilder, build_hybrid_graph, estimate_adaptive_radius  # noqa: E402
+
+
+@pytest.mark.parametrize("tag", ["nobatch", "batch"])
+def test_hybrid_graph_golden(gg, oracle, tag):
+    x = gg["hyb_x"]
+    K, kf, _ = (int(v) for v in gg["hyb_meta"])
+    r = float(gg["hyb_r"][0])
+    ptr = torch.tensor([0, 200, 400, 600])
+    batch = torch.arange(3, device=DEV).repeat_interleave(200) if tag == "batch" else None
+    g = HybridGraphBuilder(max_num_neighbors=K, knn_fallback_k=kf)._build_hybrid_graph(
+        torch.from_numpy(x).to(DEV), r, ptr, batch)
+    t = f"hyb_{tag}_"
+    row, col = g.row.cpu().numpy(), g.col.cpu().numpy()
+    assert np.array_equal(row, gg[t + "row"]) and np.array_equal(col, gg[t + "col"])  # same order too
+    cs, pm, ns, ne = oracle.sort_and_build_csr(col, x.shape[0])  # stable, as the reference's CUDA sort
+    assert np.array_equal(g.col_sorted.cpu().numpy(), cs) and np.array_equal(g.perm.cpu().numpy(), pm)
+    assert np.array_equal(g.node_start.cpu().numpy(), ns) and np.array_equal(g.node_end.cpu().numpy(), ne)
+    assert same_csr(ns, ne, gg[t + "node_start"], gg[t + "node_end"])
+    _, dist, direction, sph = oracle.edge_geometry(x, row, col)
+    assert bits_equal(g.dist.cpu().numpy(), dist) and bits_equal(g.dist.cpu().numpy(), gg[t + "dist"])
+    assert bits_equal(g.direction.cpu().numpy(), direction) and bits_equal(g.Y.cpu().numpy(), sph)
+    avg = g.avg_degree.cpu().numpy()
+    if tag == "batch":
+        assert bits_equal(avg, gg[t + "avg_degree"])
+    else:
+        assert np.allclose(avg, gg[t + "avg_degree"], rtol=2e-7, atol=0)
+    est = estimate_adaptive_radius(torch.from_numpy(x).to(DEV), ptr.to(DEV), 4.0)
+    assert abs(est - gg["hyb_adaptive_radius"][0]) <= 2e-6 * est
+
+
+@pytest.mark.parametrize("kf", [0, 1, 3, 8])
+@pytest.mark.parametrize("kind", ["uniform", "hub"])
+def test_hybrid_graph_matches_oracle(oracle, kf, kind):
+    rng = np.random.default_rng(kf + 10)
+    if kind == "uniform":
+        sizes = [1, 0, 300, 2000, 5000]
+        x = rng.random((sum(sizes), 3)).astype(np.float32)
+        r, K = 0.04, 16
+    else:  # 300 copies of one point among scattered ones, no radius edges: rows far beyond 128
+        sizes = [700, 50]
+        x = rng.random((750, 3)).astype(np.float32) * 10
+        x[100:400] = x[100]
+        r, K = 0.0, 32
+    ptr = synthetic.ptr_of(sizes)
+    xd = torch.from_numpy(x).to(DEV)
+    pt = torch.from_numpy(ptr)
+    rp, src, _ = csrc.radius_graph_csr(xd, r, pt, max_num_neighbors=K, with_dst=False)
+    knn_idx = csrc.knn_cuda(xd, xd, pt.to(DEV), pt.to(DEV), kf + 1)[0] if kf > 0 else None
+    h = csrc.hybrid_graph_cuda(rp, src, knn_idx, x.shape[0], K, kf, x=xd, max_l=2)
+    E = int(h["row_ptr"][-1])
+    want_row, want_col = oracle.hybrid_graph(rp.cpu().numpy(), src.cpu().numpy(),
+                                             None if knn_idx is None else knn_idx.cpu().numpy(), kf)
+    assert E == want_row.shape[0]
+    assert np.array_equal(h["row"][:E].cpu().numpy(), want_row) and np.array_equal(h["col"][:E].cpu().numpy(),
+                                                                                    want_col)
+    cs, pm, ns, ne = oracle.sort_and_build_csr(want_col, x.shape[0])
+    assert np.array_equal(h["col_sorted"][:E].cpu().numpy(), cs) and np.array_equal(h["perm"][:E].cpu().numpy(), pm)
+    assert np.array_equal(h["node_start"].cpu().numpy(), ns) and np.array_equal(h["node_end"].cpu().numpy(), ne)
+    assert np.array_equal(h["src_sorted"][:E].cpu().numpy(), want_row[pm])
+    _, dist, direction, sph = oracle.edge_geometry(x, want_row, want_col, max_l=2)
+    assert bits_equal(h["dist"][:E].cpu().numpy(), dist) and bits_equal(h["direction"][:E].cpu().numpy(), direction)
+    assert bits_equal(h["sph"][:E].cpu().numpy(), sph)
+    if kind == "hub" and kf > 0:
+        assert np.diff(h["row_ptr"].cpu().numpy()).max() > 128  # the one-lane sort path ran
+
+
+def test_hybrid_graph_empty():
+    e64 = torch.zeros(1, dtype=torch.int64, device=DEV)
+    h = csrc.hybrid_graph_cuda(e64, e64, None, 0, 32, 3)
+    assert int(h["row_ptr"][0]) == 0

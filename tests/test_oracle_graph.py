@@ -131,3 +131,44 @@ def test_cloud_avg_degree_rules(oracle):
     out = oracle.cloud_avg_degree(ns, ne, batch=[1, 0, 1, 0, 7], num_clouds=2)
     assert out.tolist() == [1.0, 4.5, 1.0, 4.5, 1.0]
     assert oracle.cloud_avg_degree(ns, ne).tolist() == [2.0] * 5
+
+
+def _oracle_hybrid(oracle, x, ptr, r, K, kf):
+    rp, src = oracle.radius_graph(x, ptr, r, K, dist=oracle.DIST_TORCH)
+    knn_idx, knn_d = oracle.knn(x, x, ptr, ptr, kf + 1, dist=oracle.DIST_TORCH)
+    return oracle.hybrid_graph(rp, src, knn_idx, kf), rp
+
+
+@pytest.mark.parametrize("tag", ["nobatch", "batch"])
+def test_hybrid_graph(gg, oracle, tag):
+    """_EncoderStage._build_hybrid_graph: same edges in the same (row, col) order, same CSR."""
+    x = gg["hyb_x"]
+    K, kf, _ = (int(v) for v in gg["hyb_meta"])
+    r = float(gg["hyb_r"][0])
+    ptr = np.array([0, 200, 400, 600])
+    (row, col), rp = _oracle_hybrid(oracle, x, ptr, r, K, kf)
+    t = f"hyb_{tag}_"
+    assert np.array_equal(row, gg[t + "row"]) and np.array_equal(col, gg[t + "col"])
+    # the fixture exercises the fallback: isolated nodes exist and gained edges both ways
+    assert (np.diff(rp) < kf).sum() > 50 and row.shape[0] > rp[-1]
+    cs, pm, ns, ne = oracle.sort_and_build_csr(col, x.shape[0])
+    assert np.array_equal(cs, gg[t + "col_sorted"])
+    assert same_csr(ns, ne, gg[t + "node_start"], gg[t + "node_end"])
+    for a, b in zip(ns, ne):  # the CPU argsort is unstable: same slots per segment
+        assert sorted(pm[a:b].tolist()) == sorted(gg[t + "perm"][a:b].tolist())
+    _, dist, _, _ = oracle.edge_geometry(x, row, col)
+    assert bits_equal(dist, gg[t + "dist"])
+    batch = np.repeat(np.arange(3), 200) if tag == "batch" else None
+    avg = oracle.cloud_avg_degree(ns, ne, batch=batch, num_clouds=3 if tag == "batch" else None)
+    if tag == "batch":
+        assert bits_equal(avg, gg[t + "avg_degree"])
+    else:
+        assert np.allclose(avg, gg[t + "avg_degree"], rtol=2e-7, atol=0)
+
+
+def test_adaptive_radius(gg, oracle):
+    x = gg["hyb_x"]
+    ptr = np.array([0, 200, 400, 600])
+    _, d = oracle.knn(x, x, ptr, ptr, 2, dist=oracle.DIST_TORCH)
+    est = np.sqrt(np.clip(d[:, 1].astype(np.float64), 1e-8, 1e20)).mean() * 4.0
+    assert abs(est - gg["hyb_adaptive_radius"][0]) <= 1e-6 * est
