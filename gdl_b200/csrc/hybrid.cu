@@ -159,17 +159,21 @@ __global__ void __launch_bounds__(256) hy_unique_kernel(const int32_t *__restric
     }
 }
 
-// destination-grouped union -> sort keys (source) and the segment-reduce CSR fields; slots past
-// the edge count get the key n so that they sort last
+// destination-grouped union -> sort keys (source) and the segment-reduce CSR fields; seg = {0, E}
+// bounds the sort that follows to the edges (the count is only known on the device)
 __global__ void __launch_bounds__(256) hy_emit_kernel(const int32_t *__restrict__ buf, const int64_t *__restrict__ off,
                                                       const int32_t *__restrict__ ucnt,
-                                                      const int64_t *__restrict__ rp, int64_t n, int64_t cap,
+                                                      const int64_t *__restrict__ rp, int64_t n,
                                                       uint32_t *__restrict__ keys, int32_t *__restrict__ col_sorted,
                                                       int32_t *__restrict__ src_sorted,
-                                                      int32_t *__restrict__ node_start, int32_t *__restrict__ node_end) {
+                                                      int32_t *__restrict__ node_start, int32_t *__restrict__ node_end,
+                                                      int64_t *__restrict__ seg) {
     const int lane = threadIdx.x & 31;
     const int64_t warps = (int64_t)gridDim.x * (blockDim.x >> 5);
-    const int64_t E = rp[n];
+    if (blockIdx.x == 0 && threadIdx.x == 0) {
+        seg[0] = 0;
+        seg[1] = rp[n];
+    }
     for (int64_t q = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); q < n; q += warps) {
         const int64_t o = rp[q], u = ucnt[q], b = off[q];
         for (int64_t j = lane; j < u; j += 32) {
@@ -182,8 +186,6 @@ __global__ void __launch_bounds__(256) hy_emit_kernel(const int32_t *__restrict_
             node_end[q] = u > 0 ? (int32_t)(o + u) : 0;
         }
     }
-    for (int64_t i = E + (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < cap; i += (int64_t)gridDim.x * blockDim.x)
-        keys[i] = (uint32_t)n;
 }
 
 // position i of the (row, col) order: the edge at destination-grouped slot p = sorted_pos[i]; one
@@ -218,7 +220,7 @@ __global__ void __launch_bounds__(256) hy_order_kernel(const uint32_t *__restric
 
 struct HybridWs {
     int32_t *own, *tot, *fillc, *ucnt, *buf, *spos;
-    int64_t *off, *scan_scratch;
+    int64_t *off, *scan_scratch, *seg;
     uint32_t *keys, *skeys;
     RadixScratch rs;
 };
@@ -240,6 +242,7 @@ inline size_t hybrid_ws(int64_t n, int64_t cap, char *base, HybridWs *w) {
     t.ucnt = (int32_t *)take(4 * nn);
     t.off = (int64_t *)take(8 * (nn + 1));
     t.scan_scratch = (int64_t *)take(8 * (scan_blocks(nn) + 1));
+    t.seg = (int64_t *)take(8 * 2);
     t.buf = (int32_t *)take(4 * cc);
     t.keys = (uint32_t *)take(4 * cc);
     t.skeys = (uint32_t *)take(4 * cc);
@@ -307,11 +310,11 @@ extern "C" int gdl_hybrid_graph(const float *x, const int64_t *radius_row_ptr, c
                                                   w.buf);
     hy_unique_kernel<<<hy_grid(n, 8), 256, 0, st>>>(w.tot, w.off, n, w.buf, w.ucnt);
     GDL_CUDA_TRY((exclusive_scan<int32_t, int64_t>(w.ucnt, out_row_ptr, n, w.scan_scratch, out_row_ptr + n, st)));
-    hy_emit_kernel<<<hy_grid(n, 8), 256, 0, st>>>(w.buf, w.off, w.ucnt, out_row_ptr, n, cap, w.keys, col_sorted,
-                                                  src_sorted, node_start, node_end);
+    hy_emit_kernel<<<hy_grid(n, 8), 256, 0, st>>>(w.buf, w.off, w.ucnt, out_row_ptr, n, w.keys, col_sorted,
+                                                  src_sorted, node_start, node_end, w.seg);
     int bits = 1;
-    while (bits < 32 && ((int64_t)1 << bits) <= n) ++bits;  // keys 0 .. n
-    GDL_CUDA_TRY(radix_sort_pairs(w.keys, nullptr, w.skeys, w.spos, cap, nullptr, 1, (bits + 7) / 8, nullptr, w.rs,
+    while (bits < 32 && ((int64_t)1 << bits) < n) ++bits;  // keys 0 .. n - 1
+    GDL_CUDA_TRY(radix_sort_pairs(w.keys, nullptr, w.skeys, w.spos, cap, w.seg, 1, (bits + 7) / 8, nullptr, w.rs,
                                   st));
     hy_order_kernel<<<hy_grid(cap, 256), 256, 0, st>>>(w.skeys, w.spos, col_sorted, out_row_ptr, n, out_row, out_col,
                                                        perm, geom);
