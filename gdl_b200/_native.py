@@ -28,6 +28,14 @@ class EdgeGeometry(ctypes.Structure):
 
 
 _PG = ctypes.POINTER(EdgeGeometry)
+
+
+class Se3Paths(ctypes.Structure):
+    """gdl_se3_paths: per-path node projections (nullable), their R columns, output channels."""
+    _fields_ = [("p", _P * 9), ("r_col", _I32 * 9), ("cs", _I64), ("cv", _I64), ("ct2", _I64)]
+
+
+_PS = ctypes.POINTER(Se3Paths)
 PROTOTYPES = {
     "gdl_version": (ctypes.c_int, []),
     "gdl_status_string": (ctypes.c_char_p, [ctypes.c_int]),
@@ -51,6 +59,10 @@ PROTOTYPES = {
     "gdl_hybrid_graph_workspace_size": (_SZ, [_I64, _I32, _I32]),
     "gdl_hybrid_graph": (ctypes.c_int,
                          [_P, _P, _P, _P, _I64, _I32, _I32, _P, _P, _P, _P, _P, _P, _P, _P, _PG, _P, _SZ, _P]),
+    "gdl_se3_aggregate": (ctypes.c_int, [_PS, _P, _I64, _P, _P, _I32, _P, _P, _P, _P, _P, _P, _I64, _I64, _P, _P, _P,
+                                         _P]),
+    "gdl_se3_aggregate_backward": (ctypes.c_int, [_PS, _P, _P, _P, _P, _P, _P, _I64, _P, _P, _I32, _P, _P, _P, _P, _P,
+                                                  _P, _P, _I64, _I64, _P]),
     "gdl_knn_idw_weights": (ctypes.c_int, [_P, _P, _I64, _I32, _P, _P]),
     "gdl_knn_weighted_sum": (ctypes.c_int, [_P, _I64, _I64, _P, _P, _I64, _I32, _P, _P]),
     "gdl_knn_weighted_sum_backward_workspace_size": (_SZ, [_I64, _I32, _I64]),

@@ -1,0 +1,417 @@
+// se3_aggregate.cu -- SE3Conv messages computed inside the segment reduction (sm_100a).
+//
+// The reference's SE3Conv (nn/modules/se3_conv.py:61-235, 487-545) gathers the source features
+// of every edge, runs the nine tensor-product paths per edge (matmuls over the input channels,
+// products with the radial weights R, the direction d, Y_0 and the l = 2 harmonics Y_2), writes
+// the [E, C_s + 3 C_v + 5 C_t2] messages, reduces them per target with segment_reduce and
+// divides by the cloud's average degree. Every path is linear in the source features, so the
+// channel mixing can run once per NODE instead of once per edge: with node projections
+//   P0 = s W_ss^T [N,Cs]     P1 = s W_sv^T [N,Cv]     P2 = W_vv v [N,Cv,3]    P3 = W_vs v [N,Cs,3]
+//   P4 = W_x v [N,Cv,3]      P5 = s W_st2^T [N,Ct2]   P6 = W_t2t2 t2 [N,Ct2,5]
+//   P7 = W_vt2 v [N,Ct2,3]   P8 = |t2|^2 W_t2s^T [N,Cs]
+// (plain GEMMs, done by the caller), an edge's message is a handful of products of its source's
+// projections with (R, d, Y_0, Y_2), e.g. path 3 (d . v -> s): R3 sum_k d_k P3[o, k]; path 4
+// (d x v -> v): R4 (d x P4[o]); path 7 (d (x) v -> t2 through CG(1,1,2)): R7 sum_ij d_i P7[o, j]
+// CG[i, j, m]. This kernel forms those messages while it reduces each target's segment, so no
+// [E, C] message exists. Backward: gradients w.r.t. the projections (grouped by source over a
+// source-sorted edge list, deterministic) and w.r.t. R (one warp per edge).
+#include "common.cuh"
+
+namespace gdl {
+
+struct Se3Paths {
+    const float *p[9];
+    int rc[9];  // R column of each path (-1: path off)
+    int cs, cv, ct2;
+};
+
+struct Se3Edge {  // per-edge values shared by all channels of the edge
+    float r[9];
+    float d[3];
+    float y0;
+    float y2[5];
+};
+
+__device__ __forceinline__ void load_edge(const Se3Paths &P, const float *__restrict__ R, int64_t rs,
+                                          const float *__restrict__ dir, const float *__restrict__ sph, int sd,
+                                          int64_t e, Se3Edge &x) {
+#pragma unroll
+    for (int p = 0; p < 9; ++p) x.r[p] = P.rc[p] >= 0 ? R[e * rs + P.rc[p]] : 0.0f;
+    x.d[0] = dir[3 * e];
+    x.d[1] = dir[3 * e + 1];
+    x.d[2] = dir[3 * e + 2];
+    x.y0 = sph[e * sd];
+#pragma unroll
+    for (int m = 0; m < 5; ++m) x.y2[m] = sd >= 9 ? sph[e * sd + 4 + m] : 0.0f;
+}
+
+// Term of path p in message channel f of an edge from source s (0 when path p does not feed f's
+// kind). Channels: f < cs scalar o = f; then 3 cv vector (o, k); then 5 ct2 type-2 (o, m).
+__device__ __forceinline__ float se3_term(const Se3Paths &P, const float *__restrict__ cg, const Se3Edge &x, int64_t s,
+                                          int f, int p) {
+    if (f < P.cs) {
+        const int o = f;
+        if (p == 0) return __fmul_rn(__fmul_rn(x.r[0], x.y0), P.p[0][s * P.cs + o]);
+        if (p == 3) {
+            const float *q = P.p[3] + (s * P.cs + o) * 3;
+            const float dot =
+                __fadd_rn(__fadd_rn(__fmul_rn(x.d[0], q[0]), __fmul_rn(x.d[1], q[1])), __fmul_rn(x.d[2], q[2]));
+            return __fmul_rn(x.r[3], dot);
+        }
+        if (p == 8) return __fmul_rn(x.r[8], P.p[8][s * P.cs + o]);
+        return 0.0f;
+    }
+    f -= P.cs;
+    if (f < 3 * P.cv) {
+        const int o = f / 3, k = f - 3 * o;
+        if (p == 1) return __fmul_rn(__fmul_rn(x.r[1], P.p[1][s * P.cv + o]), x.d[k]);
+        if (p == 2) return __fmul_rn(__fmul_rn(x.r[2], x.y0), P.p[2][(s * P.cv + o) * 3 + k]);
+        if (p == 4) {
+            const float *q = P.p[4] + (s * P.cv + o) * 3;
+            const int k1 = k == 2 ? 0 : k + 1, k2 = k == 0 ? 2 : k - 1;  // (d x q)_k = d_k1 q_k2 - d_k2 q_k1
+            return __fmul_rn(x.r[4], __fsub_rn(__fmul_rn(x.d[k1], q[k2]), __fmul_rn(x.d[k2], q[k1])));
+        }
+        return 0.0f;
+    }
+    f -= 3 * P.cv;
+    const int o = f / 5, m = f - 5 * o;
+    if (p == 5) return __fmul_rn(__fmul_rn(x.r[5], P.p[5][s * P.ct2 + o]), x.y2[m]);
+    if (p == 6) return __fmul_rn(__fmul_rn(x.r[6], x.y0), P.p[6][(s * P.ct2 + o) * 5 + m]);
+    if (p == 7) {
+        const float *q = P.p[7] + (s * P.ct2 + o) * 3;
+        float t = 0.0f;
+#pragma unroll
+        for (int i = 0; i < 3; ++i)
+#pragma unroll
+            for (int j = 0; j < 3; ++j) t = __fadd_rn(t, __fmul_rn(__fmul_rn(x.d[i], q[j]), cg[(i * 3 + j) * 5 + m]));
+        return __fmul_rn(x.r[7], t);
+    }
+    return 0.0f;
+}
+
+// the message of channel f: the active paths' terms added in the reference's path order
+// (scalars 0, 3, 8; vectors 1, 2, 4; type-2 5, 6, 7)
+__device__ __forceinline__ float se3_message(const Se3Paths &P, const float *__restrict__ cg, const Se3Edge &x,
+                                             int64_t s, int f) {
+    float msg = 0.0f;
+    if (f < P.cs) {
+        if (P.p[0]) msg = __fadd_rn(msg, se3_term(P, cg, x, s, f, 0));
+        if (P.p[3]) msg = __fadd_rn(msg, se3_term(P, cg, x, s, f, 3));
+        if (P.p[8]) msg = __fadd_rn(msg, se3_term(P, cg, x, s, f, 8));
+    } else if (f < P.cs + 3 * P.cv) {
+        if (P.p[1]) msg = __fadd_rn(msg, se3_term(P, cg, x, s, f, 1));
+        if (P.p[2]) msg = __fadd_rn(msg, se3_term(P, cg, x, s, f, 2));
+        if (P.p[4]) msg = __fadd_rn(msg, se3_term(P, cg, x, s, f, 4));
+    } else {
+        if (P.p[5]) msg = __fadd_rn(msg, se3_term(P, cg, x, s, f, 5));
+        if (P.p[6]) msg = __fadd_rn(msg, se3_term(P, cg, x, s, f, 6));
+        if (P.p[7]) msg = __fadd_rn(msg, se3_term(P, cg, x, s, f, 7));
+    }
+    return msg;
+}
+
+constexpr int kSe3Chunks = 4;  // output channels per lane held in registers (128 per warp pass)
+
+// one warp per target node; lanes over the flattened output channels, edges of the segment in
+// sorted-slot order, messages formed on the fly
+__global__ void __launch_bounds__(256, 2) se3_agg_fwd_kernel(Se3Paths P, const float *__restrict__ R, int64_t rs,
+                                                          const float *__restrict__ dir, const float *__restrict__ sph,
+                                                          int sd, const float *__restrict__ cg,
+                                                          const int64_t *__restrict__ row,
+                                                          const int32_t *__restrict__ perm,
+                                                          const int32_t *__restrict__ ns,
+                                                          const int32_t *__restrict__ ne,
+                                                          const float *__restrict__ avg, int64_t N,
+                                                          float *__restrict__ os, float *__restrict__ ov,
+                                                          float *__restrict__ ot) {
+    const int lane = threadIdx.x & 31;
+    const int ctot = P.cs + 3 * P.cv + 5 * P.ct2;
+    const int64_t warps = (int64_t)gridDim.x * (blockDim.x >> 5);
+    for (int64_t n = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); n < N; n += warps) {
+        const int32_t j0 = ns[n], j1 = ne[n];
+        const float a = avg[n];
+        for (int c0 = 0; c0 < ctot; c0 += 32 * kSe3Chunks) {
+            float acc[kSe3Chunks];
+#pragma unroll
+            for (int i = 0; i < kSe3Chunks; ++i) acc[i] = 0.0f;
+            for (int32_t j = j0; j < j1; ++j) {
+                const int64_t e = perm[j];
+                const int64_t s = row[e];
+                Se3Edge x;
+                load_edge(P, R, rs, dir, sph, sd, e, x);
+#pragma unroll
+                for (int i = 0; i < kSe3Chunks; ++i) {
+                    const int f = c0 + lane + 32 * i;
+                    if (f < ctot) acc[i] = __fadd_rn(acc[i], se3_message(P, cg, x, s, f));
+                }
+            }
+#pragma unroll
+            for (int i = 0; i < kSe3Chunks; ++i) {
+                int f = c0 + lane + 32 * i;
+                if (f >= ctot) continue;
+                const float v = __fdiv_rn(acc[i], a);
+                if (f < P.cs) {
+                    os[n * P.cs + f] = v;
+                } else if ((f -= P.cs) < 3 * P.cv) {
+                    ov[n * 3 * P.cv + f] = v;
+                } else {
+                    f -= 3 * P.cv;
+                    ot[n * 5 * P.ct2 + f] = v;
+                }
+            }
+        }
+    }
+}
+
+// -------------------------------------------------------------------- backward
+// g = grad_out[target] / avg[target] for channel f of the flattened output
+__device__ __forceinline__ float grad_at(const float *__restrict__ gs, const float *__restrict__ gv,
+                                         const float *__restrict__ gt, const Se3Paths &P, int64_t t, int f) {
+    if (f < P.cs) return gs[t * P.cs + f];
+    f -= P.cs;
+    if (f < 3 * P.cv) return gv[t * 3 * P.cv + f];
+    f -= 3 * P.cv;
+    return gt[t * 5 * P.ct2 + f];
+}
+
+// grad_R[e, rc[p]] = sum over output channels f of g[f] * (path p's term of channel f without R_p).
+// One warp per edge; the nine sums are lane-strided, then reduced with a fixed butterfly.
+__global__ void __launch_bounds__(256) se3_agg_grad_r_kernel(Se3Paths P, const float *__restrict__ R, int64_t rs,
+                                                             const float *__restrict__ dir,
+                                                             const float *__restrict__ sph, int sd,
+                                                             const float *__restrict__ cg,
+                                                             const int64_t *__restrict__ row,
+                                                             const int64_t *__restrict__ col,
+                                                             const float *__restrict__ avg, int64_t E,
+                                                             const float *__restrict__ gs,
+                                                             const float *__restrict__ gv,
+                                                             const float *__restrict__ gt, float *__restrict__ gR) {
+    const int lane = threadIdx.x & 31;
+    const int ctot = P.cs + 3 * P.cv + 5 * P.ct2;
+    const int64_t warps = (int64_t)gridDim.x * (blockDim.x >> 5);
+    for (int64_t e = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); e < E; e += warps) {
+        const int64_t s = row[e], t = col[e];
+        const float a = avg[t];
+        Se3Edge x;
+        load_edge(P, R, rs, dir, sph, sd, e, x);
+        Se3Edge one = x;  // unit radial weights: each path's term without its R
+#pragma unroll
+        for (int p = 0; p < 9; ++p) one.r[p] = 1.0f;
+        float part[9];
+#pragma unroll
+        for (int p = 0; p < 9; ++p) part[p] = 0.0f;
+        for (int f = lane; f < ctot; f += 32) {
+            const float g = __fdiv_rn(grad_at(gs, gv, gt, P, t, f), a);
+#pragma unroll
+            for (int p = 0; p < 9; ++p) {
+                if (P.rc[p] < 0) continue;
+                part[p] = __fadd_rn(part[p], __fmul_rn(g, se3_term(P, cg, one, s, f, p)));
+            }
+        }
+#pragma unroll
+        for (int p = 0; p < 9; ++p) {
+            if (P.rc[p] < 0) continue;
+            float v = part[p];
+            for (int off = 16; off > 0; off >>= 1) v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, off));
+            if (lane == 0) gR[e * rs + P.rc[p]] = v;
+        }
+    }
+}
+
+struct Se3Grads {
+    float *g[9];
+};
+
+// sizes of the nine projection rows: 0 cs, 1 cv, 2 3cv, 3 3cs, 4 3cv, 5 ct2, 6 5ct2, 7 3ct2, 8 cs
+__device__ __forceinline__ int proj_width(const Se3Paths &P, int p) {
+    switch (p) {
+        case 0: return P.cs;
+        case 1: return P.cv;
+        case 2: return 3 * P.cv;
+        case 3: return 3 * P.cs;
+        case 4: return 3 * P.cv;
+        case 5: return P.ct2;
+        case 6: return 5 * P.ct2;
+        case 7: return 3 * P.ct2;
+        default: return P.cs;
+    }
+}
+
+// d(message) / d(projection p entry q) contracted with g over the channels that entry feeds
+__device__ __forceinline__ float proj_grad_term(const Se3Paths &P, const float *__restrict__ cg, const Se3Edge &x,
+                                                const float *__restrict__ gs, const float *__restrict__ gv,
+                                                const float *__restrict__ gt, int64_t t, float a, int p, int q) {
+    auto G = [&](int f) { return __fdiv_rn(grad_at(gs, gv, gt, P, t, f), a); };
+    switch (p) {
+        case 0: return __fmul_rn(__fmul_rn(x.r[0], x.y0), G(q));
+        case 3: {
+            const int o = q / 3, k = q - 3 * o;
+            return __fmul_rn(__fmul_rn(x.r[3], x.d[k]), G(o));
+        }
+        case 8: return __fmul_rn(x.r[8], G(q));
+        case 1: {
+            const int b = P.cs + 3 * q;
+            float sacc = 0.0f;
+#pragma unroll
+            for (int k = 0; k < 3; ++k) sacc = __fadd_rn(sacc, __fmul_rn(x.d[k], G(b + k)));
+            return __fmul_rn(x.r[1], sacc);
+        }
+        case 2: return __fmul_rn(__fmul_rn(x.r[2], x.y0), G(P.cs + q));
+        case 4: {  // (g_v[o] x d)_j
+            const int o = q / 3, j = q - 3 * o;
+            const int j1 = j == 2 ? 0 : j + 1, j2 = j == 0 ? 2 : j - 1;
+            const int b = P.cs + 3 * o;
+            const float cr = __fsub_rn(__fmul_rn(G(b + j1), x.d[j2]), __fmul_rn(G(b + j2), x.d[j1]));
+            return __fmul_rn(x.r[4], cr);
+        }
+        case 5: {
+            const int b = P.cs + 3 * P.cv + 5 * q;
+            float sacc = 0.0f;
+#pragma unroll
+            for (int m = 0; m < 5; ++m) sacc = __fadd_rn(sacc, __fmul_rn(x.y2[m], G(b + m)));
+            return __fmul_rn(x.r[5], sacc);
+        }
+        case 6: return __fmul_rn(__fmul_rn(x.r[6], x.y0), G(P.cs + 3 * P.cv + q));
+        default: {  // 7: sum_m (sum_i d_i CG[i, j, m]) g_t[o, m]
+            const int o = q / 3, j = q - 3 * o;
+            const int b = P.cs + 3 * P.cv + 5 * o;
+            float sacc = 0.0f;
+#pragma unroll
+            for (int m = 0; m < 5; ++m) {
+                float c = 0.0f;
+#pragma unroll
+                for (int i = 0; i < 3; ++i) c = __fadd_rn(c, __fmul_rn(x.d[i], cg[(i * 3 + j) * 5 + m]));
+                sacc = __fadd_rn(sacc, __fmul_rn(c, G(b + m)));
+            }
+            return __fmul_rn(x.r[7], sacc);
+        }
+    }
+}
+
+// grad of every projection entry of source node s: one warp per source, its out-edges in
+// source-sorted order (deterministic), lanes over the entries of one projection at a time
+__global__ void __launch_bounds__(256, 2) se3_agg_grad_p_kernel(Se3Paths P, Se3Grads Gp, const float *__restrict__ R,
+                                                             int64_t rs, const float *__restrict__ dir,
+                                                             const float *__restrict__ sph, int sd,
+                                                             const float *__restrict__ cg,
+                                                             const int64_t *__restrict__ col,
+                                                             const int32_t *__restrict__ sperm,
+                                                             const int32_t *__restrict__ sns,
+                                                             const int32_t *__restrict__ sne,
+                                                             const float *__restrict__ avg, int64_t N,
+                                                             const float *__restrict__ gs,
+                                                             const float *__restrict__ gv,
+                                                             const float *__restrict__ gt) {
+    const int lane = threadIdx.x & 31;
+    const int64_t warps = (int64_t)gridDim.x * (blockDim.x >> 5);
+    for (int64_t s = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); s < N; s += warps) {
+        const int32_t j0 = sns[s], j1 = sne[s];
+        for (int p = 0; p < 9; ++p) {
+            if (!Gp.g[p]) continue;
+            const int w = proj_width(P, p);
+            for (int q0 = 0; q0 < w; q0 += 32 * kSe3Chunks) {
+                float acc[kSe3Chunks];
+#pragma unroll
+                for (int i = 0; i < kSe3Chunks; ++i) acc[i] = 0.0f;
+                for (int32_t j = j0; j < j1; ++j) {
+                    const int64_t e = sperm[j];
+                    const int64_t t = col[e];
+                    const float a = avg[t];
+                    Se3Edge x;
+                    load_edge(P, R, rs, dir, sph, sd, e, x);
+#pragma unroll
+                    for (int i = 0; i < kSe3Chunks; ++i) {
+                        const int q = q0 + lane + 32 * i;
+                        if (q < w) acc[i] = __fadd_rn(acc[i], proj_grad_term(P, cg, x, gs, gv, gt, t, a, p, q));
+                    }
+                }
+#pragma unroll
+                for (int i = 0; i < kSe3Chunks; ++i) {
+                    const int q = q0 + lane + 32 * i;
+                    if (q < w) Gp.g[p][s * w + q] = acc[i];
+                }
+            }
+        }
+    }
+}
+
+inline unsigned se3_grid(int64_t warps_needed) {
+    int64_t b = (warps_needed + 7) / 8;
+    const int64_t cap = (int64_t)kSmCount * 16;
+    return (unsigned)(b < 1 ? 1 : (b > cap ? cap : b));
+}
+
+inline bool se3_paths_ok(const gdl_se3_paths *g, Se3Paths *P) {
+    if (!g || g->cs < 0 || g->cv < 0 || g->ct2 < 0) return false;
+    P->cs = (int)g->cs;
+    P->cv = (int)g->cv;
+    P->ct2 = (int)g->ct2;
+    for (int p = 0; p < 9; ++p) {
+        P->p[p] = g->p[p];
+        P->rc[p] = g->p[p] ? g->r_col[p] : -1;
+        if (g->p[p] && g->r_col[p] < 0) return false;
+    }
+    return true;
+}
+
+}  // namespace gdl
+
+using namespace gdl;
+
+extern "C" int gdl_se3_aggregate(const gdl_se3_paths *paths, const float *R, int64_t r_stride, const float *direction,
+                                 const float *sph, int32_t sph_dim, const float *cg, const int64_t *row,
+                                 const int32_t *perm, const int32_t *node_start, const int32_t *node_end,
+                                 const float *avg_degree, int64_t n_nodes, int64_t n_edges, float *out_s, float *out_v,
+                                 float *out_t2, void *stream) {
+    cudaStream_t st = (cudaStream_t)stream;
+    Se3Paths P;
+    GDL_RETURN_IF(!se3_paths_ok(paths, &P) || n_nodes < 0 || n_edges < 0 || sph_dim < 1, GDL_ERR_INVALID);
+    for (int p = 0; p < 9; ++p) GDL_RETURN_IF(P.rc[p] >= r_stride, GDL_ERR_INVALID);
+    if (n_nodes == 0) return GDL_OK;
+    GDL_RETURN_IF(!node_start || !node_end || !avg_degree, GDL_ERR_INVALID);
+    GDL_RETURN_IF((P.cs && !out_s) || (P.cv && !out_v) || (P.ct2 && !out_t2), GDL_ERR_INVALID);
+    GDL_RETURN_IF(n_edges > 0 && (!R || !direction || !sph || !row || !perm), GDL_ERR_INVALID);
+    GDL_RETURN_IF((P.p[7] && !cg) || ((P.p[5]) && sph_dim < 9), GDL_ERR_INVALID);
+    se3_agg_fwd_kernel<<<se3_grid(n_nodes), 256, 0, st>>>(P, R, r_stride, direction, sph, sph_dim, cg, row, perm,
+                                                          node_start, node_end, avg_degree, n_nodes, out_s, out_v,
+                                                          out_t2);
+    GDL_CUDA_TRY(cudaGetLastError());
+    return GDL_OK;
+}
+
+extern "C" int gdl_se3_aggregate_backward(const gdl_se3_paths *paths, float *const *grad_proj, float *grad_R,
+                                          const float *grad_s, const float *grad_v, const float *grad_t2,
+                                          const float *R, int64_t r_stride, const float *direction, const float *sph,
+                                          int32_t sph_dim, const float *cg, const int64_t *row, const int64_t *col,
+                                          const int32_t *src_perm, const int32_t *src_start, const int32_t *src_end,
+                                          const float *avg_degree, int64_t n_nodes, int64_t n_edges, void *stream) {
+    cudaStream_t st = (cudaStream_t)stream;
+    Se3Paths P;
+    GDL_RETURN_IF(!se3_paths_ok(paths, &P) || n_nodes < 0 || n_edges < 0 || sph_dim < 1, GDL_ERR_INVALID);
+    GDL_RETURN_IF((P.cs && !grad_s) || (P.cv && !grad_v) || (P.ct2 && !grad_t2), GDL_ERR_INVALID);
+    if (n_nodes == 0) return GDL_OK;
+    GDL_RETURN_IF(!avg_degree, GDL_ERR_INVALID);
+    GDL_RETURN_IF((P.p[7] && !cg) || ((P.p[5]) && sph_dim < 9), GDL_ERR_INVALID);
+    if (grad_R && n_edges > 0) {
+        GDL_RETURN_IF(!R || !direction || !sph || !row || !col, GDL_ERR_INVALID);
+        se3_agg_grad_r_kernel<<<se3_grid(n_edges), 256, 0, st>>>(P, R, r_stride, direction, sph, sph_dim, cg, row, col,
+                                                                 avg_degree, n_edges, grad_s, grad_v, grad_t2, grad_R);
+    }
+    if (grad_proj) {
+        Se3Grads G;
+        bool any = false;
+        for (int p = 0; p < 9; ++p) {
+            G.g[p] = P.p[p] ? grad_proj[p] : nullptr;
+            any = any || G.g[p];
+        }
+        if (any) {
+            GDL_RETURN_IF(!src_perm || !src_start || !src_end || (n_edges > 0 && (!R || !direction || !sph || !col)),
+                          GDL_ERR_INVALID);
+            se3_agg_grad_p_kernel<<<se3_grid(n_nodes), 256, 0, st>>>(P, G, R, r_stride, direction, sph, sph_dim, cg, col,
+                                                                     src_perm, src_start, src_end, avg_degree, n_nodes,
+                                                                     grad_s, grad_v, grad_t2);
+        }
+    }
+    GDL_CUDA_TRY(cudaGetLastError());
+    return GDL_OK;
+}

@@ -208,6 +208,47 @@ int gdl_hybrid_graph(const float *x, const int64_t *radius_row_ptr, const int64_
                      int32_t *node_start, int32_t *node_end, const gdl_edge_geometry *geometry, void *workspace,
                      size_t workspace_bytes, void *stream);
 
+/* ------------------------------------------------------------ SE3Conv message aggregation
+ * Replaces SE3Conv's per-edge messages + segment_reduce + degree normalisation
+ * (geoembodied/nn/modules/se3_conv.py:61-235 _compute_messages, :487-545 forward) for the
+ * nine tensor-product paths, without materialising the [E, C] messages. The channel mixing of
+ * each path is linear in the source features and is passed in per NODE (GEMMs run by the
+ * caller); the kernel forms each edge's message from its source's projections and the edge's
+ * radial weights R, direction d and harmonics while it reduces the edges of each target:
+ *   p[0] [N,Cs]    = s W_ss^T       scalar  += (R0 Y0) p0[o]
+ *   p[1] [N,Cv]    = s W_sv^T       vector  += (R1 p1[o]) d_k
+ *   p[2] [N,Cv,3]  = W_vv v         vector  += (R2 Y0) p2[o,k]
+ *   p[3] [N,Cs,3]  = W_vs v         scalar  += R3 (d . p3[o])
+ *   p[4] [N,Cv,3]  = W_x v          vector  += R4 (d x p4[o])_k
+ *   p[5] [N,Ct2]   = s W_st2^T      type-2  += (R5 p5[o]) Y2_m
+ *   p[6] [N,Ct2,5] = W_t2t2 t2      type-2  += (R6 Y0) p6[o,m]
+ *   p[7] [N,Ct2,3] = W_vt2 v        type-2  += R7 sum_ij d_i p7[o,j] cg[i,j,m]
+ *   p[8] [N,Cs]    = |t2|^2 W_t2s^T scalar  += R8 p8[o]
+ * out = (sum over the target's edges in CSR slot order) / avg_degree[target].
+ * p[i] == NULL switches path i off; r_col[i] = its column of R [E, r_stride]. Y0 = sph[e, 0],
+ * Y2 = sph[e, 4:9] (sph [E, sph_dim]); cg [3, 3, 5] Cartesian CG(1,1,2) (path 7 only).
+ * Edges: row [E] (source of edge e), perm [E] (edge of CSR slot j), node_start/node_end [N].
+ * Backward: grad_R [E, r_stride] (nullable) and grad_proj[i] (nullable array / entries, shapes of
+ * p[i]) from grad_s/v/t2 [N, ...]; grad_proj needs the edges grouped by source: src_perm /
+ * src_start / src_end = gdl_sort_and_build_csr(row) (perm, node_start, node_end), and col [E].
+ * No counterpart kernel in the reference. */
+typedef struct gdl_se3_paths {
+    const float *p[9];
+    int32_t r_col[9];
+    int64_t cs, cv, ct2;
+} gdl_se3_paths;
+
+int gdl_se3_aggregate(const gdl_se3_paths *paths, const float *R, int64_t r_stride, const float *direction,
+                      const float *sph, int32_t sph_dim, const float *cg, const int64_t *row, const int32_t *perm,
+                      const int32_t *node_start, const int32_t *node_end, const float *avg_degree, int64_t n_nodes,
+                      int64_t n_edges, float *out_s, float *out_v, float *out_t2, void *stream);
+int gdl_se3_aggregate_backward(const gdl_se3_paths *paths, float *const *grad_proj, float *grad_R,
+                               const float *grad_s, const float *grad_v, const float *grad_t2, const float *R,
+                               int64_t r_stride, const float *direction, const float *sph, int32_t sph_dim,
+                               const float *cg, const int64_t *row, const int64_t *col, const int32_t *src_perm,
+                               const int32_t *src_start, const int32_t *src_end, const float *avg_degree,
+                               int64_t n_nodes, int64_t n_edges, void *stream);
+
 /* -------------------------------------------------------------------- KNN aggregation
  * Replaces the weighted neighbour sums of the reference's KNN consumers, which gather
  * [n_query, k, dim] rows with torch indexing and reduce them over k:

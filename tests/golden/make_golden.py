@@ -18,6 +18,7 @@ inputs, what the reference's public entry points return on the CPU:
   (``kernels.triton_sph_harm._spherical_harmonics_pytorch``) -> ``golden_graph.npz``.
 * ``nn.modules.multi_scale_se3_net._EncoderStage._build_hybrid_graph`` / ``_estimate_adaptive_radius``
   -> ``golden_graph.npz`` (``hyb_*``).
+* ``nn.modules.se3_conv.SE3Conv`` forward/backward over a reference-built graph -> ``golden_se3.npz``.
 * ``nn.modules.equivariant_interp.EquivariantInterpolate`` forward/backward and the weighted-sum
   lines of ``EquivariantPool`` -> ``golden_aggregate.npz``.
 
@@ -427,6 +428,41 @@ def gen_hybrid(root: str, out):
             out[f"hyb_{tag}_{f}"] = getattr(gr, f).numpy()
 
 
+def gen_se3(root: str, out):
+    """SE3Conv.forward / backward (nn/modules/se3_conv.py:287-545) on the CPU over a graph from the
+    reference's SpatialGraph.build: all nine paths (type-2 in and out), and paths 0-4 alone."""
+    _stub_data_package()
+    se3 = importlib_module("geoembodied.nn.modules.se3_conv")
+    SG = _ref_spatial_graph(root)
+    g = torch.Generator().manual_seed(31)
+    pos = torch.rand(300, 3, generator=g)
+    batch = torch.arange(2).repeat_interleave(150)
+    graph = SG.build(pos, 0.3, max_num_neighbors=32, batch=batch, num_batch_elements=2)
+    out["se3_pos"] = pos.numpy()
+    out["se3_row"], out["se3_col"] = graph.row.numpy(), graph.col.numpy()
+    for tag, dims in (("full", (16, 8, 24, 6, 4, 3)), ("sv", (16, 8, 24, 6, 0, 0))):
+        torch.manual_seed(41)
+        conv = se3.SE3Conv(*dims, radius=0.3)
+        for k, v in conv.state_dict().items():
+            out[f"se3_{tag}_sd_{k}"] = v.numpy()
+        s_in = torch.randn(300, dims[0], generator=g, requires_grad=True)
+        v_in = torch.randn(300, dims[1], 3, generator=g, requires_grad=True)
+        t_in = torch.randn(300, dims[4], 5, generator=g, requires_grad=True) if dims[4] else None
+        res = conv(s_in, v_in, graph, type2=t_in) if t_in is not None else conv(s_in, v_in, graph)
+        grads = [torch.randn(r.shape, generator=g) for r in res]
+        torch.autograd.backward(list(res), grads)
+        names = ["s", "v", "t2"]
+        for i, r in enumerate(res):
+            out[f"se3_{tag}_out_{names[i]}"] = r.detach().numpy()
+            out[f"se3_{tag}_gout_{names[i]}"] = grads[i].numpy()
+        out[f"se3_{tag}_in_s"], out[f"se3_{tag}_in_v"] = s_in.detach().numpy(), v_in.detach().numpy()
+        out[f"se3_{tag}_grad_s"], out[f"se3_{tag}_grad_v"] = s_in.grad.numpy(), v_in.grad.numpy()
+        if t_in is not None:
+            out[f"se3_{tag}_in_t2"], out[f"se3_{tag}_grad_t2"] = t_in.detach().numpy(), t_in.grad.numpy()
+        for k, prm in conv.named_parameters():
+            out[f"se3_{tag}_pgrad_{k}"] = prm.grad.numpy()
+
+
 def importlib_module(name: str):
     import importlib
 
@@ -449,6 +485,10 @@ def main():
     gen_hybrid(root, graph)
     np.savez_compressed(HERE / "golden_graph.npz", **graph)
     print("wrote", HERE / "golden_graph.npz", sum(v.nbytes for v in graph.values()) / 1e6, "MB raw")
+    se3 = {}
+    gen_se3(root, se3)
+    np.savez_compressed(HERE / "golden_se3.npz", **se3)
+    print("wrote", HERE / "golden_se3.npz", sum(v.nbytes for v in se3.values()) / 1e6, "MB raw")
     agg = {}
     gen_aggregate(root, agg)
     np.savez_compressed(HERE / "golden_aggregate.npz", **agg)

@@ -60,6 +60,14 @@ def test_argument_validation_without_gpu(lib):
     assert lib.gdl_cloud_avg_degree(None, None, 3, None, None, 0, None, None, 0, None) == 1
     assert lib.gdl_radius_csr_finish(None, None, 3, 3, None, 0, None, None, None, None, None, None) == 1
     assert lib.gdl_cloud_avg_degree_workspace_size(8) >= 128
+    paths = nat.Se3Paths()
+    paths.cs, paths.cv, paths.ct2 = 4, 2, 0
+    paths.p[0] = 16  # a path switched on without an R column
+    paths.r_col[0] = -1
+    assert lib.gdl_se3_aggregate(paths, None, 1, None, None, 1, None, None, None, None, None, None, 5, 5, None, None,
+                                 None, None) == 1
+    assert lib.gdl_se3_aggregate(None, None, 1, None, None, 1, None, None, None, None, None, None, 5, 5, None, None,
+                                 None, None) == 1
     assert lib.gdl_hybrid_graph_capacity(1000, 32, 3) == 1000 * (32 + 6)
     assert lib.gdl_hybrid_graph_workspace_size(1000, 32, 3) > 1000 * 38 * 12
     assert lib.gdl_hybrid_graph(None, None, None, None, 10, 32, 3, None, None, None, None, None, None, None, None,
