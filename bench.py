@@ -8,6 +8,9 @@ inputs with the shapes of the reference's use cases; see gdl_b200/synthetic.py):
   c2 (default)  16 clouds x 2048 points: FPS -> 512 centroids per cloud, radius graph
                 (r = 0.2, 32 neighbours) over the centroids, segment mean of 128-channel
                 features over that graph, forward and backward.
+  c2c           (auxiliary) one SE3Conv layer (scalar, vector and type-2 channels), forward and
+                backward, over c2's centroid graph: per-node channel mixing + the fused
+                message / segment-reduce kernel.
   c1            4 clouds x 2048 uniform points: FPS -> 512, KNN k=16, segment sum and max
                 (64 channels).
   c3            32 GMM clouds x 8192 points: FPS chain 8192 -> 2048 -> 512 -> 128, KNN k=32
@@ -648,6 +651,115 @@ class C3I:
             O.knn_weighted_sum_backward(self.gv_h[l].numpy()[:nd], idx, w, nc)
 
 
+class C2C:
+    """Auxiliary SE3Conv-layer workload (the reference's SE3Conv, nn/modules/se3_conv.py:287-545, on
+    config 2's graph): 16 clouds x 2048 points -> FPS 512 -> SpatialGraph.build (r = 0.2, 32) over
+    the 8192 centroids (built once); a step is one SE3Conv(128, 32 -> 128, 32; type-2 16 -> 16)
+    forward and backward through autograd: per-node channel mixing (cuBLAS), the radial MLP, the
+    fused message + segment-reduce kernel and its backward. Eager launches (autograd)."""
+    name = "c2c"
+    metric = ("centroids/sec (SE3Conv 128s+32v+16t2 -> 128s+32v+16t2, forward + backward, over the config-2 "
+              "centroid radius graph)")
+    B, N, K, R, NN = 16, 2048, 512, 0.2, 32
+    DIMS = (128, 32, 128, 32, 16, 16)
+    capture = False
+    launches_per_step = 3  # fused forward, grad of R, grad of the projections (source grouping cached)
+    cpu_fraction = 1.0
+    cpu_sample = ("full steps: the reference layer's formulas in torch fp32 on the CPU (oracle/se3_ref.py), forward "
+                  "and backward through autograd")
+    points_per_step = property(lambda self: self.B * self.K)
+
+    def _host_init(self, seed, pin=True):
+        pos, ptr = synthetic.c2_points(seed=seed, B=self.B, N=self.N)
+        self.pos_h, self.ptr_h = torch.from_numpy(pos), torch.from_numpy(ptr)
+        g = torch.Generator().manual_seed(seed + 5)
+        n = self.B * self.K
+        cs, cv, _, _, ct, _ = self.DIMS
+        self.s_h, self.v_h, self.t_h = (torch.randn(n, cs, generator=g), torch.randn(n, cv, 3, generator=g),
+                                        torch.randn(n, ct, 5, generator=g))
+
+    def __init__(self, dev, seed):
+        from gdl_b200.se3_conv import SE3Conv
+        self.dev = dev
+        self._host_init(seed)
+        idx, cent = csrc.fps_cuda(self.pos_h.to(dev), self.ptr_h, torch.full((self.B,), self.K), return_pos=True)
+        batch = torch.arange(self.B, device=dev).repeat_interleave(self.K)
+        self.graph = SpatialGraph.build(cent, self.R, max_num_neighbors=self.NN, batch=batch,
+                                        num_batch_elements=self.B)
+        torch.manual_seed(seed + 6)
+        self.conv = SE3Conv(*self.DIMS, radius=self.R).to(dev)
+        self.s = self.s_h.to(dev).requires_grad_(True)
+        self.v = self.v_h.to(dev).requires_grad_(True)
+        self.t = self.t_h.to(dev).requires_grad_(True)
+        outs = self.conv(self.s, self.v, self.graph, type2=self.t)
+        g = torch.Generator(device=dev).manual_seed(seed + 7)
+        self.gouts = [torch.randn(o.shape, device=dev, generator=g) for o in outs]
+
+    def stage_layer(self):
+        outs = self.conv(self.s, self.v, self.graph, type2=self.t)
+        torch.autograd.backward(list(outs), self.gouts)
+
+    def stage_list(self):
+        return [("se3conv_fwd_bwd", self.stage_layer)]
+
+    def step(self):
+        self.stage_layer()
+
+    def edges(self):
+        return self.graph.E
+
+    def stage_bytes(self, E):
+        n = self.B * self.K
+        cs, cv, _, _, ct, _ = self.DIMS
+        proj = cs + cv + 3 * cv + 3 * cs + 3 * cv + ct + 5 * ct + 3 * ct + cs  # floats per node, nine tables
+        out = cs + 3 * cv + 5 * ct
+        # fused kernels: per edge R (9) + direction (3) + harmonics (9) floats + slot/edge indices, in the
+        # forward and twice in the backward; node tables read and their gradients written once; outputs
+        # and their gradients once
+        return {"se3conv_fwd_bwd": 3 * E * (4 * 21 + 12) + 4 * n * proj * 3 + 4 * n * out * 3}
+
+    def e2e_step(self):
+        s = self.s_h.pin_memory().to(self.dev, non_blocking=True).requires_grad_(True)
+        v = self.v_h.pin_memory().to(self.dev, non_blocking=True).requires_grad_(True)
+        t = self.t_h.pin_memory().to(self.dev, non_blocking=True).requires_grad_(True)
+        outs = self.conv(s, v, self.graph, type2=t)
+        torch.autograd.backward(list(outs), self.gouts)
+        host = s.grad.to("cpu", non_blocking=True)
+        torch.cuda.current_stream(self.dev).synchronize()
+        return host
+
+    e2e_h2d = property(lambda self: 4 * (self.s_h.numel() + self.v_h.numel() + self.t_h.numel()))
+    e2e_d2h = property(lambda self: 4 * self.s_h.numel())
+
+    def cpu_step(self, O):
+        from oracle import se3_ref
+        if not hasattr(self, "_cpu_graph"):
+            pos = self.pos_h.numpy()
+            idx = O.fps(pos, self.ptr_h.numpy(), np.full(self.B, self.K), dist=O.DIST_CUDA)
+            cent = pos[idx]
+            rp, src = O.radius_graph(cent, np.arange(0, self.B * self.K + 1, self.K), self.R, self.NN,
+                                     dist=O.DIST_CUDA)
+            row, col = O.csr_to_coo(rp, src)
+            torch.manual_seed(6)
+            sd = {}
+            cs_i, cv_i, cs_o, cv_o, ct_i, ct_o = self.DIMS
+            for name, (o, i) in dict(w_ss=(cs_o, cs_i), w_sv=(cv_o, cs_i), w_vv_scalar=(cv_o, cv_i),
+                                     w_vs=(cs_o, cv_i), w_vv_cross=(cv_o, cv_i), w_st2=(ct_o, cs_i),
+                                     w_t2t2=(ct_o, ct_i), w_vt2=(ct_o, cv_i), w_t2s=(cs_o, ct_i)).items():
+                sd[name + ".weight"] = torch.randn(o, i) / i ** 0.5
+            sd["radial_basis.freqs"] = torch.arange(1, 17).float() * np.pi / self.R
+            sd["radial_basis.mlp.0.weight"], sd["radial_basis.mlp.0.bias"] = torch.randn(64, 16) / 4, torch.zeros(64)
+            sd["radial_basis.mlp.2.weight"], sd["radial_basis.mlp.2.bias"] = torch.randn(9, 64) / 8, torch.zeros(9)
+            sd["scalar_bias"] = torch.zeros(cs_o)
+            self._cpu_graph = (torch.from_numpy(cent), torch.from_numpy(row), torch.from_numpy(col), sd)
+        cent, row, col, sd = self._cpu_graph
+        clouds = [(b * self.K, (b + 1) * self.K) for b in range(self.B)]
+        leaf = {k: t.clone().requires_grad_(k.endswith("weight") or k.endswith("bias")) for k, t in sd.items()}
+        s, v, t = (x.clone().requires_grad_(True) for x in (self.s_h, self.v_h, self.t_h))
+        outs = se3_ref.se3_forward(leaf, self.DIMS, cent, row, col, s, v, t, clouds, self.R, dtype=torch.float32)
+        torch.autograd.backward(list(outs), [torch.ones_like(o) for o in outs])
+
+
 class C4:
     """64 source/target pairs x 16384 points: KNN k=1 target->source, 6-channel residual
     features, segment sum per cloud (64 segments x 16384 rows)."""
@@ -1105,7 +1217,7 @@ class C5S(C5G):
         O.cloud_avg_degree(ns, ne)
 
 
-CONFIGS = {"c1": C1, "c2": C2, "c3": C3, "c3i": C3I, "c4": C4, "c5": C5, "c5g": C5G, "c5h": C5H, "c5s": C5S}
+CONFIGS = {"c1": C1, "c2": C2, "c2c": C2C, "c3": C3, "c3i": C3I, "c4": C4, "c5": C5, "c5g": C5G, "c5h": C5H, "c5s": C5S}
 
 
 
@@ -1262,7 +1374,7 @@ def run_ours(args, cfg_cls):
     # each stage captured as one CUDA graph; events between the replays time the stages
     runners = [fn for _, fn in stages]
     launch = "eager"
-    if not args.eager:
+    if not args.eager and getattr(cfg, "capture", True):
         try:
             graphs = []
             for _, fn in stages:

@@ -104,7 +104,7 @@ class SE3MessageAggregate(torch.autograd.Function):
         grad_R = torch.zeros_like(R) if ctx.needs_input_grad[1] else None
         src_perm = src_start = src_end = None
         if any(need_p):
-            _, src_perm, src_start, src_end = csrc.sort_and_build_csr_cuda(g.row, N)
+            src_perm, src_start, src_end = _source_csr(g)
         st = _paths_struct(proj, r_cols, cs, cv, ct2)
         gp_arr = (ctypes.c_void_p * _PATHS)(*[nat.ptr(t) for t in grad_p])
         sph = g.Y.contiguous().float()
@@ -115,6 +115,17 @@ class SE3MessageAggregate(torch.autograd.Function):
             g.col.data_ptr(), nat.ptr(src_perm), nat.ptr(src_start), nat.ptr(src_end), g.avg_degree.data_ptr(), N, E,
             nat.stream(dev)), "gdl_se3_aggregate_backward")
         return (None, grad_R, *grad_p)
+
+
+def _source_csr(g):
+    """The graph's edges grouped by source (perm, start, end), built once per graph object and kept
+    on it: a graph is shared by every convolution of a stage, its edges never change."""
+    cached = getattr(g, "_gdl_source_csr", None)
+    if cached is None or cached[0] is not g.row:
+        _, perm, start, end = csrc.sort_and_build_csr_cuda(g.row, g.N)
+        cached = (g.row, perm, start, end)
+        object.__setattr__(g, "_gdl_source_csr", cached)
+    return cached[1:]
 
 
 def _paths_struct(proj, r_cols, cs, cv, ct2):

@@ -1,12 +1,15 @@
-"""Float64 restatement of the reference SE3Conv forward (test infrastructure).
+"""Torch restatement of the reference SE3Conv forward.
+
+TEST INFRASTRUCTURE ONLY (the checker of the fused SE3Conv message kernel and the CPU baseline
+of its benchmark configuration); the product never imports it.
 
 Restates geoembodied/nn/modules/se3_conv.py: RadialBasis (:271-284), _compute_messages paths 0-8
-(:61-235) with the reference's per-edge association, the per-target sum, the division by the
-cloud's average degree and the scalar bias (:487-545), in float64 on whatever device the inputs
-are on. ``absolute=True`` evaluates every product and sum on absolute values, which bounds the
-rounding error of any fp32 evaluation order of the same expression. Used by the tests as the
-floating-point reference of the fused kernel; pinned against the reference's own CPU outputs in
-tests/test_se3_restatement.py.
+(:61-235) with the reference's per-edge association (gather the source rows, mix channels per
+edge), the per-target sum, the division by the cloud's average degree and the scalar bias
+(:487-545), in ``dtype`` (float64 for the checks) on whatever device the inputs are on.
+``absolute=True`` evaluates every product and sum on absolute values, which bounds the rounding
+error of any fp32 evaluation order of the same expression. Pinned against the reference's own CPU
+outputs in tests/test_se3_restatement.py.
 """
 
 from __future__ import annotations
@@ -55,27 +58,29 @@ def avg_degree(col, N, clouds):
 
 
 def radial(sd, dist, cutoff, num_basis):
-    f = sd["radial_basis.freqs"].double()
+    t = dist.dtype
+    f = sd["radial_basis.freqs"].to(t)
     d = dist[:, None]
     basis = torch.sin(f * d) / d.clamp(min=1e-8)
     env = (0.5 * (1.0 + torch.cos(math.pi * dist / cutoff))).clamp(min=0.0)[:, None]
-    h = torch.nn.functional.silu((basis * env) @ sd["radial_basis.mlp.0.weight"].double().t()
-                                 + sd["radial_basis.mlp.0.bias"].double())
-    return h @ sd["radial_basis.mlp.2.weight"].double().t() + sd["radial_basis.mlp.2.bias"].double()
+    h = torch.nn.functional.silu((basis * env) @ sd["radial_basis.mlp.0.weight"].to(t).t()
+                                 + sd["radial_basis.mlp.0.bias"].to(t))
+    return h @ sd["radial_basis.mlp.2.weight"].to(t).t() + sd["radial_basis.mlp.2.bias"].to(t)
 
 
-def se3_forward(sd, dims, pos, row, col, s, v, t2, clouds, cutoff, num_basis=16, absolute=False, R=None):
-    """(s_out, v_out, t2_out) in float64; sd = state dict (tensors), dims = (Cs_in, Cv_in, Cs_out,
+def se3_forward(sd, dims, pos, row, col, s, v, t2, clouds, cutoff, num_basis=16, absolute=False, R=None,
+                dtype=torch.float64):
+    """(s_out, v_out, t2_out) in ``dtype``; sd = state dict (tensors), dims = (Cs_in, Cv_in, Cs_out,
     Cv_out, Ct2_in, Ct2_out). ``R`` (optional) replaces the radial weights."""
     cs_i, cv_i, cs_o, cv_o, ct_i, ct_o = dims
     N = pos.shape[0]
-    dist, u, Y = geometry(pos.double(), row, col)
+    dist, u, Y = geometry(pos.to(dtype), row, col)
     if R is None:
         R = radial(sd, dist, cutoff, num_basis)
-    R = R.double()
-    W = {k: sd[k].double() for k in sd if k.startswith("w_")}
-    s, v = s.double()[row], v.double()[row]
-    t2 = t2.double()[row] if t2 is not None else None
+    R = R.to(dtype)
+    W = {k: sd[k].to(dtype) for k in sd if k.startswith("w_")}
+    s, v = s.to(dtype)[row], v.to(dtype)[row]
+    t2 = t2.to(dtype)[row] if t2 is not None else None
     Y0, Y2 = Y[:, 0:1], Y[:, 4:9]
     if absolute:
         ab = torch.abs
@@ -83,9 +88,9 @@ def se3_forward(sd, dims, pos, row, col, s, v, t2, clouds, cutoff, num_basis=16,
         t2 = ab(t2) if t2 is not None else None
         W = {k: ab(w) for k, w in W.items()}
     E = row.shape[0]
-    ms = torch.zeros(E, cs_o, dtype=torch.float64, device=pos.device)
-    mv = torch.zeros(E, cv_o, 3, dtype=torch.float64, device=pos.device)
-    mt = torch.zeros(E, ct_o, 5, dtype=torch.float64, device=pos.device)
+    ms = torch.zeros(E, cs_o, dtype=dtype, device=pos.device)
+    mv = torch.zeros(E, cv_o, 3, dtype=dtype, device=pos.device)
+    mt = torch.zeros(E, ct_o, 5, dtype=dtype, device=pos.device)
     p = 0
 
     def r():
@@ -124,7 +129,7 @@ def se3_forward(sd, dims, pos, row, col, s, v, t2, clouds, cutoff, num_basis=16,
                                                              ).transpose(-1, -2)
             p += 1
         if "w_vt2.weight" in W:
-            cg = cg_cart().to(pos.device)
+            cg = cg_cart().to(device=pos.device, dtype=dtype)
             cg = torch.abs(cg) if absolute else cg
             outer = (u[:, None, :, None] * v[:, :, None, :]).reshape(E, v.shape[1], 9)
             tp = outer @ cg.reshape(9, 5)
@@ -133,11 +138,11 @@ def se3_forward(sd, dims, pos, row, col, s, v, t2, clouds, cutoff, num_basis=16,
     if "w_t2s.weight" in W and t2 is not None:
         ms = ms + r() * ((t2 * t2).sum(-1) @ W["w_t2s.weight"].t())
         p += 1
-    avg = avg_degree(col, N, clouds)
-    so = torch.zeros(N, cs_o, dtype=torch.float64, device=pos.device).index_add_(0, col, ms) / avg[:, None]
-    vo = torch.zeros(N, cv_o, 3, dtype=torch.float64, device=pos.device).index_add_(0, col, mv) / avg[:, None, None]
-    to = torch.zeros(N, ct_o, 5, dtype=torch.float64, device=pos.device).index_add_(0, col, mt) / avg[:, None, None]
+    avg = avg_degree(col, N, clouds).to(dtype)
+    so = torch.zeros(N, cs_o, dtype=dtype, device=pos.device).index_add_(0, col, ms) / avg[:, None]
+    vo = torch.zeros(N, cv_o, 3, dtype=dtype, device=pos.device).index_add_(0, col, mv) / avg[:, None, None]
+    to = torch.zeros(N, ct_o, 5, dtype=dtype, device=pos.device).index_add_(0, col, mt) / avg[:, None, None]
     if "scalar_bias" in sd and cs_o > 0:
-        b = sd["scalar_bias"].double()
+        b = sd["scalar_bias"].to(dtype)
         so = so + (torch.abs(b) if absolute else b)
     return so, vo, to

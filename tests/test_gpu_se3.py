@@ -1,7 +1,7 @@
 """GPU parity of the fused SE3Conv message aggregation (gdl_se3_aggregate + backward) through
 the SE3Conv mirror: against the reference's own fp32 outputs and gradients
 (tests/golden/golden_se3.npz) and against the float64 restatement of the reference formulas
-(tests/se3_f64.py, itself pinned to the reference in tests/test_se3_restatement.py).
+(oracle/se3_ref.py, itself pinned to the reference in tests/test_se3_restatement.py).
 
 Floating point, summed in a different order than the reference (per-node channel mixing, then
 per-edge products), so the bars are rounding bounds: outputs |ours - f64| <= 1e-5 * (the formula
@@ -14,7 +14,7 @@ import torch
 
 from gdl_b200.se3_conv import SE3Conv
 from gdl_b200.spatial_graph import SpatialGraph
-from tests import se3_f64
+from oracle import se3_ref as se3_f64
 
 pytestmark = [pytest.mark.gpu,
               pytest.mark.skipif(not torch.cuda.is_available(), reason="needs a CUDA device")]

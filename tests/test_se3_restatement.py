@@ -1,4 +1,4 @@
-"""Pin the float64 restatement of SE3Conv (tests/se3_f64.py), which the GPU tests use as the
+"""Pin the float64 restatement of SE3Conv (oracle/se3_ref.py), which the GPU tests use as the
 reference of the fused message kernel, against the reference's own CPU outputs
 (tests/golden/golden_se3.npz, made by tests/golden/make_golden.py). The reference computes in
 fp32, so the bar is its rounding bound: |ref32 - f64| <= 1e-5 * (the same expression on
@@ -8,7 +8,7 @@ import numpy as np
 import pytest
 import torch
 
-from tests import se3_f64
+from oracle import se3_ref as se3_f64
 
 
 @pytest.fixture(scope="module")
