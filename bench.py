@@ -1277,6 +1277,13 @@ ROOFLINE_NOTES = {
     "fps_chain": "see fps",
     "knn": "brute-force KNN is bound by the fp32 pipe (8 flops per pair), not by HBM; the pair rate is "
            "reported in profiles/knn_fast_kernel_c3_c4.md.",
+    "se3conv_fwd_bwd": "a whole layer step through eager autograd (cuBLAS projection GEMMs, the radial MLP, "
+                       "the fused message kernels and their backward) over a 43.9 K-edge graph: launch-bound; "
+                       "the bytes are those of the fused kernels only.",
+    "radius_geometry": "dominated by the radius search (candidate scan in L1/L2, not HBM); the geometry "
+                       "emission's own DRAM figures are in profiles/geometry_aggregation_kernels.md.",
+    "radius_graph": "the radius search scans candidate cells from L1/L2; its algorithmic HBM bytes (points, "
+                    "edges) are small next to the candidate work.",
 }
 
 
