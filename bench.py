@@ -170,20 +170,34 @@ class C2:
         }
 
     def e2e_step(self):
-        """Public API, host buffers in and out."""
+        """Public API, host buffers in and out. The feature upload runs on a second stream while
+        FPS and the radius graph run, and the result's download while the backward runs."""
+        main = torch.cuda.current_stream(self.dev)
+        if not hasattr(self, "_copy_stream"):
+            self._copy_stream = torch.cuda.Stream(self.dev)
+            self._host_out = torch.empty(self.nc, self.C, dtype=torch.float32).pin_memory()
+        cs = self._copy_stream
+        cs.wait_stream(main)  # the previous step's readers of the feature buffer are done
         pos = self.pos_h.to(self.dev, non_blocking=True)
-        feat = self.feat_h.to(self.dev, non_blocking=True)
+        with torch.cuda.stream(cs):
+            feat = self.feat_h.to(self.dev, non_blocking=True)
         idx, cent = csrc.fps_cuda(pos, self.ptr_h, self.k_h, return_pos=True)
         row_ptr, src, _, rp32, src32 = csrc.radius_graph_csr(cent, self.R, self.cptr_h, max_num_neighbors=self.NN,
                                                              int32_csr=True)
         ns, ne = rp32[:-1], rp32[1:]
+        main.wait_stream(cs)
+        feat.record_stream(main)
         out = csrc.segment_reduce_cuda(feat, src32, ns, ne, self.nc, "mean")
+        cs.wait_stream(main)
+        with torch.cuda.stream(cs):
+            self._host_out.copy_(out, non_blocking=True)
+        out.record_stream(cs)
         g = csrc.segment_reduce_backward_cuda(self.gout, self.gmsg, None, None, None, ns, ne, self.nc, "mean",
                                               grad_msg=self.gmsg)
-        host = out.to("cpu", non_blocking=True)
-        torch.cuda.current_stream(self.dev).synchronize()
+        main.synchronize()
+        cs.synchronize()
         del g
-        return host
+        return self._host_out
 
     e2e_h2d = property(lambda self: self.pos_h.numel() * 4 + self.feat_h.numel() * 4)
     e2e_d2h = property(lambda self: self.nc * self.C * 4)
