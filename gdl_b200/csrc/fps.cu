@@ -17,10 +17,12 @@
 //    a shared-memory u64 atomicMax measured ~300 cycles slower per step here);
 //  * the winner's local index is decoded from its priority (a bijection) and its coordinates
 //    read back from shared memory.
-// Clouds above one CTA's register budget run on a thread-block cluster (up to 16 CTAs, one per
-// SM): each CTA's winner record goes to every CTA of the cluster through distributed shared
-// memory and one cluster barrier per step publishes it. Larger clouds fall back to a CTA that
-// streams points from HBM with min_d in a workspace.
+// Clouds above one CTA's register budget run on a thread-block cluster (up to 16 CTAs of 13312
+// points each, one per SM): each CTA's winner record goes to every CTA of the cluster through
+// distributed shared memory (st.async + mbarrier per pick). A 131072-point cloud takes 10 CTAs,
+// the largest cluster of which 8 fit on a B200 at once (11 of 10 CTAs, 7 of 11-16 CTAs), so a
+// batch of 8 LiDAR clouds runs in one wave. Larger clouds fall back to a CTA that streams points
+// from HBM with min_d in a workspace.
 #include <cooperative_groups.h>
 
 #include "common.cuh"
@@ -152,6 +154,90 @@ struct PointRegs {
     }
 };
 
+// Register state of the cluster kernel: P points per thread with NO stored priority, so that
+// more points fit per CTA (a cluster of at most 10 CTAs per 131072-point cloud, the largest size
+// at which 8 clusters are resident at once on a B200). With THREADS = 256 and the CTA's first
+// point a multiple of 512, a thread's points i = base + tid + 256 j are ordered by either tie
+// rule as a fixed permutation of j: lowest index = ascending j; the reference's order (see
+// fps_priority) = even j ascending, then odd j ascending (its bit 27 is j's parity, its low bits
+// j / 2). The running max uses that rank in the key's low word; the thread's winner then gets
+// its true priority. Slots past the cloud (j >= nv) hold min_d = 0 and can only surface when
+// every valid minimum is 0 too; that case rescans the valid slots.
+template <int P, int TIE>
+struct WidePoints {
+    static_assert(P % 2 == 0, "points are held in pairs");
+    static constexpr int THREADS = 256;
+    uint64_t xp[P / 2], yp[P / 2], zp[P / 2];
+    float md[P];
+    int nv;    // slots j < nv hold points of the cloud
+    int base;  // local index of this CTA's first point
+
+    static __device__ __forceinline__ constexpr uint32_t pref(int j) {  // larger = preferred
+        return (uint32_t)(P - 1 - (TIE == GDL_TIE_LOWEST_INDEX ? j : ((j & 1) ? P / 2 + j / 2 : j / 2)));
+    }
+    static __device__ __forceinline__ int unpref(uint32_t p) {
+        const int q = P - 1 - (int)p;
+        return TIE == GDL_TIE_LOWEST_INDEX ? q : (q < P / 2 ? 2 * q : 2 * (q - P / 2) + 1);
+    }
+
+    __device__ __forceinline__ void load(const float *__restrict__ pos, int64_t start, int n, int b, int,
+                                         float4 *__restrict__ sxyz) {
+        base = b;
+        nv = 0;
+        float x[P], y[P], z[P];
+#pragma unroll
+        for (int j = 0; j < P; ++j) {
+            const int i = base + (int)threadIdx.x + j * THREADS;
+            if (i < n) {
+                const float *p = pos + 3 * (start + i);
+                x[j] = p[0];
+                y[j] = p[1];
+                z[j] = p[2];
+                md[j] = 1e30f;
+                sxyz[i - base] = make_float4(x[j], y[j], z[j], 0.0f);
+                nv = j + 1;
+            } else {
+                x[j] = y[j] = z[j] = 0.0f;
+                md[j] = 0.0f;
+            }
+        }
+#pragma unroll
+        for (int h = 0; h < P / 2; ++h) {
+            xp[h] = pack2(x[2 * h], x[2 * h + 1]);
+            yp[h] = pack2(y[2 * h], y[2 * h + 1]);
+            zp[h] = pack2(z[2 * h], z[2 * h + 1]);
+        }
+    }
+
+    __device__ __forceinline__ uint64_t step(float sx, float sy, float sz) {
+        const uint64_t SX = pack2(sx, sx), SY = pack2(sy, sy), SZ = pack2(sz, sz);
+        uint64_t acc[4] = {0ull, 0ull, 0ull, 0ull};
+#pragma unroll
+        for (int h = 0; h < P / 2; ++h) {
+            float d0, d1;
+            unpack2(dist2_x2(xp[h], yp[h], zp[h], SX, SY, SZ), d0, d1);
+            const float m0 = fminf(d0, md[2 * h]), m1 = fminf(d1, md[2 * h + 1]);
+            md[2 * h] = m0;
+            md[2 * h + 1] = m1;
+            const uint64_t k0 = ((uint64_t)__float_as_uint(m0) << 32) | pref(2 * h);
+            const uint64_t k1 = ((uint64_t)__float_as_uint(m1) << 32) | pref(2 * h + 1);
+            acc[h & 3] = umax64(acc[h & 3], umax64(k0, k1));
+        }
+        if (nv == 0) return 0ull;
+        uint64_t best = umax64(umax64(acc[0], acc[1]), umax64(acc[2], acc[3]));
+        int j = unpref((uint32_t)best);
+        if (j >= nv) {  // a padding slot won among zero minima: take the best valid slot
+            best = 0ull;
+#pragma unroll
+            for (int t = 0; t < P; ++t)
+                if (t < nv) best = umax64(best, ((uint64_t)__float_as_uint(md[t]) << 32) | pref(t));
+            j = unpref((uint32_t)best);
+        }
+        const uint32_t prio = fps_priority((uint32_t)(base + (int)threadIdx.x + j * THREADS), TIE);
+        return (best & 0xffffffff00000000ull) | (uint64_t)(~prio);
+    }
+};
+
 // ------------------------------------------------------------------ one CTA per cloud
 template <int THREADS, int P>
 __global__ void __launch_bounds__(THREADS) fps_cta_kernel(const float *__restrict__ pos,
@@ -216,7 +302,7 @@ __device__ __forceinline__ uint32_t mapa_u32(uint32_t a, int rank) {
 
 constexpr int kClusterWaitLimit = 1 << 20;  // mbarrier polls before a CTA gives up
 
-template <int THREADS, int P>
+template <int THREADS, int P, class PR>
 __global__ void __launch_bounds__(THREADS) fps_cluster_kernel(const float *__restrict__ pos,
                                                               const int64_t *__restrict__ ptr,
                                                               const int64_t *__restrict__ kpc, int tie,
@@ -239,7 +325,7 @@ __global__ void __launch_bounds__(THREADS) fps_cluster_kernel(const float *__res
     const int64_t actual = (kb <= 0 || n <= 0) ? 0 : (kb < n ? kb : n);
     if (rank == 0) pad_outputs(out, out_pos, o0, actual, kb, THREADS);
     const int base = rank * THREADS * P;
-    PointRegs<THREADS, P> pr;
+    PR pr;
     pr.load(pos, start, n, base, tie, sxyz);
     float sx = 0.0f, sy = 0.0f, sz = 0.0f;
     if (actual > 0) {
@@ -374,14 +460,17 @@ static cudaError_t launch_cta(int B, const float *pos, const int64_t *ptr, const
     return cudaGetLastError();
 }
 
-constexpr int kClusterThreads = 512;
-constexpr int kClusterP = 16;
-constexpr int64_t kCtaCapacity = (int64_t)kClusterThreads * kClusterP;  // points per CTA
+constexpr int kCtaCapacity = 256 * 32;         // points per single-CTA cloud (fps_cta_kernel<256, 32>)
+constexpr int kClusterThreads = 256;
+constexpr int kClusterP = 52;                   // 13312 points per CTA: 10 CTAs for 131072 points
+constexpr int64_t kClusterCapacity = (int64_t)kClusterThreads * kClusterP;
 
 static cudaError_t launch_cluster(int B, int cs, const float *pos, const int64_t *ptr, const int64_t *kpc, int tie,
                                   int64_t *out, float *out_pos, cudaStream_t st) {
-    auto kern = fps_cluster_kernel<kClusterThreads, kClusterP>;
-    const size_t smem = sizeof(float4) * kCtaCapacity;
+    auto kern = tie == GDL_TIE_LOWEST_INDEX
+                    ? fps_cluster_kernel<kClusterThreads, kClusterP, WidePoints<kClusterP, GDL_TIE_LOWEST_INDEX>>
+                    : fps_cluster_kernel<kClusterThreads, kClusterP, WidePoints<kClusterP, GDL_TIE_REFERENCE>>;
+    const size_t smem = sizeof(float4) * kClusterCapacity;
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e;
     if (cs > 8) {
@@ -433,7 +522,7 @@ extern "C" int gdl_fps(const float *pos, const int64_t *ptr, const int64_t *k_pe
     else if (m <= 4096) e = launch_cta<256, 16>(num_clouds, pos, ptr, k_per_cloud, tie_break, out_idx, out_pos, st);
     else if (m <= kCtaCapacity) e = launch_cta<256, 32>(num_clouds, pos, ptr, k_per_cloud, tie_break, out_idx, out_pos, st);
     else {
-        const int cs = (int)((m + kCtaCapacity - 1) / kCtaCapacity);
+        const int cs = (int)((m + kClusterCapacity - 1) / kClusterCapacity);
         e = cudaErrorInvalidConfiguration;
         if (cs <= 16) e = launch_cluster(num_clouds, cs, pos, ptr, k_per_cloud, tie_break, out_idx, out_pos, st);
         if (e != cudaSuccess) {

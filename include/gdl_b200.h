@@ -62,8 +62,9 @@ int gdl_check_device(int device);
  *              min(k_b, n_b) global indices in selection order, then -1 padding.
  * n_points     rows of pos.
  * max_cloud_points  host-side upper bound of max_b n_b (selects the kernel variant: one CTA
- *              per cloud up to 8192 points, a thread-block cluster up to 131072, else a
- *              streaming CTA that keeps the running minima in the workspace).
+ *              per cloud up to 8192 points, a thread-block cluster of up to 16 CTAs of 13312
+ *              points up to 212992, else a streaming CTA that keeps the running minima in the
+ *              workspace).
  * tie_break    GDL_TIE_REFERENCE: the reference kernel's argmax reduction order
  *              (bit-identical to fps_kernel<512>); GDL_TIE_LOWEST_INDEX: torch.argmax.
  * out_pos      [same slots, 3] f32 (nullable): coordinates of each pick (0 for padding), which
