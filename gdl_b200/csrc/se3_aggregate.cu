@@ -45,6 +45,26 @@ __device__ __forceinline__ void load_edge(const Se3Paths &P, const float *__rest
     for (int m = 0; m < 5; ++m) x.y2[m] = sd >= 9 ? sph[e * sd + 4 + m] : 0.0f;
 }
 
+// lane t's edge values, to every lane (the edges of a segment are loaded 32 at a time, one per
+// lane, so that their loads overlap instead of forming a dependent chain per edge)
+__device__ __forceinline__ void shfl_edge(const Se3Edge &m, int t, Se3Edge &x) {
+#pragma unroll
+    for (int p = 0; p < 9; ++p) x.r[p] = __shfl_sync(0xffffffffu, m.r[p], t);
+#pragma unroll
+    for (int k = 0; k < 3; ++k) x.d[k] = __shfl_sync(0xffffffffu, m.d[k], t);
+    x.y0 = __shfl_sync(0xffffffffu, m.y0, t);
+#pragma unroll
+    for (int k = 0; k < 5; ++k) x.y2[k] = __shfl_sync(0xffffffffu, m.y2[k], t);
+}
+
+__device__ __forceinline__ void zero_edge(Se3Edge &x) {
+#pragma unroll
+    for (int p = 0; p < 9; ++p) x.r[p] = 0.0f;
+    x.d[0] = x.d[1] = x.d[2] = x.y0 = 0.0f;
+#pragma unroll
+    for (int k = 0; k < 5; ++k) x.y2[k] = 0.0f;
+}
+
 // Term of path p in message channel f of an edge from source s (0 when path p does not feed f's
 // kind). Channels: f < cs scalar o = f; then 3 cv vector (o, k); then 5 ct2 type-2 (o, m).
 __device__ __forceinline__ float se3_term(const Se3Paths &P, const float *__restrict__ cg, const Se3Edge &x, int64_t s,
@@ -134,15 +154,26 @@ __global__ void __launch_bounds__(256, 2) se3_agg_fwd_kernel(Se3Paths P, const f
             float acc[kSe3Chunks];
 #pragma unroll
             for (int i = 0; i < kSe3Chunks; ++i) acc[i] = 0.0f;
-            for (int32_t j = j0; j < j1; ++j) {
-                const int64_t e = perm[j];
-                const int64_t s = row[e];
-                Se3Edge x;
-                load_edge(P, R, rs, dir, sph, sd, e, x);
+            for (int32_t jb = j0; jb < j1; jb += 32) {  // up to 32 edges: lane t loads edge jb + t
+                const int cnt = j1 - jb < 32 ? (int)(j1 - jb) : 32;
+                Se3Edge mine;
+                int64_t msrc = 0;
+                if (lane < cnt) {
+                    const int64_t e = perm[jb + lane];
+                    msrc = row[e];
+                    load_edge(P, R, rs, dir, sph, sd, e, mine);
+                } else {
+                    zero_edge(mine);
+                }
+                for (int t = 0; t < cnt; ++t) {  // slot order is kept: edges are folded one by one
+                    Se3Edge x;
+                    shfl_edge(mine, t, x);
+                    const int64_t s = __shfl_sync(0xffffffffu, msrc, t);
 #pragma unroll
-                for (int i = 0; i < kSe3Chunks; ++i) {
-                    const int f = c0 + lane + 32 * i;
-                    if (f < ctot) acc[i] = __fadd_rn(acc[i], se3_message(P, cg, x, s, f));
+                    for (int i = 0; i < kSe3Chunks; ++i) {
+                        const int f = c0 + lane + 32 * i;
+                        if (f < ctot) acc[i] = __fadd_rn(acc[i], se3_message(P, cg, x, s, f));
+                    }
                 }
             }
 #pragma unroll
@@ -313,16 +344,29 @@ __global__ void __launch_bounds__(256, 2) se3_agg_grad_p_kernel(Se3Paths P, Se3G
                 float acc[kSe3Chunks];
 #pragma unroll
                 for (int i = 0; i < kSe3Chunks; ++i) acc[i] = 0.0f;
-                for (int32_t j = j0; j < j1; ++j) {
-                    const int64_t e = sperm[j];
-                    const int64_t t = col[e];
-                    const float a = avg[t];
-                    Se3Edge x;
-                    load_edge(P, R, rs, dir, sph, sd, e, x);
+                for (int32_t jb = j0; jb < j1; jb += 32) {  // lane u loads out-edge jb + u
+                    const int cnt = j1 - jb < 32 ? (int)(j1 - jb) : 32;
+                    Se3Edge mine;
+                    int64_t mt = 0;
+                    float ma = 1.0f;
+                    if (lane < cnt) {
+                        const int64_t e = sperm[jb + lane];
+                        mt = col[e];
+                        ma = avg[mt];
+                        load_edge(P, R, rs, dir, sph, sd, e, mine);
+                    } else {
+                        zero_edge(mine);
+                    }
+                    for (int u = 0; u < cnt; ++u) {
+                        Se3Edge x;
+                        shfl_edge(mine, u, x);
+                        const int64_t t = __shfl_sync(0xffffffffu, mt, u);
+                        const float a = __shfl_sync(0xffffffffu, ma, u);
 #pragma unroll
-                    for (int i = 0; i < kSe3Chunks; ++i) {
-                        const int q = q0 + lane + 32 * i;
-                        if (q < w) acc[i] = __fadd_rn(acc[i], proj_grad_term(P, cg, x, gs, gv, gt, t, a, p, q));
+                        for (int i = 0; i < kSe3Chunks; ++i) {
+                            const int q = q0 + lane + 32 * i;
+                            if (q < w) acc[i] = __fadd_rn(acc[i], proj_grad_term(P, cg, x, gs, gv, gt, t, a, p, q));
+                        }
                     }
                 }
 #pragma unroll
