@@ -120,6 +120,22 @@ def test_knn_grid_path_vs_reference_kernel(ref, kind, k):
     assert torch.equal(gd.cpu().view(torch.int32), wd.cpu().view(torch.int32))
 
 
+@pytest.mark.parametrize("kind", ["uniform", "gmm", "lattice", "dup", "nonfinite"])
+@pytest.mark.parametrize("k", [16, 32, 64, 80])
+@pytest.mark.parametrize("cpu_ptr", [True, False])
+def test_knn_large_k_mid_clouds_vs_reference_kernel(ref, kind, k, cpu_ptr):
+    """k >= 16 over clouds of 4097 .. 32767 sources: the per-thread heap path with its scan split
+    over CTAs and merged (a CUDA ptr sizes the split by the mean cloud, a CPU ptr by the largest)."""
+    from gdl_b200 import csrc
+
+    x, ptr = _clouds(31, [9000, 50, 5000, 20000], kind)
+    q, pq = _clouds(32, [700, 9, 300, 1500], "huge" if kind == "nonfinite" else kind)
+    wi, wd = ref["knn"].knn_cuda(q.to(DEV), x.to(DEV), pq.to(DEV), ptr.to(DEV), k)
+    gi, gd = csrc.knn_cuda(q.to(DEV), x.to(DEV), pq.to(DEV), ptr if cpu_ptr else ptr.to(DEV), k)
+    assert torch.equal(gi.cpu(), wi.cpu())
+    assert torch.equal(gd.cpu().view(torch.int32), wd.cpu().view(torch.int32))
+
+
 def _edge_set(row, col):
     r = row.cpu().numpy().astype(np.int64)
     c = col.cpu().numpy().astype(np.int64)
