@@ -136,6 +136,17 @@ def require_cuda(*tensors: torch.Tensor, what: str) -> torch.device:
     return dev
 
 
+def to_device(t: torch.Tensor, device: torch.device, dtype: torch.dtype | None = None) -> torch.Tensor:
+    """``t`` on ``device`` (converted to ``dtype``), contiguous. A CPU tensor is staged in pinned
+    memory first: a copy from pageable memory makes the host wait for the work already queued on
+    the stream, which would serialise the caller's Python with the GPU."""
+    if dtype is not None and t.dtype != dtype:
+        t = t.to(dtype)
+    if t.is_cuda:
+        return t.to(device).contiguous()
+    return t.contiguous().pin_memory().to(device, non_blocking=True)
+
+
 def ptr(t) -> int | None:
     return None if t is None else t.data_ptr()
 

@@ -78,8 +78,8 @@ def fps_cuda(pos: torch.Tensor, ptr: torch.Tensor, k_per_batch: torch.Tensor, *,
         e = torch.empty(0, dtype=torch.int64, device=dev)
         return (e, torch.empty(0, 3, device=dev)) if return_pos else e
     max_n = int((ptr_h[1:] - ptr_h[:-1]).max())
-    ptr_d = ptr_h.to(dev, non_blocking=True) if not ptr.is_cuda else ptr.to(torch.int64).contiguous()
-    k_d = k_h.to(dev, non_blocking=True) if not k_per_batch.is_cuda else k_per_batch.to(torch.int64).contiguous()
+    ptr_d = nat.to_device(ptr_h, dev) if not ptr.is_cuda else ptr.to(torch.int64).contiguous()
+    k_d = nat.to_device(k_h, dev) if not k_per_batch.is_cuda else k_per_batch.to(torch.int64).contiguous()
     out = torch.empty(total, dtype=torch.int64, device=dev)
     opos = torch.empty(total, 3, dtype=torch.float32, device=dev) if return_pos else None
     L = nat.load()
@@ -103,8 +103,8 @@ def knn_cuda(query: torch.Tensor, source: torch.Tensor, ptr_q: torch.Tensor, ptr
     query = query.contiguous().float()
     source = source.contiguous().float()
     ptr_s_host = ptr_s.to(torch.int64) if not ptr_s.is_cuda else None
-    ptr_q = ptr_q.to(device=dev, dtype=torch.int64).contiguous()
-    ptr_s = ptr_s.to(device=dev, dtype=torch.int64).contiguous()
+    ptr_q = nat.to_device(ptr_q, dev, torch.int64)
+    ptr_s = nat.to_device(ptr_s, dev, torch.int64)
     K = int(k)
     nq = query.shape[0]
     if nq == 0 or K <= 0:
@@ -140,7 +140,7 @@ def _radius_call(x, r, ptr, max_num_neighbors, loop, mask, with_dst, max_cloud_p
     N = x.shape[0]
     if max_cloud_points is None:
         max_cloud_points = int((ptr[1:] - ptr[:-1]).max()) if (not ptr.is_cuda and ptr.numel() > 1) else 0
-    ptr = ptr.to(device=dev, dtype=torch.int64).contiguous()
+    ptr = nat.to_device(ptr, dev, torch.int64)
     B = ptr.numel() - 1
     cap_k = 16 if max_num_neighbors <= 16 else 32 if max_num_neighbors <= 32 else 64
     cap = max(N * cap_k, 1)
@@ -151,7 +151,7 @@ def _radius_call(x, r, ptr, max_num_neighbors, loop, mask, with_dst, max_cloud_p
     src32 = torch.empty(cap, dtype=torch.int32, device=dev) if int32_csr else None
     m = None
     if mask is not None and mask.numel() > 0:
-        m = mask.to(device=dev).contiguous()
+        m = nat.to_device(mask, dev)
         m = m.view(torch.uint8) if m.dtype == torch.bool else m.to(torch.uint8)
     L = nat.load()
     ws = nat.workspace(L.gdl_radius_graph_workspace_size(N, B, int(max_num_neighbors)), dev)
@@ -270,10 +270,10 @@ def cloud_avg_degree_cuda(node_start: torch.Tensor, node_end: torch.Tensor, *, b
     b = p = None
     B = 0
     if batch is not None:
-        b = batch.to(device=dev, dtype=torch.int64).contiguous()
+        b = nat.to_device(batch, dev, torch.int64)
         B = int(num_clouds) if num_clouds is not None else (int(b.max().item()) + 1 if N else 1)
     elif ptr is not None:
-        p = ptr.to(device=dev, dtype=torch.int64).contiguous()
+        p = nat.to_device(ptr, dev, torch.int64)
         B = p.numel() - 1
     L = nat.load()
     ws = nat.workspace(L.gdl_cloud_avg_degree_workspace_size(max(B, 1)), dev)
