@@ -150,20 +150,30 @@ __global__ void __launch_bounds__(256, 2) se3_agg_fwd_kernel(Se3Paths P, const f
     for (int64_t n = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); n < N; n += warps) {
         const int32_t j0 = ns[n], j1 = ne[n];
         const float a = avg[n];
+        // a segment of at most 32 edges (the usual case) is loaded once for all channel passes
+        const bool single = j1 - j0 <= 32;
+        Se3Edge mine;
+        int64_t msrc = 0;
+        zero_edge(mine);
+        if (single && lane < j1 - j0) {
+            const int64_t e = perm[j0 + lane];
+            msrc = row[e];
+            load_edge(P, R, rs, dir, sph, sd, e, mine);
+        }
         for (int c0 = 0; c0 < ctot; c0 += 32 * kSe3Chunks) {
             float acc[kSe3Chunks];
 #pragma unroll
             for (int i = 0; i < kSe3Chunks; ++i) acc[i] = 0.0f;
             for (int32_t jb = j0; jb < j1; jb += 32) {  // up to 32 edges: lane t loads edge jb + t
                 const int cnt = j1 - jb < 32 ? (int)(j1 - jb) : 32;
-                Se3Edge mine;
-                int64_t msrc = 0;
-                if (lane < cnt) {
-                    const int64_t e = perm[jb + lane];
-                    msrc = row[e];
-                    load_edge(P, R, rs, dir, sph, sd, e, mine);
-                } else {
+                if (!single) {
+                    msrc = 0;
                     zero_edge(mine);
+                    if (lane < cnt) {
+                        const int64_t e = perm[jb + lane];
+                        msrc = row[e];
+                        load_edge(P, R, rs, dir, sph, sd, e, mine);
+                    }
                 }
                 for (int t = 0; t < cnt; ++t) {  // slot order is kept: edges are folded one by one
                     Se3Edge x;
@@ -337,6 +347,18 @@ __global__ void __launch_bounds__(256, 2) se3_agg_grad_p_kernel(Se3Paths P, Se3G
     const int64_t warps = (int64_t)gridDim.x * (blockDim.x >> 5);
     for (int64_t s = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); s < N; s += warps) {
         const int32_t j0 = sns[s], j1 = sne[s];
+        // at most 32 out-edges (the usual case): loaded once for all projections and passes
+        const bool single = j1 - j0 <= 32;
+        Se3Edge mine;
+        int64_t mt = 0;
+        float ma = 1.0f;
+        zero_edge(mine);
+        if (single && lane < j1 - j0) {
+            const int64_t e = sperm[j0 + lane];
+            mt = col[e];
+            ma = avg[mt];
+            load_edge(P, R, rs, dir, sph, sd, e, mine);
+        }
         for (int p = 0; p < 9; ++p) {
             if (!Gp.g[p]) continue;
             const int w = proj_width(P, p);
@@ -346,16 +368,16 @@ __global__ void __launch_bounds__(256, 2) se3_agg_grad_p_kernel(Se3Paths P, Se3G
                 for (int i = 0; i < kSe3Chunks; ++i) acc[i] = 0.0f;
                 for (int32_t jb = j0; jb < j1; jb += 32) {  // lane u loads out-edge jb + u
                     const int cnt = j1 - jb < 32 ? (int)(j1 - jb) : 32;
-                    Se3Edge mine;
-                    int64_t mt = 0;
-                    float ma = 1.0f;
-                    if (lane < cnt) {
-                        const int64_t e = sperm[jb + lane];
-                        mt = col[e];
-                        ma = avg[mt];
-                        load_edge(P, R, rs, dir, sph, sd, e, mine);
-                    } else {
+                    if (!single) {
+                        mt = 0;
+                        ma = 1.0f;
                         zero_edge(mine);
+                        if (lane < cnt) {
+                            const int64_t e = sperm[jb + lane];
+                            mt = col[e];
+                            ma = avg[mt];
+                            load_edge(P, R, rs, dir, sph, sd, e, mine);
+                        }
                     }
                     for (int u = 0; u < cnt; ++u) {
                         Se3Edge x;
