@@ -329,6 +329,55 @@ __device__ __forceinline__ float proj_grad_term(const Se3Paths &P, const float *
     }
 }
 
+// one projection's gradient rows for source s (PI fixed at compile time, so that the inner loop
+// holds only that projection's term)
+template <int PI>
+__device__ __forceinline__ void grad_p_pass(const Se3Paths &P, float *__restrict__ gp, const float *__restrict__ R,
+                                            int64_t rs, const float *__restrict__ dir,
+                                            const float *__restrict__ sph, int sd, const float *__restrict__ cg,
+                                            const int64_t *__restrict__ col, const int32_t *__restrict__ sperm,
+                                            const float *__restrict__ avg, const float *__restrict__ gs,
+                                            const float *__restrict__ gv, const float *__restrict__ gt,
+                                            int64_t s, int32_t j0, int32_t j1, bool single, Se3Edge &mine,
+                                            int64_t &mt, float &ma, int lane) {
+    const int w = proj_width(P, PI);
+    for (int q0 = 0; q0 < w; q0 += 32 * kSe3Chunks) {
+        float acc[kSe3Chunks];
+#pragma unroll
+        for (int i = 0; i < kSe3Chunks; ++i) acc[i] = 0.0f;
+        for (int32_t jb = j0; jb < j1; jb += 32) {  // lane u loads out-edge jb + u
+            const int cnt = j1 - jb < 32 ? (int)(j1 - jb) : 32;
+            if (!single) {
+                mt = 0;
+                ma = 1.0f;
+                zero_edge(mine);
+                if (lane < cnt) {
+                    const int64_t e = sperm[jb + lane];
+                    mt = col[e];
+                    ma = avg[mt];
+                    load_edge(P, R, rs, dir, sph, sd, e, mine);
+                }
+            }
+            for (int u = 0; u < cnt; ++u) {
+                Se3Edge x;
+                shfl_edge(mine, u, x);
+                const int64_t t = __shfl_sync(0xffffffffu, mt, u);
+                const float a = __shfl_sync(0xffffffffu, ma, u);
+#pragma unroll
+                for (int i = 0; i < kSe3Chunks; ++i) {
+                    const int q = q0 + lane + 32 * i;
+                    if (q < w) acc[i] = __fadd_rn(acc[i], proj_grad_term(P, cg, x, gs, gv, gt, t, a, PI, q));
+                }
+            }
+        }
+#pragma unroll
+        for (int i = 0; i < kSe3Chunks; ++i) {
+            const int q = q0 + lane + 32 * i;
+            if (q < w) gp[s * w + q] = acc[i];
+        }
+    }
+}
+
 // grad of every projection entry of source node s: one warp per source, its out-edges in
 // source-sorted order (deterministic), lanes over the entries of one projection at a time
 __global__ void __launch_bounds__(256, 2) se3_agg_grad_p_kernel(Se3Paths P, Se3Grads Gp, const float *__restrict__ R,
@@ -359,45 +408,20 @@ __global__ void __launch_bounds__(256, 2) se3_agg_grad_p_kernel(Se3Paths P, Se3G
             ma = avg[mt];
             load_edge(P, R, rs, dir, sph, sd, e, mine);
         }
-        for (int p = 0; p < 9; ++p) {
-            if (!Gp.g[p]) continue;
-            const int w = proj_width(P, p);
-            for (int q0 = 0; q0 < w; q0 += 32 * kSe3Chunks) {
-                float acc[kSe3Chunks];
-#pragma unroll
-                for (int i = 0; i < kSe3Chunks; ++i) acc[i] = 0.0f;
-                for (int32_t jb = j0; jb < j1; jb += 32) {  // lane u loads out-edge jb + u
-                    const int cnt = j1 - jb < 32 ? (int)(j1 - jb) : 32;
-                    if (!single) {
-                        mt = 0;
-                        ma = 1.0f;
-                        zero_edge(mine);
-                        if (lane < cnt) {
-                            const int64_t e = sperm[jb + lane];
-                            mt = col[e];
-                            ma = avg[mt];
-                            load_edge(P, R, rs, dir, sph, sd, e, mine);
-                        }
-                    }
-                    for (int u = 0; u < cnt; ++u) {
-                        Se3Edge x;
-                        shfl_edge(mine, u, x);
-                        const int64_t t = __shfl_sync(0xffffffffu, mt, u);
-                        const float a = __shfl_sync(0xffffffffu, ma, u);
-#pragma unroll
-                        for (int i = 0; i < kSe3Chunks; ++i) {
-                            const int q = q0 + lane + 32 * i;
-                            if (q < w) acc[i] = __fadd_rn(acc[i], proj_grad_term(P, cg, x, gs, gv, gt, t, a, p, q));
-                        }
-                    }
-                }
-#pragma unroll
-                for (int i = 0; i < kSe3Chunks; ++i) {
-                    const int q = q0 + lane + 32 * i;
-                    if (q < w) Gp.g[p][s * w + q] = acc[i];
-                }
-            }
-        }
+#define GDL_SE3_PASS(PI)                                                                                          \
+    if (Gp.g[PI])                                                                                                 \
+        grad_p_pass<PI>(P, Gp.g[PI], R, rs, dir, sph, sd, cg, col, sperm, avg, gs, gv, gt, s, j0, j1, single, mine, \
+                        mt, ma, lane);
+        GDL_SE3_PASS(0)
+        GDL_SE3_PASS(1)
+        GDL_SE3_PASS(2)
+        GDL_SE3_PASS(3)
+        GDL_SE3_PASS(4)
+        GDL_SE3_PASS(5)
+        GDL_SE3_PASS(6)
+        GDL_SE3_PASS(7)
+        GDL_SE3_PASS(8)
+#undef GDL_SE3_PASS
     }
 }
 
