@@ -65,36 +65,33 @@ __device__ __forceinline__ void zero_edge(Se3Edge &x) {
     for (int k = 0; k < 5; ++k) x.y2[k] = 0.0f;
 }
 
-// Term of path p in message channel f of an edge from source s (0 when path p does not feed f's
-// kind). Channels: f < cs scalar o = f; then 3 cv vector (o, k); then 5 ct2 type-2 (o, m).
-__device__ __forceinline__ float se3_term(const Se3Paths &P, const float *__restrict__ cg, const Se3Edge &x, int64_t s,
-                                          int f, int p) {
-    if (f < P.cs) {
-        const int o = f;
-        if (p == 0) return __fmul_rn(__fmul_rn(x.r[0], x.y0), P.p[0][s * P.cs + o]);
-        if (p == 3) {
-            const float *q = P.p[3] + (s * P.cs + o) * 3;
-            const float dot =
-                __fadd_rn(__fadd_rn(__fmul_rn(x.d[0], q[0]), __fmul_rn(x.d[1], q[1])), __fmul_rn(x.d[2], q[2]));
-            return __fmul_rn(x.r[3], dot);
-        }
-        if (p == 8) return __fmul_rn(x.r[8], P.p[8][s * P.cs + o]);
-        return 0.0f;
+// Term of path p in the message of an edge from source s: scalar channel o (paths 0, 3, 8),
+// vector channel (o, k) (paths 1, 2, 4), type-2 channel (o, m) (paths 5, 6, 7).
+__device__ __forceinline__ float se3_term_s(const Se3Paths &P, const Se3Edge &x, int64_t s, int o, int p) {
+    if (p == 0) return __fmul_rn(__fmul_rn(x.r[0], x.y0), P.p[0][s * P.cs + o]);
+    if (p == 3) {
+        const float *q = P.p[3] + (s * P.cs + o) * 3;
+        const float dot =
+            __fadd_rn(__fadd_rn(__fmul_rn(x.d[0], q[0]), __fmul_rn(x.d[1], q[1])), __fmul_rn(x.d[2], q[2]));
+        return __fmul_rn(x.r[3], dot);
     }
-    f -= P.cs;
-    if (f < 3 * P.cv) {
-        const int o = f / 3, k = f - 3 * o;
-        if (p == 1) return __fmul_rn(__fmul_rn(x.r[1], P.p[1][s * P.cv + o]), x.d[k]);
-        if (p == 2) return __fmul_rn(__fmul_rn(x.r[2], x.y0), P.p[2][(s * P.cv + o) * 3 + k]);
-        if (p == 4) {
-            const float *q = P.p[4] + (s * P.cv + o) * 3;
-            const int k1 = k == 2 ? 0 : k + 1, k2 = k == 0 ? 2 : k - 1;  // (d x q)_k = d_k1 q_k2 - d_k2 q_k1
-            return __fmul_rn(x.r[4], __fsub_rn(__fmul_rn(x.d[k1], q[k2]), __fmul_rn(x.d[k2], q[k1])));
-        }
-        return 0.0f;
+    if (p == 8) return __fmul_rn(x.r[8], P.p[8][s * P.cs + o]);
+    return 0.0f;
+}
+
+__device__ __forceinline__ float se3_term_v(const Se3Paths &P, const Se3Edge &x, int64_t s, int o, int k, int p) {
+    if (p == 1) return __fmul_rn(__fmul_rn(x.r[1], P.p[1][s * P.cv + o]), x.d[k]);
+    if (p == 2) return __fmul_rn(__fmul_rn(x.r[2], x.y0), P.p[2][(s * P.cv + o) * 3 + k]);
+    if (p == 4) {
+        const float *q = P.p[4] + (s * P.cv + o) * 3;
+        const int k1 = k == 2 ? 0 : k + 1, k2 = k == 0 ? 2 : k - 1;  // (d x q)_k = d_k1 q_k2 - d_k2 q_k1
+        return __fmul_rn(x.r[4], __fsub_rn(__fmul_rn(x.d[k1], q[k2]), __fmul_rn(x.d[k2], q[k1])));
     }
-    f -= 3 * P.cv;
-    const int o = f / 5, m = f - 5 * o;
+    return 0.0f;
+}
+
+__device__ __forceinline__ float se3_term_t(const Se3Paths &P, const float *__restrict__ cg, const Se3Edge &x,
+                                            int64_t s, int o, int m, int p) {
     if (p == 5) return __fmul_rn(__fmul_rn(x.r[5], P.p[5][s * P.ct2 + o]), x.y2[m]);
     if (p == 6) return __fmul_rn(__fmul_rn(x.r[6], x.y0), P.p[6][(s * P.ct2 + o) * 5 + m]);
     if (p == 7) {
@@ -109,31 +106,88 @@ __device__ __forceinline__ float se3_term(const Se3Paths &P, const float *__rest
     return 0.0f;
 }
 
-// the message of channel f: the active paths' terms added in the reference's path order
-// (scalars 0, 3, 8; vectors 1, 2, 4; type-2 5, 6, 7)
-__device__ __forceinline__ float se3_message(const Se3Paths &P, const float *__restrict__ cg, const Se3Edge &x,
-                                             int64_t s, int f) {
+// the same over the flattened channel index f: cs scalars, then 3 cv vector, then 5 ct2 type-2
+__device__ __forceinline__ float se3_term(const Se3Paths &P, const float *__restrict__ cg, const Se3Edge &x, int64_t s,
+                                          int f, int p) {
+    if (f < P.cs) return se3_term_s(P, x, s, f, p);
+    f -= P.cs;
+    if (f < 3 * P.cv) return se3_term_v(P, x, s, f / 3, f - 3 * (f / 3), p);
+    f -= 3 * P.cv;
+    return se3_term_t(P, cg, x, s, f / 5, f - 5 * (f / 5), p);
+}
+
+// the message of one channel of kind KIND (0 scalar, 1 vector, 2 type-2; fl indexes that kind's
+// channels): the active paths' terms added in the reference's path order (scalars 0, 3, 8;
+// vectors 1, 2, 4; type-2 5, 6, 7)
+template <int KIND>
+__device__ __forceinline__ float se3_message_kind(const Se3Paths &P, const float *__restrict__ cg, const Se3Edge &x,
+                                                  int64_t s, int fl) {
     float msg = 0.0f;
-    if (f < P.cs) {
-        if (P.p[0]) msg = __fadd_rn(msg, se3_term(P, cg, x, s, f, 0));
-        if (P.p[3]) msg = __fadd_rn(msg, se3_term(P, cg, x, s, f, 3));
-        if (P.p[8]) msg = __fadd_rn(msg, se3_term(P, cg, x, s, f, 8));
-    } else if (f < P.cs + 3 * P.cv) {
-        if (P.p[1]) msg = __fadd_rn(msg, se3_term(P, cg, x, s, f, 1));
-        if (P.p[2]) msg = __fadd_rn(msg, se3_term(P, cg, x, s, f, 2));
-        if (P.p[4]) msg = __fadd_rn(msg, se3_term(P, cg, x, s, f, 4));
+    if constexpr (KIND == 0) {
+        if (P.p[0]) msg = __fadd_rn(msg, se3_term_s(P, x, s, fl, 0));
+        if (P.p[3]) msg = __fadd_rn(msg, se3_term_s(P, x, s, fl, 3));
+        if (P.p[8]) msg = __fadd_rn(msg, se3_term_s(P, x, s, fl, 8));
+    } else if constexpr (KIND == 1) {
+        const int o = fl / 3, k = fl - 3 * o;
+        if (P.p[1]) msg = __fadd_rn(msg, se3_term_v(P, x, s, o, k, 1));
+        if (P.p[2]) msg = __fadd_rn(msg, se3_term_v(P, x, s, o, k, 2));
+        if (P.p[4]) msg = __fadd_rn(msg, se3_term_v(P, x, s, o, k, 4));
     } else {
-        if (P.p[5]) msg = __fadd_rn(msg, se3_term(P, cg, x, s, f, 5));
-        if (P.p[6]) msg = __fadd_rn(msg, se3_term(P, cg, x, s, f, 6));
-        if (P.p[7]) msg = __fadd_rn(msg, se3_term(P, cg, x, s, f, 7));
+        const int o = fl / 5, m = fl - 5 * o;
+        if (P.p[5]) msg = __fadd_rn(msg, se3_term_t(P, cg, x, s, o, m, 5));
+        if (P.p[6]) msg = __fadd_rn(msg, se3_term_t(P, cg, x, s, o, m, 6));
+        if (P.p[7]) msg = __fadd_rn(msg, se3_term_t(P, cg, x, s, o, m, 7));
     }
     return msg;
 }
 
 constexpr int kSe3Chunks = 4;  // output channels per lane held in registers (128 per warp pass)
 
-// one warp per target node; lanes over the flattened output channels, edges of the segment in
-// sorted-slot order, messages formed on the fly
+// the channels of one kind for target n: lanes over channels (kSe3Chunks per lane per pass), the
+// segment's edges in slot order, each message formed on the fly, the fold divided by the degree
+template <int KIND>
+__device__ __forceinline__ void fwd_kind_pass(const Se3Paths &P, const float *__restrict__ R, int64_t rs,
+                                              const float *__restrict__ dir, const float *__restrict__ sph, int sd,
+                                              const float *__restrict__ cg, const int64_t *__restrict__ row,
+                                              const int32_t *__restrict__ perm, int32_t j0, int32_t j1, bool single,
+                                              Se3Edge &mine, int64_t &msrc, int64_t n, float a,
+                                              float *__restrict__ out, int width, int lane) {
+    for (int c0 = 0; c0 < width; c0 += 32 * kSe3Chunks) {
+        float acc[kSe3Chunks];
+#pragma unroll
+        for (int i = 0; i < kSe3Chunks; ++i) acc[i] = 0.0f;
+        for (int32_t jb = j0; jb < j1; jb += 32) {  // up to 32 edges: lane t loads edge jb + t
+            const int cnt = j1 - jb < 32 ? (int)(j1 - jb) : 32;
+            if (!single) {
+                msrc = 0;
+                zero_edge(mine);
+                if (lane < cnt) {
+                    const int64_t e = perm[jb + lane];
+                    msrc = row[e];
+                    load_edge(P, R, rs, dir, sph, sd, e, mine);
+                }
+            }
+            for (int t = 0; t < cnt; ++t) {  // slot order is kept: edges are folded one by one
+                Se3Edge x;
+                shfl_edge(mine, t, x);
+                const int64_t s = __shfl_sync(0xffffffffu, msrc, t);
+#pragma unroll
+                for (int i = 0; i < kSe3Chunks; ++i) {
+                    const int f = c0 + lane + 32 * i;
+                    if (f < width) acc[i] = __fadd_rn(acc[i], se3_message_kind<KIND>(P, cg, x, s, f));
+                }
+            }
+        }
+#pragma unroll
+        for (int i = 0; i < kSe3Chunks; ++i) {
+            const int f = c0 + lane + 32 * i;
+            if (f < width) out[n * width + f] = __fdiv_rn(acc[i], a);
+        }
+    }
+}
+
+// one warp per target node; its three channel kinds in turn, edges of the segment in sorted-slot
+// order, messages formed on the fly
 __global__ void __launch_bounds__(256, 2) se3_agg_fwd_kernel(Se3Paths P, const float *__restrict__ R, int64_t rs,
                                                           const float *__restrict__ dir, const float *__restrict__ sph,
                                                           int sd, const float *__restrict__ cg,
@@ -145,7 +199,6 @@ __global__ void __launch_bounds__(256, 2) se3_agg_fwd_kernel(Se3Paths P, const f
                                                           float *__restrict__ os, float *__restrict__ ov,
                                                           float *__restrict__ ot) {
     const int lane = threadIdx.x & 31;
-    const int ctot = P.cs + 3 * P.cv + 5 * P.ct2;
     const int64_t warps = (int64_t)gridDim.x * (blockDim.x >> 5);
     for (int64_t n = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); n < N; n += warps) {
         const int32_t j0 = ns[n], j1 = ne[n];
@@ -160,47 +213,11 @@ __global__ void __launch_bounds__(256, 2) se3_agg_fwd_kernel(Se3Paths P, const f
             msrc = row[e];
             load_edge(P, R, rs, dir, sph, sd, e, mine);
         }
-        for (int c0 = 0; c0 < ctot; c0 += 32 * kSe3Chunks) {
-            float acc[kSe3Chunks];
-#pragma unroll
-            for (int i = 0; i < kSe3Chunks; ++i) acc[i] = 0.0f;
-            for (int32_t jb = j0; jb < j1; jb += 32) {  // up to 32 edges: lane t loads edge jb + t
-                const int cnt = j1 - jb < 32 ? (int)(j1 - jb) : 32;
-                if (!single) {
-                    msrc = 0;
-                    zero_edge(mine);
-                    if (lane < cnt) {
-                        const int64_t e = perm[jb + lane];
-                        msrc = row[e];
-                        load_edge(P, R, rs, dir, sph, sd, e, mine);
-                    }
-                }
-                for (int t = 0; t < cnt; ++t) {  // slot order is kept: edges are folded one by one
-                    Se3Edge x;
-                    shfl_edge(mine, t, x);
-                    const int64_t s = __shfl_sync(0xffffffffu, msrc, t);
-#pragma unroll
-                    for (int i = 0; i < kSe3Chunks; ++i) {
-                        const int f = c0 + lane + 32 * i;
-                        if (f < ctot) acc[i] = __fadd_rn(acc[i], se3_message(P, cg, x, s, f));
-                    }
-                }
-            }
-#pragma unroll
-            for (int i = 0; i < kSe3Chunks; ++i) {
-                int f = c0 + lane + 32 * i;
-                if (f >= ctot) continue;
-                const float v = __fdiv_rn(acc[i], a);
-                if (f < P.cs) {
-                    os[n * P.cs + f] = v;
-                } else if ((f -= P.cs) < 3 * P.cv) {
-                    ov[n * 3 * P.cv + f] = v;
-                } else {
-                    f -= 3 * P.cv;
-                    ot[n * 5 * P.ct2 + f] = v;
-                }
-            }
-        }
+        fwd_kind_pass<0>(P, R, rs, dir, sph, sd, cg, row, perm, j0, j1, single, mine, msrc, n, a, os, P.cs, lane);
+        fwd_kind_pass<1>(P, R, rs, dir, sph, sd, cg, row, perm, j0, j1, single, mine, msrc, n, a, ov, 3 * P.cv,
+                         lane);
+        fwd_kind_pass<2>(P, R, rs, dir, sph, sd, cg, row, perm, j0, j1, single, mine, msrc, n, a, ot, 5 * P.ct2,
+                         lane);
     }
 }
 
