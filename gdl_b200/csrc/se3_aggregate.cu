@@ -106,16 +106,6 @@ __device__ __forceinline__ float se3_term_t(const Se3Paths &P, const float *__re
     return 0.0f;
 }
 
-// the same over the flattened channel index f: cs scalars, then 3 cv vector, then 5 ct2 type-2
-__device__ __forceinline__ float se3_term(const Se3Paths &P, const float *__restrict__ cg, const Se3Edge &x, int64_t s,
-                                          int f, int p) {
-    if (f < P.cs) return se3_term_s(P, x, s, f, p);
-    f -= P.cs;
-    if (f < 3 * P.cv) return se3_term_v(P, x, s, f / 3, f - 3 * (f / 3), p);
-    f -= 3 * P.cv;
-    return se3_term_t(P, cg, x, s, f / 5, f - 5 * (f / 5), p);
-}
-
 // the message of one channel of kind KIND (0 scalar, 1 vector, 2 type-2; fl indexes that kind's
 // channels): the active paths' terms added in the reference's path order (scalars 0, 3, 8;
 // vectors 1, 2, 4; type-2 5, 6, 7)
@@ -245,7 +235,6 @@ __global__ void __launch_bounds__(256) se3_agg_grad_r_kernel(Se3Paths P, const f
                                                              const float *__restrict__ gv,
                                                              const float *__restrict__ gt, float *__restrict__ gR) {
     const int lane = threadIdx.x & 31;
-    const int ctot = P.cs + 3 * P.cv + 5 * P.ct2;
     const int64_t warps = (int64_t)gridDim.x * (blockDim.x >> 5);
     for (int64_t e = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); e < E; e += warps) {
         const int64_t s = row[e], t = col[e];
@@ -258,13 +247,26 @@ __global__ void __launch_bounds__(256) se3_agg_grad_r_kernel(Se3Paths P, const f
         float part[9];
 #pragma unroll
         for (int p = 0; p < 9; ++p) part[p] = 0.0f;
-        for (int f = lane; f < ctot; f += 32) {
-            const float g = __fdiv_rn(grad_at(gs, gv, gt, P, t, f), a);
-#pragma unroll
-            for (int p = 0; p < 9; ++p) {
-                if (P.rc[p] < 0) continue;
-                part[p] = __fadd_rn(part[p], __fmul_rn(g, se3_term(P, cg, one, s, f, p)));
-            }
+        // lane-strided over each channel kind in turn; a kind feeds only its three paths
+        for (int o = lane; o < P.cs; o += 32) {
+            const float g = __fdiv_rn(gs[t * P.cs + o], a);
+            if (P.p[0]) part[0] = __fadd_rn(part[0], __fmul_rn(g, se3_term_s(P, one, s, o, 0)));
+            if (P.p[3]) part[3] = __fadd_rn(part[3], __fmul_rn(g, se3_term_s(P, one, s, o, 3)));
+            if (P.p[8]) part[8] = __fadd_rn(part[8], __fmul_rn(g, se3_term_s(P, one, s, o, 8)));
+        }
+        for (int f = lane; f < 3 * P.cv; f += 32) {
+            const float g = __fdiv_rn(gv[t * 3 * P.cv + f], a);
+            const int o = f / 3, k = f - 3 * o;
+            if (P.p[1]) part[1] = __fadd_rn(part[1], __fmul_rn(g, se3_term_v(P, one, s, o, k, 1)));
+            if (P.p[2]) part[2] = __fadd_rn(part[2], __fmul_rn(g, se3_term_v(P, one, s, o, k, 2)));
+            if (P.p[4]) part[4] = __fadd_rn(part[4], __fmul_rn(g, se3_term_v(P, one, s, o, k, 4)));
+        }
+        for (int f = lane; f < 5 * P.ct2; f += 32) {
+            const float g = __fdiv_rn(gt[t * 5 * P.ct2 + f], a);
+            const int o = f / 5, m = f - 5 * o;
+            if (P.p[5]) part[5] = __fadd_rn(part[5], __fmul_rn(g, se3_term_t(P, cg, one, s, o, m, 5)));
+            if (P.p[6]) part[6] = __fadd_rn(part[6], __fmul_rn(g, se3_term_t(P, cg, one, s, o, m, 6)));
+            if (P.p[7]) part[7] = __fadd_rn(part[7], __fmul_rn(g, se3_term_t(P, cg, one, s, o, m, 7)));
         }
 #pragma unroll
         for (int p = 0; p < 9; ++p) {
