@@ -32,7 +32,7 @@ _PG = ctypes.POINTER(EdgeGeometry)
 
 class Se3Paths(ctypes.Structure):
     """gdl_se3_paths: per-path node projections (nullable), their R columns, output channels."""
-    _fields_ = [("p", _P * 9), ("r_col", _I32 * 9), ("cs", _I64), ("cv", _I64), ("ct2", _I64)]
+    _fields_ = [("p", _P * 9), ("r_col", _I32 * 9), ("ld", _I64 * 9), ("cs", _I64), ("cv", _I64), ("ct2", _I64)]
 
 
 _PS = ctypes.POINTER(Se3Paths)

@@ -21,7 +21,8 @@ namespace gdl {
 
 struct Se3Paths {
     const float *p[9];
-    int rc[9];  // R column of each path (-1: path off)
+    int rc[9];      // R column of each path (-1: path off)
+    int64_t ld[9];  // floats between consecutive nodes' rows of each projection
     int cs, cv, ct2;
 };
 
@@ -68,22 +69,22 @@ __device__ __forceinline__ void zero_edge(Se3Edge &x) {
 // Term of path p in the message of an edge from source s: scalar channel o (paths 0, 3, 8),
 // vector channel (o, k) (paths 1, 2, 4), type-2 channel (o, m) (paths 5, 6, 7).
 __device__ __forceinline__ float se3_term_s(const Se3Paths &P, const Se3Edge &x, int64_t s, int o, int p) {
-    if (p == 0) return __fmul_rn(__fmul_rn(x.r[0], x.y0), P.p[0][s * P.cs + o]);
+    if (p == 0) return __fmul_rn(__fmul_rn(x.r[0], x.y0), P.p[0][s * P.ld[0] + o]);
     if (p == 3) {
-        const float *q = P.p[3] + (s * P.cs + o) * 3;
+        const float *q = P.p[3] + s * P.ld[3] + o * 3;
         const float dot =
             __fadd_rn(__fadd_rn(__fmul_rn(x.d[0], q[0]), __fmul_rn(x.d[1], q[1])), __fmul_rn(x.d[2], q[2]));
         return __fmul_rn(x.r[3], dot);
     }
-    if (p == 8) return __fmul_rn(x.r[8], P.p[8][s * P.cs + o]);
+    if (p == 8) return __fmul_rn(x.r[8], P.p[8][s * P.ld[8] + o]);
     return 0.0f;
 }
 
 __device__ __forceinline__ float se3_term_v(const Se3Paths &P, const Se3Edge &x, int64_t s, int o, int k, int p) {
-    if (p == 1) return __fmul_rn(__fmul_rn(x.r[1], P.p[1][s * P.cv + o]), x.d[k]);
-    if (p == 2) return __fmul_rn(__fmul_rn(x.r[2], x.y0), P.p[2][(s * P.cv + o) * 3 + k]);
+    if (p == 1) return __fmul_rn(__fmul_rn(x.r[1], P.p[1][s * P.ld[1] + o]), x.d[k]);
+    if (p == 2) return __fmul_rn(__fmul_rn(x.r[2], x.y0), P.p[2][s * P.ld[2] + o * 3 + k]);
     if (p == 4) {
-        const float *q = P.p[4] + (s * P.cv + o) * 3;
+        const float *q = P.p[4] + s * P.ld[4] + o * 3;
         const int k1 = k == 2 ? 0 : k + 1, k2 = k == 0 ? 2 : k - 1;  // (d x q)_k = d_k1 q_k2 - d_k2 q_k1
         return __fmul_rn(x.r[4], __fsub_rn(__fmul_rn(x.d[k1], q[k2]), __fmul_rn(x.d[k2], q[k1])));
     }
@@ -92,10 +93,10 @@ __device__ __forceinline__ float se3_term_v(const Se3Paths &P, const Se3Edge &x,
 
 __device__ __forceinline__ float se3_term_t(const Se3Paths &P, const float *__restrict__ cg, const Se3Edge &x,
                                             int64_t s, int o, int m, int p) {
-    if (p == 5) return __fmul_rn(__fmul_rn(x.r[5], P.p[5][s * P.ct2 + o]), x.y2[m]);
-    if (p == 6) return __fmul_rn(__fmul_rn(x.r[6], x.y0), P.p[6][(s * P.ct2 + o) * 5 + m]);
+    if (p == 5) return __fmul_rn(__fmul_rn(x.r[5], P.p[5][s * P.ld[5] + o]), x.y2[m]);
+    if (p == 6) return __fmul_rn(__fmul_rn(x.r[6], x.y0), P.p[6][s * P.ld[6] + o * 5 + m]);
     if (p == 7) {
-        const float *q = P.p[7] + (s * P.ct2 + o) * 3;
+        const float *q = P.p[7] + s * P.ld[7] + o * 3;
         float t = 0.0f;
 #pragma unroll
         for (int i = 0; i < 3; ++i)
@@ -392,7 +393,7 @@ __device__ __forceinline__ void grad_p_pass(const Se3Paths &P, float *__restrict
 #pragma unroll
         for (int i = 0; i < kSe3Chunks; ++i) {
             const int q = q0 + lane + 32 * i;
-            if (q < w) gp[s * w + q] = acc[i];
+            if (q < w) gp[s * P.ld[PI] + q] = acc[i];
         }
     }
 }
@@ -455,10 +456,12 @@ inline bool se3_paths_ok(const gdl_se3_paths *g, Se3Paths *P) {
     P->cs = (int)g->cs;
     P->cv = (int)g->cv;
     P->ct2 = (int)g->ct2;
+    const int64_t dense[9] = {g->cs, g->cv, 3 * g->cv, 3 * g->cs, 3 * g->cv, g->ct2, 5 * g->ct2, 3 * g->ct2, g->cs};
     for (int p = 0; p < 9; ++p) {
         P->p[p] = g->p[p];
         P->rc[p] = g->p[p] ? g->r_col[p] : -1;
-        if (g->p[p] && g->r_col[p] < 0) return false;
+        P->ld[p] = g->ld[p] > 0 ? g->ld[p] : dense[p];
+        if (g->p[p] && (g->r_col[p] < 0 || P->ld[p] < dense[p])) return false;
     }
     return true;
 }

@@ -62,19 +62,21 @@ class RadialBasis(nn.Module):
 
 
 class SE3MessageAggregate(torch.autograd.Function):
-    """(out_s, out_v, out_t2) = gdl_se3_aggregate over a graph; differentiable w.r.t. R and the nine
-    node projections (the graph's geometry and CSR are constants)."""
+    """(out_s, out_v, out_t2) = gdl_se3_aggregate over a graph; differentiable w.r.t. R and the node
+    projections. The projections come as a few GEMM results ("groups"); ``layout[i]`` = (group,
+    float offset of path i's columns in a row, floats per row) places path i inside its group, or
+    None when the path is off. The graph's geometry and CSR are constants."""
 
     @staticmethod
-    def forward(ctx, meta, R: Tensor, *proj):
-        g, cg, r_cols, (cs, cv, ct2) = meta
+    def forward(ctx, meta, R: Tensor, *groups):
+        g, cg, r_cols, layout, (cs, cv, ct2) = meta
         dev = R.device
         N, E = g.N, g.E
         f32 = dict(dtype=torch.float32, device=dev)
         out_s = torch.empty(N, cs, **f32)
         out_v = torch.empty(N, cv, 3, **f32)
         out_t2 = torch.empty(N, ct2, 5, **f32)
-        st = _paths_struct(proj, r_cols, cs, cv, ct2)
+        st = _paths_struct(groups, layout, r_cols, cs, cv, ct2)
         sph = g.Y.contiguous().float()
         L = nat.load()
         nat.check(L.gdl_se3_aggregate(ctypes.byref(st), R.data_ptr(), R.shape[1], g.direction.contiguous().data_ptr(),
@@ -85,36 +87,39 @@ class SE3MessageAggregate(torch.autograd.Function):
                                       nat.ptr(out_t2) if out_t2.numel() else None, nat.stream(dev)),
                   "gdl_se3_aggregate")
         ctx.meta = meta
-        ctx.save_for_backward(R, *[p if p is not None else torch.empty(0) for p in proj])
-        ctx.present = [p is not None for p in proj]
+        ctx.save_for_backward(R, *groups)
         return out_s, out_v, out_t2
 
     @staticmethod
     def backward(ctx, gs: Tensor, gv: Tensor, gt: Tensor):
-        g, cg, r_cols, (cs, cv, ct2) = ctx.meta
-        R, *saved = ctx.saved_tensors
-        proj = [p if present else None for p, present in zip(saved, ctx.present)]
+        g, cg, r_cols, layout, (cs, cv, ct2) = ctx.meta
+        R, *groups = ctx.saved_tensors
         dev = R.device
         N, E = g.N, g.E
         gs = torch.zeros(N, cs, device=dev) if gs is None else gs.contiguous().float()
         gv = torch.zeros(N, cv, 3, device=dev) if gv is None else gv.contiguous().float()
         gt = torch.zeros(N, ct2, 5, device=dev) if gt is None else gt.contiguous().float()
-        need_p = [proj[i] is not None and ctx.needs_input_grad[2 + i] for i in range(_PATHS)]
-        grad_p = [torch.empty_like(proj[i]) if need_p[i] else None for i in range(_PATHS)]
+        # each group is covered by its paths' columns, so the kernel writes every entry
+        grad_g = [torch.empty_like(t) if ctx.needs_input_grad[2 + k] else None for k, t in enumerate(groups)]
+        gp = [None] * _PATHS
+        for i, lay in enumerate(layout):
+            if lay is not None and grad_g[lay[0]] is not None:
+                gp[i] = grad_g[lay[0]].data_ptr() + 4 * lay[1]
+        need_p = any(p is not None for p in gp)
         grad_R = torch.zeros_like(R) if ctx.needs_input_grad[1] else None
         src_perm = src_start = src_end = None
-        if any(need_p):
+        if need_p:
             src_perm, src_start, src_end = _source_csr(g)
-        st = _paths_struct(proj, r_cols, cs, cv, ct2)
-        gp_arr = (ctypes.c_void_p * _PATHS)(*[nat.ptr(t) for t in grad_p])
+        st = _paths_struct(groups, layout, r_cols, cs, cv, ct2)
+        gp_arr = (ctypes.c_void_p * _PATHS)(*gp)
         sph = g.Y.contiguous().float()
         nat.check(nat.load().gdl_se3_aggregate_backward(
-            ctypes.byref(st), gp_arr if any(need_p) else None, nat.ptr(grad_R), nat.ptr(gs) if gs.numel() else None,
+            ctypes.byref(st), gp_arr if need_p else None, nat.ptr(grad_R), nat.ptr(gs) if gs.numel() else None,
             nat.ptr(gv) if gv.numel() else None, nat.ptr(gt) if gt.numel() else None, R.data_ptr(), R.shape[1],
             g.direction.contiguous().data_ptr(), sph.data_ptr(), sph.shape[1], nat.ptr(cg), g.row.data_ptr(),
             g.col.data_ptr(), nat.ptr(src_perm), nat.ptr(src_start), nat.ptr(src_end), g.avg_degree.data_ptr(), N, E,
             nat.stream(dev)), "gdl_se3_aggregate_backward")
-        return (None, grad_R, *grad_p)
+        return (None, grad_R, *grad_g)
 
 
 def _source_csr(g):
@@ -128,10 +133,13 @@ def _source_csr(g):
     return cached[1:]
 
 
-def _paths_struct(proj, r_cols, cs, cv, ct2):
+def _paths_struct(groups, layout, r_cols, cs, cv, ct2):
     st = nat.Se3Paths()
     for i in range(_PATHS):
-        st.p[i] = nat.ptr(proj[i]) if proj[i] is not None else None
+        if layout[i] is not None:
+            k, off, ld = layout[i]
+            st.p[i] = groups[k].data_ptr() + 4 * off
+            st.ld[i] = ld
         st.r_col[i] = r_cols[i]
     st.cs, st.cv, st.ct2 = cs, cv, ct2
     return st
@@ -205,36 +213,43 @@ class SE3Conv(nn.Module):
             v = vectors.float()
             t2 = type2.float() if (type2 is not None and self.in_type2_channels > 0) else None
             y2_ok = ct2 > 0 and graph.Y.shape[-1] >= 9
-            # each path's node projection, in the reference's path order; a path runs (and takes
-            # the next column of R) exactly when the reference's _compute_messages runs it
+            # a path runs (and takes the next column of R) exactly when the reference's
+            # _compute_messages runs it
             w = self._weights()
-            proj: List[Optional[Tensor]] = [None] * _PATHS
-            if w[0] is not None:
-                proj[0] = (s @ w[0].weight.t()).contiguous()
-            if w[1] is not None:
-                proj[1] = (s @ w[1].weight.t()).contiguous()
-            if w[2] is not None:
-                proj[2] = _mix(v, w[2].weight)
-            if w[3] is not None:
-                proj[3] = _mix(v, w[3].weight)
-            if w[4] is not None:
-                proj[4] = _mix(v, w[4].weight)
-            if w[5] is not None and y2_ok:
-                proj[5] = (s @ w[5].weight.t()).contiguous()
-            if w[6] is not None and t2 is not None and ct2 > 0:
-                proj[6] = _mix(t2, w[6].weight)
-            if w[7] is not None and ct2 > 0:
-                proj[7] = _mix(v, w[7].weight)
-            if w[8] is not None and t2 is not None:
-                proj[8] = ((t2 * t2).sum(dim=-1) @ w[8].weight.t()).contiguous()
+            on = [w[i] is not None for i in range(_PATHS)]
+            on[5] = on[5] and y2_ok
+            on[6] = on[6] and t2 is not None and ct2 > 0
+            on[7] = on[7] and ct2 > 0
+            on[8] = on[8] and t2 is not None
+            # the node projections, one GEMM per input: the scalars feed paths 0, 1, 5 ([N, C]
+            # rows), the vectors paths 2, 3, 4, 7 ([N, C, 3] rows); each path reads its columns of
+            # the group in place through a row stride
+            groups: List[Tensor] = []
+            layout: List[Optional[Tuple[int, int, int]]] = [None] * _PATHS
+            for inp, paths, m in ((s, (0, 1, 5), 1), (v, (2, 3, 4, 7), 3)):
+                paths = [i for i in paths if on[i]]
+                if not paths:
+                    continue
+                W = torch.cat([w[i].weight for i in paths]) if len(paths) > 1 else w[paths[0]].weight
+                groups.append((inp @ W.t()).contiguous() if m == 1 else _mix(inp, W))
+                off = 0
+                for i in paths:
+                    layout[i] = (len(groups) - 1, off * m, W.shape[0] * m)
+                    off += w[i].weight.shape[0]
+            if on[6]:
+                groups.append(_mix(t2, w[6].weight))
+                layout[6] = (len(groups) - 1, 0, 5 * ct2)
+            if on[8]:
+                groups.append(((t2 * t2).sum(dim=-1) @ w[8].weight.t()).contiguous())
+                layout[8] = (len(groups) - 1, 0, cs)
             r_cols, col = [], 0
-            for p in proj:
-                r_cols.append(col if p is not None else -1)
-                col += p is not None
+            for lay in layout:
+                r_cols.append(col if lay is not None else -1)
+                col += lay is not None
             R = self.radial_basis(graph.dist.float()).contiguous()
-            cg = self.cg_11_2.float().contiguous() if (proj[7] is not None) else None
-            meta = (graph, cg, r_cols, (cs, cv, ct2))
-            s_out, v_out, t2_out = SE3MessageAggregate.apply(meta, R, *proj)
+            cg = self.cg_11_2.float().contiguous() if on[7] else None
+            meta = (graph, cg, r_cols, layout, (cs, cv, ct2))
+            s_out, v_out, t2_out = SE3MessageAggregate.apply(meta, R, *groups)
             if self.scalar_bias is not None:
                 s_out = s_out + self.scalar_bias
             if mask is not None:

@@ -229,13 +229,15 @@ int gdl_hybrid_graph(const float *x, const int64_t *radius_row_ptr, const int64_
  * p[i] == NULL switches path i off; r_col[i] = its column of R [E, r_stride]. Y0 = sph[e, 0],
  * Y2 = sph[e, 4:9] (sph [E, sph_dim]); cg [3, 3, 5] Cartesian CG(1,1,2) (path 7 only).
  * Edges: row [E] (source of edge e), perm [E] (edge of CSR slot j), node_start/node_end [N].
- * Backward: grad_R [E, r_stride] (nullable) and grad_proj[i] (nullable array / entries, shapes of
- * p[i]) from grad_s/v/t2 [N, ...]; grad_proj needs the edges grouped by source: src_perm /
+ * Backward: grad_R [E, r_stride] (nullable) and grad_proj[i] (nullable array / entries, shapes and
+ * row strides ld[i] of p[i]; every entry of each row is written) from grad_s/v/t2 [N, ...]; grad_proj needs the edges grouped by source: src_perm /
  * src_start / src_end = gdl_sort_and_build_csr(row) (perm, node_start, node_end), and col [E].
  * No counterpart kernel in the reference. */
 typedef struct gdl_se3_paths {
     const float *p[9];
     int32_t r_col[9];
+    int64_t ld[9]; /* floats from one node's row of p[i] to the next (0: the dense row width above),
+                      so that projections of one input can be column slices of one GEMM result */
     int64_t cs, cv, ct2;
 } gdl_se3_paths;
 
