@@ -72,6 +72,8 @@ PROTOTYPES = {
     "gdl_sort_and_build_csr": (ctypes.c_int, [_P, _I64, _I64, _P, _P, _P, _P, _P, _SZ, _P]),
     "gdl_segment_reduce_workspace_size": (_SZ, [_I64, _I64]),
     "gdl_segment_reduce": (ctypes.c_int, [_P, _I32, _I64, _I64, _P, _P, _P, _I64, _I32, _P, _P, _P, _SZ, _P]),
+    "gdl_weight_grad_workspace_size": (ctypes.c_size_t, [_I64, _I32, _I32, _I32]),
+    "gdl_weight_grad": (ctypes.c_int, [_P, _I64, _P, _I64, _I64, _I32, _I32, _I32, _P, _P, _P, ctypes.c_size_t, _P]),
     "gdl_segment_reduce_noalloc": (ctypes.c_int, [_P, _I32, _I64, _I64, _P, _P, _P, _I64, _I32, _P, _P, _P]),
     "gdl_segment_reduce_backward": (ctypes.c_int,
                                     [_P, _P, _I32, _P, _P, _I64, _I64, _P, _P, _P, _I64, _I32, _P, _P, _SZ, _P]),

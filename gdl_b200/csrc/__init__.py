@@ -17,6 +17,7 @@ libgdl_b200.so on the current CUDA stream. Differences, all deliberate:
 from __future__ import annotations
 
 import ctypes
+import math
 from typing import Optional, Tuple
 
 import numpy as np
@@ -487,6 +488,36 @@ def knn_weighted_sum_weight_grad_cuda(grad_outs, srcs, idx: torch.Tensor) -> tor
                                                      nat.ptr(gw) if gw.numel() else None, nat.stream(dev)),
                   "gdl_knn_weighted_sum_weight_grad")
     return gw
+
+
+# --------------------------------------------------------------------------- weight gradients
+def _row_matrix(t: torch.Tensor) -> torch.Tensor:
+    """[rows, ...] float32 as a [rows, width] matrix with unit inner stride (a view when possible)."""
+    if t.dtype != torch.float32:
+        t = t.float()
+    t = t.reshape(t.shape[0], math.prod(t.shape[1:]))
+    if t.shape[1] > 0 and (t.stride(1) != 1 or t.stride(0) < t.shape[1]):
+        t = t.contiguous()
+    return t
+
+
+def weight_grad_cuda(grad_out: torch.Tensor, inp: torch.Tensor, sub: int = 1, col_sum: bool = False):
+    """Weight (and bias) gradient of a per-row linear map: grad_out [rows, M, sub] (or [rows, M] for
+    sub 1), inp [rows, N, sub] -> (C [M, N] = sum_{r, j} grad_out[r, :, j]^T inp[r, :, j], column sums
+    of grad_out [M] or None), deterministic (gdl_weight_grad)."""
+    dev = nat.require_cuda(grad_out, inp, what="weight_grad_cuda")
+    A, B = _row_matrix(grad_out), _row_matrix(inp)
+    rows = A.shape[0]
+    M, N = A.shape[1] // sub, B.shape[1] // sub
+    C = torch.empty(M, N, dtype=torch.float32, device=dev)
+    cs = torch.empty(M, dtype=torch.float32, device=dev) if col_sum else None
+    L = nat.load()
+    ws = nat.workspace(L.gdl_weight_grad_workspace_size(rows, M, N, sub), dev)
+    nat.check(L.gdl_weight_grad(nat.ptr(A) if A.numel() else None, A.stride(0) if A.numel() else M * sub,
+                                nat.ptr(B) if B.numel() else None, B.stride(0) if B.numel() else N * sub, rows, M, N,
+                                sub, nat.ptr(C) if C.numel() else None, nat.ptr(cs), ws.data_ptr(), ws.numel(),
+                                nat.stream(dev)), "gdl_weight_grad")
+    return C, cs
 
 
 # --------------------------------------------------------------------------- hybrid graph

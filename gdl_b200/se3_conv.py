@@ -58,7 +58,52 @@ class RadialBasis(nn.Module):
         d = dist.unsqueeze(-1)
         basis = torch.sin(self.freqs * d) / d.clamp(min=1e-8)
         envelope = (0.5 * (1.0 + torch.cos(math.pi * dist / self.cutoff))).clamp(min=0.0).unsqueeze(-1)
-        return self.mlp(basis * envelope)
+        h = basis * envelope
+        if not h.is_cuda or h.dtype != torch.float32 or self.mlp[0].weight.dtype != torch.float32:
+            return self.mlp(h)
+        l0, act, l1 = self.mlp
+        return _RowLinear.apply(act(_RowLinear.apply(h, l0.weight, l0.bias)), l1.weight, l1.bias)
+
+
+class _RowLinear(torch.autograd.Function):
+    """y = x W^T (+ b) over the rows of x [rows, N]: nn.Linear's forward (cuBLAS) and input
+    gradient, with the weight and bias gradients from gdl_weight_grad. Those contract over all rows
+    (edges or nodes) into a small [M, N] output, which a GEMM library spreads over only a few CTAs;
+    gdl_weight_grad splits the rows across the SMs and adds the slices in a fixed order."""
+
+    @staticmethod
+    def forward(ctx, x: Tensor, W: Tensor, b: Optional[Tensor]):
+        ctx.save_for_backward(x, W)
+        ctx.has_b = b is not None
+        return nn.functional.linear(x, W, b)
+
+    @staticmethod
+    def backward(ctx, gy: Tensor):
+        x, W = ctx.saved_tensors
+        gx = (gy.to(W.dtype) @ W).to(x.dtype) if ctx.needs_input_grad[0] else None
+        gW = gb = None
+        want_b = ctx.has_b and ctx.needs_input_grad[2]
+        if ctx.needs_input_grad[1] or want_b:
+            gW, gb = csrc.weight_grad_cuda(gy, x, 1, col_sum=want_b)
+        return gx, gW if ctx.needs_input_grad[1] else None, gb
+
+
+class _ChannelMix(torch.autograd.Function):
+    """[rows, C_in, m] features mixed over channels by W [C_out, C_in] -> [rows, C_out, m] (the
+    reference's nn.Linear applied to each of the m components), with the weight gradient
+    sum_{r, j} g[r, :, j]^T x[r, :, j] from gdl_weight_grad."""
+
+    @staticmethod
+    def forward(ctx, x: Tensor, W: Tensor):
+        ctx.save_for_backward(x, W)
+        return _mix(x, W)
+
+    @staticmethod
+    def backward(ctx, g: Tensor):
+        x, W = ctx.saved_tensors
+        gx = _mix(g, W.t()) if ctx.needs_input_grad[0] else None
+        gW = csrc.weight_grad_cuda(g, x, x.shape[-1])[0] if ctx.needs_input_grad[1] else None
+        return gx, gW
 
 
 class SE3MessageAggregate(torch.autograd.Function):
@@ -231,16 +276,16 @@ class SE3Conv(nn.Module):
                 if not paths:
                     continue
                 W = torch.cat([w[i].weight for i in paths]) if len(paths) > 1 else w[paths[0]].weight
-                groups.append((inp @ W.t()).contiguous() if m == 1 else _mix(inp, W))
+                groups.append(_RowLinear.apply(inp, W, None) if m == 1 else _ChannelMix.apply(inp, W))
                 off = 0
                 for i in paths:
                     layout[i] = (len(groups) - 1, off * m, W.shape[0] * m)
                     off += w[i].weight.shape[0]
             if on[6]:
-                groups.append(_mix(t2, w[6].weight))
+                groups.append(_ChannelMix.apply(t2, w[6].weight))
                 layout[6] = (len(groups) - 1, 0, 5 * ct2)
             if on[8]:
-                groups.append(((t2 * t2).sum(dim=-1) @ w[8].weight.t()).contiguous())
+                groups.append(_RowLinear.apply((t2 * t2).sum(dim=-1), w[8].weight, None))
                 layout[8] = (len(groups) - 1, 0, cs)
             r_cols, col = [], 0
             for lay in layout:

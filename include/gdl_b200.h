@@ -252,6 +252,21 @@ int gdl_se3_aggregate_backward(const gdl_se3_paths *paths, float *const *grad_pr
                                const int32_t *src_start, const int32_t *src_end, const float *avg_degree,
                                int64_t n_nodes, int64_t n_edges, void *stream);
 
+/* ------------------------------------------------------------ channel-mixing weight gradient
+ * Replaces the weight gradients torch autograd takes through SE3Conv's nn.Linear layers: the node
+ * projections W [M, N] (geoembodied/nn/modules/se3_conv.py:343-413, applied to [rows, N, sub]
+ * features: sub = 1 scalars, 3 vectors, 5 type-2) and the radial MLP (se3_conv.py:266-268, sub = 1).
+ * The rows (nodes or edges) run to the hundreds of thousands, M and N to a few hundred:
+ *   C[m, n]    = sum_{r < rows} sum_{j < sub} A[r * lda + m * sub + j] * B[r * ldb + n * sub + j]
+ *   col_sum[m] = sum_{r < rows} A[r * lda + m]   (nullable, sub == 1 only: the bias gradient)
+ * A = the layer's output gradient, B = its input (lda >= M * sub, ldb >= N * sub, in floats); C [M, N]
+ * dense row-major and col_sum [M] are overwritten (zeros when rows == 0). The rows are split into a
+ * fixed number of slices and the partial results added in slice order: deterministic.
+ */
+size_t gdl_weight_grad_workspace_size(int64_t rows, int32_t M, int32_t N, int32_t sub);
+int gdl_weight_grad(const float *A, int64_t lda, const float *B, int64_t ldb, int64_t rows, int32_t M, int32_t N,
+                    int32_t sub, float *C, float *col_sum, void *workspace, size_t workspace_bytes, void *stream);
+
 /* -------------------------------------------------------------------- KNN aggregation
  * Replaces the weighted neighbour sums of the reference's KNN consumers, which gather
  * [n_query, k, dim] rows with torch indexing and reduce them over k:

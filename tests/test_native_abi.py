@@ -72,6 +72,11 @@ def test_argument_validation_without_gpu(lib):
     assert lib.gdl_hybrid_graph_workspace_size(1000, 32, 3) > 1000 * 38 * 12
     assert lib.gdl_hybrid_graph(None, None, None, None, 10, 32, 3, None, None, None, None, None, None, None, None,
                                 None, None, 0, None) == 1
+    assert lib.gdl_weight_grad(None, 4, None, 4, 10, 4, 4, 2, None, None, None, 0, None) == 1  # sub 2
+    assert lib.gdl_weight_grad(None, 12, None, 12, 10, 4, 4, 3, 16, 16, None, 0, None) == 1  # bias with sub 3
+    assert lib.gdl_weight_grad(16, 3, 16, 4, 10, 4, 4, 1, 16, None, None, 0, None) == 1  # lda < M
+    assert lib.gdl_weight_grad(16, 4, 16, 4, 10, 4, 4, 1, 16, None, None, 0, None) == 2  # no workspace
+    assert lib.gdl_weight_grad_workspace_size(100_000, 9, 64, 1) >= 9 * 64 * 4
 
 
 def test_cpu_tensors_raise():
