@@ -225,6 +225,7 @@ __device__ __forceinline__ float grad_at(const float *__restrict__ gs, const flo
 
 // grad_R[e, rc[p]] = sum over output channels f of g[f] * (path p's term of channel f without R_p).
 // One warp per edge; the nine sums are lane-strided, then reduced with a fixed butterfly.
+template <bool DIV>
 __global__ void __launch_bounds__(256) se3_agg_grad_r_kernel(Se3Paths P, const float *__restrict__ R, int64_t rs,
                                                              const float *__restrict__ dir,
                                                              const float *__restrict__ sph, int sd,
@@ -239,7 +240,7 @@ __global__ void __launch_bounds__(256) se3_agg_grad_r_kernel(Se3Paths P, const f
     const int64_t warps = (int64_t)gridDim.x * (blockDim.x >> 5);
     for (int64_t e = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); e < E; e += warps) {
         const int64_t s = row[e], t = col[e];
-        const float a = avg[t];
+        const float a = DIV ? avg[t] : 1.0f;
         Se3Edge x;
         load_edge(P, R, rs, dir, sph, sd, e, x);
         Se3Edge one = x;  // unit radial weights: each path's term without its R
@@ -250,20 +251,20 @@ __global__ void __launch_bounds__(256) se3_agg_grad_r_kernel(Se3Paths P, const f
         for (int p = 0; p < 9; ++p) part[p] = 0.0f;
         // lane-strided over each channel kind in turn; a kind feeds only its three paths
         for (int o = lane; o < P.cs; o += 32) {
-            const float g = __fdiv_rn(gs[t * P.cs + o], a);
+            const float g = DIV ? __fdiv_rn(gs[t * P.cs + o], a) : gs[t * P.cs + o];
             if (P.p[0]) part[0] = __fadd_rn(part[0], __fmul_rn(g, se3_term_s(P, one, s, o, 0)));
             if (P.p[3]) part[3] = __fadd_rn(part[3], __fmul_rn(g, se3_term_s(P, one, s, o, 3)));
             if (P.p[8]) part[8] = __fadd_rn(part[8], __fmul_rn(g, se3_term_s(P, one, s, o, 8)));
         }
         for (int f = lane; f < 3 * P.cv; f += 32) {
-            const float g = __fdiv_rn(gv[t * 3 * P.cv + f], a);
+            const float g = DIV ? __fdiv_rn(gv[t * 3 * P.cv + f], a) : gv[t * 3 * P.cv + f];
             const int o = f / 3, k = f - 3 * o;
             if (P.p[1]) part[1] = __fadd_rn(part[1], __fmul_rn(g, se3_term_v(P, one, s, o, k, 1)));
             if (P.p[2]) part[2] = __fadd_rn(part[2], __fmul_rn(g, se3_term_v(P, one, s, o, k, 2)));
             if (P.p[4]) part[4] = __fadd_rn(part[4], __fmul_rn(g, se3_term_v(P, one, s, o, k, 4)));
         }
         for (int f = lane; f < 5 * P.ct2; f += 32) {
-            const float g = __fdiv_rn(gt[t * 5 * P.ct2 + f], a);
+            const float g = DIV ? __fdiv_rn(gt[t * 5 * P.ct2 + f], a) : gt[t * 5 * P.ct2 + f];
             const int o = f / 5, m = f - 5 * o;
             if (P.p[5]) part[5] = __fadd_rn(part[5], __fmul_rn(g, se3_term_t(P, cg, one, s, o, m, 5)));
             if (P.p[6]) part[6] = __fadd_rn(part[6], __fmul_rn(g, se3_term_t(P, cg, one, s, o, m, 6)));
@@ -299,10 +300,14 @@ __device__ __forceinline__ int proj_width(const Se3Paths &P, int p) {
 }
 
 // d(message) / d(projection p entry q) contracted with g over the channels that entry feeds
+template <bool DIV>
 __device__ __forceinline__ float proj_grad_term(const Se3Paths &P, const float *__restrict__ cg, const Se3Edge &x,
                                                 const float *__restrict__ gs, const float *__restrict__ gv,
                                                 const float *__restrict__ gt, int64_t t, float a, int p, int q) {
-    auto G = [&](int f) { return __fdiv_rn(grad_at(gs, gv, gt, P, t, f), a); };
+    auto G = [&](int f) {
+        const float g = grad_at(gs, gv, gt, P, t, f);
+        return DIV ? __fdiv_rn(g, a) : g;
+    };
     switch (p) {
         case 0: return __fmul_rn(__fmul_rn(x.r[0], x.y0), G(q));
         case 3: {
@@ -351,7 +356,7 @@ __device__ __forceinline__ float proj_grad_term(const Se3Paths &P, const float *
 
 // one projection's gradient rows for source s (PI fixed at compile time, so that the inner loop
 // holds only that projection's term)
-template <int PI>
+template <int PI, bool DIV>
 __device__ __forceinline__ void grad_p_pass(const Se3Paths &P, float *__restrict__ gp, const float *__restrict__ R,
                                             int64_t rs, const float *__restrict__ dir,
                                             const float *__restrict__ sph, int sd, const float *__restrict__ cg,
@@ -374,7 +379,7 @@ __device__ __forceinline__ void grad_p_pass(const Se3Paths &P, float *__restrict
                 if (lane < cnt) {
                     const int64_t e = sperm[jb + lane];
                     mt = col[e];
-                    ma = avg[mt];
+                    ma = DIV ? avg[mt] : 1.0f;
                     load_edge(P, R, rs, dir, sph, sd, e, mine);
                 }
             }
@@ -386,7 +391,7 @@ __device__ __forceinline__ void grad_p_pass(const Se3Paths &P, float *__restrict
 #pragma unroll
                 for (int i = 0; i < kSe3Chunks; ++i) {
                     const int q = q0 + lane + 32 * i;
-                    if (q < w) acc[i] = __fadd_rn(acc[i], proj_grad_term(P, cg, x, gs, gv, gt, t, a, PI, q));
+                    if (q < w) acc[i] = __fadd_rn(acc[i], proj_grad_term<DIV>(P, cg, x, gs, gv, gt, t, a, PI, q));
                 }
             }
         }
@@ -400,6 +405,7 @@ __device__ __forceinline__ void grad_p_pass(const Se3Paths &P, float *__restrict
 
 // grad of every projection entry of source node s: one warp per source, its out-edges in
 // source-sorted order (deterministic), lanes over the entries of one projection at a time
+template <bool DIV>
 __global__ void __launch_bounds__(256, 2) se3_agg_grad_p_kernel(Se3Paths P, Se3Grads Gp, const float *__restrict__ R,
                                                              int64_t rs, const float *__restrict__ dir,
                                                              const float *__restrict__ sph, int sd,
@@ -425,12 +431,12 @@ __global__ void __launch_bounds__(256, 2) se3_agg_grad_p_kernel(Se3Paths P, Se3G
         if (single && lane < j1 - j0) {
             const int64_t e = sperm[j0 + lane];
             mt = col[e];
-            ma = avg[mt];
+            ma = DIV ? avg[mt] : 1.0f;
             load_edge(P, R, rs, dir, sph, sd, e, mine);
         }
 #define GDL_SE3_PASS(PI)                                                                                          \
     if (Gp.g[PI])                                                                                                 \
-        grad_p_pass<PI>(P, Gp.g[PI], R, rs, dir, sph, sd, cg, col, sperm, avg, gs, gv, gt, s, j0, j1, single, mine, \
+        grad_p_pass<PI, DIV>(P, Gp.g[PI], R, rs, dir, sph, sd, cg, col, sperm, avg, gs, gv, gt, s, j0, j1, single, mine, \
                         mt, ma, lane);
         GDL_SE3_PASS(0)
         GDL_SE3_PASS(1)
@@ -502,12 +508,15 @@ extern "C" int gdl_se3_aggregate_backward(const gdl_se3_paths *paths, float *con
     GDL_RETURN_IF(!se3_paths_ok(paths, &P) || n_nodes < 0 || n_edges < 0 || sph_dim < 1, GDL_ERR_INVALID);
     GDL_RETURN_IF((P.cs && !grad_s) || (P.cv && !grad_v) || (P.ct2 && !grad_t2), GDL_ERR_INVALID);
     if (n_nodes == 0) return GDL_OK;
-    GDL_RETURN_IF(!avg_degree, GDL_ERR_INVALID);
     GDL_RETURN_IF((P.p[7] && !cg) || ((P.p[5]) && sph_dim < 9), GDL_ERR_INVALID);
     if (grad_R && n_edges > 0) {
         GDL_RETURN_IF(!R || !direction || !sph || !row || !col, GDL_ERR_INVALID);
-        se3_agg_grad_r_kernel<<<se3_grid(n_edges), 256, 0, st>>>(P, R, r_stride, direction, sph, sph_dim, cg, row, col,
-                                                                 avg_degree, n_edges, grad_s, grad_v, grad_t2, grad_R);
+        if (avg_degree)
+            se3_agg_grad_r_kernel<true><<<se3_grid(n_edges), 256, 0, st>>>(
+                P, R, r_stride, direction, sph, sph_dim, cg, row, col, avg_degree, n_edges, grad_s, grad_v, grad_t2, grad_R);
+        else
+            se3_agg_grad_r_kernel<false><<<se3_grid(n_edges), 256, 0, st>>>(
+                P, R, r_stride, direction, sph, sph_dim, cg, row, col, avg_degree, n_edges, grad_s, grad_v, grad_t2, grad_R);
     }
     if (grad_proj) {
         Se3Grads G;
@@ -519,9 +528,14 @@ extern "C" int gdl_se3_aggregate_backward(const gdl_se3_paths *paths, float *con
         if (any) {
             GDL_RETURN_IF(!src_perm || !src_start || !src_end || (n_edges > 0 && (!R || !direction || !sph || !col)),
                           GDL_ERR_INVALID);
-            se3_agg_grad_p_kernel<<<se3_grid(n_nodes), 256, 0, st>>>(P, G, R, r_stride, direction, sph, sph_dim, cg, col,
-                                                                     src_perm, src_start, src_end, avg_degree, n_nodes,
-                                                                     grad_s, grad_v, grad_t2);
+            if (avg_degree)
+                se3_agg_grad_p_kernel<true><<<se3_grid(n_nodes), 256, 0, st>>>(
+                    P, G, R, r_stride, direction, sph, sph_dim, cg, col, src_perm, src_start, src_end, avg_degree, n_nodes,
+                    grad_s, grad_v, grad_t2);
+            else
+                se3_agg_grad_p_kernel<false><<<se3_grid(n_nodes), 256, 0, st>>>(
+                    P, G, R, r_stride, direction, sph, sph_dim, cg, col, src_perm, src_start, src_end, avg_degree, n_nodes,
+                    grad_s, grad_v, grad_t2);
         }
     }
     GDL_CUDA_TRY(cudaGetLastError());

@@ -144,6 +144,10 @@ class SE3MessageAggregate(torch.autograd.Function):
         gs = torch.zeros(N, cs, device=dev) if gs is None else gs.contiguous().float()
         gv = torch.zeros(N, cv, 3, device=dev) if gv is None else gv.contiguous().float()
         gt = torch.zeros(N, ct2, 5, device=dev) if gt is None else gt.contiguous().float()
+        # d out / d message = 1 / avg_degree[target]: divided once per node and channel here, so the
+        # kernels (avg_degree = NULL) do no division per edge term
+        deg = g.avg_degree.reshape(N, 1)
+        gs, gv, gt = gs / deg, gv / deg.unsqueeze(-1), gt / deg.unsqueeze(-1)
         # each group is covered by its paths' columns, so the kernel writes every entry
         grad_g = [torch.empty_like(t) if ctx.needs_input_grad[2 + k] else None for k, t in enumerate(groups)]
         gp = [None] * _PATHS
@@ -162,7 +166,7 @@ class SE3MessageAggregate(torch.autograd.Function):
             ctypes.byref(st), gp_arr if need_p else None, nat.ptr(grad_R), nat.ptr(gs) if gs.numel() else None,
             nat.ptr(gv) if gv.numel() else None, nat.ptr(gt) if gt.numel() else None, R.data_ptr(), R.shape[1],
             g.direction.contiguous().data_ptr(), sph.data_ptr(), sph.shape[1], nat.ptr(cg), g.row.data_ptr(),
-            g.col.data_ptr(), nat.ptr(src_perm), nat.ptr(src_start), nat.ptr(src_end), g.avg_degree.data_ptr(), N, E,
+            g.col.data_ptr(), nat.ptr(src_perm), nat.ptr(src_start), nat.ptr(src_end), None, N, E,
             nat.stream(dev)), "gdl_se3_aggregate_backward")
         return (None, grad_R, *grad_g)
 

@@ -232,6 +232,8 @@ int gdl_hybrid_graph(const float *x, const int64_t *radius_row_ptr, const int64_
  * Backward: grad_R [E, r_stride] (nullable) and grad_proj[i] (nullable array / entries, shapes and
  * row strides ld[i] of p[i]; every entry of each row is written) from grad_s/v/t2 [N, ...]; grad_proj needs the edges grouped by source: src_perm /
  * src_start / src_end = gdl_sort_and_build_csr(row) (perm, node_start, node_end), and col [E].
+ * avg_degree may be NULL in the backward: grad_s/v/t2 then come already divided by their target's
+ * average degree (one division per node and channel instead of one per edge term).
  * No counterpart kernel in the reference. */
 typedef struct gdl_se3_paths {
     const float *p[9];

@@ -129,3 +129,52 @@ def test_se3conv_empty_graph_and_mask():
     mask = torch.rand(200, device=DEV) > 0.3
     s_out, v_out = conv(torch.randn(200, 4, device=DEV), torch.randn(200, 2, 3, device=DEV), g, mask=mask)
     assert torch.all(s_out[~mask] == 0) and torch.all(v_out[~mask] == 0)
+
+
+def test_backward_degree_division_in_kernel_equals_prescaled():
+    """gdl_se3_aggregate_backward divides by the average degree itself (avg_degree given) or takes
+    gradients already divided (avg_degree NULL, what SE3Conv passes): both IEEE divisions of the
+    same numbers, so every gradient is bit-identical."""
+    import ctypes
+
+    from gdl_b200 import _native as nat
+    from gdl_b200.se3_conv import _source_csr, cg_11_2_cartesian
+
+    torch.manual_seed(3)
+    pos = torch.rand(3000, 3, device=DEV) * 4.0
+    batch = torch.repeat_interleave(torch.arange(3, device=DEV), 1000)
+    g = SpatialGraph.build(pos, 0.5, max_num_neighbors=32, batch=batch, max_l=2, num_batch_elements=3)
+    N, E = g.N, g.E
+    cs, cv, ct2 = 20, 7, 5
+    widths = [cs, cv, 3 * cv, 3 * cs, 3 * cv, ct2, 5 * ct2, 3 * ct2, cs]
+    proj = [torch.randn(N, w, device=DEV) for w in widths]
+    R = torch.randn(E, 9, device=DEV)
+    cg = cg_11_2_cartesian().to(DEV).contiguous()
+    sph = g.Y.contiguous()
+    gs, gv, gt = torch.randn(N, cs, device=DEV), torch.randn(N, cv, 3, device=DEV), torch.randn(N, ct2, 5, device=DEV)
+    sperm, sstart, send = _source_csr(g)
+    st = nat.Se3Paths()
+    for i in range(9):
+        st.p[i] = proj[i].data_ptr()
+        st.r_col[i] = i
+    st.cs, st.cv, st.ct2 = cs, cv, ct2
+    L = nat.load()
+
+    def run(gs_, gv_, gt_, avg):
+        gp = [torch.empty_like(p) for p in proj]
+        gR = torch.zeros_like(R)
+        arr = (ctypes.c_void_p * 9)(*[t.data_ptr() for t in gp])
+        nat.check(L.gdl_se3_aggregate_backward(
+            ctypes.byref(st), arr, gR.data_ptr(), gs_.data_ptr(), gv_.data_ptr(), gt_.data_ptr(), R.data_ptr(), 9,
+            g.direction.contiguous().data_ptr(), sph.data_ptr(), sph.shape[1], cg.data_ptr(), g.row.data_ptr(),
+            g.col.data_ptr(), sperm.data_ptr(), sstart.data_ptr(), send.data_ptr(), avg, N, E,
+            nat.stream(torch.device(DEV))), "gdl_se3_aggregate_backward")
+        return gp, gR
+
+    deg = g.avg_degree.reshape(N, 1)
+    a_gp, a_gR = run(gs, gv, gt, g.avg_degree.data_ptr())
+    b_gp, b_gR = run((gs / deg).contiguous(), (gv / deg.unsqueeze(-1)).contiguous(),
+                     (gt / deg.unsqueeze(-1)).contiguous(), None)
+    assert E > 0 and torch.equal(a_gR, b_gR)
+    for x, y in zip(a_gp, b_gp):
+        assert torch.equal(x, y)
