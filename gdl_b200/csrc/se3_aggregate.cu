@@ -406,7 +406,7 @@ __device__ __forceinline__ void grad_p_pass(const Se3Paths &P, float *__restrict
 // grad of every projection entry of source node s: one warp per source, its out-edges in
 // source-sorted order (deterministic), lanes over the entries of one projection at a time
 template <bool DIV>
-__global__ void __launch_bounds__(256, 2) se3_agg_grad_p_kernel(Se3Paths P, Se3Grads Gp, const float *__restrict__ R,
+__global__ void __launch_bounds__(256, 3) se3_agg_grad_p_kernel(Se3Paths P, Se3Grads Gp, const float *__restrict__ R,
                                                              int64_t rs, const float *__restrict__ dir,
                                                              const float *__restrict__ sph, int sd,
                                                              const float *__restrict__ cg,
