@@ -179,7 +179,7 @@ __device__ __forceinline__ void fwd_kind_pass(const Se3Paths &P, const float *__
 
 // one warp per target node; its three channel kinds in turn, edges of the segment in sorted-slot
 // order, messages formed on the fly
-__global__ void __launch_bounds__(256, 2) se3_agg_fwd_kernel(Se3Paths P, const float *__restrict__ R, int64_t rs,
+__global__ void __launch_bounds__(256, 3) se3_agg_fwd_kernel(Se3Paths P, const float *__restrict__ R, int64_t rs,
                                                           const float *__restrict__ dir, const float *__restrict__ sph,
                                                           int sd, const float *__restrict__ cg,
                                                           const int64_t *__restrict__ row,
