@@ -1,25 +1,27 @@
 """Benchmark of the B200 point-cloud graph pipeline (one JSON line on rank 0).
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--config c2] [--impl ours|reference]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--config c5] [--impl ours|reference]
 
 A step is one pass of a configuration's pipeline over its batch of clouds (seeded synthetic
 inputs with the shapes of the reference's use cases; see gdl_b200/synthetic.py):
 
-  c2 (default)  16 clouds x 2048 points: FPS -> 512 centroids per cloud, radius graph
+  c5 (default)  8 clouds x 131072 LiDAR points (the largest configuration): FPS -> 16384
+                centroids per cloud, radius graph (r = 1 m, 64) over the centroids, segment sum
+                of 64-channel features. Under torchrun the 8 clouds are split over the ranks
+                by cloud (strong scaling); a whole batch per rank is measured too (weak_scaling).
+  c1            4 clouds x 2048 uniform points: FPS -> 512, KNN k=16, segment sum and max
+                (64 channels).
+  c2            16 clouds x 2048 points: FPS -> 512 centroids per cloud, radius graph
                 (r = 0.2, 32 neighbours) over the centroids, segment mean of 128-channel
                 features over that graph, forward and backward.
+  c3            32 GMM clouds x 8192 points: FPS chain 8192 -> 2048 -> 512 -> 128, KNN k=32
+                per level, segment max over gathered bf16 features, forward and backward.
+  c4            64 source/target pairs x 16384 points: KNN k=1, residual segment sum.
   c2c           (auxiliary) one SE3Conv layer (scalar, vector and type-2 channels), forward and
                 backward, over c2's centroid graph: per-node channel mixing + the fused
                 message / segment-reduce kernel.
-  c1            4 clouds x 2048 uniform points: FPS -> 512, KNN k=16, segment sum and max
-                (64 channels).
-  c3            32 GMM clouds x 8192 points: FPS chain 8192 -> 2048 -> 512 -> 128, KNN k=32
-                per level, segment max over gathered bf16 features, forward and backward.
   c3i           (auxiliary) c3's clouds: the decoder's KNN k=3 inverse-distance interpolation
                 128 -> 512 -> 2048 -> 8192 of scalar + vector features, forward and backward.
-  c4            64 source/target pairs x 16384 points: KNN k=1, residual segment sum.
-  c5            8 clouds x 131072 LiDAR points: FPS -> 16384, radius graph (r = 1 m, 64),
-                segment sum of 64-channel features.
   c5g           (auxiliary) c5's clouds: radius graph r = 1 m, 64 over all points, segment sum.
   c5h           (auxiliary) c5 with the reference encoder's hybrid graph (radius graph + symmetric
                 KNN-3 fallback, deduplicated, with edge geometry) over the FPS centroids.
@@ -31,7 +33,10 @@ value : input points per second with inputs resident in HBM, timed with CUDA eve
         launching stream, L2 flushed (256 MiB write) between steps, max over ranks.
 e2e   : the same through the public Python API (gdl_b200.functional / csrc) with inputs
         copied from pinned host memory and the result copied back inside each timed step.
-Under torchrun each rank processes its own batch (weak scaling, no collective in a step).
+roofline : the dominant stage against its bound -- HBM (measured copy bandwidth), FP32 (the
+        packed-FMA throughput measured in the same run) or, for FPS, the per-pick latency of
+        the same kernel on duplicated points (its exchange chain alone).
+per_config : at N=1, configurations 1-4 measured the same way in the same run.
 --impl reference times the reference algorithm's CPU implementation (the C restatement
 in oracle/, all host threads) on the same configuration.
 """
@@ -60,6 +65,7 @@ from gdl_b200 import functional as F  # noqa: E402
 from gdl_b200.spatial_graph import SpatialGraph  # noqa: E402
 
 L2_FLUSH_BYTES = 256 << 20
+FPS_BUCKETED_LAUNCHES = 1 + 1 + 13 + 1  # clouds > 4096 points: box, Morton keys, radix sort, FPS
 
 
 # ----------------------------------------------------------------------------- configs
@@ -105,7 +111,7 @@ class C2:
         self.dst = torch.zeros(self.cap, dtype=torch.int64, device=dev)
         self.out = torch.empty(self.nc, self.C, dtype=torch.float32, device=dev)
         self.gmsg = torch.empty(self.cap, self.C, dtype=torch.float32, device=dev)
-        self.ws_fps = nat.workspace(L.gdl_fps_workspace_size(self.n_points, self.N), dev)
+        self.ws_fps = nat.workspace(L.gdl_fps_workspace_size(self.n_points, self.B, self.N), dev)
         self.ws_rad = nat.workspace(L.gdl_radius_graph_workspace_size(self.nc, self.B, self.NN), dev)
         self.ws_seg = nat.workspace(L.gdl_segment_reduce_workspace_size(self.cap, self.nc), dev)
 
@@ -151,6 +157,9 @@ class C2:
         return [("fps", self.stage_fps), ("radius_graph", self.stage_radius),
                 ("segment_mean_fwd", self.stage_seg_fwd), ("segment_mean_bwd", self.stage_seg_bwd)]
 
+    def fps_chain_picks(self):
+        return self.K
+
     def step(self):
         for _, fn in self.stage_list():
             fn()
@@ -165,7 +174,8 @@ class C2:
         return {
             "fps": 12 * self.n_points + 8 * nc,  # coordinates read once, indices written
             "radius_graph": 12 * nc + 16 * E + 8 * (nc + 1),  # points in, (src, dst) i64 + row_ptr out
-            "segment_mean_fwd": 4 * E * C + 4 * nc * C + 4 * (E + 2 * nc),
+            # messages are node features gathered through src32: the node table once, not E rows
+            "segment_mean_fwd": 4 * nc * C + 4 * nc * C + 4 * (E + 2 * nc),
             "segment_mean_bwd": 4 * nc * C + 4 * E * C + 4 * 2 * nc,
         }
 
@@ -256,7 +266,7 @@ class C1:
         self.out_sum = torch.empty(self.nq, self.C, device=dev)
         self.out_max = torch.empty(self.nq, self.C, device=dev)
         self.arg = torch.empty(self.nq, self.C, dtype=torch.int32, device=dev)
-        self.ws_fps = nat.workspace(L.gdl_fps_workspace_size(self.n_points, self.N), dev)
+        self.ws_fps = nat.workspace(L.gdl_fps_workspace_size(self.n_points, self.B, self.N), dev)
         self.ws_knn = nat.workspace(L.gdl_knn_workspace_size(self.nq, self.B, self.KNN, self.N), dev)
         self.ws_seg = nat.workspace(L.gdl_segment_reduce_workspace_size(self.nq * self.KNN, self.nq), dev)
 
@@ -283,6 +293,12 @@ class C1:
         return [("fps", self.stage_fps), ("knn", self.stage_knn),
                 ("segment_sum", lambda: self._seg(0, self.out_sum, None)),
                 ("segment_max", lambda: self._seg(2, self.out_max, self.arg))]
+
+    def fps_chain_picks(self):
+        return self.K
+
+    def knn_pairs(self):
+        return self.B * self.K * self.N
 
     def step(self):
         for _, fn in self.stage_list():
@@ -333,7 +349,9 @@ class C3:
     CH = (64, 128, 256)
     # per level: fps 1; knn tiles + pad + fast + merge + exact replay 5; gather 1; segment max fwd 2
     # (short + long pass) and bwd 2
-    launches_per_step = 3 * (1 + 5 + 1 + 2 + 2)
+    # fps: level 0 bucketed, levels 1-2 one CTA kernel each; per level: knn tiles + pad + fast +
+    # merge + exact replay 5; gather 1; segment max fwd 2 (short + long pass) and bwd 2
+    launches_per_step = FPS_BUCKETED_LAUNCHES + 2 + 3 * (5 + 1 + 2 + 2)
     points_per_step = property(lambda self: self.B * self.N)
 
     def _sizes(self):
@@ -374,7 +392,7 @@ class C3:
         self.gmsg = [torch.empty_like(m) for m in self.msg]
         self.out = [torch.empty(nq[l], self.CH[l], device=dev) for l in range(3)]
         self.arg = [torch.empty(nq[l], self.CH[l], dtype=torch.int32, device=dev) for l in range(3)]
-        self.ws_fps = [nat.workspace(L.gdl_fps_workspace_size(self.B * sz[l], sz[l]), dev) for l in range(3)]
+        self.ws_fps = [nat.workspace(L.gdl_fps_workspace_size(self.B * sz[l], self.B, sz[l]), dev) for l in range(3)]
         self.ws_knn = [nat.workspace(L.gdl_knn_workspace_size(nq[l], self.B, self.KNN, sz[l]), dev) for l in range(3)]
         self.ws_seg = [nat.workspace(L.gdl_segment_reduce_workspace_size(nq[l] * self.KNN, nq[l]), dev)
                        for l in range(3)]
@@ -430,6 +448,13 @@ class C3:
     def stage_list(self):
         return [("fps_chain", self.stage_fps), ("knn", self.stage_knn), ("gather", self.stage_gather),
                 ("segment_max_fwd", self.stage_seg_fwd), ("segment_max_bwd", self.stage_seg_bwd)]
+
+    def fps_chain_picks(self):
+        return sum(self.LEVELS)
+
+    def knn_pairs(self):
+        sz = self._sizes()
+        return sum(self.B * self.LEVELS[l] * sz[l] for l in range(3))
 
     def step(self):
         for _, fn in self.stage_list():
@@ -825,6 +850,9 @@ class C4:
     def stage_list(self):
         return [("knn", self.stage_knn), ("residual", self.stage_residual), ("segment_sum", self.stage_seg)]
 
+    def knn_pairs(self):
+        return self.B * self.N * self.N
+
     def step(self):
         for _, fn in self.stage_list():
             fn()
@@ -874,10 +902,19 @@ class C5:
     name = "c5"
     metric = "points/sec (FPS 16384 + radius graph r=1 k=64 + segment sum C=64), config 5"
     B, N, K, R, NN, C = 8, 131072, 16384, 1.0, 64, 64
-    launches_per_step = 1 + 25 + 2
+    launches_per_step = FPS_BUCKETED_LAUNCHES + 25 + 2
 
-    def _host_init(self, seed, pin=True):
-        pos, ptr = synthetic.c5_points(seed=seed, B=self.B, N=self.N)
+    shardable = True  # the batch of clouds can be split over ranks (strong scaling)
+
+    def _clouds(self, seed, clouds):
+        """This rank's clouds [c0, c1) of the seeded 8-cloud batch (all of it by default)."""
+        c0, c1 = clouds if clouds is not None else (0, type(self).B)
+        pos, _ = synthetic.c5_points(seed=seed, B=type(self).B, N=self.N)
+        self.B = c1 - c0
+        return pos[c0 * self.N:c1 * self.N].copy(), synthetic.ptr_of([self.N] * self.B), (c0, c1)
+
+    def _host_init(self, seed, pin=True, clouds=None):
+        pos, ptr, (c0, c1) = self._clouds(seed, clouds)
         self.n_points = pos.shape[0]
         self.nc = self.B * self.K
         self.pos_h = torch.from_numpy(pos)
@@ -885,13 +922,13 @@ class C5:
         self.k_h = torch.full((self.B,), self.K, dtype=torch.int64)
         self.cptr_h = torch.arange(0, self.nc + 1, self.K, dtype=torch.int64)
         g = torch.Generator().manual_seed(seed + 1)
-        self.feat_h = torch.randn(self.nc, self.C, generator=g)
+        self.feat_h = torch.randn(type(self).B * self.K, self.C, generator=g)[c0 * self.K:c1 * self.K].contiguous()
         if pin:
             self.pos_h, self.feat_h = self.pos_h.pin_memory(), self.feat_h.pin_memory()
 
-    def __init__(self, dev, seed):
+    def __init__(self, dev, seed, clouds=None):
         self.dev = dev
-        self._host_init(seed)
+        self._host_init(seed, clouds=clouds)
         self.pos, self.ptr, self.k, self.cptr = (t.to(dev) for t in (self.pos_h, self.ptr_h, self.k_h, self.cptr_h))
         self.feat = self.feat_h.to(dev)
         self.cap = self.nc * self.NN
@@ -904,7 +941,7 @@ class C5:
         self.ns, self.ne = self.row_ptr32[:-1], self.row_ptr32[1:]
         self.src32 = torch.zeros(self.cap, dtype=torch.int32, device=dev)
         self.out = torch.empty(self.nc, self.C, device=dev)
-        self.ws_fps = nat.workspace(L.gdl_fps_workspace_size(self.n_points, self.N), dev)
+        self.ws_fps = nat.workspace(L.gdl_fps_workspace_size(self.n_points, self.B, self.N), dev)
         self.ws_rad = nat.workspace(L.gdl_radius_graph_workspace_size(self.nc, self.B, self.NN), dev)
         self.ws_seg = nat.workspace(L.gdl_segment_reduce_workspace_size(self.cap, self.nc), dev)
 
@@ -930,6 +967,12 @@ class C5:
     def stage_list(self):
         return [("fps", self.stage_fps), ("radius_graph", self.stage_radius), ("segment_sum", self.stage_seg)]
 
+    def fps_chain_picks(self):
+        return self.K
+
+    def knn_pairs(self):  # the hybrid graph's self-KNN over the centroids
+        return self.B * self.K * self.K
+
     def step(self):
         for _, fn in self.stage_list():
             fn()
@@ -939,8 +982,9 @@ class C5:
 
     def stage_bytes(self, E):
         nc, C = self.nc, self.C
+        # the segment sum gathers node features through src32: the node table is read once
         return {"fps": 12 * self.n_points + 20 * nc, "radius_graph": 12 * nc + 12 * E + 12 * (nc + 1),
-                "segment_sum": 4 * E * C + 4 * nc * C + 4 * (E + 2 * nc)}
+                "segment_sum": 4 * min(E, nc) * C + 4 * nc * C + 4 * (E + 2 * nc)}
 
     def e2e_step(self):
         pos = self.pos_h.to(self.dev, non_blocking=True)
@@ -956,10 +1000,11 @@ class C5:
     e2e_h2d = property(lambda self: self.pos_h.numel() * 4 + self.feat_h.numel() * 4)
     e2e_d2h = property(lambda self: self.nc * self.C * 4)
 
-    cpu_clouds = 1      # the CPU sample: one cloud, first 2048 FPS picks, scaled to the full step
-    cpu_picks = 2048
-    cpu_fraction = (2048 / 16384) / 8
-    cpu_sample = "FPS of 2048 of 16384 picks on 1 of 8 clouds per sample, scaled x64 (FPS dominates this step)"
+    cpu_clouds = 1      # the CPU sample: one cloud, first 256 FPS picks, scaled to the full step
+    cpu_picks = 256
+    cpu_fraction = (256 / 16384) / 8
+    cpu_sample = ("FPS of 256 of 16384 picks on 1 of 8 clouds per sample, scaled x512 (FPS dominates this step; "
+                  "every pick scans the whole cloud, so its cost is the same for every pick)")
 
     def cpu_step(self, O):
         pos = self.pos_h.numpy()[:self.N]
@@ -975,20 +1020,20 @@ class C5G(C5):
     metric = "points/sec (radius graph r=1 k=64 over all points + segment sum C=64), config 5 clouds"
     launches_per_step = 25 + 2
 
-    def _host_init(self, seed, pin=True):
-        pos, ptr = synthetic.c5_points(seed=seed, B=self.B, N=self.N)
+    def _host_init(self, seed, pin=True, clouds=None):
+        pos, ptr, (c0, c1) = self._clouds(seed, clouds)
         self.n_points = pos.shape[0]
         self.nc = self.n_points
         self.pos_h = torch.from_numpy(pos)
         self.ptr_h = torch.from_numpy(ptr)
         g = torch.Generator().manual_seed(seed + 1)
-        self.feat_h = torch.randn(self.n_points, self.C, generator=g)
+        self.feat_h = torch.randn(type(self).B * self.N, self.C, generator=g)[c0 * self.N:c1 * self.N].contiguous()
         if pin:
             self.pos_h, self.feat_h = self.pos_h.pin_memory(), self.feat_h.pin_memory()
 
-    def __init__(self, dev, seed):
+    def __init__(self, dev, seed, clouds=None):
         self.dev = dev
-        self._host_init(seed)
+        self._host_init(seed, clouds=clouds)
         self.pos, self.ptr = self.pos_h.to(dev), self.ptr_h.to(dev)
         self.feat = self.feat_h.to(dev)
         self.cap = self.nc * self.NN
@@ -1014,7 +1059,7 @@ class C5G(C5):
     def stage_bytes(self, E):
         nc, C = self.nc, self.C
         return {"radius_graph": 12 * nc + 12 * E + 12 * (nc + 1),
-                "segment_sum": 4 * E * C + 4 * nc * C + 4 * (E + 2 * nc)}
+                "segment_sum": 4 * min(E, nc) * C + 4 * nc * C + 4 * (E + 2 * nc)}
 
     def e2e_step(self):
         pos = self.pos_h.to(self.dev, non_blocking=True)
@@ -1059,10 +1104,10 @@ class C5H(C5):
         radix = 1 + 4 * ((bits + 7) // 8)
         # fps 1; radius (general path) 25 - 2 segment launches of C5's count; knn 5; hybrid: count,
         # scan 3, fill, unique, scan 3, emit, radix, order; avg degree 2; segment 2
-        return 1 + 23 + 5 + (1 + 3 + 1 + 1 + 3 + 1 + radix + 1) + 2 + 2
+        return FPS_BUCKETED_LAUNCHES + 23 + 5 + (1 + 3 + 1 + 1 + 3 + 1 + radix + 1) + 2 + 2
 
-    def __init__(self, dev, seed):
-        super().__init__(dev, seed)
+    def __init__(self, dev, seed, clouds=None):
+        super().__init__(dev, seed, clouds)
         L = self.L
         nc = self.nc
         self.cap_h = int(L.gdl_hybrid_graph_capacity(nc, self.NN, self.KF))
@@ -1123,7 +1168,7 @@ class C5H(C5):
         # radius CSR + knn in; per edge (row, col) i64 + col_sorted, perm, src_sorted i32 + dist,
         # direction, 9 harmonics out; node start/end + average degree
         b["hybrid_graph"] = 8 * (nc + 1) + 8 * nc * k + E * (16 + 12 + 52) + 20 * nc
-        b["segment_sum"] = 4 * E * C + 4 * nc * C + 4 * (E + 2 * nc)
+        b["segment_sum"] = 4 * min(E, nc) * C + 4 * nc * C + 4 * (E + 2 * nc)
         return b
 
     def e2e_step(self):
@@ -1139,6 +1184,7 @@ class C5H(C5):
         return host
 
     cpu_clouds = 1
+    cpu_picks = 2048
     cpu_fraction = (2048 / 16384) / 8
     cpu_sample = ("FPS of 2048 of 16384 picks on 1 of 8 clouds per sample, scaled x64 (FPS dominates this step; "
                   "the hybrid graph of those centroids runs in the same sample)")
@@ -1167,8 +1213,8 @@ class C5S(C5G):
     launches_per_step = 25 + 1
     MAX_L = 2
 
-    def __init__(self, dev, seed):
-        super().__init__(dev, seed)
+    def __init__(self, dev, seed, clouds=None):
+        super().__init__(dev, seed, clouds)
         f = dict(dtype=torch.float32, device=dev)
         self.dst = torch.zeros(self.cap, dtype=torch.int64, device=dev)
         self.dist = torch.empty(self.cap, **f)
@@ -1285,12 +1331,16 @@ class ClockSampler:
 
 
 ROOFLINE_NOTES = {
-    "fps": "FPS is one argmax per pick over the whole cloud, a serial latency chain on one CTA (or "
-           "cluster) per cloud; its HBM fraction is tiny by nature -- the kernel reads the points once. "
-           "Its bound is issue and latency per pick (ncu: profiles/fps_cta_kernel_c2.md).",
-    "fps_chain": "see fps",
-    "knn": "brute-force KNN is bound by the fp32 pipe (8 flops per pair), not by HBM; the pair rate is "
-           "reported in profiles/knn_fast_kernel_c3_c4.md.",
+    "fps": "FPS is a serial chain of picks per cloud (one argmax over the cloud per pick). Its bound is "
+           "the per-pick latency: `peak` is the per-pick time of the same kernel and launch shape on "
+           "clouds of duplicated points (no minimum changes after the first pick, so only the "
+           "warp/CTA/cluster exchange chain runs); the rest of `achieved` is the bucket updates. "
+           "HBM is irrelevant (the points are read once).",
+    "fps_chain": "see fps: the three levels' chains run back to back; `peak` is the same chain on "
+                 "duplicated points",
+    "knn": "the distance scan is bound by the FP32 pipe (8 flops per tested pair, packed fp32x2); "
+           "`peak` is the packed-FMA throughput measured in this run (gdl_fp32_peak); `achieved` "
+           "counts the brute-force pairs (every query against every source of its cloud).",
     "se3conv_fwd_bwd": "a whole layer step through eager autograd (cuBLAS projection GEMMs, the radial MLP, "
                        "the fused message kernels and their backward) over a 43.9 K-edge graph: launch-bound; "
                        "the bytes are those of the fused kernels only.",
@@ -1299,6 +1349,8 @@ ROOFLINE_NOTES = {
     "radius_graph": "the radius search scans candidate cells from L1/L2; its algorithmic HBM bytes (points, "
                     "edges) are small next to the candidate work.",
 }
+
+STAGE_BOUND = {"fps": "latency", "fps_chain": "latency", "knn": "fp32"}
 
 
 def measured_peak():
@@ -1317,6 +1369,27 @@ def ncu_traffic(config, stage):
     return json.loads(p.read_text()).get(config, {}).get(stage)
 
 
+def fp32_peaks(dev):
+    """FP32 FMA throughput of this GPU in TFLOP/s, scalar and packed (gdl_fp32_peak, every SM busy)."""
+    L = nat.load()
+    blocks, iters = 8 * 148, 4096
+    out = torch.empty(blocks * 256, device=dev)
+    st = torch.cuda.current_stream(dev).cuda_stream
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
+    res = {}
+    for packed in (0, 1):
+        best = None
+        for _ in range(4):
+            ev[0].record()
+            nat.check(L.gdl_fp32_peak(out.data_ptr(), iters, packed, blocks, st), "fp32 peak")
+            ev[1].record()
+            ev[1].synchronize()
+            t = ev[0].elapsed_time(ev[1])
+            best = t if best is None else min(best, t)
+        res["fp32x2" if packed else "fp32"] = L.gdl_fp32_peak_flops(iters, packed, blocks) / (best / 1000) / 1e12
+    return res
+
+
 def dist_env():
     ws = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -1325,6 +1398,15 @@ def dist_env():
 
 
 # ----------------------------------------------------------------------------- arms
+def config_of(cfg_cls, n_gpus):
+    """The workload description both arms print (identical for the same configuration and N)."""
+    strong = getattr(cfg_cls, "shardable", False)
+    return {"workload": f"{cfg_cls.name}: {cfg_cls.B} clouds x {cfg_cls.N} points" + ("" if strong else " per GPU"),
+            "clouds": cfg_cls.B, "points_per_cloud": cfg_cls.N, "l2": "flushed between steps (256 MiB write)",
+            "parallelism": (f"the {cfg_cls.B} clouds sharded by cloud over {n_gpus} GPU(s), no collective in a step"
+                            if strong else f"one batch per GPU on {n_gpus} GPU(s), no collective in a step")}
+
+
 def run_reference_arm(args, cfg_cls):
     ws, rank, _ = dist_env()
     if rank != 0:
@@ -1345,10 +1427,10 @@ def run_reference_arm(args, cfg_cls):
     ms = 1000 * sum(t) / len(t) / cfg.cpu_fraction
     value = cfg.points_per_step / (ms / 1000)
     line = {"metric": cfg_cls.metric, "value": value, "unit": "points/s", "n_gpus": args.gpus, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+            "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+            "scaling": "strong" if getattr(cfg_cls, "shardable", False) else "weak",
             "vs_baseline": None, "dtype": "f32", "data": "synthetic", "impl": "reference",
-            "config": {"workload": f"{cfg_cls.name}: {cfg_cls.B} clouds x {cfg_cls.N} points", "clouds": cfg_cls.B,
-                       "points_per_cloud": cfg_cls.N},
+            "config": config_of(cfg_cls, args.gpus),
             "cpu_baseline": {"value": value, "unit": "points/s", "cores": threads, "kind": "port",
                              "sample": f"each step: {cfg.cpu_sample}, on the C restatement of the reference "
                                        f"algorithm (oracle/)"},
@@ -1375,6 +1457,147 @@ def cpu_baseline(cfg, seconds=10.0):
                       f"({dt * 1000:.1f} ms per full step)"}
 
 
+class Timed:
+    """A configuration's stages, each captured as one CUDA graph (eager if capture fails), timed
+    with CUDA events on the launching stream; L2 flushed by a 256 MiB write before each step."""
+
+    def __init__(self, cfg, dev, eager=False):
+        self.cfg, self.dev = cfg, dev
+        self.stages = cfg.stage_list()
+        self.flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
+        self.runners = [fn for _, fn in self.stages]
+        self.launch = "eager"
+        if not eager and getattr(cfg, "capture", True):
+            try:
+                graphs = []
+                for _, fn in self.stages:
+                    g = torch.cuda.CUDAGraph()
+                    with torch.cuda.graph(g):
+                        fn()
+                    graphs.append(g)
+                self.runners = [g.replay for g in graphs]
+                self.graphs = graphs
+                self.launch = "one CUDA graph per stage"
+            except Exception as e:  # keep going eagerly, say so in the line
+                print(f"[bench] graph capture failed, eager launches: {e!r}", file=sys.stderr)
+            torch.cuda.synchronize(dev)
+
+    def run(self, steps, barrier=None):
+        ev = [torch.cuda.Event(enable_timing=True) for _ in range(len(self.stages) + 1)]
+        step_ms, acc = [], [0.0] * len(self.stages)
+        if barrier:
+            barrier()
+        for _ in range(steps):
+            self.flush.zero_()
+            ev[0].record()
+            for i, run in enumerate(self.runners):
+                run()
+                ev[i + 1].record()
+            ev[-1].synchronize()
+            step_ms.append(ev[0].elapsed_time(ev[-1]))
+            for i in range(len(self.stages)):
+                acc[i] += ev[i].elapsed_time(ev[i + 1])
+        if barrier:
+            barrier()
+        return sum(step_ms), {name: acc[i] / steps for i, (name, _) in enumerate(self.stages)}
+
+    def stage_time(self, name, reps=3):
+        """Best-of-`reps` device time of one stage's runner (after one warm replay)."""
+        i = [n for n, _ in self.stages].index(name)
+        ev = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
+        self.runners[i]()
+        best = None
+        for _ in range(reps):
+            self.flush.zero_()
+            ev[0].record()
+            self.runners[i]()
+            ev[1].record()
+            ev[1].synchronize()
+            t = ev[0].elapsed_time(ev[1])
+            best = t if best is None else min(best, t)
+        return best
+
+
+def fps_floor_ms(timed, stage):
+    """The FPS stage on clouds of duplicated points (every coordinate 0): after the first pick no
+    minimum changes, so the bucketed kernel skips every update and only its exchange chain runs."""
+    cfg = timed.cfg
+    saved = cfg.pos.clone()
+    cfg.pos.zero_()
+    try:
+        return timed.stage_time(stage)
+    finally:
+        cfg.pos.copy_(saved)
+        torch.cuda.synchronize(timed.dev)
+
+
+def roofline_of(cfg, timed, stage_ms, E, peaks):
+    """Roofline object of the configuration's dominant stage (the largest device time)."""
+    hbm, hbm_kind = measured_peak()
+    dom = max(stage_ms, key=stage_ms.get)
+    bound = STAGE_BOUND.get(dom, "hbm")
+    r = {"kernel": dom, "bound": bound, "note": ROOFLINE_NOTES.get(dom, "")}
+    if bound == "latency":
+        picks = cfg.fps_chain_picks()
+        floor = fps_floor_ms(timed, dom)
+        ach, pk = 1000 * stage_ms[dom] / picks, 1000 * floor / picks
+        r.update({"unit": "us/pick", "achieved": ach, "peak": pk, "frac": pk / ach,
+                  "picks_per_cloud_chain": picks,
+                  "peak_source": "measured in this run: the same stage on duplicated points (exchange chain only)",
+                  "traffic": ncu_traffic(cfg.name, dom)})
+    elif bound == "fp32":
+        pairs = cfg.knn_pairs()
+        ach = 8 * pairs / (stage_ms[dom] / 1000) / 1e12
+        pk = peaks.get("fp32x2")
+        r.update({"unit": "TFLOP/s", "achieved": ach, "peak": pk, "frac": ach / pk if pk else None,
+                  "pairs_per_launch": pairs, "peak_source": "measured in this run (gdl_fp32_peak, packed fp32x2 FMA)",
+                  "traffic": ncu_traffic(cfg.name, dom),
+                  "hbm_gbs": cfg.stage_bytes(E)[dom] / (stage_ms[dom] / 1000) / 1e9})
+    else:
+        algo = cfg.stage_bytes(E)[dom]
+        ach = algo / (stage_ms[dom] / 1000) / 1e9
+        r.update({"unit": "GB/s", "achieved": ach, "peak": hbm, "frac": ach / hbm,
+                  "algorithmic_bytes_per_launch": algo, "traffic": ncu_traffic(cfg.name, dom),
+                  "peak_source": (f"{hbm_kind} (MEASURED_PEAKS.json hbm_gbs)" if hbm_kind == "measured"
+                                  else "fallback 6.65 TB/s")})
+    return r
+
+
+def e2e_ms_of(cfg, steps, barrier=None):
+    for _ in range(2):
+        cfg.e2e_step()
+    if barrier:
+        barrier()
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        cfg.e2e_step()
+    return 1000 * (time.perf_counter() - t0) / steps
+
+
+def per_config_line(name, dev, args, peaks):
+    """One other configuration, measured the same way (steps of its pipeline, HBM-resident inputs)."""
+    cfg = CONFIGS[name](dev, seed=0)
+    for _ in range(3):
+        cfg.step()
+    torch.cuda.synchronize(dev)
+    timed = Timed(cfg, dev, args.eager)
+    steps = args.per_config_steps
+    total, stage_ms = timed.run(steps)
+    E = cfg.edges()
+    out = {"value": cfg.points_per_step * steps / (total / 1000), "unit": "points/s",
+           "ms_per_step": total / steps, "steps": steps, "stage_ms": stage_ms,
+           "workload": f"{cfg.name}: {cfg.B} clouds x {cfg.N} points", "launch": timed.launch,
+           "roofline": roofline_of(cfg, timed, stage_ms, E, peaks)}
+    if not args.no_e2e:
+        ms = e2e_ms_of(cfg, max(3, min(steps, 10)))
+        out["e2e"] = {"value": cfg.points_per_step / (ms / 1000), "unit": "points/s",
+                      "h2d_bytes_per_step": cfg.e2e_h2d, "d2h_bytes_per_step": cfg.e2e_d2h}
+    if not args.no_cpu_baseline:
+        out["cpu_baseline"] = cpu_baseline(cfg, seconds=min(args.cpu_seconds, 3.0))
+    del timed
+    return out
+
+
 def run_ours(args, cfg_cls):
     ws, rank, local = dist_env()
     if ws > 1:
@@ -1384,103 +1607,94 @@ def run_ours(args, cfg_cls):
         torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=120))
     dev = torch.device("cuda", local if ws > 1 else 0)
     torch.cuda.set_device(dev)
-    cfg = cfg_cls(dev, seed=1000 * rank)
-    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
-    stages = cfg.stage_list()
-    ev = [torch.cuda.Event(enable_timing=True) for _ in range(len(stages) + 1)]
-    for _ in range(max(args.warmup, 3)):
-        cfg.step()
-    torch.cuda.synchronize(dev)
-
-    # each stage captured as one CUDA graph; events between the replays time the stages
-    runners = [fn for _, fn in stages]
-    launch = "eager"
-    if not args.eager and getattr(cfg, "capture", True):
-        try:
-            graphs = []
-            for _, fn in stages:
-                g = torch.cuda.CUDAGraph()
-                with torch.cuda.graph(g):
-                    fn()
-                graphs.append(g)
-            runners = [g.replay for g in graphs]
-            launch = "one CUDA graph per stage"
-        except Exception as e:  # keep going eagerly, say so in the line
-            print(f"[bench] graph capture failed, eager launches: {e!r}", file=sys.stderr)
-        torch.cuda.synchronize(dev)
 
     def barrier():
         if ws > 1:
             torch.distributed.barrier()
         torch.cuda.synchronize(dev)
 
-    step_ms, stage_acc = [], [0.0] * len(stages)
-    barrier()
-    with ClockSampler(dev.index if dev.index is not None else 0) as clk:
-        for _ in range(args.steps):
-            flush.zero_()
-            ev[0].record()
-            for i, run in enumerate(runners):
-                run()
-                ev[i + 1].record()
-            ev[-1].synchronize()
-            step_ms.append(ev[0].elapsed_time(ev[-1]))
-            for i in range(len(stages)):
-                stage_acc[i] += ev[i].elapsed_time(ev[i + 1])
-    barrier()
-    total_ms = sum(step_ms)
-    stage_ms = {name: stage_acc[i] / args.steps for i, (name, _) in enumerate(stages)}
-    E = cfg.edges()
+    def max_over_ranks(*vals):
+        t = torch.tensor([float(v) for v in vals], dtype=torch.float64, device=dev)
+        if ws > 1:
+            torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        return [float(x) for x in t]
 
-    # end-to-end through the public API, host buffers in and out
+    peaks = fp32_peaks(dev)
+    # Strong scaling where the batch shards by cloud (8 clouds
+    # over up to 8 GPUs): every rank builds the same seeded batch and keeps its own clouds. Other
+    # configurations run a full batch per rank (weak scaling).
+    strong = getattr(cfg_cls, "shardable", False)
+    if strong:
+        from gdl_b200.sharding import shard_clouds
+
+        if ws > cfg_cls.B:
+            raise SystemExit(f"{cfg_cls.name} has {cfg_cls.B} clouds: at most {cfg_cls.B} ranks")
+        c0, c1 = shard_clouds([cfg_cls.N * getattr(cfg_cls, "K", 1)] * cfg_cls.B, ws, rank)
+        cfg = cfg_cls(dev, seed=0, clouds=(c0, c1))
+        global_points = cfg_cls.B * cfg_cls.N
+    else:
+        cfg = cfg_cls(dev, seed=1000 * rank)
+        global_points = ws * cfg.points_per_step
+    for _ in range(max(args.warmup, 3)):
+        cfg.step()
+    torch.cuda.synchronize(dev)
+    timed = Timed(cfg, dev, args.eager)
+    with ClockSampler(dev.index if dev.index is not None else 0) as clk:
+        total_ms, stage_ms = timed.run(args.steps, barrier)
+    E = cfg.edges()
+    launch = timed.launch
+    roof = roofline_of(cfg, timed, stage_ms, E, peaks) if rank == 0 else None
+
     e2e_ms = None
     if not args.no_e2e:
-        for _ in range(2):
-            cfg.e2e_step()
-        barrier()
-        e2e_steps = max(3, min(args.steps, 50))
-        t0 = time.perf_counter()
-        for _ in range(e2e_steps):
-            cfg.e2e_step()
-        e2e_ms = 1000 * (time.perf_counter() - t0) / e2e_steps
+        e2e_ms = e2e_ms_of(cfg, max(3, min(args.steps, 50)), barrier)
+    total_ms, e2e_max = max_over_ranks(total_ms, e2e_ms or 0.0)
+    value = global_points * args.steps / (total_ms / 1000)
 
-    t = torch.tensor([total_ms, e2e_ms or 0.0], dtype=torch.float64, device=dev)
-    if ws > 1:
-        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
-    total_ms, e2e_ms = float(t[0]), (float(t[1]) if e2e_ms is not None else None)
-    pts = cfg.points_per_step
-    value = ws * pts * args.steps / (total_ms / 1000)
+    weak = None
+    if strong and ws > 1:  # the same configuration with a whole batch per rank, for comparison
+        del timed
+        wcfg = cfg_cls(dev, seed=1000 * rank)
+        for _ in range(3):
+            wcfg.step()
+        wt = Timed(wcfg, dev, args.eager)
+        wsteps = max(3, min(args.steps, 20))
+        wms, _ = wt.run(wsteps, barrier)
+        (wms,) = max_over_ranks(wms)
+        weak = {"value": ws * wcfg.points_per_step * wsteps / (wms / 1000), "unit": "points/s",
+                "ms_per_step": wms / wsteps, "clouds_per_gpu": wcfg.B}
+        del wt, wcfg
 
     if rank == 0:
-        peak, peak_kind = measured_peak()
-        dom = max(stage_ms, key=stage_ms.get)
-        algo = cfg.stage_bytes(E)[dom]
-        achieved = algo / (stage_ms[dom] / 1000) / 1e9
         line = {
             "metric": cfg.metric, "value": value, "unit": "points/s", "n_gpus": ws, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": total_ms / args.steps, "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-            "config": {"workload": f"{cfg.name}: {cfg.B} clouds x {cfg.N} points per GPU", "clouds": cfg.B,
-                       "points_per_cloud": cfg.N, "edges": E, "l2": "flushed between steps (256 MiB write)",
-                       "launch": launch,
-                       "parallelism": f"clouds sharded over {ws} GPU(s), no collective in a step"},
+            "scaling": "strong" if strong else "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": config_of(cfg_cls, ws),
+            "run": {"clouds_rank0": cfg.B, "edges_rank0": E, "launch": launch},
             "stage_ms": stage_ms,
-            "roofline": {"kernel": dom, "bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
-                         "frac": achieved / peak, "traffic": ncu_traffic(cfg.name, dom),
-                         "peak_source": (f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured"
-                                         else "fallback 6.65 TB/s"),
-                         "algorithmic_bytes_per_launch": algo,
-                         "note": ROOFLINE_NOTES.get(dom, "")},
+            "roofline": roof,
+            "peaks": {"fp32_tflops": peaks.get("fp32"), "fp32x2_tflops": peaks.get("fp32x2"),
+                      "hbm_gbs": measured_peak()[0]},
             "gpu_launches": cfg.launches_per_step * args.steps,
             "clocks": clk.summary(),
         }
+        if strong:
+            line["note"] = ("strong scaling: the 8-cloud batch is split over the ranks; each cloud's FPS is a "
+                            "serial chain of 16384 picks on one thread-block cluster, so a rank's time is bounded "
+                            "below by one cloud's chain (fps_bucket_kernel) however few clouds it holds")
+        if weak:
+            line["weak_scaling"] = weak
         if e2e_ms is not None:
-            line["e2e"] = {"value": ws * pts / (e2e_ms / 1000), "unit": "points/s",
+            line["e2e"] = {"value": global_points / (e2e_max / 1000), "unit": "points/s",
                            "h2d_bytes_per_step": cfg.e2e_h2d, "d2h_bytes_per_step": cfg.e2e_d2h}
-        if not args.no_cpu_baseline:
+        if not args.no_cpu_baseline and ws == 1:
             line["cpu_baseline"] = cpu_baseline(cfg, seconds=args.cpu_seconds)
+        if ws == 1 and not args.no_per_config:
+            del timed
+            line["per_config"] = {n: per_config_line(n, dev, args, peaks) for n in args.per_config.split(",") if n}
         print(json.dumps(line), flush=True)
-    runners = None
+    timed = None
     if ws > 1:
         torch.distributed.barrier()
         torch.distributed.destroy_process_group()
@@ -1492,12 +1706,16 @@ def main():
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=5)
-    ap.add_argument("--config", default="c2", choices=sorted(CONFIGS))
+    ap.add_argument("--config", default="c5", choices=sorted(CONFIGS))
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--eager", action="store_true", help="launch kernels one by one instead of a CUDA graph")
+    ap.add_argument("--per-config", default="c1,c2,c3,c4",
+                    help="other configurations measured in the same run (N=1 only), in the line's per_config")
+    ap.add_argument("--per-config-steps", type=int, default=30)
+    ap.add_argument("--no-per-config", action="store_true")
     args = ap.parse_args()
     cfg_cls = CONFIGS[args.config]
     if args.impl == "reference":

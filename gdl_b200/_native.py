@@ -40,8 +40,11 @@ PROTOTYPES = {
     "gdl_version": (ctypes.c_int, []),
     "gdl_status_string": (ctypes.c_char_p, [ctypes.c_int]),
     "gdl_check_device": (ctypes.c_int, [ctypes.c_int]),
-    "gdl_fps_workspace_size": (_SZ, [_I64, _I64]),
+    "gdl_fp32_peak_flops": (_I64, [_I64, _I32, _I32]),
+    "gdl_fp32_peak": (ctypes.c_int, [_P, _I64, _I32, _I32, _P]),
+    "gdl_fps_workspace_size": (_SZ, [_I64, _I32, _I64]),
     "gdl_fps": (ctypes.c_int, [_P, _P, _P, _I32, _I64, _I64, _I32, _P, _P, _P, _SZ, _P]),
+    "gdl_fps_ex": (ctypes.c_int, [_P, _P, _P, _I32, _I64, _I64, _I32, _P, _P, _P, _SZ, _P, _I32, _I32, _I64, _P]),
     "gdl_knn_workspace_size": (_SZ, [_I64, _I32, _I32, _I64]),
     "gdl_knn": (ctypes.c_int, [_P, _P, _P, _P, _I32, _I64, _I32, _I64, _P, _P, _P, _SZ, _P]),
     "gdl_radius_graph_workspace_size": (_SZ, [_I64, _I32, _I32]),

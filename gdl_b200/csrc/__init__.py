@@ -84,7 +84,7 @@ def fps_cuda(pos: torch.Tensor, ptr: torch.Tensor, k_per_batch: torch.Tensor, *,
     out = torch.empty(total, dtype=torch.int64, device=dev)
     opos = torch.empty(total, 3, dtype=torch.float32, device=dev) if return_pos else None
     L = nat.load()
-    ws = nat.workspace(L.gdl_fps_workspace_size(pos.shape[0], max_n), dev)
+    ws = nat.workspace(L.gdl_fps_workspace_size(pos.shape[0], B, max_n), dev)
     nat.check(L.gdl_fps(pos.data_ptr(), ptr_d.data_ptr(), k_d.data_ptr(), B, pos.shape[0], max_n,
                         nat.TIE[tie_break], out.data_ptr(), nat.ptr(opos), ws.data_ptr(), ws.numel(),
                         nat.stream(dev)), "gdl_fps")

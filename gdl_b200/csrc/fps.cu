@@ -8,24 +8,30 @@
 // reduction order (GDL_TIE_REFERENCE, see fps_priority) or the lowest index.
 //
 // Design (B200). The step is a pure latency chain (one argmax per selected point), so the
-// kernel minimises the work between two picks:
-//  * a cloud's coordinates and running minima stay in REGISTERS for the whole run (P points
-//    per thread); a float4 copy of the coordinates in shared memory serves the winner lookup;
-//  * the argmax is a single u64 key (min_d bits << 32 | ~priority): a tree max over the
-//    thread's P keys, two redux.sync per warp, warp winners into a double-buffered slot
-//    array, one __syncthreads, then every warp reduces the slots itself (no second barrier;
-//    a shared-memory u64 atomicMax measured ~300 cycles slower per step here);
-//  * the winner's local index is decoded from its priority (a bijection) and its coordinates
-//    read back from shared memory.
-// Clouds above one CTA's register budget run on a thread-block cluster (up to 16 CTAs of 13312
-// points each, one per SM): each CTA's winner record goes to every CTA of the cluster through
-// distributed shared memory (st.async + mbarrier per pick). A 131072-point cloud takes 10 CTAs,
-// the largest cluster of which 8 fit on a B200 at once (11 of 10 CTAs, 7 of 11-16 CTAs), so a
-// batch of 8 LiDAR clouds runs in one wave. Larger clouds fall back to a CTA that streams points
-// from HBM with min_d in a workspace.
+// kernels minimise the work between two picks. The argmax is a single u64 key (min_d bits << 32
+// | ~priority), so any grouping of the points gives the same winner.
+//  * Clouds of at most 4096 points: one CTA per cloud, P points per thread in REGISTERS, a tree
+//    max over the thread's keys, two redux.sync per warp, warp winners into a double-buffered
+//    slot array, one __syncthreads per pick (fps_cta_kernel).
+//  * Larger clouds (bucketed FPS): each cloud is first put in Morton order (bounding box, 30-bit
+//    codes, segmented radix sort), so that every thread owns a compact run of P points -- a
+//    bucket with an axis-aligned box. Per pick a thread first bounds the distance from the new
+//    sample to its box with the same rounded operations as the point distances; the bound is
+//    <= every point's rounded distance (rounding is monotone), so when it is >= the bucket's
+//    largest minimum no minimum of the bucket can change and the thread skips its P updates
+//    and keeps its cached best key. Late in the run only the few buckets around each new sample
+//    update. The points sit in shared memory (SoA float2 pairs, conflict-free per lane, each
+//    thread's in priority order so that a (min-distance, slot) key reduced as a tree orders them
+//    exactly), the minima in registers. One CTA serves up to 13824 points; larger clouds run on
+//    a thread-block cluster of up to 16 CTAs whose winners cross through distributed shared
+//    memory: st.async stores completing bytes on each receiver's mbarrier, one bounded wait per
+//    pick, no cluster-wide barrier (fps_bucket_kernel).
+//  * Clouds beyond 16 x 13824 points: a CTA that streams points from HBM with min_d in the
+//    workspace (fps_stream_kernel).
 #include <cooperative_groups.h>
 
 #include "common.cuh"
+#include "radix.cuh"
 
 namespace cg = cooperative_groups;
 
@@ -154,89 +160,6 @@ struct PointRegs {
     }
 };
 
-// Register state of the cluster kernel: P points per thread with NO stored priority, so that
-// more points fit per CTA (a cluster of at most 10 CTAs per 131072-point cloud, the largest size
-// at which 8 clusters are resident at once on a B200). With THREADS = 256 and the CTA's first
-// point a multiple of 512, a thread's points i = base + tid + 256 j are ordered by either tie
-// rule as a fixed permutation of j: lowest index = ascending j; the reference's order (see
-// fps_priority) = even j ascending, then odd j ascending (its bit 27 is j's parity, its low bits
-// j / 2). The running max uses that rank in the key's low word; the thread's winner then gets
-// its true priority. Slots past the cloud (j >= nv) hold min_d = 0 and can only surface when
-// every valid minimum is 0 too; that case rescans the valid slots.
-template <int P, int TIE>
-struct WidePoints {
-    static_assert(P % 2 == 0, "points are held in pairs");
-    static constexpr int THREADS = 256;
-    uint64_t xp[P / 2], yp[P / 2], zp[P / 2];
-    float md[P];
-    int nv;    // slots j < nv hold points of the cloud
-    int base;  // local index of this CTA's first point
-
-    static __device__ __forceinline__ constexpr uint32_t pref(int j) {  // larger = preferred
-        return (uint32_t)(P - 1 - (TIE == GDL_TIE_LOWEST_INDEX ? j : ((j & 1) ? P / 2 + j / 2 : j / 2)));
-    }
-    static __device__ __forceinline__ int unpref(uint32_t p) {
-        const int q = P - 1 - (int)p;
-        return TIE == GDL_TIE_LOWEST_INDEX ? q : (q < P / 2 ? 2 * q : 2 * (q - P / 2) + 1);
-    }
-
-    __device__ __forceinline__ void load(const float *__restrict__ pos, int64_t start, int n, int b, int,
-                                         float4 *__restrict__ sxyz) {
-        base = b;
-        nv = 0;
-        float x[P], y[P], z[P];
-#pragma unroll
-        for (int j = 0; j < P; ++j) {
-            const int i = base + (int)threadIdx.x + j * THREADS;
-            if (i < n) {
-                const float *p = pos + 3 * (start + i);
-                x[j] = p[0];
-                y[j] = p[1];
-                z[j] = p[2];
-                md[j] = 1e30f;
-                sxyz[i - base] = make_float4(x[j], y[j], z[j], 0.0f);
-                nv = j + 1;
-            } else {
-                x[j] = y[j] = z[j] = 0.0f;
-                md[j] = 0.0f;
-            }
-        }
-#pragma unroll
-        for (int h = 0; h < P / 2; ++h) {
-            xp[h] = pack2(x[2 * h], x[2 * h + 1]);
-            yp[h] = pack2(y[2 * h], y[2 * h + 1]);
-            zp[h] = pack2(z[2 * h], z[2 * h + 1]);
-        }
-    }
-
-    __device__ __forceinline__ uint64_t step(float sx, float sy, float sz) {
-        const uint64_t SX = pack2(sx, sx), SY = pack2(sy, sy), SZ = pack2(sz, sz);
-        uint64_t acc[4] = {0ull, 0ull, 0ull, 0ull};
-#pragma unroll
-        for (int h = 0; h < P / 2; ++h) {
-            float d0, d1;
-            unpack2(dist2_x2(xp[h], yp[h], zp[h], SX, SY, SZ), d0, d1);
-            const float m0 = fminf(d0, md[2 * h]), m1 = fminf(d1, md[2 * h + 1]);
-            md[2 * h] = m0;
-            md[2 * h + 1] = m1;
-            const uint64_t k0 = ((uint64_t)__float_as_uint(m0) << 32) | pref(2 * h);
-            const uint64_t k1 = ((uint64_t)__float_as_uint(m1) << 32) | pref(2 * h + 1);
-            acc[h & 3] = umax64(acc[h & 3], umax64(k0, k1));
-        }
-        if (nv == 0) return 0ull;
-        uint64_t best = umax64(umax64(acc[0], acc[1]), umax64(acc[2], acc[3]));
-        int j = unpref((uint32_t)best);
-        if (j >= nv) {  // a padding slot won among zero minima: take the best valid slot
-            best = 0ull;
-#pragma unroll
-            for (int t = 0; t < P; ++t)
-                if (t < nv) best = umax64(best, ((uint64_t)__float_as_uint(md[t]) << 32) | pref(t));
-            j = unpref((uint32_t)best);
-        }
-        const uint32_t prio = fps_priority((uint32_t)(base + (int)threadIdx.x + j * THREADS), TIE);
-        return (best & 0xffffffff00000000ull) | (uint64_t)(~prio);
-    }
-};
 
 // ------------------------------------------------------------------ one CTA per cloud
 template <int THREADS, int P>
@@ -278,19 +201,103 @@ __global__ void __launch_bounds__(THREADS) fps_cta_kernel(const float *__restric
     }
 }
 
-// ------------------------------------------------------------------ cluster per cloud
-// Per pick, warp 0 of every CTA sends its winner record to every CTA of the cluster with
-// st.async stores into distributed shared memory, each completing 24 bytes of a transaction on
-// the receiving CTA's mbarrier; a CTA then waits on its own mbarrier only (no cluster-wide
-// barrier per pick: 1.18 vs 1.63 us per pick at 16 CTAs). Two record buffers and two mbarriers
-// alternate between picks: a CTA's record for pick k+2 can only be sent after the CTA received
-// this CTA's record for pick k+1, which is sent after this CTA finished reading pick k's.
-// Every wait is bounded; a CTA that gives up stops, and rank 0 then marks the cloud's remaining
-// picks with -2 (never observed; a broken cluster exchange would show up there, not as a hang).
-struct __align__(32) Rec {  // one CTA's best point
-    unsigned long long key;
-    float x, y, z, pad;
-};
+// ------------------------------------------------------------------ Morton order of each cloud
+// Only the grouping of points into buckets depends on this order; the picks do not (the argmax
+// key carries each point's own priority), so the quantisation below may round freely.
+constexpr int kBoxThreads = 1024;
+
+__device__ __forceinline__ uint32_t spread10(uint32_t v) {  // bits 0..9 -> bits 0, 3, ..., 27
+    v &= 0x3ffu;
+    v = (v | (v << 16)) & 0x030000ffu;
+    v = (v | (v << 8)) & 0x0300f00fu;
+    v = (v | (v << 4)) & 0x030c30c3u;
+    v = (v | (v << 2)) & 0x09249249u;
+    return v;
+}
+
+// Bounding box of each cloud: box[6b..6b+5] = (min x, y, z, max x, y, z); fminf / fmaxf skip NaN.
+__global__ void __launch_bounds__(kBoxThreads) fps_box_kernel(const float *__restrict__ pos,
+                                                              const int64_t *__restrict__ ptr,
+                                                              float *__restrict__ box) {
+    __shared__ float part[6][kBoxThreads / 32];
+    const int b = blockIdx.x;
+    const int64_t start = ptr[b], n = ptr[b + 1] - start;
+    float v[6] = {INFINITY, INFINITY, INFINITY, -INFINITY, -INFINITY, -INFINITY};
+    for (int64_t i = threadIdx.x; i < n; i += kBoxThreads) {
+        const float *p = pos + 3 * (start + i);
+#pragma unroll
+        for (int c = 0; c < 3; ++c) {
+            const float x = p[c];
+            v[c] = fminf(v[c], x);
+            v[3 + c] = fmaxf(v[3 + c], x);
+        }
+    }
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1)
+#pragma unroll
+        for (int c = 0; c < 3; ++c) {
+            v[c] = fminf(v[c], __shfl_xor_sync(0xffffffffu, v[c], o));
+            v[3 + c] = fmaxf(v[3 + c], __shfl_xor_sync(0xffffffffu, v[3 + c], o));
+        }
+    if (lane == 0)
+#pragma unroll
+        for (int c = 0; c < 6; ++c) part[c][warp] = v[c];
+    __syncthreads();
+    if (warp == 0) {
+#pragma unroll
+        for (int c = 0; c < 6; ++c) {
+            float x = part[c][lane];
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) {
+                const float y = __shfl_xor_sync(0xffffffffu, x, o);
+                x = c < 3 ? fminf(x, y) : fmaxf(x, y);
+            }
+            if (lane == 0) box[6 * b + c] = x;
+        }
+    }
+}
+
+__device__ __forceinline__ uint32_t morton_cell(float x, float lo, float scale) {
+    const float t = (x - lo) * scale;
+    if (!(t > 0.0f)) return 0u;  // below the box, NaN, or a degenerate axis
+    return t >= 1023.0f ? 1023u : (uint32_t)t;
+}
+
+// 30-bit Morton code of every point over its cloud's box (1024 cells per axis).
+__global__ void fps_morton_kernel(const float *__restrict__ pos, const int64_t *__restrict__ ptr, int B,
+                                  const float *__restrict__ box, uint32_t *__restrict__ keys) {
+    const int64_t first = ptr[0], last = ptr[B];
+    for (int64_t i = first + (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < last;
+         i += (int64_t)gridDim.x * blockDim.x) {
+        int lo = 0, hi = B - 1;  // the cloud of i: the last b with ptr[b] <= i
+        while (lo < hi) {
+            const int mid = (lo + hi + 1) >> 1;
+            if (ptr[mid] <= i) lo = mid;
+            else hi = mid - 1;
+        }
+        const float *bx = box + 6 * lo;
+        uint32_t code = 0;
+#pragma unroll
+        for (int c = 0; c < 3; ++c) {
+            const float ext = bx[3 + c] - bx[c];
+            const float scale = (ext > 0.0f && ext < INFINITY) ? 1024.0f / ext : 0.0f;
+            code |= spread10(morton_cell(pos[3 * i + c], bx[c], scale)) << c;
+        }
+        keys[i] = code;
+    }
+}
+
+// ------------------------------------------------------------------ bucketed FPS
+constexpr int kMaxCluster = 16;
+constexpr int kDefaultWaitPolls = 1 << 20;   // mbarrier polls before a wait gives up
+constexpr int kMaxDynSmem = 227 * 1024;
+constexpr int kRecBytes = 24;                // one record: key (8 B), x, y (16-B store) + z (8-B store)
+
+__host__ __device__ constexpr size_t bucket_points_bytes(int T, int P) { return (size_t)16 * T * P; }
+__host__ __device__ constexpr size_t bucket_smem_bytes(int T, int P, int cs) {
+    return bucket_points_bytes(T, P) + (size_t)2 * cs * (16 + 8);
+}
 
 __device__ __forceinline__ uint32_t smem_u32(const void *p) { return (uint32_t)__cvta_generic_to_shared(p); }
 
@@ -300,102 +307,263 @@ __device__ __forceinline__ uint32_t mapa_u32(uint32_t a, int rank) {
     return r;
 }
 
-constexpr int kClusterWaitLimit = 1 << 20;  // mbarrier polls before a CTA gives up
+__device__ __forceinline__ uint32_t mbar_try_wait(uint32_t bar, uint32_t parity) {
+    uint32_t done;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\tselp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(done)
+        : "r"(bar), "r"(parity)
+        : "memory");
+    return done;
+}
 
-template <int THREADS, int P, class PR>
-__global__ void __launch_bounds__(THREADS) fps_cluster_kernel(const float *__restrict__ pos,
-                                                              const int64_t *__restrict__ ptr,
-                                                              const int64_t *__restrict__ kpc, int tie,
-                                                              int64_t *__restrict__ out, float *__restrict__ out_pos) {
-    constexpr int kMaxCluster = 16;
-    constexpr int NW = THREADS / 32;
-    extern __shared__ float4 sxyz[];  // this CTA's THREADS * P points
-    __shared__ unsigned long long slots[2][NW];
-    __shared__ Rec recs[2][kMaxCluster];
+// One winner record into CTA `dst`'s slots: (key, x, y) in 16 bytes and (z) in 8, both completing
+// bytes of a transaction on that CTA's mbarrier.
+__device__ __forceinline__ void st_async_rec(uint32_t da, uint32_t db, uint32_t rb, uint64_t key, float x, float y,
+                                             float z) {
+    asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.v4.b32 [%0], {%1, %2, %3, %4}, [%5];" ::"r"(da),
+                 "r"((uint32_t)key), "r"((uint32_t)(key >> 32)), "r"(__float_as_uint(x)), "r"(__float_as_uint(y)),
+                 "r"(rb)
+                 : "memory");
+    asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.v2.b32 [%0], {%1, %2}, [%3];" ::"r"(db),
+                 "r"(__float_as_uint(z)), "r"(0u), "r"(rb)
+                 : "memory");
+}
+
+// Lower bound of dist2(p, s) over every p of the box [lo, hi]. Per axis the gap is the larger of
+// lo - s, s - hi and 0, each difference rounded like the point differences: a point's
+// |p - s| rounds to at least the gap's rounding (rounding is monotone), and the same fma chain
+// keeps that order, so the bound never exceeds a point's rounded distance. A NaN sample gives gaps
+// of 0 (fmaxf), and then every distance is NaN and no minimum changes anyway; an infinite box
+// side gives an infinite gap only when every point of the box is infinite on that side.
+__device__ __forceinline__ float box_dist2_lb(float sx, float sy, float sz, const float (&bx)[6]) {
+    const float gx = fmaxf(fmaxf(sub_ftz(bx[0], sx), sub_ftz(sx, bx[3])), 0.0f);
+    const float gy = fmaxf(fmaxf(sub_ftz(bx[1], sy), sub_ftz(sy, bx[4])), 0.0f);
+    const float gz = fmaxf(fmaxf(sub_ftz(bx[2], sz), sub_ftz(sz, bx[5])), 0.0f);
+    return fma_ftz(gz, gz, fma_ftz(gx, gx, mul_ftz(gy, gy)));
+}
+
+// T threads per CTA, P points per thread -- a bucket of consecutive points in Morton order, kept
+// in priority order in shared memory, with its box, its minima in registers and its best key;
+// a cluster of cs CTAs serves one cloud of at most cs * T * P points, which `order` (global
+// indices, Morton order within each cloud) lists. Warp-sized chunks of 32 threads' buckets go
+// round-robin over the cluster's CTAs, so that the buckets around one pick (neighbours in Morton
+// order) update on several SMs.
+// Per pick: each warp's winner lane writes its record into a double-buffered slot array, one
+// barrier, every warp reduces the slots itself (the CTA's winner); a lone CTA is done there, a
+// cluster's CTAs send their winner to every CTA with st.async and wait (bounded) on their own
+// mbarrier for the cluster's records.
+// status (nullable) receives GDL_ERR_TIMEOUT when a bounded wait gives up; the cloud's picks from
+// that one on are then -2 (coordinates 0). hold_rank / hold_pick: the CTA of that rank in every
+// cluster sends no record at that pick, which makes every wait of the pick run out (the failure
+// path's test); -1 disables it. A lone CTA never waits, unless hold_rank asks it to exchange.
+template <int T, int P, int TIE>
+__global__ void __launch_bounds__(T, 1) fps_bucket_kernel(const float *__restrict__ pos,
+                                                           const int32_t *__restrict__ order,
+                                                           const int64_t *__restrict__ ptr,
+                                                           const int64_t *__restrict__ kpc,
+                                                           int64_t *__restrict__ out, float *__restrict__ out_pos,
+                                                           int32_t *__restrict__ status, int wait_polls,
+                                                           int hold_rank, int64_t hold_pick) {
+    constexpr int NW = T / 32, PH = P / 2;
+    static_assert(P % 2 == 0, "points are held in pairs");
+    extern __shared__ __align__(16) unsigned char smem[];
     __shared__ __align__(8) unsigned long long mbar[2];
     __shared__ int64_t red[NW];
+    __shared__ uint4 slotA[2][NW];  // warp winners: key, x, y
+    __shared__ float slotZ[2][NW];
+    float2 *sx2 = reinterpret_cast<float2 *>(smem);  // pair h of thread t at h * T + t
+    float2 *sy2 = sx2 + PH * T;
+    float2 *sz2 = sy2 + PH * T;
+    uint2 *sn2 = reinterpret_cast<uint2 *>(sz2 + PH * T);  // ~priority, 0 for padding
+
     cg::cluster_group cluster = cg::this_cluster();
     const int cs = (int)cluster.num_blocks();
     const int rank = (int)cluster.block_rank();
+    uint4 *recA = reinterpret_cast<uint4 *>(smem + bucket_points_bytes(T, P));  // [2][cs]: key, x, y
+    uint2 *recB = reinterpret_cast<uint2 *>(recA + 2 * cs);                     // [2][cs]: z, 0
+
     const int b = blockIdx.x / cs;
     const int64_t start = ptr[b];
     const int n = (int)(ptr[b + 1] - start);
     const int64_t kb = kpc[b];
     const int64_t o0 = block_out_offset(kpc, b, red);
     const int64_t actual = (kb <= 0 || n <= 0) ? 0 : (kb < n ? kb : n);
-    if (rank == 0) pad_outputs(out, out_pos, o0, actual, kb, THREADS);
-    const int base = rank * THREADS * P;
-    PR pr;
-    pr.load(pos, start, n, base, tie, sxyz);
+    if (rank == 0) pad_outputs(out, out_pos, o0, actual, kb, T);
+    {  // the launch must give every CTA the shared memory this kernel indexes (the same for all
+       // CTAs of the cluster, so they all leave here together, before any remote access)
+        uint32_t dyn;
+        asm("mov.u32 %0, %%dynamic_smem_size;" : "=r"(dyn));
+        if ((size_t)dyn < bucket_smem_bytes(T, P, cs)) {
+            if (threadIdx.x == 0 && status) atomicExch(status, (int32_t)GDL_ERR_INVALID);
+            if (rank == 0)
+                for (int64_t j = threadIdx.x; j < actual; j += T) out[o0 + j] = -2;
+            return;
+        }
+    }
+
+    const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
+    const int q0 = ((warp * cs + rank) * 32 + lane) * P;  // this thread's first sorted position
+    float md[P];
+    float box[6] = {INFINITY, INFINITY, INFINITY, -INFINITY, -INFINITY, -INFINITY};
+    {
+        float x[P], y[P], z[P];
+        uint32_t np[P];  // ~priority; 0 marks a padding slot (key 0, never wins)
+#pragma unroll
+        for (int j = 0; j < P; ++j) {
+            const int q = q0 + j;
+            x[j] = y[j] = z[j] = 0.0f;
+            np[j] = 0u;
+            if (q < n) {
+                const int64_t v = order[start + q];
+                x[j] = pos[3 * v];
+                y[j] = pos[3 * v + 1];
+                z[j] = pos[3 * v + 2];
+                np[j] = ~fps_priority((uint32_t)(v - start), TIE);
+            }
+        }
+        // the thread's points in priority order (slot 0 preferred, padding last): a thread-local
+        // key (min-distance, P - 1 - slot) then orders them exactly as (min-distance, ~priority)
+#pragma unroll
+        for (int r = 0; r < P; ++r)
+#pragma unroll
+            for (int j = r & 1; j + 1 < P; j += 2)
+                if (np[j] < np[j + 1]) {
+                    const float tx = x[j], ty = y[j], tz = z[j];
+                    const uint32_t tn = np[j];
+                    x[j] = x[j + 1], y[j] = y[j + 1], z[j] = z[j + 1], np[j] = np[j + 1];
+                    x[j + 1] = tx, y[j + 1] = ty, z[j + 1] = tz, np[j + 1] = tn;
+                }
+#pragma unroll
+        for (int j = 0; j < P; ++j) {
+            md[j] = np[j] ? 1e30f : 0.0f;
+            if (np[j]) {
+                box[0] = fminf(box[0], x[j]);
+                box[1] = fminf(box[1], y[j]);
+                box[2] = fminf(box[2], z[j]);
+                box[3] = fmaxf(box[3], x[j]);
+                box[4] = fmaxf(box[4], y[j]);
+                box[5] = fmaxf(box[5], z[j]);
+            }
+            const int o = (j >> 1) * T + t, c = j & 1;
+            reinterpret_cast<float *>(&sx2[o])[c] = x[j];
+            reinterpret_cast<float *>(&sy2[o])[c] = y[j];
+            reinterpret_cast<float *>(&sz2[o])[c] = z[j];
+            reinterpret_cast<uint32_t *>(&sn2[o])[c] = np[j];
+        }
+    }
+    // the bucket's best thread-local key (min-distance, P - 1 - slot): its first slot (slots are
+    // in priority order, padding last) while every minimum is 1e30
+    uint64_t lkey = md[0] > 0.0f ? make_key(md[0], (uint32_t)(P - 1)) : 0ull;
+    uint64_t bestkey;  // the same point's (min-distance, ~priority) key, and its coordinates
+    float bx, by, bz;
+    auto thread_best = [&]() {
+        const int bj = P - 1 - (int)(uint32_t)lkey;
+        const int o = (bj >> 1) * T + t;
+        const float2 X = sx2[o], Y = sy2[o], Z = sz2[o];
+        const uint2 N = sn2[o];
+        bestkey = (lkey & 0xffffffff00000000ull) | (uint64_t)((bj & 1) ? N.y : N.x);
+        bx = (bj & 1) ? X.y : X.x;
+        by = (bj & 1) ? Y.y : Y.x;
+        bz = (bj & 1) ? Z.y : Z.x;
+    };
+    thread_best();
+
     float sx = 0.0f, sy = 0.0f, sz = 0.0f;
     if (actual > 0) {
         sx = pos[3 * start];
         sy = pos[3 * start + 1];
         sz = pos[3 * start + 2];
-        if (rank == 0 && threadIdx.x == 0) emit(out, out_pos, o0, start, 0, sx, sy, sz);
+        if (rank == 0 && t == 0) emit(out, out_pos, o0, start, 0, sx, sy, sz);
     }
-    if (threadIdx.x == 0) {
+    if (t == 0) {
         for (int p = 0; p < 2; ++p) asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(smem_u32(&mbar[p])));
         asm volatile("fence.mbarrier_init.release.cluster;");
     }
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    uint32_t phase[2] = {0u, 0u};
-    cluster.sync();  // every CTA resident, its barriers initialised, before any remote store
+    cluster.sync();  // every CTA resident, its points stored and its barriers initialised
+
+    const bool exchange = cs > 1 || hold_rank >= 0;  // a lone CTA's winner is the pick
+    uint32_t phase = 0u;                              // bit p: parity of the next phase of mbar[p]
     int64_t k = 1;
+    bool ok = true;
     for (; k < actual; ++k) {
-        const uint64_t wk = warp_max_key(pr.step(sx, sy, sz));
-        const int par = (int)(k & 1);
-        if (lane == 0) slots[par][warp] = wk;
-        __syncthreads();
-        if (warp == 0) {  // this CTA's winner, sent into every CTA's record slot [rank]
-            const unsigned long long key = warp_max_key(lane < NW ? slots[par][lane] : 0ull);
-            float rx = 0.0f, ry = 0.0f, rz = 0.0f;
-            if (key != 0ull) {
-                const float4 c = sxyz[fps_index(~(uint32_t)key, tie) - base];
-                rx = c.x;
-                ry = c.y;
-                rz = c.z;
+        // 1. the bucket's minima against the last pick, unless its box is too far to matter
+        const float lb = box_dist2_lb(sx, sy, sz, box);
+        if (!(lb >= __uint_as_float((uint32_t)(lkey >> 32)))) {
+            const uint64_t SX = pack2(sx, sx), SY = pack2(sy, sy), SZ = pack2(sz, sz);
+            uint64_t kk[P];  // (min-distance, P - 1 - slot), reduced as a tree: no serial chain
+#pragma unroll
+            for (int h = 0; h < PH; ++h) {
+                const float2 X = sx2[h * T + t], Y = sy2[h * T + t], Z = sz2[h * T + t];
+                float d0, d1;
+                unpack2(dist2_x2(pack2(X.x, X.y), pack2(Y.x, Y.y), pack2(Z.x, Z.y), SX, SY, SZ), d0, d1);
+                const float m0 = fminf(d0, md[2 * h]), m1 = fminf(d1, md[2 * h + 1]);
+                md[2 * h] = m0;
+                md[2 * h + 1] = m1;
+                kk[2 * h] = make_key(m0, (uint32_t)(P - 1 - 2 * h));
+                kk[2 * h + 1] = make_key(m1, (uint32_t)(P - 2 - 2 * h));
             }
-            if (lane == 0)  // this CTA expects one 24-byte record from each CTA for this pick
-                asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(&mbar[par])),
-                             "r"(cs * 24)
-                             : "memory");
-            if (lane < cs) {
-                const uint32_t dst = mapa_u32(smem_u32(&recs[par][rank]), lane);
-                const uint32_t bar = mapa_u32(smem_u32(&mbar[par]), lane);
-                asm volatile(
-                    "st.async.shared::cluster.mbarrier::complete_tx::bytes.v4.b32 [%0], {%1, %2, %3, %4}, [%5];" ::"r"(
-                        dst),
-                    "r"((uint32_t)key), "r"((uint32_t)(key >> 32)), "r"(__float_as_uint(rx)), "r"(__float_as_uint(ry)),
-                    "r"(bar)
-                    : "memory");
-                asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.v2.b32 [%0], {%1, %2}, [%3];" ::"r"(
-                                 dst + 16),
-                             "r"(__float_as_uint(rz)), "r"(0u), "r"(bar)
-                             : "memory");
-            }
+#pragma unroll
+            for (int w = 1; w < P; w <<= 1)
+#pragma unroll
+                for (int j = 0; j + w < P; j += 2 * w) kk[j] = umax64(kk[j], kk[j + w]);
+            lkey = kk[0];
+            thread_best();
         }
-        uint32_t done = 0;
-        for (int it = 0; it < kClusterWaitLimit && !done; ++it)
-            asm volatile(
-                "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\tselp.u32 %0, 1, 0, "
-                "p;\n\t}"
-                : "=r"(done)
-                : "r"(smem_u32(&mbar[par])), "r"(phase[par])
-                : "memory");
-        phase[par] ^= 1u;
-        if (!__syncthreads_and(done)) break;  // the whole CTA stops if any thread gave up
-        const unsigned long long mine = lane < cs ? recs[par][lane].key : 0ull;
-        const uint64_t best = warp_max_key(mine);
-        const int src = __ffs(__ballot_sync(0xffffffffu, lane < cs && mine == best)) - 1;
-        const Rec w = recs[par][src];
-        sx = w.x;
-        sy = w.y;
-        sz = w.z;
-        if (rank == 0 && threadIdx.x == 0) emit(out, out_pos, o0 + k, start, fps_index(~(uint32_t)best, tie), sx, sy, sz);
+        // 2. the warp's winner lane writes the warp's record (several lanes only when the whole
+        // warp holds key 0, which never wins)
+        const uint64_t wk = warp_max_key(bestkey);
+        const int par = (int)(k & 1);
+        if (bestkey == wk) {
+            slotA[par][warp] = make_uint4((uint32_t)wk, (uint32_t)(wk >> 32), __float_as_uint(bx), __float_as_uint(by));
+            slotZ[par][warp] = bz;
+        }
+        __syncthreads();
+        // 3. the CTA's winner: every warp reduces the slots itself
+        const uint2 kv = lane < NW ? *reinterpret_cast<const uint2 *>(&slotA[par][lane]) : make_uint2(0u, 0u);
+        const uint64_t key = ((uint64_t)kv.y << 32) | kv.x;
+        uint64_t gk = warp_max_key(key);
+        const int cw = __ffs(__ballot_sync(0xffffffffu, key == gk)) - 1;
+        const uint4 ca = slotA[par][cw];
+        sx = __uint_as_float(ca.z);
+        sy = __uint_as_float(ca.w);
+        sz = slotZ[par][cw];
+        if (exchange) {
+            // 4. every CTA's winner to every CTA, bounded wait for the cluster's records
+            const uint32_t bar = smem_u32(&mbar[par]);
+            if (t == 0)
+                asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(cs * kRecBytes)
+                             : "memory");
+            if (warp == 0 && lane < cs && !(rank == hold_rank && k == hold_pick))
+                st_async_rec(mapa_u32(smem_u32(&recA[par * cs + rank]), lane),
+                             mapa_u32(smem_u32(&recB[par * cs + rank]), lane), mapa_u32(bar, lane), gk, sx, sy, sz);
+            const uint32_t want = (phase >> par) & 1u;
+            uint32_t done = 0;
+            for (int it = 0; it < wait_polls && !done; ++it) done = mbar_try_wait(bar, want);
+            phase ^= 1u << par;
+            if (!__all_sync(0xffffffffu, done)) {
+                ok = false;
+                break;
+            }
+            const uint2 rk = lane < cs ? *reinterpret_cast<const uint2 *>(&recA[par * cs + lane]) : make_uint2(0u, 0u);
+            const uint64_t g = ((uint64_t)rk.y << 32) | rk.x;
+            gk = warp_max_key(g);
+            const int gi = __ffs(__ballot_sync(0xffffffffu, g == gk)) - 1;
+            const uint4 ra = recA[par * cs + gi];
+            sx = __uint_as_float(ra.z);
+            sy = __uint_as_float(ra.w);
+            sz = __uint_as_float(recB[par * cs + gi].x);
+        }
+        if (rank == 0 && t == 0) emit(out, out_pos, o0 + k, start, fps_index(~(uint32_t)gk, TIE), sx, sy, sz);
     }
-    if (k < actual && rank == 0)  // a wait gave up: mark the picks this cloud did not make
-        for (int64_t j = k + threadIdx.x; j < actual; j += THREADS) out[o0 + j] = -2;
+    if (!ok) {
+        if (lane == 0 && status) atomicExch(status, (int32_t)GDL_ERR_TIMEOUT);
+        if (rank == 0 && warp == 0)  // mark the picks this cloud did not make
+            for (int64_t j = k + lane; j < actual; j += 32) {
+                out[o0 + j] = -2;
+                if (out_pos) out_pos[3 * (o0 + j)] = out_pos[3 * (o0 + j) + 1] = out_pos[3 * (o0 + j) + 2] = 0.0f;
+            }
+    }
     cluster.sync();  // no CTA leaves while a peer may still write into it
 }
 
@@ -460,17 +628,23 @@ static cudaError_t launch_cta(int B, const float *pos, const int64_t *ptr, const
     return cudaGetLastError();
 }
 
-constexpr int kCtaCapacity = 256 * 32;         // points per single-CTA cloud (fps_cta_kernel<256, 32>)
-constexpr int kClusterThreads = 256;
-constexpr int kClusterP = 52;                   // 13312 points per CTA: 10 CTAs for 131072 points
-constexpr int64_t kClusterCapacity = (int64_t)kClusterThreads * kClusterP;
+constexpr int kCtaCapacity = 4096;            // fps_cta_kernel<256, 16>; larger clouds are bucketed
+// Bucketed launch shapes, from a sweep on a B200 (per-pick times of configuration 5's LiDAR
+// clouds and configuration 3's 8192-point level): clouds of up to 8192 points take one CTA of
+// 512 x 16, larger ones CTAs of 384 x 36 = 13824 points -- one, or a cluster (10 CTAs for 131072
+// points, a size of which 11 clusters fit on a B200 at once, so 8 LiDAR clouds run in one wave).
+// More warps lengthen every pick's exchange, more points per thread every bucket update.
+constexpr int kSmallT = 512, kSmallP = 16;
+constexpr int kBigT = 384, kBigP = 36;
+constexpr int64_t kBucketCapacity = (int64_t)kBigT * kBigP;
 
-static cudaError_t launch_cluster(int B, int cs, const float *pos, const int64_t *ptr, const int64_t *kpc, int tie,
-                                  int64_t *out, float *out_pos, cudaStream_t st) {
-    auto kern = tie == GDL_TIE_LOWEST_INDEX
-                    ? fps_cluster_kernel<kClusterThreads, kClusterP, WidePoints<kClusterP, GDL_TIE_LOWEST_INDEX>>
-                    : fps_cluster_kernel<kClusterThreads, kClusterP, WidePoints<kClusterP, GDL_TIE_REFERENCE>>;
-    const size_t smem = sizeof(float4) * kClusterCapacity;
+template <int T, int P, int TIE>
+static cudaError_t launch_bucket(int B, int cs, const float *pos, const int32_t *order, const int64_t *ptr,
+                                 const int64_t *kpc, int64_t *out, float *out_pos, int32_t *status, int polls,
+                                 int hold_rank, int64_t hold_pick, cudaStream_t st) {
+    auto kern = fps_bucket_kernel<T, P, TIE>;
+    const size_t smem = bucket_smem_bytes(T, P, cs);
+    if (cs < 1 || cs > kMaxCluster || smem > (size_t)kMaxDynSmem) return cudaErrorInvalidConfiguration;
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e;
     if (cs > 8) {
@@ -479,7 +653,7 @@ static cudaError_t launch_cluster(int B, int cs, const float *pos, const int64_t
     }
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((unsigned)(B * cs));
-    cfg.blockDim = dim3(kClusterThreads);
+    cfg.blockDim = dim3(T);
     cfg.dynamicSmemBytes = smem;
     cfg.stream = st;
     cudaLaunchAttribute attr[1];
@@ -492,46 +666,117 @@ static cudaError_t launch_cluster(int B, int cs, const float *pos, const int64_t
     int max_clusters = 0;
     e = cudaOccupancyMaxActiveClusters(&max_clusters, kern, &cfg);
     if (e != cudaSuccess || max_clusters < 1) return e != cudaSuccess ? e : cudaErrorInvalidConfiguration;
-    return cudaLaunchKernelEx(&cfg, kern, pos, ptr, kpc, tie, out, out_pos);
+    return cudaLaunchKernelEx(&cfg, kern, pos, order, ptr, kpc, out, out_pos, status, polls, hold_rank, hold_pick);
+}
+
+template <int T, int P>
+static cudaError_t launch_bucket_tie(int tie, int B, int cs, const float *pos, const int32_t *order,
+                                     const int64_t *ptr, const int64_t *kpc, int64_t *out, float *out_pos,
+                                     int32_t *status, int polls, int hold_rank, int64_t hold_pick, cudaStream_t st) {
+    return tie == GDL_TIE_LOWEST_INDEX
+               ? launch_bucket<T, P, GDL_TIE_LOWEST_INDEX>(B, cs, pos, order, ptr, kpc, out, out_pos, status,
+                                                               polls, hold_rank, hold_pick, st)
+               : launch_bucket<T, P, GDL_TIE_REFERENCE>(B, cs, pos, order, ptr, kpc, out, out_pos, status, polls,
+                                                            hold_rank, hold_pick, st);
+}
+
+// Workspace of the bucketed path: cloud boxes, Morton keys, sorted keys, the order, radix scratch.
+struct FpsWork {
+    float *box;
+    uint32_t *keys, *sorted_keys;
+    int32_t *order;
+    RadixScratch rs;
+};
+
+static size_t fps_carve(char *base, int64_t n, int32_t B, FpsWork *w) {
+    char *p = base;
+    auto take = [&](size_t bytes) {
+        char *r = p;
+        p += (bytes + 255) & ~size_t(255);
+        return r;
+    };
+    const int64_t nn = n > 0 ? n : 1;
+    char *box = take(sizeof(float) * 6 * (size_t)(B > 0 ? B : 1));
+    char *keys = take(sizeof(uint32_t) * nn);
+    char *skeys = take(sizeof(uint32_t) * nn);
+    char *ord = take(sizeof(int32_t) * nn);
+    char *rb = take(radix_scratch_bytes(nn, B > 0 ? B : 1));
+    if (base) {
+        w->box = (float *)box;
+        w->keys = (uint32_t *)keys;
+        w->sorted_keys = (uint32_t *)skeys;
+        w->order = (int32_t *)ord;
+        w->rs = radix_carve(rb, nn, B > 0 ? B : 1);
+    }
+    return (size_t)(p - base);
 }
 
 }  // namespace gdl
 
 using namespace gdl;
 
-extern "C" size_t gdl_fps_workspace_size(int64_t n_points, int64_t max_cloud_points) {
-    // the cluster variant may be refused by the device; the streaming fallback needs n floats
-    if (max_cloud_points <= kCtaCapacity) return 0;
-    return sizeof(float) * (size_t)(n_points > 0 ? n_points : 1);
+extern "C" size_t gdl_fps_workspace_size(int64_t n_points, int32_t num_clouds, int64_t max_cloud_points) {
+    if (max_cloud_points <= kCtaCapacity || n_points <= 0) return 0;
+    FpsWork w;
+    // (the streaming fallback keeps its n floats of running minima in the keys region)
+    return fps_carve(nullptr, n_points, num_clouds, &w);
 }
 
-extern "C" int gdl_fps(const float *pos, const int64_t *ptr, const int64_t *k_per_cloud, int32_t num_clouds,
-                       int64_t n_points, int64_t max_cloud_points, int32_t tie_break, int64_t *out_idx,
-                       float *out_pos, void *workspace, size_t workspace_bytes, void *stream) {
+extern "C" int gdl_fps_ex(const float *pos, const int64_t *ptr, const int64_t *k_per_cloud, int32_t num_clouds,
+                          int64_t n_points, int64_t max_cloud_points, int32_t tie_break, int64_t *out_idx,
+                          float *out_pos, void *workspace, size_t workspace_bytes, int32_t *status, int32_t wait_polls,
+                          int32_t hold_rank, int64_t hold_pick, void *stream) {
     cudaStream_t st = (cudaStream_t)stream;
     GDL_RETURN_IF(num_clouds < 0 || max_cloud_points < 0 || n_points < 0, GDL_ERR_INVALID);
     GDL_RETURN_IF(tie_break != GDL_TIE_REFERENCE && tie_break != GDL_TIE_LOWEST_INDEX, GDL_ERR_INVALID);
     if (num_clouds == 0) return GDL_OK;
     GDL_RETURN_IF(!ptr || !k_per_cloud || !out_idx || (n_points > 0 && !pos), GDL_ERR_INVALID);
-    GDL_RETURN_IF(max_cloud_points >= INT32_MAX, GDL_ERR_OVERFLOW);
+    GDL_RETURN_IF(max_cloud_points >= INT32_MAX || n_points >= INT32_MAX, GDL_ERR_OVERFLOW);
     const int64_t m = max_cloud_points;
+    const int polls = wait_polls > 0 ? wait_polls : kDefaultWaitPolls;
     cudaError_t e;
     if (m <= 512) e = launch_cta<128, 4>(num_clouds, pos, ptr, k_per_cloud, tie_break, out_idx, out_pos, st);
     else if (m <= 1024) e = launch_cta<256, 4>(num_clouds, pos, ptr, k_per_cloud, tie_break, out_idx, out_pos, st);
     else if (m <= 2048) e = launch_cta<256, 8>(num_clouds, pos, ptr, k_per_cloud, tie_break, out_idx, out_pos, st);
-    else if (m <= 4096) e = launch_cta<256, 16>(num_clouds, pos, ptr, k_per_cloud, tie_break, out_idx, out_pos, st);
-    else if (m <= kCtaCapacity) e = launch_cta<256, 32>(num_clouds, pos, ptr, k_per_cloud, tie_break, out_idx, out_pos, st);
+    else if (m <= kCtaCapacity) e = launch_cta<256, 16>(num_clouds, pos, ptr, k_per_cloud, tie_break, out_idx, out_pos, st);
     else {
-        const int cs = (int)((m + kClusterCapacity - 1) / kClusterCapacity);
+        GDL_RETURN_IF(!workspace || workspace_bytes < gdl_fps_workspace_size(n_points, num_clouds, m),
+                      GDL_ERR_WORKSPACE);
+        FpsWork w;
+        fps_carve((char *)workspace, n_points, num_clouds, &w);
+        const int cs = (int)((m + kBucketCapacity - 1) / kBucketCapacity);
         e = cudaErrorInvalidConfiguration;
-        if (cs <= 16) e = launch_cluster(num_clouds, cs, pos, ptr, k_per_cloud, tie_break, out_idx, out_pos, st);
+        if (cs <= kMaxCluster) {
+            // Morton order of every cloud (the buckets), then the bucketed kernel
+            fps_box_kernel<<<num_clouds, kBoxThreads, 0, st>>>(pos, ptr, w.box);
+            const int64_t blocks = (n_points + 255) / 256;
+            fps_morton_kernel<<<(unsigned)(blocks < 4 * kSmCount ? (blocks > 0 ? blocks : 1) : 4 * kSmCount), 256, 0,
+                                st>>>(pos, ptr, num_clouds, w.box, w.keys);
+            GDL_CUDA_TRY(cudaGetLastError());
+            GDL_CUDA_TRY(radix_sort_pairs(w.keys, nullptr, w.sorted_keys, w.order, n_points, ptr, num_clouds, 4,
+                                          nullptr, w.rs, st));
+            if (m <= (int64_t)kSmallT * kSmallP)
+                e = launch_bucket_tie<kSmallT, kSmallP>(tie_break, num_clouds, 1, pos, w.order, ptr,
+                                                                  k_per_cloud, out_idx, out_pos, status, polls,
+                                                                  hold_rank, hold_pick, st);
+            else
+                e = launch_bucket_tie<kBigT, kBigP>(tie_break, num_clouds, cs, pos, w.order, ptr, k_per_cloud,
+                                                            out_idx, out_pos, status, polls, hold_rank, hold_pick,
+                                                            st);
+        }
         if (e != cudaSuccess) {
             (void)cudaGetLastError();  // clear a refused cluster launch, use the streaming kernel
-            GDL_RETURN_IF(!workspace || workspace_bytes < sizeof(float) * (size_t)n_points, GDL_ERR_WORKSPACE);
             fps_stream_kernel<<<num_clouds, kStreamThreads, 0, st>>>(pos, ptr, k_per_cloud, tie_break,
-                                                                     (float *)workspace, out_idx, out_pos);
+                                                                     (float *)w.keys, out_idx, out_pos);
             e = cudaGetLastError();
         }
     }
     return e == cudaSuccess ? GDL_OK : GDL_ERR_CUDA;
+}
+
+extern "C" int gdl_fps(const float *pos, const int64_t *ptr, const int64_t *k_per_cloud, int32_t num_clouds,
+                       int64_t n_points, int64_t max_cloud_points, int32_t tie_break, int64_t *out_idx,
+                       float *out_pos, void *workspace, size_t workspace_bytes, void *stream) {
+    return gdl_fps_ex(pos, ptr, k_per_cloud, num_clouds, n_points, max_cloud_points, tie_break, out_idx, out_pos,
+                      workspace, workspace_bytes, nullptr, 0, -1, -1, stream);
 }

@@ -13,9 +13,9 @@
  *  - Scratch memory is caller-provided (`workspace`, `workspace_bytes`); each operator
  *    that needs it has a *_workspace_size() query evaluated on the host. A workspace
  *    must be 256-byte aligned and may be reused once the stream has moved past the call.
- *  - Return value: a gdl_status for argument and launch errors. The kernels contain no
- *    spin-waits; launches are asynchronous, so execution faults surface at the caller's
- *    next synchronisation like any CUDA error.
+ *  - Return value: a gdl_status for argument and launch errors. Launches are asynchronous,
+ *    so execution faults surface at the caller's next synchronisation like any CUDA error.
+ *    The only device-side waits (FPS's exchange between warps and CTAs) are bounded.
  *  - Clouds are packed CSR-style: cloud b owns points [ptr[b], ptr[b+1]); ptr is int64.
  */
 #ifndef GDL_B200_H
@@ -51,6 +51,14 @@ const char *gdl_status_string(int status);
 /* GDL_OK if `device` is an sm_100 GPU this library was built for. */
 int gdl_check_device(int device);
 
+/* FP32 FMA throughput probe (no counterpart in the reference): `blocks` CTAs of 256 threads each
+ * run `iters` rounds of 8 independent FMAs (scalar fma.rn.f32, or packed fma.rn.f32x2 when
+ * `packed`), so that a benchmark can state FP32 fractions (KNN's distance scan) against a number
+ * measured on this device. out [blocks * 256] f32 is written only to keep the work live.
+ * gdl_fp32_peak_flops: the floating-point operations one such launch performs (2 per FMA lane). */
+int64_t gdl_fp32_peak_flops(int64_t iters, int32_t packed, int32_t blocks);
+int gdl_fp32_peak(float *out, int64_t iters, int32_t packed, int32_t blocks, void *stream);
+
 /* ------------------------------------------------------------------------------ FPS
  * Replaces fps_cuda(pos, ptr, k_per_batch) -- geoembodied/csrc/fps_kernel.cu:160-209,
  * Python dispatch geoembodied/csrc/__init__.py:566-597.
@@ -61,20 +69,38 @@ int gdl_check_device(int device);
  * out_idx      [sum(max(k_b, 0))] i64: cloud b's picks start at sum_{c<b} max(k_c, 0);
  *              min(k_b, n_b) global indices in selection order, then -1 padding.
  * n_points     rows of pos.
- * max_cloud_points  host-side upper bound of max_b n_b (selects the kernel variant: one CTA
- *              per cloud up to 8192 points, a thread-block cluster of up to 16 CTAs of 13312
- *              points up to 212992, else a streaming CTA that keeps the running minima in the
- *              workspace).
+ * max_cloud_points  host-side upper bound of max_b n_b. It selects the kernel variant: one CTA
+ *              per cloud with the points in registers up to 4096 points; above that the clouds
+ *              are put in Morton order (in the workspace) and run bucketed, one CTA of up to 8192
+ *              or 13824 points or a thread-block cluster of up to 16 CTAs of 13824 points (up to
+ *              221184); beyond that, or if the device refuses the cluster, a streaming CTA that
+ *              keeps the running minima in the workspace.
  * tie_break    GDL_TIE_REFERENCE: the reference kernel's argmax reduction order
  *              (bit-identical to fps_kernel<512>); GDL_TIE_LOWEST_INDEX: torch.argmax.
  * out_pos      [same slots, 3] f32 (nullable): coordinates of each pick (0 for padding), which
  *              saves the caller a gather of pos[out_idx].
  * Seed is the first point of each cloud; distances use the reference's rounding.
+ * The bucketed kernel's CTAs (a cluster's, or one CTA's warps) exchange each pick's winners
+ * through shared-memory barriers with a bounded wait; a wait that gives up (never observed)
+ * writes -2 into the cloud's remaining picks (coordinates 0) -- gdl_fps_ex also reports it.
  */
-size_t gdl_fps_workspace_size(int64_t n_points, int64_t max_cloud_points);
+size_t gdl_fps_workspace_size(int64_t n_points, int32_t num_clouds, int64_t max_cloud_points);
 int gdl_fps(const float *pos, const int64_t *ptr, const int64_t *k_per_cloud, int32_t num_clouds, int64_t n_points,
             int64_t max_cloud_points, int32_t tie_break, int64_t *out_idx, float *out_pos, void *workspace,
             size_t workspace_bytes, void *stream);
+
+/* gdl_fps with the bounded waits exposed (same reference interface as gdl_fps).
+ * status      [1] i32 device (nullable): set to GDL_ERR_TIMEOUT when a wait of the bucketed
+ *             kernel gave up (the caller zeroes it; read it after the stream has run the call).
+ * wait_polls  mbarrier polls before a wait gives up (<= 0: 2^20).
+ * hold_rank, hold_pick  failure injection for tests (-1: off): in every cluster the CTA of this
+ *             rank sends no records at this pick, so every wait of that pick runs out and
+ *             the call takes its failure path (status, -2 picks) without faulting anything.
+ */
+int gdl_fps_ex(const float *pos, const int64_t *ptr, const int64_t *k_per_cloud, int32_t num_clouds,
+               int64_t n_points, int64_t max_cloud_points, int32_t tie_break, int64_t *out_idx, float *out_pos,
+               void *workspace, size_t workspace_bytes, int32_t *status, int32_t wait_polls, int32_t hold_rank,
+               int64_t hold_pick, void *stream);
 
 /* ------------------------------------------------------------------------------ KNN
  * Replaces knn_cuda(query, source, ptr_q, ptr_s, k) and knn_self_cuda(points, ptr, k)

@@ -1,0 +1,66 @@
+"""The bucketed FPS kernel's bounded waits, through the C ABI (gdl_fps_ex).
+
+The warps and CTAs of a cloud exchange every pick's winners through shared-memory barriers.
+These tests make one CTA withhold its records at one pick (the ABI's failure injection), so
+that every wait of that pick runs out after a short poll limit; nothing faults or hangs. The
+call must then report GDL_ERR_TIMEOUT in its status word, keep the picks made before the
+failure (checked against the CPU restatement), write -2 with zero coordinates into the rest,
+and leave the context usable: the next plain call is exact again.
+"""
+
+import ctypes
+
+import numpy as np
+import pytest
+import torch
+
+from gdl_b200 import _native as nat
+from gdl_b200 import synthetic
+
+pytestmark = [pytest.mark.gpu,
+              pytest.mark.skipif(not torch.cuda.is_available(), reason="needs a CUDA device")]
+DEV = "cuda"
+GDL_ERR_TIMEOUT = 6
+
+
+def _call(x, ptr, k, *, hold_rank=-1, hold_pick=-1, polls=0):
+    L = nat.load()
+    dev = torch.device(DEV)
+    B = ptr.numel() - 1
+    n = x.shape[0]
+    m = int((ptr[1:] - ptr[:-1]).max())
+    xd, pd, kd = x.to(dev), ptr.to(dev), k.to(dev)
+    total = int(k.clamp(min=0).sum())
+    out = torch.full((total,), -7, dtype=torch.int64, device=dev)
+    opos = torch.full((total, 3), 7.0, dtype=torch.float32, device=dev)
+    status = torch.zeros(1, dtype=torch.int32, device=dev)
+    ws = nat.workspace(L.gdl_fps_workspace_size(n, B, m), dev)
+    rc = L.gdl_fps_ex(xd.data_ptr(), pd.data_ptr(), kd.data_ptr(), B, n, m, 0, out.data_ptr(), opos.data_ptr(),
+                      ws.data_ptr(), ws.numel(), status.data_ptr(), polls, hold_rank, hold_pick,
+                      torch.cuda.current_stream(dev).cuda_stream)
+    torch.cuda.synchronize(dev)
+    return rc, int(status.item()), out.cpu().numpy(), opos.cpu().numpy()
+
+
+@pytest.mark.parametrize("sizes,hold_rank", [([30000], 1), ([6000, 7000], 0), ([131072], 9)])
+def test_fps_withheld_records_time_out_and_report(oracle, sizes, hold_rank):
+    rng = np.random.default_rng(sum(sizes))
+    x = (rng.random((sum(sizes), 3), dtype=np.float32) * 2 - 1).astype(np.float32)
+    ptr = synthetic.ptr_of(sizes)
+    k = np.minimum(np.diff(ptr), 64)
+    hold = 5
+    want = oracle.fps(x, ptr, k, tie=oracle.TIE_REFERENCE, dist=oracle.DIST_CUDA)
+    xt, pt, kt = torch.from_numpy(x), torch.from_numpy(ptr), torch.from_numpy(k)
+
+    rc, status, out, opos = _call(xt, pt, kt, hold_rank=hold_rank, hold_pick=hold, polls=2000)
+    assert rc == 0 and status == GDL_ERR_TIMEOUT
+    offs = np.concatenate([[0], np.cumsum(k)])
+    for b in range(len(sizes)):
+        got = out[offs[b]:offs[b + 1]]
+        assert np.array_equal(got[:hold], want[offs[b]:offs[b] + hold])  # picks before the failure
+        assert np.all(got[hold:] == -2)
+        assert np.all(opos[offs[b] + hold:offs[b + 1]] == 0.0)
+
+    rc, status, out, _ = _call(xt, pt, kt)  # the context is still usable and exact
+    assert rc == 0 and status == 0
+    assert np.array_equal(out, want)

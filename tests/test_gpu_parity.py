@@ -34,8 +34,8 @@ def _rand_clouds(seed, sizes, kind="uniform"):
 # ----------------------------------------------------------------------------- FPS
 @pytest.mark.parametrize("tie", ["reference", "lowest_index"])
 @pytest.mark.parametrize("sizes,k", [([2048] * 4, 512), ([1, 2, 3, 600, 0, 1025], 300), ([4097, 8192], 1000),
-                                     ([20000], 300), ([9000, 30000, 13312, 13313], 200), ([140000], 64),
-                                     ([220000], 48)])
+                                     ([20000], 300), ([9000, 30000, 13824, 13825], 200), ([140000], 64),
+                                     ([222000], 48)])
 @pytest.mark.parametrize("kind", ["uniform", "lattice"])
 def test_fps_matches_oracle(oracle, tie, sizes, k, kind):
     x, ptr = _rand_clouds(sum(sizes) + k, sizes, kind)

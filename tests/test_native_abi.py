@@ -40,8 +40,10 @@ def test_host_only_queries(lib):
     assert lib.gdl_version() >= 100
     assert lib.gdl_status_string(0) == b"ok"
     assert lib.gdl_status_string(2) == b"workspace too small"
-    assert lib.gdl_fps_workspace_size(1000, 8192) == 0  # registers/shared memory only
-    assert lib.gdl_fps_workspace_size(10**6, 10**6) >= 4 * 10**6
+    assert lib.gdl_fps_workspace_size(1000, 1, 4096) == 0  # registers/shared memory only
+    # bucketed clouds: Morton keys, sorted keys and the order (12 B per point) plus radix scratch
+    assert lib.gdl_fps_workspace_size(8 * 131072, 8, 131072) >= 12 * 8 * 131072
+    assert lib.gdl_fps_workspace_size(10**6, 1, 10**6) >= 4 * 10**6
     w1 = lib.gdl_knn_workspace_size(2048, 4, 16, 8192)
     w2 = lib.gdl_knn_workspace_size(10**6, 64, 1, 16384)
     assert w1 > 0 and w2 > 0
@@ -53,6 +55,7 @@ def test_host_only_queries(lib):
 def test_argument_validation_without_gpu(lib):
     # invalid arguments are rejected before any CUDA call
     assert lib.gdl_fps(None, None, None, 1, 10, 10, 7, None, None, None, 0, None) == 1
+    assert lib.gdl_fps_ex(None, None, None, 1, 10, 10, 7, None, None, None, 0, None, 0, -1, -1, None) == 1
     assert lib.gdl_segment_reduce(None, 5, 1, 1, None, None, None, 1, 0, None, None, None, 0, None) == 1
     assert lib.gdl_knn(None, None, None, None, 1, 10, 4, 10, None, None, None, 0, None) == 1
     bad = nat.EdgeGeometry(None, None, None, 1, 3)  # harmonics of degree 3 are not provided
