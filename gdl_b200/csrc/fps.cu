@@ -31,6 +31,7 @@
 #include <cooperative_groups.h>
 
 #include "common.cuh"
+#include "morton.cuh"
 #include "radix.cuh"
 
 namespace cg = cooperative_groups;
@@ -198,93 +199,6 @@ __global__ void __launch_bounds__(THREADS) fps_cta_kernel(const float *__restric
         const uint32_t idx = fps_index(~(uint32_t)best, tie);
         s = sxyz[idx];
         if (threadIdx.x == 0) emit(out, out_pos, o0 + k, start, idx, s.x, s.y, s.z);
-    }
-}
-
-// ------------------------------------------------------------------ Morton order of each cloud
-// Only the grouping of points into buckets depends on this order; the picks do not (the argmax
-// key carries each point's own priority), so the quantisation below may round freely.
-constexpr int kBoxThreads = 1024;
-
-__device__ __forceinline__ uint32_t spread10(uint32_t v) {  // bits 0..9 -> bits 0, 3, ..., 27
-    v &= 0x3ffu;
-    v = (v | (v << 16)) & 0x030000ffu;
-    v = (v | (v << 8)) & 0x0300f00fu;
-    v = (v | (v << 4)) & 0x030c30c3u;
-    v = (v | (v << 2)) & 0x09249249u;
-    return v;
-}
-
-// Bounding box of each cloud: box[6b..6b+5] = (min x, y, z, max x, y, z); fminf / fmaxf skip NaN.
-__global__ void __launch_bounds__(kBoxThreads) fps_box_kernel(const float *__restrict__ pos,
-                                                              const int64_t *__restrict__ ptr,
-                                                              float *__restrict__ box) {
-    __shared__ float part[6][kBoxThreads / 32];
-    const int b = blockIdx.x;
-    const int64_t start = ptr[b], n = ptr[b + 1] - start;
-    float v[6] = {INFINITY, INFINITY, INFINITY, -INFINITY, -INFINITY, -INFINITY};
-    for (int64_t i = threadIdx.x; i < n; i += kBoxThreads) {
-        const float *p = pos + 3 * (start + i);
-#pragma unroll
-        for (int c = 0; c < 3; ++c) {
-            const float x = p[c];
-            v[c] = fminf(v[c], x);
-            v[3 + c] = fmaxf(v[3 + c], x);
-        }
-    }
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1)
-#pragma unroll
-        for (int c = 0; c < 3; ++c) {
-            v[c] = fminf(v[c], __shfl_xor_sync(0xffffffffu, v[c], o));
-            v[3 + c] = fmaxf(v[3 + c], __shfl_xor_sync(0xffffffffu, v[3 + c], o));
-        }
-    if (lane == 0)
-#pragma unroll
-        for (int c = 0; c < 6; ++c) part[c][warp] = v[c];
-    __syncthreads();
-    if (warp == 0) {
-#pragma unroll
-        for (int c = 0; c < 6; ++c) {
-            float x = part[c][lane];
-#pragma unroll
-            for (int o = 16; o > 0; o >>= 1) {
-                const float y = __shfl_xor_sync(0xffffffffu, x, o);
-                x = c < 3 ? fminf(x, y) : fmaxf(x, y);
-            }
-            if (lane == 0) box[6 * b + c] = x;
-        }
-    }
-}
-
-__device__ __forceinline__ uint32_t morton_cell(float x, float lo, float scale) {
-    const float t = (x - lo) * scale;
-    if (!(t > 0.0f)) return 0u;  // below the box, NaN, or a degenerate axis
-    return t >= 1023.0f ? 1023u : (uint32_t)t;
-}
-
-// 30-bit Morton code of every point over its cloud's box (1024 cells per axis).
-__global__ void fps_morton_kernel(const float *__restrict__ pos, const int64_t *__restrict__ ptr, int B,
-                                  const float *__restrict__ box, uint32_t *__restrict__ keys) {
-    const int64_t first = ptr[0], last = ptr[B];
-    for (int64_t i = first + (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < last;
-         i += (int64_t)gridDim.x * blockDim.x) {
-        int lo = 0, hi = B - 1;  // the cloud of i: the last b with ptr[b] <= i
-        while (lo < hi) {
-            const int mid = (lo + hi + 1) >> 1;
-            if (ptr[mid] <= i) lo = mid;
-            else hi = mid - 1;
-        }
-        const float *bx = box + 6 * lo;
-        uint32_t code = 0;
-#pragma unroll
-        for (int c = 0; c < 3; ++c) {
-            const float ext = bx[3 + c] - bx[c];
-            const float scale = (ext > 0.0f && ext < INFINITY) ? 1024.0f / ext : 0.0f;
-            code |= spread10(morton_cell(pos[3 * i + c], bx[c], scale)) << c;
-        }
-        keys[i] = code;
     }
 }
 
@@ -748,10 +662,10 @@ extern "C" int gdl_fps_ex(const float *pos, const int64_t *ptr, const int64_t *k
         e = cudaErrorInvalidConfiguration;
         if (cs <= kMaxCluster) {
             // Morton order of every cloud (the buckets), then the bucketed kernel
-            fps_box_kernel<<<num_clouds, kBoxThreads, 0, st>>>(pos, ptr, w.box);
+            cloud_box_kernel<<<num_clouds, kBoxThreads, 0, st>>>(pos, ptr, w.box, nullptr);
             const int64_t blocks = (n_points + 255) / 256;
-            fps_morton_kernel<<<(unsigned)(blocks < 4 * kSmCount ? (blocks > 0 ? blocks : 1) : 4 * kSmCount), 256, 0,
-                                st>>>(pos, ptr, num_clouds, w.box, w.keys);
+            morton_code_kernel<<<(unsigned)(blocks < 4 * kSmCount ? (blocks > 0 ? blocks : 1) : 4 * kSmCount), 256, 0,
+                                 st>>>(pos, ptr, num_clouds, w.box, w.keys, false, n_points);
             GDL_CUDA_TRY(cudaGetLastError());
             GDL_CUDA_TRY(radix_sort_pairs(w.keys, nullptr, w.sorted_keys, w.order, n_points, ptr, num_clouds, 4,
                                           nullptr, w.rs, st));

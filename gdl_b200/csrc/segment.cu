@@ -945,6 +945,8 @@ constexpr int kNoAllocMaxDevices = 64;
 static __device__ __align__(256) int32_t g_seg_noalloc_scratch[kNoAllocSlots];
 
 // device address of g_seg_noalloc_scratch, looked up once per device with that device current
+// and kept for the process's life (a cudaDeviceReset() ends the context that owns the array;
+// the header forbids calls after one)
 static int32_t *g_noalloc_ptr[kNoAllocMaxDevices];
 static std::mutex g_noalloc_mutex;
 

@@ -193,6 +193,19 @@ size_t wg_bytes(const WgPlan &p, int M, int N) {
 
 using namespace gdl;
 
+namespace gdl {
+// column sums of A alone (a layer without output columns still has a bias gradient): one
+// thread per column, rows in order, double accumulator (deterministic)
+static __global__ void wg_colsum_kernel(const float *__restrict__ A, int64_t lda, int64_t rows, int32_t M,
+                                        float *__restrict__ col_sum) {
+    const int m = blockIdx.x * blockDim.x + threadIdx.x;
+    if (m >= M) return;
+    double s = 0.0;
+    for (int64_t r = 0; r < rows; ++r) s += (double)A[r * lda + m];
+    col_sum[m] = (float)s;
+}
+}  // namespace gdl
+
 extern "C" size_t gdl_weight_grad_workspace_size(int64_t rows, int32_t M, int32_t N, int32_t sub) {
     if (rows <= 0 || M <= 0 || N <= 0 || (sub != 1 && sub != 3 && sub != 5)) return 256;
     return wg_bytes(wg_plan(rows, M, N), M, N);
@@ -204,7 +217,19 @@ extern "C" int gdl_weight_grad(const float *A, int64_t lda, const float *B, int6
     cudaStream_t st = (cudaStream_t)stream;
     GDL_RETURN_IF(rows < 0 || M < 0 || N < 0 || (sub != 1 && sub != 3 && sub != 5), GDL_ERR_INVALID);
     GDL_RETURN_IF(col_sum && sub != 1, GDL_ERR_INVALID);
-    if (M == 0 || N == 0) return GDL_OK;
+    if (M == 0) return GDL_OK;
+    if (N == 0) {  // no C entries; the column sums of A (a bias gradient) do not depend on N
+        if (col_sum) {
+            if (rows == 0) {
+                GDL_CUDA_TRY(cudaMemsetAsync(col_sum, 0, (size_t)M * sizeof(float), st));
+            } else {
+                GDL_RETURN_IF(!A || lda < (int64_t)M, GDL_ERR_INVALID);
+                wg_colsum_kernel<<<(unsigned)((M + 127) / 128), 128, 0, st>>>(A, lda, rows, M, col_sum);
+                GDL_CUDA_TRY(cudaGetLastError());
+            }
+        }
+        return GDL_OK;
+    }
     GDL_RETURN_IF(!C, GDL_ERR_INVALID);
     if (rows == 0) {
         GDL_CUDA_TRY(cudaMemsetAsync(C, 0, (size_t)M * N * sizeof(float), st));

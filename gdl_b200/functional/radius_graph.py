@@ -12,14 +12,13 @@ from .. import _native as nat
 from .. import csrc
 
 
-def _ptr_from_batch(batch: Tensor, B: Optional[int]):
-    """CSR offsets of a sorted batch vector, on the host (one device->host copy)."""
-    batch = batch.to(torch.int64)
-    nb = int(B) if B is not None else (int(batch.max().item()) + 1 if batch.numel() else 0)
-    counts = torch.bincount(batch, minlength=nb).cpu()
-    ptr = torch.zeros(nb + 1, dtype=torch.int64)
-    ptr[1:] = counts.cumsum(0)
-    return ptr
+def _ptr_from_batch(batch_sorted: Tensor, B: Optional[int]) -> Tensor:
+    """CSR offsets of a sorted batch vector, built on the device (searchsorted); only when the
+    cloud count B is not given is it read from the device (one synchronisation)."""
+    if B is None:
+        B = int(batch_sorted[-1].item()) + 1 if batch_sorted.numel() else 0
+    marks = torch.arange(int(B) + 1, dtype=torch.int64, device=batch_sorted.device)
+    return torch.searchsorted(batch_sorted, marks)
 
 
 def radius_graph_csr(x: Tensor, r: float, ptr: Tensor, *, max_num_neighbors: int = 32, loop: bool = False,
@@ -42,12 +41,14 @@ def radius_graph(x: Tensor, r: float, *, max_num_neighbors: int = 32, batch: Opt
     """
     N = x.shape[0]
     if batch is not None:
+        # clouds in any order: a stable sort by cloud on the device (no host read), offsets by
+        # searchsorted; the only synchronisations are the edge count below (the output's size)
+        # and, without num_batch_elements, the cloud count
         batch = batch.to(torch.int64)
-        sorted_ok = N < 2 or bool((batch[1:] >= batch[:-1]).all())
-        order = None if sorted_ok else torch.argsort(batch, stable=True)
-        xb = x if order is None else x[order]
-        mb = mask if (mask is None or order is None) else mask[order]
-        ptr = _ptr_from_batch(batch if order is None else batch[order], num_batch_elements)
+        order = torch.argsort(batch, stable=True)
+        xb = x[order]
+        mb = mask if mask is None else mask[order]
+        ptr = _ptr_from_batch(batch[order], num_batch_elements)
     else:
         order, xb, mb = None, x, mask
         B = num_batch_elements if num_batch_elements is not None else 1

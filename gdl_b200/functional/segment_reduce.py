@@ -2,9 +2,10 @@
 (reference: geoembodied/functional/segment_reduce.py:41-313).
 
 ``segment_reduce`` keeps the reference signature and adds ``reduce`` ("sum" default, "mean",
-"max"). Each variant is a ``torch.library.custom_op`` (namespace ``gdl_b200``) with a fake
-implementation and a registered autograd formula, so ``torch.compile`` traces through it
-without graph breaks, as in the reference (:206-279). Forward and backward are the
+"max"). Each variant is a ``torch.library.custom_op`` (namespace ``gdl_b200``, and also the
+reference's ``geoembodied`` namespace when that is free) with a fake implementation and a
+registered autograd formula, so ``torch.compile`` traces through it without graph breaks, as in
+the reference (:206-279). Forward and backward are the
 sm_100a kernels; nothing uses atomics on values, so results are bit-reproducible.
 """
 
@@ -29,41 +30,41 @@ def _fake_out(msg: Tensor, N: int) -> Tensor:
     return msg.new_empty(N, C, dtype=torch.float32)
 
 
-# ----------------------------------------------------------------------------- sum
-@torch.library.custom_op("gdl_b200::segment_reduce_sum", mutates_args=())
-def _seg_sum(msg: Tensor, col_sorted: Tensor, perm: Optional[Tensor], node_start: Tensor, node_end: Tensor,
-             N: int) -> Tensor:
-    return csrc.segment_reduce_cuda(msg, perm, node_start, node_end, N, "sum")
+def _define_ops(ns: str, perm_optional: bool):
+    """The three reductions as torch.library custom ops in namespace `ns`, each with a fake
+    implementation and a registered autograd formula (reference: segment_reduce.py:206-279)."""
+    perm_t = "Tensor?" if perm_optional else "Tensor"
+    args = f"(Tensor msg, Tensor col_sorted, {perm_t} perm, Tensor node_start, Tensor node_end, SymInt N)"
 
+    @torch.library.custom_op(f"{ns}::segment_reduce_sum", mutates_args=(), schema=f"{args} -> Tensor")
+    def seg_sum(msg, col_sorted, perm, node_start, node_end, N):
+        return csrc.segment_reduce_cuda(msg, perm, node_start, node_end, N, "sum")
 
-@_seg_sum.register_fake
-def _(msg, col_sorted, perm, node_start, node_end, N):
-    return _fake_out(msg, N)
+    @seg_sum.register_fake
+    def _(msg, col_sorted, perm, node_start, node_end, N):
+        return _fake_out(msg, N)
 
+    @torch.library.custom_op(f"{ns}::segment_reduce_mean", mutates_args=(), schema=f"{args} -> Tensor")
+    def seg_mean(msg, col_sorted, perm, node_start, node_end, N):
+        return csrc.segment_reduce_cuda(msg, perm, node_start, node_end, N, "mean")
 
-# ----------------------------------------------------------------------------- mean
-@torch.library.custom_op("gdl_b200::segment_reduce_mean", mutates_args=())
-def _seg_mean(msg: Tensor, col_sorted: Tensor, perm: Optional[Tensor], node_start: Tensor, node_end: Tensor,
-              N: int) -> Tensor:
-    return csrc.segment_reduce_cuda(msg, perm, node_start, node_end, N, "mean")
+    @seg_mean.register_fake
+    def _(msg, col_sorted, perm, node_start, node_end, N):
+        return _fake_out(msg, N)
 
+    @torch.library.custom_op(f"{ns}::segment_reduce_max", mutates_args=(), schema=f"{args} -> (Tensor, Tensor)")
+    def seg_max(msg, col_sorted, perm, node_start, node_end, N):
+        return csrc.segment_reduce_cuda(msg, perm, node_start, node_end, N, "max", with_arg=True)
 
-@_seg_mean.register_fake
-def _(msg, col_sorted, perm, node_start, node_end, N):
-    return _fake_out(msg, N)
+    @seg_max.register_fake
+    def _(msg, col_sorted, perm, node_start, node_end, N):
+        out = _fake_out(msg, N)
+        return out, out.new_empty(out.shape, dtype=torch.int32)
 
-
-# ----------------------------------------------------------------------------- max
-@torch.library.custom_op("gdl_b200::segment_reduce_max", mutates_args=())
-def _seg_max(msg: Tensor, col_sorted: Tensor, perm: Optional[Tensor], node_start: Tensor, node_end: Tensor,
-             N: int) -> Tuple[Tensor, Tensor]:
-    return csrc.segment_reduce_cuda(msg, perm, node_start, node_end, N, "max", with_arg=True)
-
-
-@_seg_max.register_fake
-def _(msg, col_sorted, perm, node_start, node_end, N):
-    out = _fake_out(msg, N)
-    return out, out.new_empty(out.shape, dtype=torch.int32)
+    seg_sum.register_autograd(_backward_for("sum"), setup_context=_setup)
+    seg_mean.register_autograd(_backward_for("mean"), setup_context=_setup)
+    seg_max.register_autograd(_backward_for("max"), setup_context=_setup)
+    return seg_sum, seg_mean, seg_max
 
 
 # ----------------------------------------------------------------------------- autograd
@@ -85,9 +86,25 @@ def _backward_for(reduce: str):
     return backward
 
 
-_seg_sum.register_autograd(_backward_for("sum"), setup_context=_setup)
-_seg_mean.register_autograd(_backward_for("mean"), setup_context=_setup)
-_seg_max.register_autograd(_backward_for("max"), setup_context=_setup)
+_seg_sum, _seg_mean, _seg_max = _define_ops("gdl_b200", perm_optional=True)
+
+
+def _op_exists(ns: str, name: str) -> bool:
+    try:
+        return hasattr(getattr(torch.ops, ns), name)
+    except Exception:
+        return False
+
+
+# The reference's own op name, torch.ops.geoembodied.segment_reduce_sum (segment_reduce.py:223,
+# called at :311), with its schema (perm a Tensor), so that code and saved graphs that name it
+# resolve to these kernels; plus geoembodied::segment_reduce_{mean,max}. Skipped when the
+# namespace already holds the ops (the reference package was imported first: its own
+# registration then stands, and callers reach these kernels through the geoembodied.csrc
+# redirect instead).
+GEOEMBODIED_OPS = None
+if not _op_exists("geoembodied", "segment_reduce_sum"):
+    GEOEMBODIED_OPS = _define_ops("geoembodied", perm_optional=False)
 
 
 def segment_reduce(msg: Tensor, col_sorted: Tensor, perm: Optional[Tensor], node_start: Tensor, node_end: Tensor,

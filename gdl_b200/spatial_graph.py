@@ -47,8 +47,8 @@ class SpatialGraph:
         """Radius graph + geometry + CSR + average degree (spatial_graph.py:88-167).
 
         One device->host read (the edge count), like the reference's ``row.shape[0]``; a
-        ``batch`` vector costs one more (its cloud sizes), as in the reference without
-        ``num_batch_elements``."""
+        ``batch`` vector costs one more (whether it is sorted) and, without
+        ``num_batch_elements``, another (the cloud count); its offsets are built on the device."""
         _no_grad_positions(pos)
         N = pos.shape[0]
         dev = nat.require_cuda(pos, what="SpatialGraph.build")

@@ -115,8 +115,18 @@ int gdl_fps_ex(const float *pos, const int64_t *ptr, const int64_t *k_per_cloud,
  * or any value with num_clouds * max_cloud_sources >= ptr_s[num_clouds] - ptr_s[0] (e.g. the mean
  * rounded up). Calls with max_cloud_sources >= 32768 search a grid of each cloud's sources (exact;
  * knn_grid.cu); if the bound is violated there, every query falls back to the exact heap replay.
+ * Calls with 4097 <= max_cloud_sources < 32768 and at least 592 queries put each cloud's sources
+ * in Morton order, in blocks of 32 with a box each, and visit them nearest-first per tile of 128
+ * Morton-ordered queries, skipping blocks by an exact distance bound (the workspace holds the
+ * orders and boxes).
  */
 size_t gdl_knn_workspace_size(int64_t n_query, int32_t num_clouds, int32_t k, int64_t max_cloud_sources);
+/* Distances (query, source pairs) the last gdl_knn call with this workspace and these sizes
+ * evaluated, read back synchronously into *out (host): the work a roofline counts once clouds of
+ * 4097 .. 32767 sources skip blocks of sources (brute force evaluates every pair). The grid path
+ * (clouds of >= 32768 sources) does not count its searches. No counterpart in the reference. */
+int gdl_knn_distance_count(const void *workspace, int64_t n_query, int32_t num_clouds, int32_t k,
+                           int64_t max_cloud_sources, unsigned long long *out);
 int gdl_knn(const float *query, const float *source, const int64_t *ptr_q, const int64_t *ptr_s,
             int32_t num_clouds, int64_t n_query, int32_t k, int64_t max_cloud_sources, int64_t *out_idx,
             float *out_dist, void *workspace, size_t workspace_bytes, void *stream);
@@ -288,8 +298,9 @@ int gdl_se3_aggregate_backward(const gdl_se3_paths *paths, float *const *grad_pr
  *   C[m, n]    = sum_{r < rows} sum_{j < sub} A[r * lda + m * sub + j] * B[r * ldb + n * sub + j]
  *   col_sum[m] = sum_{r < rows} A[r * lda + m]   (nullable, sub == 1 only: the bias gradient)
  * A = the layer's output gradient, B = its input (lda >= M * sub, ldb >= N * sub, in floats); C [M, N]
- * dense row-major and col_sum [M] are overwritten (zeros when rows == 0). The rows are split into a
- * fixed number of slices and the partial results added in slice order: deterministic.
+ * dense row-major and col_sum [M] are overwritten (zeros when rows == 0; col_sum is still written
+ * when N == 0). The rows are split into a fixed number of slices and the partial results added in
+ * slice order: deterministic.
  */
 size_t gdl_weight_grad_workspace_size(int64_t rows, int32_t M, int32_t N, int32_t sub);
 int gdl_weight_grad(const float *A, int64_t lda, const float *B, int64_t ldb, int64_t rows, int32_t M, int32_t N,
@@ -382,7 +393,9 @@ int gdl_segment_reduce_backward(const float *grad_out, const void *msg, int32_t 
  *  - num_rows must not exceed 66,863,040 (16,320 queued segments x 4,097 slots); larger inputs
  *    return GDL_ERR_OVERFLOW.
  *  - The first call on a device looks up the array's device address (cudaGetSymbolAddress) with
- *    that device current; make that first call before any stream capture.
+ *    that device current; make that first call before any stream capture. The address is kept
+ *    for the life of the process: after a cudaDeviceReset() on that device (which destroys the
+ *    context owning the array) this entry point must not be called again in that process.
  *  - All calls on a device share the array. Each call clears the part that must start at zero,
  *    but calls whose kernels may overlap on the GPU (unordered streams) race and must not be
  *    issued; order them on one stream or with events.

@@ -12,7 +12,9 @@ against the reference kernels themselves. It runs only where the reference tree
 exists (the build container); the built ``.so`` files travel with the repository
 snapshot to the GPU box.
 
-Usage: ``python oracle/build_ref.py [REFERENCE_ROOT]``
+Usage: ``python oracle/build_ref.py [REFERENCE_ROOT]``. Without the argument the root comes from
+the environment variable GDL_REFERENCE_ROOT, else from ``reference_path`` in the repository's
+BASELINE.json (the record of where the reference was mounted for this build).
 """
 
 import os
@@ -21,6 +23,24 @@ from pathlib import Path
 
 HERE = Path(__file__).resolve().parent
 OUT = HERE / "_ref"
+
+
+def reference_root(argv_root=None):
+    """The reference tree: the given path, GDL_REFERENCE_ROOT, or BASELINE.json's reference_path
+    (None if none is set)."""
+    if argv_root:
+        return Path(argv_root)
+    env = os.environ.get("GDL_REFERENCE_ROOT")
+    if env:
+        return Path(env)
+    baseline = HERE.parent / "BASELINE.json"
+    if baseline.exists():
+        import json
+
+        p = json.loads(baseline.read_text()).get("reference_path")
+        if p:
+            return Path(p)
+    return None
 
 # (module name used by the reference loader, source file)
 # geoembodied/csrc/__init__.py:95, :230, :346, :536
@@ -58,9 +78,9 @@ def build(ref_root: Path, only=None) -> None:
 
 
 if __name__ == "__main__":
-    root = Path(sys.argv[1]) if len(sys.argv) > 1 else Path("/root/reference")
+    root = reference_root(sys.argv[1] if len(sys.argv) > 1 else None)
     only = sys.argv[2:] or None
-    if not (root / "geoembodied" / "csrc").is_dir():
+    if root is None or not (root / "geoembodied" / "csrc").is_dir():
         print(f"[build_ref] reference tree not found at {root}; nothing to build")
         sys.exit(0)
     build(root, only)

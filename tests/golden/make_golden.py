@@ -470,7 +470,16 @@ def importlib_module(name: str):
 
 
 def main():
-    root = sys.argv[1] if len(sys.argv) > 1 else "/root/reference"
+    import importlib.util
+
+    spec = importlib.util.spec_from_file_location("gdl_build_ref",
+                                                  Path(__file__).resolve().parents[2] / "oracle" / "build_ref.py")
+    build_ref = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(build_ref)
+    root = build_ref.reference_root(sys.argv[1] if len(sys.argv) > 1 else None)
+    if root is None:
+        raise SystemExit("usage: make_golden.py REFERENCE_ROOT (or set GDL_REFERENCE_ROOT)")
+    root = str(root)
     F, K, R, S = _ref(root)
     torch.set_num_threads(os.cpu_count() or 1)
     out = {}

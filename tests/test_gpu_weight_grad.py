@@ -75,6 +75,17 @@ def test_weight_grad_empty_rows_give_zeros():
     assert C.shape == (7, 5) and torch.all(C == 0) and torch.all(cs == 0)
 
 
+def test_weight_grad_no_input_columns_still_sums_the_output_gradient():
+    """A layer with zero input features (N == 0) has no weight entries but a bias gradient."""
+    g = torch.Generator().manual_seed(9)
+    A = torch.randn(3000, 7, generator=g).to(DEV)
+    B = torch.empty(3000, 0, device=DEV)
+    C, cs = csrc.weight_grad_cuda(A, B, 1, col_sum=True)
+    assert C.shape == (7, 0)
+    want = A.double().sum(0).float()
+    assert torch.allclose(cs, want, rtol=1e-6, atol=1e-5)
+
+
 def test_radial_mlp_gradients_match_nn_linear():
     """The radial MLP through the row-linear function gives nn.Linear's gradients (float64 run of
     the same weights as the reference)."""
