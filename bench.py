@@ -28,6 +28,8 @@ inputs with the shapes of the reference's use cases; see gdl_b200/synthetic.py):
   c5s           (auxiliary) c5's clouds: SpatialGraph.build -- radius graph r = 1 m, 64 over all
                 points with each edge's distance, direction and l <= 2 spherical harmonics, the
                 CSR fields and the per-cloud average degree.
+  seg           (auxiliary) segment reduce alone: 65536 segments x 32 rows x 64 f32 channels, sum
+                and max, forward and backward (the metric's segment-reduce GB/s).
 
 value : input points per second with inputs resident in HBM, timed with CUDA events on the
         launching stream, L2 flushed (256 MiB write) between steps, max over ranks.
@@ -1297,7 +1299,98 @@ class C5S(C5G):
         O.cloud_avg_degree(ns, ne)
 
 
-CONFIGS = {"c1": C1, "c2": C2, "c2c": C2C, "c3": C3, "c3i": C3I, "c4": C4, "c5": C5, "c5g": C5G, "c5h": C5H, "c5s": C5S}
+class SEG:
+    """Auxiliary segment-reduce workload (the metric's "segment-reduce HBM GB/s"): 65536 segments x
+    32 rows of 64-channel f32 messages (2.1 M rows, 537 MB), read directly (no gather); a step is the
+    sum and max forward and their backward (the max's tie-splitting gradient)."""
+    name = "seg"
+    metric = "points/sec (segment sum + max fwd + bwd, 65536 segments x 32 rows x 64 f32 channels)"
+    B, N, DEG, C = 65536, 32, 32, 64
+    launches_per_step = 2 + 2 + 2 + 3  # fwd (short + long) x 2; bwd sum 2; bwd max 2 + tie fix-up
+    points_per_step = property(lambda self: self.B * self.DEG)  # rows reduced per step
+    cpu_fraction = 1 / 64
+    cpu_sample = "1024 of 65536 segments (sum and max, forward and backward) per sample, scaled x64"
+
+    def _host_init(self, seed, pin=True):
+        g = torch.Generator().manual_seed(seed)
+        self.rows = self.B * self.DEG
+        self.msg_h = torch.randn(self.rows, self.C, generator=g)
+        self.gout_h = torch.randn(self.B, self.C, generator=g)
+        if pin:
+            self.msg_h = self.msg_h.pin_memory()
+
+    def __init__(self, dev, seed):
+        self.dev = dev
+        self._host_init(seed)
+        self.msg = self.msg_h.to(dev)
+        self.gout = self.gout_h.to(dev)
+        self.ns, self.ne = _csr_uniform(self.B, self.DEG, dev)
+        self.out_sum = torch.empty(self.B, self.C, device=dev)
+        self.out_max = torch.empty(self.B, self.C, device=dev)
+        self.arg = torch.empty(self.B, self.C, dtype=torch.int32, device=dev)
+        self.g_sum = torch.empty_like(self.msg)
+        self.g_max = torch.empty_like(self.msg)
+        self.L = nat.load()
+        self.ws = nat.workspace(self.L.gdl_segment_reduce_workspace_size(self.rows, self.B), dev)
+
+    def _s(self):
+        return torch.cuda.current_stream(self.dev).cuda_stream
+
+    def _fwd(self, red, out, arg):
+        nat.check(self.L.gdl_segment_reduce(self.msg.data_ptr(), 0, self.rows, self.C, None, self.ns.data_ptr(),
+                                            self.ne.data_ptr(), self.B, red, out.data_ptr(), nat.ptr(arg),
+                                            self.ws.data_ptr(), self.ws.numel(), self._s()), "segment fwd")
+
+    def _bwd(self, red, out, arg, g):
+        nat.check(self.L.gdl_segment_reduce_backward(self.gout.data_ptr(), self.msg.data_ptr(), 0, nat.ptr(out),
+                                                     nat.ptr(arg), self.rows, self.C, None, self.ns.data_ptr(),
+                                                     self.ne.data_ptr(), self.B, red, g.data_ptr(),
+                                                     self.ws.data_ptr(), self.ws.numel(), self._s()), "segment bwd")
+
+    def stage_list(self):
+        return [("segment_sum_fwd", lambda: self._fwd(0, self.out_sum, None)),
+                ("segment_max_fwd", lambda: self._fwd(2, self.out_max, self.arg)),
+                ("segment_sum_bwd", lambda: self._bwd(0, None, None, self.g_sum)),
+                ("segment_max_bwd", lambda: self._bwd(2, self.out_max, self.arg, self.g_max))]
+
+    def step(self):
+        for _, fn in self.stage_list():
+            fn()
+
+    def edges(self):
+        return self.rows
+
+    def stage_bytes(self, E):
+        rows, B, C = self.rows, self.B, self.C
+        idx = 8 * B  # node start / end
+        return {"segment_sum_fwd": 4 * rows * C + 4 * B * C + idx,
+                "segment_max_fwd": 4 * rows * C + 8 * B * C + idx,  # + the int32 arg
+                "segment_sum_bwd": 4 * B * C + 4 * rows * C + idx,
+                "segment_max_bwd": 8 * B * C + 4 * rows * C + idx}  # grad_out + arg in
+
+    def e2e_step(self):
+        msg = self.msg_h.to(self.dev, non_blocking=True)
+        s_ = csrc.segment_reduce_cuda(msg, None, self.ns, self.ne, self.B, "sum")
+        m_, a_ = csrc.segment_reduce_cuda(msg, None, self.ns, self.ne, self.B, "max", with_arg=True)
+        host = [t.to("cpu", non_blocking=True) for t in (s_, m_)]
+        torch.cuda.current_stream(self.dev).synchronize()
+        return host
+
+    e2e_h2d = property(lambda self: self.rows * self.C * 4)
+    e2e_d2h = property(lambda self: 2 * self.B * self.C * 4)
+
+    def cpu_step(self, O):
+        m = 1024
+        msg = self.msg_h.numpy()[: m * self.DEG]
+        ns = (np.arange(m) * self.DEG).astype(np.int32)
+        out = O.segment_reduce(msg, None, ns, ns + self.DEG, m, "sum")
+        mx = O.segment_reduce(msg, None, ns, ns + self.DEG, m, "max")
+        O.segment_reduce_backward(self.gout_h.numpy()[:m], msg, out, None, ns, ns + self.DEG, m, "sum")
+        O.segment_reduce_backward(self.gout_h.numpy()[:m], msg, mx, None, ns, ns + self.DEG, m, "max")
+
+
+CONFIGS = {"c1": C1, "c2": C2, "c2c": C2C, "c3": C3, "c3i": C3I, "c4": C4, "c5": C5, "c5g": C5G, "c5h": C5H, "c5s": C5S,
+           "seg": SEG}
 
 
 
@@ -1663,8 +1756,10 @@ def run_ours(args, cfg_cls):
         if ws > cfg_cls.B:
             raise SystemExit(f"{cfg_cls.name} has {cfg_cls.B} clouds: at most {cfg_cls.B} ranks")
         c0, c1 = shard_clouds([cfg_cls.N * getattr(cfg_cls, "K", 1)] * cfg_cls.B, ws, rank)
+        if args.clouds:  # a smaller batch (the first clouds), e.g. for a profiler capture
+            c0, c1 = min(c0, args.clouds), min(c1, args.clouds)
         cfg = cfg_cls(dev, seed=0, clouds=(c0, c1))
-        global_points = cfg_cls.B * cfg_cls.N
+        global_points = (min(cfg_cls.B, args.clouds) if args.clouds else cfg_cls.B) * cfg_cls.N
     else:
         cfg = cfg_cls(dev, seed=1000 * rank)
         global_points = ws * cfg.points_per_step
@@ -1749,6 +1844,8 @@ def main():
                     help="other configurations measured in the same run (N=1 only), in the line's per_config")
     ap.add_argument("--per-config-steps", type=int, default=30)
     ap.add_argument("--no-per-config", action="store_true")
+    ap.add_argument("--clouds", type=int, default=0,
+                    help="LiDAR configurations (c5*): only the first N clouds of the batch (profiling; 0 = all)")
     args = ap.parse_args()
     cfg_cls = CONFIGS[args.config]
     if args.impl == "reference":

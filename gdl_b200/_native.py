@@ -163,3 +163,20 @@ def stream(device: torch.device) -> int:
 
 def workspace(nbytes: int, device: torch.device) -> torch.Tensor:
     return torch.empty(max(int(nbytes), 1), dtype=torch.uint8, device=device)
+
+
+_stream_ws = {}
+
+
+def stream_workspace(nbytes: int, device: torch.device) -> torch.Tensor:
+    """A scratch buffer of at least `nbytes` kept per (device, current stream) and reused by the
+    next call on that stream: work queued on one stream runs in order, so the next call's kernels
+    start after this call's are done with it. Saves an allocation per call on small, launch-bound
+    operators."""
+    s = torch.cuda.current_stream(device)
+    key = (device.index if device.index is not None else torch.cuda.current_device(), s.cuda_stream)
+    buf = _stream_ws.get(key)
+    if buf is None or buf.numel() < nbytes:
+        buf = torch.empty(max(int(nbytes), 256), dtype=torch.uint8, device=device)
+        _stream_ws[key] = buf
+    return buf

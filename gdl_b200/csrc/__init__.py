@@ -343,7 +343,7 @@ def segment_reduce_cuda(msg: torch.Tensor, perm: Optional[torch.Tensor], node_st
     ne = node_end.to(torch.int32).contiguous()
     pm = None if perm is None else perm.to(torch.int32).contiguous()
     L = nat.load()
-    ws = nat.workspace(L.gdl_segment_reduce_workspace_size(E, N), dev)
+    ws = nat.stream_workspace(L.gdl_segment_reduce_workspace_size(E, N), dev)
     if N > 0 and C > 0:
         nat.check(L.gdl_segment_reduce(msg.data_ptr() if E else None, nat.DTYPE[msg.dtype], E, C, nat.ptr(pm),
                                        ns.data_ptr(), ne.data_ptr(), int(N), nat.REDUCE[reduce], out.data_ptr(),

@@ -892,72 +892,57 @@ __device__ __forceinline__ int find_cloud(const int64_t *__restrict__ ptr, int B
     return lo;
 }
 
-constexpr int kExactRounds = 16;
+// The reference kernel's heap, replayed exactly for flagged queries: one CTA per query. All its
+// warps compute the distances of a stretch of kExactStretch sources into shared memory; then warp
+// 0 walks them in source order, 32 at a time: a candidate the heap rejects now (full and d >= root
+// -- the root never grows while distances are ordered) is rejected at its turn too, so only the
+// ballot of the others is walked, and every lane applies the same MinKHeap::add to its own copy of
+// the heap. A chunk with a NaN distance (or a NaN root) walks every candidate.
+constexpr int kExactThreads = 256;
+constexpr int kExactStretch = 4096;
 
-// The reference kernel's heap, replayed exactly for flagged queries: one warp per query.
-// The lanes compute 32 distances at a time; a candidate the heap would reject at the start
-// of the batch (full and d >= root -- the root never grows while distances are ordered) is
-// rejected at its turn too, so only the ballot of the others is walked, in source order,
-// and every lane applies the same MinKHeap::add to its own copy of the heap. A batch with a
-// NaN distance (or a NaN root) walks every candidate.
-__global__ void __launch_bounds__(kKnnThreads) knn_exact_kernel(
+__global__ void __launch_bounds__(kExactThreads) knn_exact_kernel(
     const float *__restrict__ query, const float *__restrict__ source, const int64_t *__restrict__ ptr_q,
     const int64_t *__restrict__ ptr_s, int32_t B, int k, const int32_t *__restrict__ flag_list,
     const int32_t *__restrict__ flag_count, int64_t *__restrict__ out_idx, float *__restrict__ out_dist,
     unsigned long long *__restrict__ pairs) {
+    __shared__ float sd[kExactStretch];
     const int nflag = *flag_count;
-    const int lane = threadIdx.x & 31;
-    const int warps = gridDim.x * (kKnnThreads / 32);
-    for (int f = blockIdx.x * (kKnnThreads / 32) + (threadIdx.x >> 5); f < nflag; f += warps) {
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    for (int f = blockIdx.x; f < nflag; f += gridDim.x) {  // uniform over the CTA
         const int64_t q = flag_list[f];
         const int b = find_cloud(ptr_q, B, q);
         const float qx = query[3 * q], qy = query[3 * q + 1], qz = query[3 * q + 2];
         MinKHeap h;
         h.init(knn_bucket(k));
-        const int64_t se = ptr_s[b + 1];
-        // one warp replays a whole cloud: the loads of kExactRounds rounds are in flight together,
-        // so the scan is not one memory latency per 32 sources
-        for (int64_t c0 = ptr_s[b]; c0 < se; c0 += 32 * kExactRounds) {
-            float px[kExactRounds], py[kExactRounds], pz[kExactRounds];
-#pragma unroll
-            for (int u = 0; u < kExactRounds; ++u) {
-                const int64_t s = c0 + 32 * u + lane;
-                px[u] = py[u] = pz[u] = 0.0f;
-                if (s < se) {
-                    px[u] = source[3 * s];
-                    py[u] = source[3 * s + 1];
-                    pz[u] = source[3 * s + 2];
-                }
+        const int64_t s0 = ptr_s[b], se = ptr_s[b + 1];
+        for (int64_t c0 = s0; c0 < se; c0 += kExactStretch) {
+            const int m = (int)(se - c0 < kExactStretch ? se - c0 : kExactStretch);
+            __syncthreads();  // the previous stretch's walk is done
+            for (int i = tid; i < m; i += kExactThreads) {
+                const float *p = source + 3 * (c0 + i);
+                sd[i] = dist2(qx, qy, qz, p[0], p[1], p[2]);
             }
-            // candidates the heap rejects at the start of the batch (full and d >= root) are rejected
-            // at their turn too -- the root never grows while distances are ordered -- so one
-            // filter for the whole batch leaves only the others to walk, in source order
-            const bool full = h.count >= h.cap;
-            const float root = h.d[0];
-            float d[kExactRounds];
-            bool nan = full && root != root;
-#pragma unroll
-            for (int u = 0; u < kExactRounds; ++u) {
-                d[u] = dist2(qx, qy, qz, px[u], py[u], pz[u]);
-                nan |= c0 + 32 * u + lane < se && d[u] != d[u];
-            }
-            // a NaN distance or root is unordered: then every candidate of the batch goes through add()
-            const bool unordered = __any_sync(0xffffffffu, nan);
-#pragma unroll
-            for (int u = 0; u < kExactRounds; ++u) {
-                const bool in = c0 + 32 * u + lane < se;
-                unsigned live = __ballot_sync(0xffffffffu, in && (unordered || !(full && d[u] >= root)));
-                while (live) {
-                    const int l = __ffs(live) - 1;
-                    live &= live - 1;
-                    h.add(__shfl_sync(0xffffffffu, d[u], l), (int)(c0 + 32 * u + l));
+            __syncthreads();
+            if (warp == 0) {
+                for (int j0 = 0; j0 < m; j0 += 32) {
+                    const bool in = j0 + lane < m;
+                    const float d = in ? sd[j0 + lane] : 0.0f;
+                    const bool full = h.count >= h.cap;
+                    const bool unordered = __any_sync(0xffffffffu, in && d != d) || (full && h.d[0] != h.d[0]);
+                    unsigned live = __ballot_sync(0xffffffffu, in && (unordered || !(full && d >= h.d[0])));
+                    while (live) {
+                        const int l = __ffs(live) - 1;
+                        live &= live - 1;
+                        h.add(__shfl_sync(0xffffffffu, d, l), (int)(c0 + j0 + l));
+                    }
                 }
             }
         }
-        h.sort_ascending();
-        if (lane == 0) {
+        if (tid == 0) {
+            h.sort_ascending();
             write_row(out_idx + q * k, out_dist + q * k, k, h.count < k ? h.count : k, h.d, h.i);
-            atomicAdd(pairs, (unsigned long long)(se - ptr_s[b]));
+            atomicAdd(pairs, (unsigned long long)(se - s0));
         }
     }
 }
@@ -1198,7 +1183,7 @@ extern "C" int gdl_knn(const float *query, const float *source, const int64_t *p
     if (w.grid) {  // large clouds: exact search over a grid of each cloud's sources
         GDL_CUDA_TRY(knn_grid_run(query, source, ptr_q, ptr_s, num_clouds, n_query, k, max_cloud_sources, w.kg,
                                   out_idx, out_dist, w.flag_list, w.flag_count, st));
-        knn_exact_kernel<<<kSmCount, kKnnThreads, 0, st>>>(query, source, ptr_q, ptr_s, num_clouds, k, w.flag_list,
+        knn_exact_kernel<<<kSmCount, kExactThreads, 0, st>>>(query, source, ptr_q, ptr_s, num_clouds, k, w.flag_list,
                                                            w.flag_count, out_idx, out_dist, w.pairs);
         GDL_CUDA_TRY(cudaGetLastError());
         return GDL_OK;
@@ -1206,7 +1191,7 @@ extern "C" int gdl_knn(const float *query, const float *source, const int64_t *p
     if (w.block) {  // mid-size clouds: Morton-ordered source blocks, nearest first
         GDL_CUDA_TRY(knn_block_run(query, source, ptr_q, ptr_s, num_clouds, n_query, k, max_cloud_sources, w,
                                    out_idx, out_dist, st));
-        knn_exact_kernel<<<kSmCount, kKnnThreads, 0, st>>>(query, source, ptr_q, ptr_s, num_clouds, k, w.flag_list,
+        knn_exact_kernel<<<kSmCount, kExactThreads, 0, st>>>(query, source, ptr_q, ptr_s, num_clouds, k, w.flag_list,
                                                            w.flag_count, out_idx, out_dist, w.pairs);
         GDL_CUDA_TRY(cudaGetLastError());
         return GDL_OK;
@@ -1223,7 +1208,7 @@ extern "C" int gdl_knn(const float *query, const float *source, const int64_t *p
         else
             knn_warp_kernel<3><<<grid, kWarpQ * 32, 0, st>>>(query, source, ptr_q, ptr_s, num_clouds, k, w.tile_base,
                                                              out_idx, out_dist, w.flag_list, w.flag_count, w.pairs);
-        knn_exact_kernel<<<kSmCount, kKnnThreads, 0, st>>>(query, source, ptr_q, ptr_s, num_clouds, k, w.flag_list,
+        knn_exact_kernel<<<kSmCount, kExactThreads, 0, st>>>(query, source, ptr_q, ptr_s, num_clouds, k, w.flag_list,
                                                            w.flag_count, out_idx, out_dist, w.pairs);
         GDL_CUDA_TRY(cudaGetLastError());
         return GDL_OK;
@@ -1236,7 +1221,7 @@ extern "C" int gdl_knn(const float *query, const float *source, const int64_t *p
     case 32: knn_launch<32>(query, source, ptr_q, ptr_s, num_clouds, n_query, k, split, w, out_idx, out_dist, st); break;
     default: knn_launch<64>(query, source, ptr_q, ptr_s, num_clouds, n_query, k, split, w, out_idx, out_dist, st); break;
     }
-    knn_exact_kernel<<<kSmCount, kKnnThreads, 0, st>>>(query, source, ptr_q, ptr_s, num_clouds, k, w.flag_list,
+    knn_exact_kernel<<<kSmCount, kExactThreads, 0, st>>>(query, source, ptr_q, ptr_s, num_clouds, k, w.flag_list,
                                                        w.flag_count, out_idx, out_dist, w.pairs);
     GDL_CUDA_TRY(cudaGetLastError());
     return GDL_OK;
