@@ -481,6 +481,7 @@ constexpr int kKbStage = 8;         // blocks staged in shared memory per pass
 constexpr int kKbMaxBlocks = 1024;  // blocks a tile orders (32768 sources); larger clouds go in index order
 constexpr int kKbBins = 64;
 constexpr int kBwMinK = 8;          // k from which one warp serves one query (knn_bwarp_kernel)
+constexpr int kBwBulk = 4;          // accepted candidates of a block above which they are merged in bulk
 
 template <int L>
 struct KbSmem {
@@ -772,6 +773,8 @@ __global__ void __launch_bounds__(kBwWarps * 32) knn_bwarp_kernel(
     float *__restrict__ out_dist, int32_t *__restrict__ flag_list, int32_t *__restrict__ flag_count,
     unsigned long long *__restrict__ pairs) {
     __shared__ float lbs[kBwWarps][kKbMaxBlocks];
+    __shared__ float mrg_d[kBwWarps][32 * NR];  // the bulk merge's staging
+    __shared__ int mrg_i[kBwWarps][32 * NR];
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int64_t p = ptr_q[0] + (int64_t)blockIdx.x * kBwWarps + warp;
     if (p >= ptr_q[B]) return;  // uniform over the warp; no block-wide barrier follows
@@ -831,6 +834,15 @@ __global__ void __launch_bounds__(kBwWarps * 32) knn_bwarp_kernel(
             si = __float_as_int(sp.w);
         }
         unsigned acc = __ballot_sync(0xffffffffu, d < thr);
+        if (__popc(acc) > kBwBulk) {  // many candidates: one bulk merge
+            const bool in = (acc >> lane) & 1u;
+            warp_list_merge<NR>(ed, ei, in ? d : kInf, in ? si : -1, L, lane, mrg_d[warp], mrg_i[warp]);
+            cnt += __popc(acc);
+#pragma unroll
+            for (int r = 0; r < NR; ++r)
+                if ((L - 1) / 32 == r) thr = __shfl_sync(0xffffffffu, ed[r], (L - 1) & 31);
+            acc = 0u;
+        }
         while (acc) {
             const int l = __ffs(acc) - 1;
             acc &= acc - 1;

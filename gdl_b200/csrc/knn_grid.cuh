@@ -43,6 +43,80 @@ __device__ __forceinline__ void warp_list_insert(float (&ed)[NR], int (&ei)[NR],
     }
 }
 
+// Bulk form of warp_list_insert: every lane offers one candidate (d, i) (d = +inf for none). The
+// candidates are sorted across the warp (bitonic, ascending distance, then index), each one's
+// place in the merged list is its rank plus the number of entries <= it, each entry's its index
+// plus the number of candidates < it (a stable merge, entries first), and the L smallest are
+// written through `stage` (2 * 32 * NR words of shared memory for this warp) back into the
+// registers. For many candidates at once this costs a few dozen shuffles instead of one insert
+// network per candidate.
+template <int NR>
+__device__ __forceinline__ void warp_list_merge(float (&ed)[NR], int (&ei)[NR], float d, int i, int L, int lane,
+                                                float *stage_d, int *stage_i) {
+#pragma unroll
+    for (int k = 2; k <= 32; k <<= 1)  // bitonic sort of the 32 candidates
+#pragma unroll
+        for (int j = k >> 1; j > 0; j >>= 1) {
+            const float od = __shfl_xor_sync(0xffffffffu, d, j);
+            const int oi = __shfl_xor_sync(0xffffffffu, i, j);
+            const bool up = (lane & k) == 0;          // this run ascends
+            const bool low = (lane & j) == 0;         // this lane holds the smaller slot
+            const bool other_less = od < d || (od == d && oi < i);
+            if (other_less == (low == up)) {
+                d = od;
+                i = oi;
+            }
+        }
+    // binary search range: a power of two above 32 * NR, since a candidate can follow every entry
+    constexpr int P = NR == 1 ? 64 : 128;
+    // entries <= d (the candidate's place among them)
+    int le = 0;
+#pragma unroll
+    for (int half = P / 2; half >= 1; half >>= 1) {
+        const int probe = le + half - 1;
+        float v = __int_as_float(0x7f800000);
+#pragma unroll
+        for (int r = 0; r < NR; ++r) {
+            const float x = __shfl_sync(0xffffffffu, ed[r], probe & 31);
+            if ((probe >> 5) == r) v = x;
+        }
+        if (probe < 32 * NR && v <= d) le += half;
+    }
+    const int pc = lane + le;
+    // candidates < entry (the entry's place among them): the candidates are sorted in lane order
+    int pe[NR];
+#pragma unroll
+    for (int r = 0; r < NR; ++r) {
+        int lt = 0;
+#pragma unroll
+        for (int half = 32; half >= 1; half >>= 1) {  // lt runs 0..32
+            const int probe = lt + half - 1;
+            const float x = __shfl_sync(0xffffffffu, d, probe & 31);
+            if (probe < 32 && x < ed[r]) lt += half;
+        }
+        pe[r] = lane + 32 * r + lt;
+    }
+    __syncwarp();
+    if (pc < L) {
+        stage_d[pc] = d;
+        stage_i[pc] = i;
+    }
+#pragma unroll
+    for (int r = 0; r < NR; ++r)
+        if (pe[r] < L) {
+            stage_d[pe[r]] = ed[r];
+            stage_i[pe[r]] = ei[r];
+        }
+    __syncwarp();
+#pragma unroll
+    for (int r = 0; r < NR; ++r) {
+        const int at = lane + 32 * r;
+        ed[r] = at < L ? stage_d[at] : __int_as_float(0x7f800000);
+        ei[r] = at < L ? stage_i[at] : -1;
+    }
+    __syncwarp();
+}
+
 struct KGrid {
     float mn[3];
     float h, inv;
