@@ -15,17 +15,20 @@
 //    slot array, one __syncthreads per pick (fps_cta_kernel).
 //  * Larger clouds (bucketed FPS): each cloud is first put in Morton order (bounding box, 30-bit
 //    codes, segmented radix sort), so that every thread owns a compact run of P points -- a
-//    bucket with an axis-aligned box. Per pick a thread first bounds the distance from the new
-//    sample to its box with the same rounded operations as the point distances; the bound is
-//    <= every point's rounded distance (rounding is monotone), so when it is >= the bucket's
-//    largest minimum no minimum of the bucket can change and the thread skips its P updates
-//    and keeps its cached best key. Late in the run only the few buckets around each new sample
-//    update. The points sit in shared memory (SoA float2 pairs, conflict-free per lane, each
-//    thread's in priority order so that a (min-distance, slot) key reduced as a tree orders them
-//    exactly), the minima in registers. One CTA serves up to 13824 points; larger clouds run on
-//    a thread-block cluster of up to 16 CTAs whose winners cross through distributed shared
-//    memory: st.async stores completing bytes on each receiver's mbarrier, one bounded wait per
-//    pick, no cluster-wide barrier (fps_bucket_kernel).
+//    bucket with an axis-aligned box. A thread first bounds the distance from a new sample to its
+//    box with the same rounded operations as the point distances; the bound is <= every point's
+//    rounded distance (rounding is monotone), so when it is >= the bucket's largest minimum no
+//    minimum of the bucket can change and the thread skips its P updates. The points sit in shared
+//    memory (SoA float2 pairs, each thread's in priority order so that a (min-distance, slot) key
+//    reduced as a tree orders them exactly), the minima in registers. One CTA serves up to 8192
+//    or 13824 points; larger clouds run on a thread-block cluster of up to 16 CTAs whose records
+//    cross through distributed shared memory (st.async stores completing bytes on each receiver's
+//    mbarrier, one bounded wait per round). The picks are made in rounds of up to eight: each
+//    warp, and in a cluster each CTA, reports its best point with a bound on its other points,
+//    and the records are taken in decreasing key order while each provably remains the next pick
+//    of the one-at-a-time chain (its minimum survives the picks taken before it in the round, it
+//    beats their bounds); the result is bit-identical to one pick per exchange, with about three
+//    and a half picks per exchange on LiDAR clouds (fps_bucket_kernel).
 //  * Clouds beyond 16 x 13824 points: a CTA that streams points from HBM with min_d in the
 //    workspace (fps_stream_kernel).
 #include <cooperative_groups.h>
@@ -68,6 +71,17 @@ __device__ __forceinline__ uint64_t warp_max_key(uint64_t k) {
     const uint32_t mhi = __reduce_max_sync(0xffffffffu, hi);
     const uint32_t mlo = __reduce_max_sync(0xffffffffu, hi == mhi ? (uint32_t)k : 0u);
     return ((uint64_t)mhi << 32) | mlo;
+}
+
+// lane holding the warp's largest u64 key (the lowest such lane) and that key's high word: one
+// redux on the high words, the low words only when several lanes share the largest high word
+__device__ __forceinline__ int warp_argmax_key(uint64_t k, uint32_t &mhi) {
+    const uint32_t hi = (uint32_t)(k >> 32);
+    mhi = __reduce_max_sync(0xffffffffu, hi);
+    const uint32_t tied = __ballot_sync(0xffffffffu, hi == mhi);
+    if ((tied & (tied - 1u)) == 0u) return __ffs(tied) - 1;
+    const uint32_t mlo = __reduce_max_sync(0xffffffffu, hi == mhi ? (uint32_t)k : 0u);
+    return __ffs(__ballot_sync(0xffffffffu, hi == mhi && (uint32_t)k == mlo)) - 1;
 }
 
 // out offset of cloud b = sum_{c<b} max(k_c, 0)
@@ -206,11 +220,13 @@ __global__ void __launch_bounds__(THREADS) fps_cta_kernel(const float *__restric
 constexpr int kMaxCluster = 16;
 constexpr int kDefaultWaitPolls = 1 << 20;   // mbarrier polls before a wait gives up
 constexpr int kMaxDynSmem = 227 * 1024;
-constexpr int kRecBytes = 24;                // one record: key (8 B), x, y (16-B store) + z (8-B store)
+constexpr int kRecBytes = 24;                // one record: key, x, y (16-B store) + z, bound (8-B store)
+constexpr int kRoundPicks = 8;               // picks one round may make
 
 __host__ __device__ constexpr size_t bucket_points_bytes(int T, int P) { return (size_t)16 * T * P; }
+// records per round: one per CTA of the cluster, double-buffered
 __host__ __device__ constexpr size_t bucket_smem_bytes(int T, int P, int cs) {
-    return bucket_points_bytes(T, P) + (size_t)2 * cs * (16 + 8);
+    return bucket_points_bytes(T, P) + (size_t)2 * cs * kRecBytes;
 }
 
 __device__ __forceinline__ uint32_t smem_u32(const void *p) { return (uint32_t)__cvta_generic_to_shared(p); }
@@ -231,16 +247,16 @@ __device__ __forceinline__ uint32_t mbar_try_wait(uint32_t bar, uint32_t parity)
     return done;
 }
 
-// One winner record into CTA `dst`'s slots: (key, x, y) in 16 bytes and (z) in 8, both completing
+// One warp record into a CTA's slot: (key, x, y) in 16 bytes and (z, bound) in 8, both completing
 // bytes of a transaction on that CTA's mbarrier.
 __device__ __forceinline__ void st_async_rec(uint32_t da, uint32_t db, uint32_t rb, uint64_t key, float x, float y,
-                                             float z) {
+                                             float z, uint32_t bound) {
     asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.v4.b32 [%0], {%1, %2, %3, %4}, [%5];" ::"r"(da),
                  "r"((uint32_t)key), "r"((uint32_t)(key >> 32)), "r"(__float_as_uint(x)), "r"(__float_as_uint(y)),
                  "r"(rb)
                  : "memory");
     asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.v2.b32 [%0], {%1, %2}, [%3];" ::"r"(db),
-                 "r"(__float_as_uint(z)), "r"(0u), "r"(rb)
+                 "r"(__float_as_uint(z)), "r"(bound), "r"(rb)
                  : "memory");
 }
 
@@ -257,21 +273,45 @@ __device__ __forceinline__ float box_dist2_lb(float sx, float sy, float sz, cons
     return fma_ftz(gz, gz, fma_ftz(gx, gx, mul_ftz(gy, gy)));
 }
 
+// the rounded distance of point (px, py, pz) to sample (sx, sy, sz), computed exactly as the
+// bucket update computes it (packed, lane 0 of the pair)
+__device__ __forceinline__ float pair_dist2(float px, float py, float pz, float sx, float sy, float sz) {
+    float d0, d1;
+    unpack2(dist2_x2(pack2(px, px), pack2(py, py), pack2(pz, pz), pack2(sx, sx), pack2(sy, sy), pack2(sz, sz)), d0,
+            d1);
+    return d0;
+}
+
 // T threads per CTA, P points per thread -- a bucket of consecutive points in Morton order, kept
-// in priority order in shared memory, with its box, its minima in registers and its best key;
-// a cluster of cs CTAs serves one cloud of at most cs * T * P points, which `order` (global
-// indices, Morton order within each cloud) lists. Warp-sized chunks of 32 threads' buckets go
-// round-robin over the cluster's CTAs, so that the buckets around one pick (neighbours in Morton
-// order) update on several SMs.
-// Per pick: each warp's winner lane writes its record into a double-buffered slot array, one
-// barrier, every warp reduces the slots itself (the CTA's winner); a lone CTA is done there, a
-// cluster's CTAs send their winner to every CTA with st.async and wait (bounded) on their own
-// mbarrier for the cluster's records.
+// in priority order in shared memory, with its box, its minima in registers, its best key and the
+// largest minimum among its other points; a cluster of cs CTAs serves one cloud of at most
+// cs * T * P points, which `order` (global indices, Morton order within each cloud) lists.
+// Warp-sized chunks of 32 threads' buckets go round-robin over the cluster's CTAs, so that the
+// buckets around one pick (neighbours in Morton order) update on several SMs.
+//
+// The picks are made in rounds of up to M. Per round:
+//  1. every bucket applies the previous round's picks (skipping each whose distance bound to the
+//     bucket's box is >= the bucket's largest minimum);
+//  2. every warp sends one record to every CTA of the cluster (st.async completing bytes on the
+//     receiver's mbarrier; a lone CTA writes its own slots and meets one barrier): the warp's best
+//     key, that point, and a bound on the keys of the warp's other points (the other lanes' best
+//     keys and the winning bucket's second minimum);
+//  3. after a bounded wait for the cluster's records every warp takes them in decreasing key
+//     order. The first is the argmax, as in the one-pick chain. A later one, c, is the next pick
+//     of the same chain exactly when every point other than c holds a smaller key once the
+//     accepted picks a_1..a_j have updated the minima: c's own minimum must survive them
+//     (!(dist2(c, a_i) < min(c))), c must beat the bound of each a_i's warp (the points that a_i
+//     hid from the records), each a_i's minimum must drop to 0 (dist2(a_i, a_i) == 0: finite
+//     coordinates) below c's (min(c) > 0); every other record's warp holds keys no larger than its
+//     record, which is smaller than c. The first record that fails ends the round. Minima only
+//     decrease and fminf over a set of samples does not depend on their order, so the result is
+//     bit-identical to picking one point per exchange.
 // status (nullable) receives GDL_ERR_TIMEOUT when a bounded wait gives up; the cloud's picks from
 // that one on are then -2 (coordinates 0). hold_rank / hold_pick: the CTA of that rank in every
-// cluster sends no record at that pick, which makes every wait of the pick run out (the failure
-// path's test); -1 disables it. A lone CTA never waits, unless hold_rank asks it to exchange.
-template <int T, int P, int TIE>
+// cluster sends no records in the round that starts at that pick (rounds never cross it while a
+// hold is set), which makes every wait of the round run out (the failure path's test); -1
+// disables it. A lone CTA never waits, unless hold_rank asks it to exchange.
+template <int T, int P, int TIE, int M>
 __global__ void __launch_bounds__(T, 1) fps_bucket_kernel(const float *__restrict__ pos,
                                                            const int32_t *__restrict__ order,
                                                            const int64_t *__restrict__ ptr,
@@ -281,11 +321,15 @@ __global__ void __launch_bounds__(T, 1) fps_bucket_kernel(const float *__restric
                                                            int hold_rank, int64_t hold_pick) {
     constexpr int NW = T / 32, PH = P / 2;
     static_assert(P % 2 == 0, "points are held in pairs");
+    constexpr int kMaxRecords = NW > kMaxCluster ? NW : kMaxCluster;  // records a round selects from
+    static_assert(M >= 1 && M <= 32 && kMaxRecords <= 32, "one record and one pick per lane");
     extern __shared__ __align__(16) unsigned char smem[];
     __shared__ __align__(8) unsigned long long mbar[2];
     __shared__ int64_t red[NW];
-    __shared__ uint4 slotA[2][NW];  // warp winners: key, x, y
-    __shared__ float slotZ[2][NW];
+    __shared__ uint4 slotA[NW];  // warp records: key, x, y
+    __shared__ uint2 slotB[NW];  // z, bound
+    __shared__ float4 s_pick[M];  // the round's picks
+    __shared__ int s_count;       // how many (-1: a wait gave up)
     float2 *sx2 = reinterpret_cast<float2 *>(smem);  // pair h of thread t at h * T + t
     float2 *sy2 = sx2 + PH * T;
     float2 *sz2 = sy2 + PH * T;
@@ -295,7 +339,7 @@ __global__ void __launch_bounds__(T, 1) fps_bucket_kernel(const float *__restric
     const int cs = (int)cluster.num_blocks();
     const int rank = (int)cluster.block_rank();
     uint4 *recA = reinterpret_cast<uint4 *>(smem + bucket_points_bytes(T, P));  // [2][cs]: key, x, y
-    uint2 *recB = reinterpret_cast<uint2 *>(recA + 2 * cs);                     // [2][cs]: z, 0
+    uint2 *recB = reinterpret_cast<uint2 *>(recA + 2 * cs);                     // [2][cs]: z, bound
 
     const int b = blockIdx.x / cs;
     const int64_t start = ptr[b];
@@ -366,13 +410,30 @@ __global__ void __launch_bounds__(T, 1) fps_bucket_kernel(const float *__restric
             reinterpret_cast<uint32_t *>(&sn2[o])[c] = np[j];
         }
     }
-    // the bucket's best thread-local key (min-distance, P - 1 - slot): its first slot (slots are
-    // in priority order, padding last) while every minimum is 1e30
-    uint64_t lkey = md[0] > 0.0f ? make_key(md[0], (uint32_t)(P - 1)) : 0ull;
-    uint64_t bestkey;  // the same point's (min-distance, ~priority) key, and its coordinates
+    // lkey: the bucket's best thread-local key (min-distance, P - 1 - slot), reduced as a tree;
+    // bestkey: the same point's (min-distance, ~priority) key and (bx, by, bz) its coordinates;
+    // sec: the largest minimum among the bucket's other slots (float bits; minima are >= 0)
+    uint64_t lkey, bestkey;
+    uint32_t sec;
     float bx, by, bz;
-    auto thread_best = [&]() {
+    auto rekey = [&]() {
+        uint64_t kk[P];
+#pragma unroll
+        for (int j = 0; j < P; ++j) kk[j] = make_key(md[j], (uint32_t)(P - 1 - j));
+#pragma unroll
+        for (int w = 1; w < P; w <<= 1)
+#pragma unroll
+            for (int j = 0; j + w < P; j += 2 * w) kk[j] = umax64(kk[j], kk[j + w]);
+        lkey = kk[0];
         const int bj = P - 1 - (int)(uint32_t)lkey;
+        uint32_t sb[P];
+#pragma unroll
+        for (int j = 0; j < P; ++j) sb[j] = j == bj ? 0u : __float_as_uint(md[j]);
+#pragma unroll
+        for (int w = 1; w < P; w <<= 1)
+#pragma unroll
+            for (int j = 0; j + w < P; j += 2 * w) sb[j] = sb[j] > sb[j + w] ? sb[j] : sb[j + w];
+        sec = sb[0];
         const int o = (bj >> 1) * T + t;
         const float2 X = sx2[o], Y = sy2[o], Z = sz2[o];
         const uint2 N = sn2[o];
@@ -381,97 +442,172 @@ __global__ void __launch_bounds__(T, 1) fps_bucket_kernel(const float *__restric
         by = (bj & 1) ? Y.y : Y.x;
         bz = (bj & 1) ? Z.y : Z.x;
     };
-    thread_best();
+    rekey();
 
-    float sx = 0.0f, sy = 0.0f, sz = 0.0f;
-    if (actual > 0) {
-        sx = pos[3 * start];
-        sy = pos[3 * start + 1];
-        sz = pos[3 * start + 2];
-        if (rank == 0 && t == 0) emit(out, out_pos, o0, start, 0, sx, sy, sz);
-    }
     if (t == 0) {
+        if (actual > 0) {  // the first pick: the cloud's first point
+            const float x0 = pos[3 * start], y0 = pos[3 * start + 1], z0 = pos[3 * start + 2];
+            s_pick[0] = make_float4(x0, y0, z0, 0.0f);
+            if (rank == 0) emit(out, out_pos, o0, start, 0, x0, y0, z0);
+        }
+        s_count = actual > 0 ? 1 : 0;
         for (int p = 0; p < 2; ++p) asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(smem_u32(&mbar[p])));
         asm volatile("fence.mbarrier_init.release.cluster;");
     }
     cluster.sync();  // every CTA resident, its points stored and its barriers initialised
 
-    const bool exchange = cs > 1 || hold_rank >= 0;  // a lone CTA's winner is the pick
+    const bool exchange = cs > 1 || hold_rank >= 0;  // a lone CTA selects from its warps' records
     uint32_t phase = 0u;                              // bit p: parity of the next phase of mbar[p]
     int64_t k = 1;
+    int par = 0;
     bool ok = true;
-    for (; k < actual; ++k) {
-        // 1. the bucket's minima against the last pick, unless its box is too far to matter
-        const float lb = box_dist2_lb(sx, sy, sz, box);
-        if (!(lb >= __uint_as_float((uint32_t)(lkey >> 32)))) {
-            const uint64_t SX = pack2(sx, sx), SY = pack2(sy, sy), SZ = pack2(sz, sz);
-            uint64_t kk[P];  // (min-distance, P - 1 - slot), reduced as a tree: no serial chain
-#pragma unroll
-            for (int h = 0; h < PH; ++h) {
-                const float2 X = sx2[h * T + t], Y = sy2[h * T + t], Z = sz2[h * T + t];
-                float d0, d1;
-                unpack2(dist2_x2(pack2(X.x, X.y), pack2(Y.x, Y.y), pack2(Z.x, Z.y), SX, SY, SZ), d0, d1);
-                const float m0 = fminf(d0, md[2 * h]), m1 = fminf(d1, md[2 * h + 1]);
-                md[2 * h] = m0;
-                md[2 * h + 1] = m1;
-                kk[2 * h] = make_key(m0, (uint32_t)(P - 1 - 2 * h));
-                kk[2 * h + 1] = make_key(m1, (uint32_t)(P - 2 - 2 * h));
+    while (k < actual) {
+        // 1. the bucket's minima against the previous round's picks (s_pick[0, s_count)): one pass
+        // over the points per pick that some lane of the warp needs (a lane whose box is too far from
+        // the pick -- bound >= its largest minimum -- gets fminf(d, m) == m, so computing it there
+        // changes nothing)
+        {
+            const int npick = s_count;
+            const float curmax = __uint_as_float((uint32_t)(lkey >> 32));
+            uint32_t need = 0u;
+#pragma unroll 1
+            for (int i = 0; i < npick; ++i) {
+                const float4 p = s_pick[i];
+                if (!(box_dist2_lb(p.x, p.y, p.z, box) >= curmax)) need |= 1u << i;
             }
+            uint32_t wneed = __reduce_or_sync(0xffffffffu, need);
+            if (wneed) {
+#pragma unroll 1
+                while (wneed) {
+                    const int i = __ffs(wneed) - 1;
+                    wneed &= wneed - 1u;
+                    const float4 p = s_pick[i];
+                    const uint64_t SX = pack2(p.x, p.x), SY = pack2(p.y, p.y), SZ = pack2(p.z, p.z);
 #pragma unroll
-            for (int w = 1; w < P; w <<= 1)
-#pragma unroll
-                for (int j = 0; j + w < P; j += 2 * w) kk[j] = umax64(kk[j], kk[j + w]);
-            lkey = kk[0];
-            thread_best();
+                    for (int h = 0; h < PH; ++h) {
+                        const float2 X = sx2[h * T + t], Y = sy2[h * T + t], Z = sz2[h * T + t];
+                        float d0, d1;
+                        unpack2(dist2_x2(pack2(X.x, X.y), pack2(Y.x, Y.y), pack2(Z.x, Z.y), SX, SY, SZ), d0, d1);
+                        md[2 * h] = fminf(d0, md[2 * h]);
+                        md[2 * h + 1] = fminf(d1, md[2 * h + 1]);
+                    }
+                }
+                rekey();
+            }
         }
-        // 2. the warp's winner lane writes the warp's record (several lanes only when the whole
-        // warp holds key 0, which never wins)
-        const uint64_t wk = warp_max_key(bestkey);
-        const int par = (int)(k & 1);
-        if (bestkey == wk) {
-            slotA[par][warp] = make_uint4((uint32_t)wk, (uint32_t)(wk >> 32), __float_as_uint(bx), __float_as_uint(by));
-            slotZ[par][warp] = bz;
+        // 2. the warp's record: its best key and point, and a bound on its other points' keys
+        {
+            uint32_t mhi;
+            const int wl = warp_argmax_key(bestkey, mhi);
+            const uint32_t wb = __reduce_max_sync(0xffffffffu, lane == wl ? sec : (uint32_t)(bestkey >> 32));
+            if (lane == wl) {
+                slotA[warp] = make_uint4((uint32_t)bestkey, (uint32_t)(bestkey >> 32), __float_as_uint(bx),
+                                         __float_as_uint(by));
+                slotB[warp] = make_uint2(__float_as_uint(bz), wb);
+            }
         }
         __syncthreads();
-        // 3. the CTA's winner: every warp reduces the slots itself
-        const uint2 kv = lane < NW ? *reinterpret_cast<const uint2 *>(&slotA[par][lane]) : make_uint2(0u, 0u);
-        const uint64_t key = ((uint64_t)kv.y << 32) | kv.x;
-        uint64_t gk = warp_max_key(key);
-        const int cw = __ffs(__ballot_sync(0xffffffffu, key == gk)) - 1;
-        const uint4 ca = slotA[par][cw];
-        sx = __uint_as_float(ca.z);
-        sy = __uint_as_float(ca.w);
-        sz = slotZ[par][cw];
-        if (exchange) {
-            // 4. every CTA's winner to every CTA, bounded wait for the cluster's records
-            const uint32_t bar = smem_u32(&mbar[par]);
-            if (t == 0)
-                asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(cs * kRecBytes)
-                             : "memory");
-            if (warp == 0 && lane < cs && !(rank == hold_rank && k == hold_pick))
-                st_async_rec(mapa_u32(smem_u32(&recA[par * cs + rank]), lane),
-                             mapa_u32(smem_u32(&recB[par * cs + rank]), lane), mapa_u32(bar, lane), gk, sx, sy, sz);
-            const uint32_t want = (phase >> par) & 1u;
-            uint32_t done = 0;
-            for (int it = 0; it < wait_polls && !done; ++it) done = mbar_try_wait(bar, want);
-            phase ^= 1u << par;
-            if (!__all_sync(0xffffffffu, done)) {
-                ok = false;
-                break;
+        // 3. warp 0 makes the round's picks; the other warps wait at the next barrier
+        if (warp == 0) {
+            int64_t limit = actual - k;
+            if (hold_pick > k && hold_pick - k < limit) limit = hold_pick - k;  // only while a hold is set
+            // the records the picks are taken from, one per lane: a lone CTA's warp records, or the
+            // cluster's CTA records (a CTA's best and a bound on its other points: the other warps'
+            // best keys and the winning warp's bound), exchanged through st.async and a bounded wait
+            uint4 ra = make_uint4(0u, 0u, 0u, 0u);
+            uint2 rc = make_uint2(0u, 0u);
+            const uint4 *SA = slotA;
+            const uint2 *SB = slotB;
+            int S = NW;
+            bool got = true;
+            if (lane < NW) {
+                ra = slotA[lane];
+                rc = slotB[lane];
             }
-            const uint2 rk = lane < cs ? *reinterpret_cast<const uint2 *>(&recA[par * cs + lane]) : make_uint2(0u, 0u);
-            const uint64_t g = ((uint64_t)rk.y << 32) | rk.x;
-            gk = warp_max_key(g);
-            const int gi = __ffs(__ballot_sync(0xffffffffu, g == gk)) - 1;
-            const uint4 ra = recA[par * cs + gi];
-            sx = __uint_as_float(ra.z);
-            sy = __uint_as_float(ra.w);
-            sz = __uint_as_float(recB[par * cs + gi].x);
+            if (exchange) {
+                const uint64_t sk = ((uint64_t)ra.y << 32) | ra.x;
+                uint32_t mhi;
+                const int cw = warp_argmax_key(sk, mhi);
+                const uint32_t cb = __reduce_max_sync(0xffffffffu, lane == cw ? rc.y : ra.y);
+                const uint32_t bar = smem_u32(&mbar[par]);
+                if (lane == 0)
+                    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar),
+                                 "r"(cs * kRecBytes)
+                                 : "memory");
+                const uint4 w = slotA[cw];
+                const uint32_t wz = slotB[cw].x;
+                if (lane < cs && !(rank == hold_rank && k == hold_pick))
+                    st_async_rec(mapa_u32(smem_u32(&recA[par * cs + rank]), lane),
+                                 mapa_u32(smem_u32(&recB[par * cs + rank]), lane), mapa_u32(bar, lane),
+                                 ((uint64_t)w.y << 32) | w.x, __uint_as_float(w.z), __uint_as_float(w.w),
+                                 __uint_as_float(wz), cb);
+                const uint32_t want = (phase >> par) & 1u;
+                // the warp leaves the poll loop together (a lane-divergent exit would leave the warp
+                // split for the code that follows)
+                bool done = false;
+                for (int it = 0; it < wait_polls && !done; ++it) done = __all_sync(0xffffffffu, mbar_try_wait(bar, want));
+                phase ^= 1u << par;
+                got = done;
+                ra = make_uint4(0u, 0u, 0u, 0u);
+                rc = make_uint2(0u, 0u);
+                SA = recA + par * cs;
+                SB = recB + par * cs;
+                S = cs;
+                if (lane < cs) {
+                    ra = SA[lane];
+                    rc = SB[lane];
+                }
+            }
+            if (!got) {
+                if (lane == 0) s_count = -1;
+            } else {
+                // Every record's rank (how many records hold a larger key) and whether it may follow
+                // every record ahead of it within the round: its minimum survives each of them, it beats
+                // each one's bound, each of them is finite (its own distance is then 0, below this
+                // minimum, which must be > 0). The round takes the records ahead of the first that may
+                // not; the first record (rank 0) is always taken.
+                const uint64_t mk = ((uint64_t)ra.y << 32) | ra.x;
+                const float mx = __uint_as_float(ra.z), my = __uint_as_float(ra.w), mz = __uint_as_float(rc.x);
+                const uint32_t mhi = ra.y;
+                const float mmd = __uint_as_float(mhi);
+                int rnk = 0;
+                bool bad = mhi == 0u;
+#pragma unroll 4
+                for (int j = 0; j < S; ++j) {
+                    const uint4 a = SA[j];
+                    const uint2 c = SB[j];
+                    const uint64_t kj = ((uint64_t)a.y << 32) | a.x;
+                    const float xj = __uint_as_float(a.z), yj = __uint_as_float(a.w), zj = __uint_as_float(c.x);
+                    const bool ahead = kj > mk;
+                    // (bitwise: no branch per record)
+                    const bool fin = (fabsf(xj) < INFINITY) & (fabsf(yj) < INFINITY) & (fabsf(zj) < INFINITY);
+                    const bool clash = !(mhi > c.y) | !fin | (dist2(mx, my, mz, xj, yj, zj) < mmd);
+                    rnk += ahead ? 1 : 0;
+                    bad |= ahead & clash;
+                }
+                const int lim = (int64_t)M < limit ? M : (int)limit;
+                int A = __reduce_min_sync(0xffffffffu, (mk != 0ull && bad && rnk > 0) ? rnk : 32);
+                const int nrec = __popc(__ballot_sync(0xffffffffu, mk != 0ull));
+                A = A < nrec ? A : nrec;
+                A = A < lim ? A : lim;
+                if (mk != 0ull && rnk < A) {
+                    s_pick[rnk] = make_float4(mx, my, mz, 0.0f);
+                    if (rank == 0) emit(out, out_pos, o0 + k + rnk, start, fps_index(~(uint32_t)mk, TIE), mx, my, mz);
+                }
+                if (lane == 0) s_count = A;
+            }
         }
-        if (rank == 0 && t == 0) emit(out, out_pos, o0 + k, start, fps_index(~(uint32_t)gk, TIE), sx, sy, sz);
+        __syncthreads();
+        const int A = s_count;
+        if (A < 0) {
+            ok = false;
+            break;
+        }
+        k += A;
+        par ^= 1;
     }
     if (!ok) {
-        if (lane == 0 && status) atomicExch(status, (int32_t)GDL_ERR_TIMEOUT);
+        if (t == 0 && status) atomicExch(status, (int32_t)GDL_ERR_TIMEOUT);
         if (rank == 0 && warp == 0)  // mark the picks this cloud did not make
             for (int64_t j = k + lane; j < actual; j += 32) {
                 out[o0 + j] = -2;
@@ -543,20 +679,23 @@ static cudaError_t launch_cta(int B, const float *pos, const int64_t *ptr, const
 }
 
 constexpr int kCtaCapacity = 4096;            // fps_cta_kernel<256, 16>; larger clouds are bucketed
-// Bucketed launch shapes, from a sweep on a B200 (per-pick times of configuration 5's LiDAR
-// clouds and configuration 3's 8192-point level): clouds of up to 8192 points take one CTA of
-// 512 x 16, larger ones CTAs of 384 x 36 = 13824 points -- one, or a cluster (10 CTAs for 131072
-// points, a size of which 11 clusters fit on a B200 at once, so 8 LiDAR clouds run in one wave).
-// More warps lengthen every pick's exchange, more points per thread every bucket update.
+// Bucketed launch shapes, from a sweep on a B200 (configuration 5's LiDAR clouds, configuration 3's
+// 8192-point level): CTAs of 512 x 16 = 8192 points (one CTA per cloud up to 8192 points; up to 16
+// in a cluster) or of 384 x 36 = 13824 points (clusters of up to 16, 10 for a 131072-point cloud).
+// A B200 holds 11 clusters of 10 CTAs at once but only 7 of 11-16, so eight LiDAR clouds run in
+// one wave only as 10-CTA clusters, while up to seven take the 16-CTA shape, whose smaller buckets
+// update faster. The launch takes the shape that needs fewer waves of clusters, the smaller
+// buckets on a tie.
 constexpr int kSmallT = 512, kSmallP = 16;
 constexpr int kBigT = 384, kBigP = 36;
+constexpr int64_t kSmallCapacity = (int64_t)kSmallT * kSmallP;
 constexpr int64_t kBucketCapacity = (int64_t)kBigT * kBigP;
+constexpr int kMaxDevices = 64;
 
-template <int T, int P, int TIE>
-static cudaError_t launch_bucket(int B, int cs, const float *pos, const int32_t *order, const int64_t *ptr,
-                                 const int64_t *kpc, int64_t *out, float *out_pos, int32_t *status, int polls,
-                                 int hold_rank, int64_t hold_pick, cudaStream_t st) {
-    auto kern = fps_bucket_kernel<T, P, TIE>;
+// launch configuration of the bucketed kernel for B clouds on clusters of cs CTAs
+template <int T, int P, int TIE, int M>
+static cudaError_t bucket_config(int B, int cs, cudaStream_t st, cudaLaunchConfig_t &cfg, cudaLaunchAttribute &attr) {
+    auto kern = fps_bucket_kernel<T, P, TIE, M>;
     const size_t smem = bucket_smem_bytes(T, P, cs);
     if (cs < 1 || cs > kMaxCluster || smem > (size_t)kMaxDynSmem) return cudaErrorInvalidConfiguration;
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
@@ -565,33 +704,66 @@ static cudaError_t launch_bucket(int B, int cs, const float *pos, const int32_t 
         e = cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
         if (e != cudaSuccess) return e;
     }
-    cudaLaunchConfig_t cfg = {};
+    cfg = {};
     cfg.gridDim = dim3((unsigned)(B * cs));
     cfg.blockDim = dim3(T);
     cfg.dynamicSmemBytes = smem;
     cfg.stream = st;
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeClusterDimension;
-    attr[0].val.clusterDim.x = (unsigned)cs;
-    attr[0].val.clusterDim.y = 1;
-    attr[0].val.clusterDim.z = 1;
-    cfg.attrs = attr;
+    attr.id = cudaLaunchAttributeClusterDimension;
+    attr.val.clusterDim.x = (unsigned)cs;
+    attr.val.clusterDim.y = 1;
+    attr.val.clusterDim.z = 1;
+    cfg.attrs = &attr;
     cfg.numAttrs = 1;
-    int max_clusters = 0;
-    e = cudaOccupancyMaxActiveClusters(&max_clusters, kern, &cfg);
-    if (e != cudaSuccess || max_clusters < 1) return e != cudaSuccess ? e : cudaErrorInvalidConfiguration;
-    return cudaLaunchKernelEx(&cfg, kern, pos, order, ptr, kpc, out, out_pos, status, polls, hold_rank, hold_pick);
+    return cudaSuccess;
 }
 
-template <int T, int P>
+// clusters of cs CTAs of this shape resident at once on the current device (0: none), cached
+template <int T, int P, int TIE, int M>
+static int bucket_max_clusters(int cs) {
+    static int cache[kMaxDevices][kMaxCluster + 1];  // 0: not asked yet; -1: none fit
+    int dev = 0;
+    if (cs < 1 || cs > kMaxCluster || cudaGetDevice(&dev) != cudaSuccess) return 0;
+    if (dev >= 0 && dev < kMaxDevices && cache[dev][cs] != 0) return cache[dev][cs] > 0 ? cache[dev][cs] : 0;
+    cudaLaunchConfig_t cfg;
+    cudaLaunchAttribute attr;
+    int mc = 0;
+    if (bucket_config<T, P, TIE, M>(1, cs, 0, cfg, attr) != cudaSuccess ||
+        cudaOccupancyMaxActiveClusters(&mc, fps_bucket_kernel<T, P, TIE, M>, &cfg) != cudaSuccess)
+        mc = 0;
+    (void)cudaGetLastError();
+    if (dev >= 0 && dev < kMaxDevices) cache[dev][cs] = mc > 0 ? mc : -1;
+    return mc > 0 ? mc : 0;
+}
+
+template <int T, int P, int TIE, int M>
+static cudaError_t launch_bucket(int B, int cs, const float *pos, const int32_t *order, const int64_t *ptr,
+                                 const int64_t *kpc, int64_t *out, float *out_pos, int32_t *status, int polls,
+                                 int hold_rank, int64_t hold_pick, cudaStream_t st) {
+    if (bucket_max_clusters<T, P, TIE, M>(cs) < 1) return cudaErrorInvalidConfiguration;
+    cudaLaunchConfig_t cfg;
+    cudaLaunchAttribute attr;
+    cudaError_t e = bucket_config<T, P, TIE, M>(B, cs, st, cfg, attr);
+    if (e != cudaSuccess) return e;
+    return cudaLaunchKernelEx(&cfg, fps_bucket_kernel<T, P, TIE, M>, pos, order, ptr, kpc, out, out_pos, status, polls,
+                              hold_rank, hold_pick);
+}
+
+template <int T, int P, int M>
 static cudaError_t launch_bucket_tie(int tie, int B, int cs, const float *pos, const int32_t *order,
                                      const int64_t *ptr, const int64_t *kpc, int64_t *out, float *out_pos,
                                      int32_t *status, int polls, int hold_rank, int64_t hold_pick, cudaStream_t st) {
     return tie == GDL_TIE_LOWEST_INDEX
-               ? launch_bucket<T, P, GDL_TIE_LOWEST_INDEX>(B, cs, pos, order, ptr, kpc, out, out_pos, status,
+               ? launch_bucket<T, P, GDL_TIE_LOWEST_INDEX, M>(B, cs, pos, order, ptr, kpc, out, out_pos, status,
                                                                polls, hold_rank, hold_pick, st)
-               : launch_bucket<T, P, GDL_TIE_REFERENCE>(B, cs, pos, order, ptr, kpc, out, out_pos, status, polls,
+               : launch_bucket<T, P, GDL_TIE_REFERENCE, M>(B, cs, pos, order, ptr, kpc, out, out_pos, status, polls,
                                                             hold_rank, hold_pick, st);
+}
+
+template <int T, int P, int M>
+static int bucket_max_clusters_tie(int tie, int cs) {
+    return tie == GDL_TIE_LOWEST_INDEX ? bucket_max_clusters<T, P, GDL_TIE_LOWEST_INDEX, M>(cs)
+                                       : bucket_max_clusters<T, P, GDL_TIE_REFERENCE, M>(cs);
 }
 
 // Workspace of the bucketed path: cloud boxes, Morton keys, sorted keys, the order, radix scratch.
@@ -658,7 +830,18 @@ extern "C" int gdl_fps_ex(const float *pos, const int64_t *ptr, const int64_t *k
                       GDL_ERR_WORKSPACE);
         FpsWork w;
         fps_carve((char *)workspace, n_points, num_clouds, &w);
-        const int cs = (int)((m + kBucketCapacity - 1) / kBucketCapacity);
+        // the shape: 512 x 16 CTAs (clusters of up to 16) or 384 x 36 (clusters of up to 16), whichever
+        // needs fewer waves of clusters for these clouds, the smaller buckets on a tie
+        const int cs_s = (int)((m + kSmallCapacity - 1) / kSmallCapacity);
+        const int cs_b = (int)((m + kBucketCapacity - 1) / kBucketCapacity);
+        bool small = cs_s == 1;
+        if (!small && cs_s <= kMaxCluster) {
+            const int mcs = bucket_max_clusters_tie<kSmallT, kSmallP, kRoundPicks>(tie_break, cs_s);
+            const int mcb =
+                cs_b <= kMaxCluster ? bucket_max_clusters_tie<kBigT, kBigP, kRoundPicks>(tie_break, cs_b) : 0;
+            small = mcs > 0 && (mcb <= 0 || (num_clouds + mcs - 1) / mcs <= (num_clouds + mcb - 1) / mcb);
+        }
+        const int cs = small ? cs_s : cs_b;
         e = cudaErrorInvalidConfiguration;
         if (cs <= kMaxCluster) {
             // Morton order of every cloud (the buckets), then the bucketed kernel
@@ -669,14 +852,14 @@ extern "C" int gdl_fps_ex(const float *pos, const int64_t *ptr, const int64_t *k
             GDL_CUDA_TRY(cudaGetLastError());
             GDL_CUDA_TRY(radix_sort_pairs(w.keys, nullptr, w.sorted_keys, w.order, n_points, ptr, num_clouds, 4,
                                           nullptr, w.rs, st));
-            if (m <= (int64_t)kSmallT * kSmallP)
-                e = launch_bucket_tie<kSmallT, kSmallP>(tie_break, num_clouds, 1, pos, w.order, ptr,
-                                                                  k_per_cloud, out_idx, out_pos, status, polls,
-                                                                  hold_rank, hold_pick, st);
+            if (small)
+                e = launch_bucket_tie<kSmallT, kSmallP, kRoundPicks>(tie_break, num_clouds, cs, pos, w.order, ptr,
+                                                                     k_per_cloud, out_idx, out_pos, status, polls,
+                                                                     hold_rank, hold_pick, st);
             else
-                e = launch_bucket_tie<kBigT, kBigP>(tie_break, num_clouds, cs, pos, w.order, ptr, k_per_cloud,
-                                                            out_idx, out_pos, status, polls, hold_rank, hold_pick,
-                                                            st);
+                e = launch_bucket_tie<kBigT, kBigP, kRoundPicks>(tie_break, num_clouds, cs, pos, w.order, ptr,
+                                                                 k_per_cloud, out_idx, out_pos, status, polls,
+                                                                 hold_rank, hold_pick, st);
         }
         if (e != cudaSuccess) {
             (void)cudaGetLastError();  // clear a refused cluster launch, use the streaming kernel
