@@ -162,6 +162,9 @@ class C2:
     def fps_chain_picks(self):
         return self.K
 
+    def fps_chain_rounds(self):
+        return fps_rounds(self.ws_fps, self.n_points, self.B, self.N, self.K)
+
     def step(self):
         for _, fn in self.stage_list():
             fn()
@@ -298,6 +301,9 @@ class C1:
 
     def fps_chain_picks(self):
         return self.K
+
+    def fps_chain_rounds(self):
+        return fps_rounds(self.ws_fps, self.n_points, self.B, self.N, self.K)
 
     def knn_pairs(self):
         return self.B * self.K * self.N
@@ -456,6 +462,10 @@ class C3:
 
     def fps_chain_picks(self):
         return sum(self.LEVELS)
+
+    def fps_chain_rounds(self):
+        sz = self._sizes()
+        return sum(fps_rounds(self.ws_fps[l], self.B * sz[l], self.B, sz[l], self.LEVELS[l]) for l in range(3))
 
     def knn_pairs(self):
         sz = self._sizes()
@@ -989,6 +999,9 @@ class C5:
     def fps_chain_picks(self):
         return self.K
 
+    def fps_chain_rounds(self):
+        return fps_rounds(self.ws_fps, self.n_points, self.B, self.N, self.K)
+
     def knn_pairs(self):  # the hybrid graph's self-KNN over the centroids
         return self.B * self.K * self.K
 
@@ -1444,13 +1457,14 @@ class ClockSampler:
 
 
 ROOFLINE_NOTES = {
-    "fps": "FPS is a serial chain of picks per cloud (one argmax over the cloud per pick). Its bound is "
-           "the per-pick latency: `peak` is the per-pick time of the same kernel and launch shape on "
-           "clouds of duplicated points (no minimum changes after the first pick, so only the "
-           "warp/CTA/cluster exchange chain runs); the rest of `achieved` is the bucket updates. "
-           "HBM is irrelevant (the points are read once).",
-    "fps_chain": "see fps: the three levels' chains run back to back; `peak` is the same chain on "
-                 "duplicated points",
+    "fps": "FPS is a serial chain of picks per cloud. The bucketed kernel makes them in exchange rounds "
+           "of up to 12 exact picks (about 5-6 on LiDAR clouds); its bound is the latency of those "
+           "rounds: `peak` is the time per pick of a chain with this run's exchange rounds and nothing "
+           "to update (the per-round time of the same kernel and launch shape on clouds of duplicated "
+           "points, where every round makes one pick, times `exchange_rounds`, per pick); the rest of "
+           "`achieved` is the bucket updates. HBM is irrelevant (the points are read once).",
+    "fps_chain": "see fps: the three levels' chains run back to back (the two small levels one pick per "
+                 "exchange); `peak` uses the chain's mean per-round time on duplicated points",
     "knn": "the distance scan runs on the FP32 pipe (8 flops per evaluated distance, packed fp32x2); "
            "`peak` is the packed-FMA throughput measured in this run (gdl_fp32_peak); `achieved` counts "
            "the distances the kernels evaluated (gdl_knn_distance_count): clouds of 4097-32767 sources "
@@ -1482,6 +1496,16 @@ def ncu_traffic(config, stage):
     if not p.exists():
         return None
     return json.loads(p.read_text()).get(config, {}).get(stage)
+
+
+def fps_rounds(ws, n_points, B, max_cloud_points, picks):
+    """Exchange rounds of the last FPS call on this workspace for its longest cloud: the bucketed
+    kernel's counter (gdl_fps_round_count), or one round per pick for clouds of <= 4096 points."""
+    L = nat.load()
+    out = ctypes.c_ulonglong(0)
+    nat.check(L.gdl_fps_round_count(ws.data_ptr(), n_points, B, max_cloud_points, ctypes.byref(out)),
+              "gdl_fps_round_count")
+    return int(out.value) if out.value else max(picks - 1, 0)
 
 
 def knn_distances(ws, n_q, B, k, max_src):
@@ -1661,12 +1685,22 @@ def roofline_of(cfg, timed, stage_ms, E, peaks):
     bound = STAGE_BOUND.get(dom, "hbm")
     r = {"kernel": dom, "bound": bound, "note": ROOFLINE_NOTES.get(dom, "")}
     if bound == "latency":
+        # The FPS chain is a sequence of exchange rounds (up to 12 exact picks each in the bucketed
+        # kernel, one in the small-cloud kernel); its floor is the same number of rounds with
+        # nothing to update: the time per round of the stage on duplicated points (one pick per
+        # round there) times this run's round count.
         picks = cfg.fps_chain_picks()
+        timed.stage_time(dom)
+        rounds = cfg.fps_chain_rounds()
         floor = fps_floor_ms(timed, dom)
-        ach, pk = 1000 * stage_ms[dom] / picks, 1000 * floor / picks
+        dup_rounds = cfg.fps_chain_rounds()
+        floor_round_us = 1000 * floor / max(dup_rounds, 1)
+        ach, pk = 1000 * stage_ms[dom] / picks, floor_round_us * rounds / picks
         r.update({"unit": "us/pick", "achieved": ach, "peak": pk, "frac": pk / ach,
-                  "picks_per_cloud_chain": picks,
-                  "peak_source": "measured in this run: the same stage on duplicated points (exchange chain only)",
+                  "picks_per_cloud_chain": picks, "exchange_rounds": rounds,
+                  "picks_per_round": picks / max(rounds, 1), "floor_us_per_round": floor_round_us,
+                  "peak_source": ("measured in this run: the exchange-only time per round (the same stage on "
+                                  "duplicated points, one pick per round) x this run's exchange rounds"),
                   "traffic": ncu_traffic(cfg.name, dom)})
     elif bound == "fp32":
         pairs = cfg.knn_pairs()

@@ -45,6 +45,7 @@ PROTOTYPES = {
     "gdl_fps_workspace_size": (_SZ, [_I64, _I32, _I64]),
     "gdl_fps": (ctypes.c_int, [_P, _P, _P, _I32, _I64, _I64, _I32, _P, _P, _P, _SZ, _P]),
     "gdl_fps_ex": (ctypes.c_int, [_P, _P, _P, _I32, _I64, _I64, _I32, _P, _P, _P, _SZ, _P, _I32, _I32, _I64, _P]),
+    "gdl_fps_round_count": (ctypes.c_int, [_P, _I64, _I32, _I64, _P]),
     "gdl_knn_workspace_size": (_SZ, [_I64, _I32, _I32, _I64]),
     "gdl_knn_distance_count": (ctypes.c_int, [_P, _I64, _I32, _I32, _I64, ctypes.POINTER(ctypes.c_ulonglong)]),
     "gdl_knn": (ctypes.c_int, [_P, _P, _P, _P, _I32, _I64, _I32, _I64, _P, _P, _P, _SZ, _P]),

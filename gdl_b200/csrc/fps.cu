@@ -221,12 +221,18 @@ constexpr int kMaxCluster = 16;
 constexpr int kDefaultWaitPolls = 1 << 20;   // mbarrier polls before a wait gives up
 constexpr int kMaxDynSmem = 227 * 1024;
 constexpr int kRecBytes = 24;                // one record: key, x, y (16-B store) + z, bound (8-B store)
-constexpr int kRoundPicks = 8;               // picks one round may make
+constexpr int kCtaRecords = 2;               // records a CTA of a cluster sends per round
+// A record's bound: the largest minimum (float bits, >= 0) among the points it stands for other
+// than its own, with the top bit set when its own coordinates are not finite (its distance to
+// itself is then NaN, not 0, so no pick may follow it in the same round); either way, a later
+// pick's minimum bits must exceed the bound.
+constexpr uint32_t kNonFinite = 0x80000000u;
+constexpr int kRoundPicks = 12;              // picks one round may make
 
 __host__ __device__ constexpr size_t bucket_points_bytes(int T, int P) { return (size_t)16 * T * P; }
 // records per round: one per CTA of the cluster, double-buffered
 __host__ __device__ constexpr size_t bucket_smem_bytes(int T, int P, int cs) {
-    return bucket_points_bytes(T, P) + (size_t)2 * cs * kRecBytes;
+    return bucket_points_bytes(T, P) + (size_t)2 * kCtaRecords * cs * kRecBytes;
 }
 
 __device__ __forceinline__ uint32_t smem_u32(const void *p) { return (uint32_t)__cvta_generic_to_shared(p); }
@@ -310,7 +316,8 @@ __device__ __forceinline__ float pair_dist2(float px, float py, float pz, float 
 // that one on are then -2 (coordinates 0). hold_rank / hold_pick: the CTA of that rank in every
 // cluster sends no records in the round that starts at that pick (rounds never cross it while a
 // hold is set), which makes every wait of the round run out (the failure path's test); -1
-// disables it. A lone CTA never waits, unless hold_rank asks it to exchange.
+// disables it. A lone CTA never waits, unless hold_rank asks it to exchange. rounds (nullable):
+// the largest number of exchange rounds any cloud took (atomicMax), for the latency roofline.
 template <int T, int P, int TIE, int M>
 __global__ void __launch_bounds__(T, 1) fps_bucket_kernel(const float *__restrict__ pos,
                                                            const int32_t *__restrict__ order,
@@ -318,10 +325,11 @@ __global__ void __launch_bounds__(T, 1) fps_bucket_kernel(const float *__restric
                                                            const int64_t *__restrict__ kpc,
                                                            int64_t *__restrict__ out, float *__restrict__ out_pos,
                                                            int32_t *__restrict__ status, int wait_polls,
-                                                           int hold_rank, int64_t hold_pick) {
+                                                           int hold_rank, int64_t hold_pick,
+                                                           unsigned long long *__restrict__ rounds) {
     constexpr int NW = T / 32, PH = P / 2;
     static_assert(P % 2 == 0, "points are held in pairs");
-    constexpr int kMaxRecords = NW > kMaxCluster ? NW : kMaxCluster;  // records a round selects from
+    constexpr int kMaxRecords = NW > kCtaRecords * kMaxCluster ? NW : kCtaRecords * kMaxCluster;  // per round
     static_assert(M >= 1 && M <= 32 && kMaxRecords <= 32, "one record and one pick per lane");
     extern __shared__ __align__(16) unsigned char smem[];
     __shared__ __align__(8) unsigned long long mbar[2];
@@ -338,8 +346,9 @@ __global__ void __launch_bounds__(T, 1) fps_bucket_kernel(const float *__restric
     cg::cluster_group cluster = cg::this_cluster();
     const int cs = (int)cluster.num_blocks();
     const int rank = (int)cluster.block_rank();
-    uint4 *recA = reinterpret_cast<uint4 *>(smem + bucket_points_bytes(T, P));  // [2][cs]: key, x, y
-    uint2 *recB = reinterpret_cast<uint2 *>(recA + 2 * cs);                     // [2][cs]: z, bound
+    const int RC = kCtaRecords * cs;                                             // records per round
+    uint4 *recA = reinterpret_cast<uint4 *>(smem + bucket_points_bytes(T, P));  // [2][RC]: key, x, y
+    uint2 *recB = reinterpret_cast<uint2 *>(recA + 2 * RC);                     // [2][RC]: z, bound
 
     const int b = blockIdx.x / cs;
     const int64_t start = ptr[b];
@@ -461,7 +470,9 @@ __global__ void __launch_bounds__(T, 1) fps_bucket_kernel(const float *__restric
     int64_t k = 1;
     int par = 0;
     bool ok = true;
+    unsigned long long nround = 0;
     while (k < actual) {
+        ++nround;
         // 1. the bucket's minima against the previous round's picks (s_pick[0, s_count)): one pass
         // over the points per pick that some lane of the warp needs (a lane whose box is too far from
         // the pick -- bound >= its largest minimum -- gets fminf(d, m) == m, so computing it there
@@ -501,9 +512,10 @@ __global__ void __launch_bounds__(T, 1) fps_bucket_kernel(const float *__restric
             const int wl = warp_argmax_key(bestkey, mhi);
             const uint32_t wb = __reduce_max_sync(0xffffffffu, lane == wl ? sec : (uint32_t)(bestkey >> 32));
             if (lane == wl) {
+                const bool fin = fabsf(bx) < INFINITY && fabsf(by) < INFINITY && fabsf(bz) < INFINITY;
                 slotA[warp] = make_uint4((uint32_t)bestkey, (uint32_t)(bestkey >> 32), __float_as_uint(bx),
                                          __float_as_uint(by));
-                slotB[warp] = make_uint2(__float_as_uint(bz), wb);
+                slotB[warp] = make_uint2(__float_as_uint(bz), wb | (fin ? 0u : kNonFinite));
             }
         }
         __syncthreads();
@@ -525,35 +537,46 @@ __global__ void __launch_bounds__(T, 1) fps_bucket_kernel(const float *__restric
                 rc = slotB[lane];
             }
             if (exchange) {
+                // the CTA's two best warp records: the first keeps its warp's bound, the second's also
+                // covers the CTA's other warps (their best keys)
+                static_assert(kCtaRecords == 2, "two records per CTA");
                 const uint64_t sk = ((uint64_t)ra.y << 32) | ra.x;
                 uint32_t mhi;
-                const int cw = warp_argmax_key(sk, mhi);
-                const uint32_t cb = __reduce_max_sync(0xffffffffu, lane == cw ? rc.y : ra.y);
+                const int w1 = warp_argmax_key(sk, mhi);
+                const int w2 = warp_argmax_key(lane == w1 ? 0ull : sk, mhi);
+                const uint32_t rest = __reduce_max_sync(0xffffffffu, (lane == w1 || lane == w2) ? 0u : ra.y);
                 const uint32_t bar = smem_u32(&mbar[par]);
                 if (lane == 0)
                     asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar),
-                                 "r"(cs * kRecBytes)
+                                 "r"(RC * kRecBytes)
                                  : "memory");
-                const uint4 w = slotA[cw];
-                const uint32_t wz = slotB[cw].x;
-                if (lane < cs && !(rank == hold_rank && k == hold_pick))
-                    st_async_rec(mapa_u32(smem_u32(&recA[par * cs + rank]), lane),
-                                 mapa_u32(smem_u32(&recB[par * cs + rank]), lane), mapa_u32(bar, lane),
-                                 ((uint64_t)w.y << 32) | w.x, __uint_as_float(w.z), __uint_as_float(w.w),
-                                 __uint_as_float(wz), cb);
+                // lane r * cs + d sends record r to CTA d (a CTA with one non-empty warp has no second
+                // record: the second argmax then ties among empty keys and may return the first warp)
+                const int which = lane >= cs ? 1 : 0, dst = lane - which * cs, wsrc = which ? w2 : w1;
+                const bool empty = which && w2 == w1;
+                uint4 w = slotA[wsrc];
+                const uint2 wz = slotB[wsrc];
+                if (empty) w = make_uint4(0u, 0u, 0u, 0u);
+                const uint32_t wbnd = empty ? 0u : which ? (wz.y > rest ? wz.y : rest) : wz.y;
+                const int slot = par * RC + kCtaRecords * rank + which;
+                if (lane < RC && !(rank == hold_rank && k == hold_pick))
+                    st_async_rec(mapa_u32(smem_u32(&recA[slot]), dst), mapa_u32(smem_u32(&recB[slot]), dst),
+                                 mapa_u32(bar, dst), ((uint64_t)w.y << 32) | w.x, __uint_as_float(w.z),
+                                 __uint_as_float(w.w), __uint_as_float(wz.x), wbnd);
                 const uint32_t want = (phase >> par) & 1u;
                 // the warp leaves the poll loop together (a lane-divergent exit would leave the warp
                 // split for the code that follows)
                 bool done = false;
-                for (int it = 0; it < wait_polls && !done; ++it) done = __all_sync(0xffffffffu, mbar_try_wait(bar, want));
+                for (int it = 0; it < wait_polls && !done; ++it)
+                    done = __all_sync(0xffffffffu, mbar_try_wait(bar, want));
                 phase ^= 1u << par;
                 got = done;
                 ra = make_uint4(0u, 0u, 0u, 0u);
                 rc = make_uint2(0u, 0u);
-                SA = recA + par * cs;
-                SB = recB + par * cs;
-                S = cs;
-                if (lane < cs) {
+                SA = recA + par * RC;
+                SB = recB + par * RC;
+                S = RC;
+                if (lane < RC) {
                     ra = SA[lane];
                     rc = SB[lane];
                 }
@@ -562,10 +585,11 @@ __global__ void __launch_bounds__(T, 1) fps_bucket_kernel(const float *__restric
                 if (lane == 0) s_count = -1;
             } else {
                 // Every record's rank (how many records hold a larger key) and whether it may follow
-                // every record ahead of it within the round: its minimum survives each of them, it beats
-                // each one's bound, each of them is finite (its own distance is then 0, below this
-                // minimum, which must be > 0). The round takes the records ahead of the first that may
-                // not; the first record (rank 0) is always taken.
+                // every record ahead of it within the round: its minimum survives each of them and
+                // exceeds each one's bound (which also rules out a non-finite record ahead: its own
+                // distance is NaN, not 0, and would keep its key), and is > 0 (a taken record's minimum
+                // drops to 0). The round takes the records ahead of the first that may not; the first
+                // record (rank 0) is always taken.
                 const uint64_t mk = ((uint64_t)ra.y << 32) | ra.x;
                 const float mx = __uint_as_float(ra.z), my = __uint_as_float(ra.w), mz = __uint_as_float(rc.x);
                 const uint32_t mhi = ra.y;
@@ -579,9 +603,8 @@ __global__ void __launch_bounds__(T, 1) fps_bucket_kernel(const float *__restric
                     const uint64_t kj = ((uint64_t)a.y << 32) | a.x;
                     const float xj = __uint_as_float(a.z), yj = __uint_as_float(a.w), zj = __uint_as_float(c.x);
                     const bool ahead = kj > mk;
-                    // (bitwise: no branch per record)
-                    const bool fin = (fabsf(xj) < INFINITY) & (fabsf(yj) < INFINITY) & (fabsf(zj) < INFINITY);
-                    const bool clash = !(mhi > c.y) | !fin | (dist2(mx, my, mz, xj, yj, zj) < mmd);
+                    // (bitwise: no branch per record; a non-finite record's bound exceeds every minimum)
+                    const bool clash = !(mhi > c.y) | (dist2(mx, my, mz, xj, yj, zj) < mmd);
                     rnk += ahead ? 1 : 0;
                     bad |= ahead & clash;
                 }
@@ -614,6 +637,7 @@ __global__ void __launch_bounds__(T, 1) fps_bucket_kernel(const float *__restric
                 if (out_pos) out_pos[3 * (o0 + j)] = out_pos[3 * (o0 + j) + 1] = out_pos[3 * (o0 + j) + 2] = 0.0f;
             }
     }
+    if (rounds && rank == 0 && t == 0) atomicMax(rounds, nround);
     cluster.sync();  // no CTA leaves while a peer may still write into it
 }
 
@@ -739,25 +763,26 @@ static int bucket_max_clusters(int cs) {
 template <int T, int P, int TIE, int M>
 static cudaError_t launch_bucket(int B, int cs, const float *pos, const int32_t *order, const int64_t *ptr,
                                  const int64_t *kpc, int64_t *out, float *out_pos, int32_t *status, int polls,
-                                 int hold_rank, int64_t hold_pick, cudaStream_t st) {
+                                 int hold_rank, int64_t hold_pick, unsigned long long *rounds, cudaStream_t st) {
     if (bucket_max_clusters<T, P, TIE, M>(cs) < 1) return cudaErrorInvalidConfiguration;
     cudaLaunchConfig_t cfg;
     cudaLaunchAttribute attr;
     cudaError_t e = bucket_config<T, P, TIE, M>(B, cs, st, cfg, attr);
     if (e != cudaSuccess) return e;
     return cudaLaunchKernelEx(&cfg, fps_bucket_kernel<T, P, TIE, M>, pos, order, ptr, kpc, out, out_pos, status, polls,
-                              hold_rank, hold_pick);
+                              hold_rank, hold_pick, rounds);
 }
 
 template <int T, int P, int M>
 static cudaError_t launch_bucket_tie(int tie, int B, int cs, const float *pos, const int32_t *order,
                                      const int64_t *ptr, const int64_t *kpc, int64_t *out, float *out_pos,
-                                     int32_t *status, int polls, int hold_rank, int64_t hold_pick, cudaStream_t st) {
+                                     int32_t *status, int polls, int hold_rank, int64_t hold_pick,
+                                     unsigned long long *rounds, cudaStream_t st) {
     return tie == GDL_TIE_LOWEST_INDEX
                ? launch_bucket<T, P, GDL_TIE_LOWEST_INDEX, M>(B, cs, pos, order, ptr, kpc, out, out_pos, status,
-                                                               polls, hold_rank, hold_pick, st)
+                                                               polls, hold_rank, hold_pick, rounds, st)
                : launch_bucket<T, P, GDL_TIE_REFERENCE, M>(B, cs, pos, order, ptr, kpc, out, out_pos, status, polls,
-                                                            hold_rank, hold_pick, st);
+                                                            hold_rank, hold_pick, rounds, st);
 }
 
 template <int T, int P, int M>
@@ -768,6 +793,7 @@ static int bucket_max_clusters_tie(int tie, int cs) {
 
 // Workspace of the bucketed path: cloud boxes, Morton keys, sorted keys, the order, radix scratch.
 struct FpsWork {
+    unsigned long long *rounds;  // exchange rounds of the last bucketed launch (its longest cloud)
     float *box;
     uint32_t *keys, *sorted_keys;
     int32_t *order;
@@ -782,12 +808,14 @@ static size_t fps_carve(char *base, int64_t n, int32_t B, FpsWork *w) {
         return r;
     };
     const int64_t nn = n > 0 ? n : 1;
+    char *rounds = take(sizeof(unsigned long long));
     char *box = take(sizeof(float) * 6 * (size_t)(B > 0 ? B : 1));
     char *keys = take(sizeof(uint32_t) * nn);
     char *skeys = take(sizeof(uint32_t) * nn);
     char *ord = take(sizeof(int32_t) * nn);
     char *rb = take(radix_scratch_bytes(nn, B > 0 ? B : 1));
     if (base) {
+        w->rounds = (unsigned long long *)rounds;
         w->box = (float *)box;
         w->keys = (uint32_t *)keys;
         w->sorted_keys = (uint32_t *)skeys;
@@ -806,6 +834,18 @@ extern "C" size_t gdl_fps_workspace_size(int64_t n_points, int32_t num_clouds, i
     FpsWork w;
     // (the streaming fallback keeps its n floats of running minima in the keys region)
     return fps_carve(nullptr, n_points, num_clouds, &w);
+}
+
+extern "C" int gdl_fps_round_count(const void *workspace, int64_t n_points, int32_t num_clouds,
+                                   int64_t max_cloud_points, unsigned long long *out) {
+    GDL_RETURN_IF(!out || num_clouds < 0 || n_points < 0, GDL_ERR_INVALID);
+    *out = 0;
+    if (max_cloud_points <= kCtaCapacity || n_points <= 0) return GDL_OK;  // one pick per exchange
+    GDL_RETURN_IF(!workspace, GDL_ERR_INVALID);
+    FpsWork w;
+    fps_carve((char *)workspace, n_points, num_clouds, &w);
+    GDL_CUDA_TRY(cudaMemcpy(out, w.rounds, sizeof(unsigned long long), cudaMemcpyDeviceToHost));
+    return GDL_OK;
 }
 
 extern "C" int gdl_fps_ex(const float *pos, const int64_t *ptr, const int64_t *k_per_cloud, int32_t num_clouds,
@@ -845,6 +885,7 @@ extern "C" int gdl_fps_ex(const float *pos, const int64_t *ptr, const int64_t *k
         e = cudaErrorInvalidConfiguration;
         if (cs <= kMaxCluster) {
             // Morton order of every cloud (the buckets), then the bucketed kernel
+            GDL_CUDA_TRY(cudaMemsetAsync(w.rounds, 0, sizeof(unsigned long long), st));
             cloud_box_kernel<<<num_clouds, kBoxThreads, 0, st>>>(pos, ptr, w.box, nullptr);
             const int64_t blocks = (n_points + 255) / 256;
             morton_code_kernel<<<(unsigned)(blocks < 4 * kSmCount ? (blocks > 0 ? blocks : 1) : 4 * kSmCount), 256, 0,
@@ -855,11 +896,11 @@ extern "C" int gdl_fps_ex(const float *pos, const int64_t *ptr, const int64_t *k
             if (small)
                 e = launch_bucket_tie<kSmallT, kSmallP, kRoundPicks>(tie_break, num_clouds, cs, pos, w.order, ptr,
                                                                      k_per_cloud, out_idx, out_pos, status, polls,
-                                                                     hold_rank, hold_pick, st);
+                                                                     hold_rank, hold_pick, w.rounds, st);
             else
                 e = launch_bucket_tie<kBigT, kBigP, kRoundPicks>(tie_break, num_clouds, cs, pos, w.order, ptr,
                                                                  k_per_cloud, out_idx, out_pos, status, polls,
-                                                                 hold_rank, hold_pick, st);
+                                                                 hold_rank, hold_pick, w.rounds, st);
         }
         if (e != cudaSuccess) {
             (void)cudaGetLastError();  // clear a refused cluster launch, use the streaming kernel

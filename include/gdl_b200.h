@@ -72,15 +72,16 @@ int gdl_fp32_peak(float *out, int64_t iters, int32_t packed, int32_t blocks, voi
  * max_cloud_points  host-side upper bound of max_b n_b. It selects the kernel variant: one CTA
  *              per cloud with the points in registers up to 4096 points; above that the clouds
  *              are put in Morton order (in the workspace) and run bucketed, one CTA of up to 8192
- *              or 13824 points or a thread-block cluster of up to 16 CTAs of 13824 points (up to
- *              221184); beyond that, or if the device refuses the cluster, a streaming CTA that
- *              keeps the running minima in the workspace.
+ *              points or a thread-block cluster of up to 16 CTAs of 8192 or 13824 points (up to
+ *              221184; the shape that needs fewer waves of resident clusters for num_clouds), in
+ *              exact rounds of up to 12 picks; beyond that, or if the device refuses the cluster,
+ *              a streaming CTA that keeps the running minima in the workspace.
  * tie_break    GDL_TIE_REFERENCE: the reference kernel's argmax reduction order
  *              (bit-identical to fps_kernel<512>); GDL_TIE_LOWEST_INDEX: torch.argmax.
  * out_pos      [same slots, 3] f32 (nullable): coordinates of each pick (0 for padding), which
  *              saves the caller a gather of pos[out_idx].
  * Seed is the first point of each cloud; distances use the reference's rounding.
- * The bucketed kernel's CTAs (a cluster's, or one CTA's warps) exchange each pick's winners
+ * The bucketed kernel's CTAs (a cluster's, or one CTA's warps) exchange each round's records
  * through shared-memory barriers with a bounded wait; a wait that gives up (never observed)
  * writes -2 into the cloud's remaining picks (coordinates 0) -- gdl_fps_ex also reports it.
  */
@@ -101,6 +102,13 @@ int gdl_fps_ex(const float *pos, const int64_t *ptr, const int64_t *k_per_cloud,
                int64_t n_points, int64_t max_cloud_points, int32_t tie_break, int64_t *out_idx, float *out_pos,
                void *workspace, size_t workspace_bytes, int32_t *status, int32_t wait_polls, int32_t hold_rank,
                int64_t hold_pick, void *stream);
+
+/* Exchange rounds the last bucketed gdl_fps / gdl_fps_ex call on this workspace took for its
+ * longest cloud, read back synchronously into *out (host); 0 for clouds of <= 4096 points, whose
+ * kernel makes one pick per exchange. For rooflines: the picks per round, and the round count a
+ * pure exchange chain would need. No counterpart in the reference. */
+int gdl_fps_round_count(const void *workspace, int64_t n_points, int32_t num_clouds, int64_t max_cloud_points,
+                        unsigned long long *out);
 
 /* ------------------------------------------------------------------------------ KNN
  * Replaces knn_cuda(query, source, ptr_q, ptr_s, k) and knn_self_cuda(points, ptr, k)
