@@ -60,7 +60,7 @@ def fps_available() -> bool:
 
 # --------------------------------------------------------------------------- FPS
 def fps_cuda(pos: torch.Tensor, ptr: torch.Tensor, k_per_batch: torch.Tensor, *,
-             tie_break: str = "reference", return_pos: bool = False):
+             tie_break: str = "reference", return_pos: bool = False, status: Optional[torch.Tensor] = None):
     """Farthest point sampling per cloud (reference: csrc/__init__.py:566-597,
     fps_kernel.cu:160-209). Returns int64 global indices, cloud b's picks at offset
     sum_{c<b} k_c; a cloud with k > n yields n indices followed by -1.
@@ -68,6 +68,11 @@ def fps_cuda(pos: torch.Tensor, ptr: torch.Tensor, k_per_batch: torch.Tensor, *,
     One device->host copy of ``ptr``/``k_per_batch`` sizes the output (the reference
     also synchronises once, fps_kernel.cu:183); pass CPU tensors to avoid it. With
     ``return_pos`` also returns the picked coordinates [total, 3] (written by the kernel).
+
+    ``status``: an int32 CUDA tensor of one element, zeroed by the caller. The large-cloud
+    kernel's exchange waits are bounded; if one gives up (never observed), that cloud's
+    remaining picks are -2 (coordinates 0) and ``status`` receives GDL_ERR_TIMEOUT (6). The
+    call does not read it back (no extra synchronisation); check it when convenient.
     """
     dev = nat.require_cuda(pos, what="fps_cuda")
     pos = pos.contiguous().float()
@@ -85,9 +90,16 @@ def fps_cuda(pos: torch.Tensor, ptr: torch.Tensor, k_per_batch: torch.Tensor, *,
     opos = torch.empty(total, 3, dtype=torch.float32, device=dev) if return_pos else None
     L = nat.load()
     ws = nat.workspace(L.gdl_fps_workspace_size(pos.shape[0], B, max_n), dev)
-    nat.check(L.gdl_fps(pos.data_ptr(), ptr_d.data_ptr(), k_d.data_ptr(), B, pos.shape[0], max_n,
-                        nat.TIE[tie_break], out.data_ptr(), nat.ptr(opos), ws.data_ptr(), ws.numel(),
-                        nat.stream(dev)), "gdl_fps")
+    if status is None:
+        nat.check(L.gdl_fps(pos.data_ptr(), ptr_d.data_ptr(), k_d.data_ptr(), B, pos.shape[0], max_n,
+                            nat.TIE[tie_break], out.data_ptr(), nat.ptr(opos), ws.data_ptr(), ws.numel(),
+                            nat.stream(dev)), "gdl_fps")
+    else:
+        if not (status.is_cuda and status.dtype == torch.int32 and status.numel() >= 1):
+            raise nat.GdlError("fps_cuda: status must be an int32 CUDA tensor of at least one element")
+        nat.check(L.gdl_fps_ex(pos.data_ptr(), ptr_d.data_ptr(), k_d.data_ptr(), B, pos.shape[0], max_n,
+                               nat.TIE[tie_break], out.data_ptr(), nat.ptr(opos), ws.data_ptr(), ws.numel(),
+                               status.data_ptr(), 0, -1, -1, nat.stream(dev)), "gdl_fps_ex")
     return (out, opos) if return_pos else out
 
 

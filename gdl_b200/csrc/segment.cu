@@ -513,7 +513,8 @@ __global__ void __launch_bounds__(kSegThreads) seg_fwd_long_kernel(
 // can receive are fixed per segment (sum: g; mean: g / deg; max: g where the slot holds the
 // maximum, 0 * g elsewhere -- torch's mask * share, signed zeros included), so they are converted
 // to T once and the slots are a pure store stream. A max channel without a unique maximum (arg
-// -1: tied or NaN) gets its values from seg_bwd_max_fix_kernel afterwards.
+// -1: tied or NaN) is written here too for f32 when arg was kept (its lane reads its row chunks to
+// find the maxima), else by seg_bwd_max_fix_kernel afterwards.
 template <typename T, int VEC, int RED>
 __device__ __forceinline__ void seg_bwd_range(const float *__restrict__ grad_out, const T *__restrict__ msg,
                                               const float *__restrict__ out, const int32_t *__restrict__ arg,
@@ -530,8 +531,63 @@ __device__ __forceinline__ void seg_bwd_range(const float *__restrict__ grad_out
         hit_v[v] = to_elem<T>(1.0f * base);
         miss_v[v] = to_elem<T>(0.0f * base);
     }
+    if constexpr (RED == GDL_REDUCE_MAX) {
+        // Channels without a unique maximum (arg -1: tied, or a NaN maximum) share the gradient
+        // evenly among the slots equal to the maximum (torch's amax rule; a NaN maximum equals no
+        // slot, so every slot gets 0 * (g / 0)). With arg kept, a lane holding such a channel
+        // counts those slots over the whole segment and writes every slot of its range itself --
+        // its own row chunks only, read twice -- instead of leaving the channel to a separate pass
+        // that would read one element per row per channel. For f32 only: ties are rare there,
+        // while bf16 channels tie often enough that most warps would take the two extra row
+        // passes (the separate pass is cheaper for them).
+        if (arg && sizeof(T) == 4) {
+            int a[VEC];
+            bool tied = false;
+#pragma unroll
+            for (int v = 0; v < VEC; ++v) {
+                a[v] = arg[n * C + c + v];
+                tied |= a[v] < 0;
+            }
+            if (tied) {
+                float mxv[VEC];
+                int cnt[VEC];
+#pragma unroll
+                for (int v = 0; v < VEC; ++v) {
+                    mxv[v] = out[n * C + c + v];
+                    cnt[v] = 0;
+                }
+#pragma unroll 4
+                for (int j = s; j < e; ++j) {
+                    float x[VEC];
+                    vec_load<T, VEC>(msg + (perm ? (int64_t)__ldg(perm + j) : (int64_t)j) * C + c, x);
+#pragma unroll
+                    for (int v = 0; v < VEC; ++v) cnt[v] += (a[v] < 0 && x[v] == mxv[v]) ? 1 : 0;
+                }
+                T thit[VEC], tmiss[VEC];
+#pragma unroll
+                for (int v = 0; v < VEC; ++v) {
+                    const float base = __fdiv_rn(g[v], (float)cnt[v]);
+                    thit[v] = to_elem<T>(1.0f * base);
+                    tmiss[v] = to_elem<T>(0.0f * base);
+                }
+#pragma unroll 4
+                for (int j = j0; j < j1; ++j) {
+                    const int64_t row = perm ? (int64_t)__ldg(perm + j) : (int64_t)j;
+                    float x[VEC];
+                    vec_load<T, VEC>(msg + row * C + c, x);
+                    T val[VEC];
+#pragma unroll
+                    for (int v = 0; v < VEC; ++v)
+                        val[v] = a[v] >= 0 ? (a[v] == j ? hit_v[v] : miss_v[v]) : (x[v] == mxv[v] ? thit[v] : tmiss[v]);
+                    VecIO<T, VEC>::store_raw(grad_msg + row * C + c, val);
+                }
+                return;
+            }
+        }
+    }
     if constexpr (RED == GDL_REDUCE_MAX && sizeof(T) == 4) {
-        // f32: select per slot and channel (a tied channel gets misses; the fix-up rewrites it)
+        // f32: select per slot and channel (every channel here has a unique maximum, or no arg was
+        // kept and the fix-up pass rewrites them all)
         int a[VEC];
 #pragma unroll
         for (int v = 0; v < VEC; ++v) a[v] = arg ? arg[n * C + c + v] : -1;
@@ -764,7 +820,7 @@ static void launch_bwd(const float *go, const void *msg, const float *out, const
     if (ml > 0)
         seg_bwd_long_kernel<T, VEC, G, RED><<<(unsigned)ml, kSegThreads, 0, st>>>(go, (const T *)msg, out, arg, C, perm,
                                                                                  ns, ne, (T *)gm, ll, lc);
-    if (RED == GDL_REDUCE_MAX) {
+    if (RED == GDL_REDUCE_MAX && (!arg || sizeof(T) != 4)) {  // f32 with arg: done above
         const int64_t fb = (N + kFixWarps - 1) / kFixWarps;
         seg_bwd_max_fix_kernel<T><<<(unsigned)(fb < 16 * kSmCount ? fb : 16 * kSmCount), kFixWarps * 32, 0, st>>>(
             go, (const T *)msg, out, arg, C, perm, ns, ne, N, (T *)gm);

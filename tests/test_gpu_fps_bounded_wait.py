@@ -64,3 +64,19 @@ def test_fps_withheld_records_time_out_and_report(oracle, sizes, hold_rank):
     rc, status, out, _ = _call(xt, pt, kt)  # the context is still usable and exact
     assert rc == 0 and status == 0
     assert np.array_equal(out, want)
+
+
+def test_python_entry_point_reports_status(oracle):
+    """fps_cuda(status=...) runs the same bounded-wait kernel and leaves the status word at 0 on a
+    normal call (the failure path itself is exercised through gdl_fps_ex above)."""
+    from gdl_b200 import csrc
+
+    rng = np.random.default_rng(3)
+    x = (rng.random((30000, 3), dtype=np.float32) * 2 - 1).astype(np.float32)
+    ptr = synthetic.ptr_of([30000])
+    k = np.array([200], np.int64)
+    status = torch.zeros(1, dtype=torch.int32, device=DEV)
+    got = csrc.fps_cuda(torch.from_numpy(x).to(DEV), torch.from_numpy(ptr), torch.from_numpy(k), status=status)
+    assert int(status.item()) == 0
+    want = oracle.fps(x, ptr, k, tie=oracle.TIE_REFERENCE, dist=oracle.DIST_CUDA)
+    assert np.array_equal(got.cpu().numpy(), want)
