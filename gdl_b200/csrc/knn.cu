@@ -1088,15 +1088,18 @@ static cudaError_t knn_block_run(const float *query, const float *source, const 
     kb_lptr_kernel<<<1, 256, 0, st>>>(ptr_s, B, cap, b.lptr, b.invalid);
     cloud_box_kernel<<<B, kBoxThreads, 0, st>>>(source, ptr_s, b.box, b.bad);
     const unsigned gs = (unsigned)((cap + 255) / 256 < 4 * kSmCount ? (cap + 255) / 256 : 4 * kSmCount);
-    morton_code_kernel<<<gs > 0 ? gs : 1, 256, 0, st>>>(source, ptr_s, B, b.box, b.skeys, true, cap);
+    // 24-bit codes (256 cells per axis: far finer than a block of 32 points in clouds of up to 32767)
+    // sort in three 8-bit passes; the order only groups nearby points -- every bound below comes
+    // from the blocks' actual boxes
+    morton_code_kernel<<<gs > 0 ? gs : 1, 256, 0, st>>>(source, ptr_s, B, b.box, b.skeys, true, cap, 6);
     const unsigned gq = (unsigned)((n_q + 255) / 256 < 4 * kSmCount ? (n_q + 255) / 256 : 4 * kSmCount);
-    morton_code_kernel<<<gq > 0 ? gq : 1, 256, 0, st>>>(query, ptr_q, B, b.box, b.qkeys, false, n_q);
+    morton_code_kernel<<<gq > 0 ? gq : 1, 256, 0, st>>>(query, ptr_q, B, b.box, b.qkeys, false, n_q, 6);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return e;
     // (with `invalid` set the offsets are all 0: the source sort sorts nothing)
-    e = radix_sort_pairs(b.skeys, nullptr, b.sskeys, b.sorder, cap, b.lptr, B, 4, nullptr, b.rs, st);
+    e = radix_sort_pairs(b.skeys, nullptr, b.sskeys, b.sorder, cap, b.lptr, B, 3, nullptr, b.rs, st);
     if (e != cudaSuccess) return e;
-    e = radix_sort_pairs(b.qkeys, nullptr, b.sqkeys, b.qorder, n_q, ptr_q, B, 4, nullptr, b.rs, st);
+    e = radix_sort_pairs(b.qkeys, nullptr, b.sqkeys, b.qorder, n_q, ptr_q, B, 3, nullptr, b.rs, st);
     if (e != cudaSuccess) return e;
     e = cudaGetLastError();
     if (e != cudaSuccess) return e;

@@ -81,9 +81,11 @@ __device__ __forceinline__ uint32_t morton_cell(float x, float lo, float scale) 
 // 30-bit Morton code of every point over its cloud's box (1024 cells per axis). `ptr` gives the
 // points' clouds, `box` one box per cloud (the points' own, or another set's with the same clouds).
 // Codes go to keys[i] (or keys[i - ptr[0]] when `relative`), for indices below `limit` only.
+// keys are 30-bit codes (10 bits per axis) shifted right by `shift` (a multiple of 3 keeps whole
+// levels: 6 gives 24-bit codes, 8 bits per axis, for a three-pass 8-bit radix sort)
 static __global__ void morton_code_kernel(const float *__restrict__ pos, const int64_t *__restrict__ ptr, int B,
                                           const float *__restrict__ box, uint32_t *__restrict__ keys,
-                                          bool relative, int64_t limit) {
+                                          bool relative, int64_t limit, int shift = 0) {
     const int64_t first = ptr[0], last = ptr[B];
     for (int64_t i = first + (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < last;
          i += (int64_t)gridDim.x * blockDim.x) {
@@ -102,7 +104,7 @@ static __global__ void morton_code_kernel(const float *__restrict__ pos, const i
             code |= spread10(morton_cell(pos[3 * i + c], bx[c], scale)) << c;
         }
         const int64_t at = relative ? i - first : i;  // relative: indexed from the first point of cloud 0
-        if (at < limit) keys[at] = code;               // `keys` holds `limit` entries
+        if (at < limit) keys[at] = code >> shift;      // `keys` holds `limit` entries
     }
 }
 
