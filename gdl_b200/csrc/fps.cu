@@ -704,16 +704,21 @@ static cudaError_t launch_cta(int B, const float *pos, const int64_t *ptr, const
 
 constexpr int kCtaCapacity = 4096;            // fps_cta_kernel<256, 16>; larger clouds are bucketed
 // Bucketed launch shapes, from sweeps on a B200 (configuration 5's LiDAR clouds, configuration 3's
-// 8192-point level): CTAs of 512 x 16 = 8192 points (one CTA per cloud up to 8192 points; up to 16
-// in a cluster), of 512 x 26 = 13312 points (10 for a 131072-point cloud; 7.2 ms for configuration
-// 5's FPS against 8.1 ms with 384 x 36) and of 384 x 36 = 13824 points (the largest clouds: up to
-// 16 x 13824). A B200 holds 11 clusters of 10 CTAs at once but only 7 of 11-16, so eight LiDAR
-// clouds run in one wave only as 10-CTA clusters, while up to seven take the 16-CTA shape, whose
-// smaller buckets update faster. The launch takes the shape that needs the fewest waves of
-// clusters, the smallest buckets on a tie.
+// 8192-point level): CTAs of 256 x 4 = 1024 points (clusters of up to 8: configuration 3's first
+// level 0.74 ms on 8-CTA clusters against 1.05 ms on one 512 x 16 CTA per cloud, which left most
+// SMs idle), of 512 x 16 = 8192 points (one CTA, or clusters of up to 16), of 512 x 26 = 13312
+// points (10 for a 131072-point cloud; 7.2 ms for configuration 5's FPS against 8.1 ms with
+// 384 x 36) and of 384 x 36 = 13824 points (the largest clouds: up to 16 x 13824). A B200 holds 11
+// clusters of 10 CTAs at once but only 7 of 11-16, so eight LiDAR clouds run in one wave only as
+// 10-CTA clusters, while up to seven take the 16-CTA shape, whose smaller buckets update faster.
+// The launch takes the shape that needs the fewest waves of clusters, the smallest buckets on a
+// tie.
+constexpr int kTinyT = 256, kTinyP = 4;
+constexpr int kTinyMaxCluster = 8;  // the tiny shape serves clouds of up to 8 x 1024 points
 constexpr int kSmallT = 512, kSmallP = 16;
 constexpr int kMidT = 512, kMidP = 26;
 constexpr int kBigT = 384, kBigP = 36;
+constexpr int64_t kTinyCapacity = (int64_t)kTinyT * kTinyP;
 constexpr int64_t kSmallCapacity = (int64_t)kSmallT * kSmallP;
 constexpr int64_t kMidCapacity = (int64_t)kMidT * kMidP;
 constexpr int64_t kBucketCapacity = (int64_t)kBigT * kBigP;
@@ -873,20 +878,19 @@ extern "C" int gdl_fps_ex(const float *pos, const int64_t *ptr, const int64_t *k
                       GDL_ERR_WORKSPACE);
         FpsWork w;
         fps_carve((char *)workspace, n_points, num_clouds, &w);
-        // the shape: 512 x 16, 512 x 26 or 384 x 36 CTAs (clusters of up to 16), whichever needs the
-        // fewest waves of resident clusters for these clouds, the smallest buckets on a tie
-        const int64_t caps[3] = {kSmallCapacity, kMidCapacity, kBucketCapacity};
+        // the shape: 256 x 4 (clusters of up to 8), 512 x 16, 512 x 26 or 384 x 36 CTAs (clusters of up
+        // to 16), whichever needs the fewest waves of resident clusters for these clouds, the
+        // smallest buckets on a tie
+        const int64_t caps[4] = {kTinyCapacity, kSmallCapacity, kMidCapacity, kBucketCapacity};
+        const int cmax[4] = {kTinyMaxCluster, kMaxCluster, kMaxCluster, kMaxCluster};
         int shape = -1, cs = 0;
         int64_t best_waves = 0;
-        for (int sh = 0; sh < 3; ++sh) {
+        for (int sh = 0; sh < 4; ++sh) {
             const int c = (int)((m + caps[sh] - 1) / caps[sh]);
-            if (c > kMaxCluster) continue;
-            if (c == 1 && sh == 0) {  // one CTA of the smallest shape holds the cloud
-                shape = 0, cs = 1;
-                break;
-            }
-            const int mc = sh == 0 ? bucket_max_clusters_tie<kSmallT, kSmallP, kRoundPicks>(tie_break, c)
-                         : sh == 1 ? bucket_max_clusters_tie<kMidT, kMidP, kRoundPicks>(tie_break, c)
+            if (c > cmax[sh]) continue;
+            const int mc = sh == 0 ? bucket_max_clusters_tie<kTinyT, kTinyP, kRoundPicks>(tie_break, c)
+                         : sh == 1 ? bucket_max_clusters_tie<kSmallT, kSmallP, kRoundPicks>(tie_break, c)
+                         : sh == 2 ? bucket_max_clusters_tie<kMidT, kMidP, kRoundPicks>(tie_break, c)
                                    : bucket_max_clusters_tie<kBigT, kBigP, kRoundPicks>(tie_break, c);
             if (mc <= 0) continue;
             const int64_t waves = (num_clouds + mc - 1) / mc;
@@ -904,10 +908,14 @@ extern "C" int gdl_fps_ex(const float *pos, const int64_t *ptr, const int64_t *k
             GDL_CUDA_TRY(radix_sort_pairs(w.keys, nullptr, w.sorted_keys, w.order, n_points, ptr, num_clouds, 4,
                                           nullptr, w.rs, st));
             if (shape == 0)
+                e = launch_bucket_tie<kTinyT, kTinyP, kRoundPicks>(tie_break, num_clouds, cs, pos, w.order, ptr,
+                                                                   k_per_cloud, out_idx, out_pos, status, polls,
+                                                                   hold_rank, hold_pick, w.rounds, st);
+            else if (shape == 1)
                 e = launch_bucket_tie<kSmallT, kSmallP, kRoundPicks>(tie_break, num_clouds, cs, pos, w.order, ptr,
                                                                      k_per_cloud, out_idx, out_pos, status, polls,
                                                                      hold_rank, hold_pick, w.rounds, st);
-            else if (shape == 1)
+            else if (shape == 2)
                 e = launch_bucket_tie<kMidT, kMidP, kRoundPicks>(tie_break, num_clouds, cs, pos, w.order, ptr,
                                                                  k_per_cloud, out_idx, out_pos, status, polls,
                                                                  hold_rank, hold_pick, w.rounds, st);

@@ -72,8 +72,9 @@ int gdl_fp32_peak(float *out, int64_t iters, int32_t packed, int32_t blocks, voi
  * max_cloud_points  host-side upper bound of max_b n_b. It selects the kernel variant: one CTA
  *              per cloud with the points in registers up to 4096 points; above that the clouds
  *              are put in Morton order (in the workspace) and run bucketed, one CTA of up to 8192
- *              points or a thread-block cluster of up to 16 CTAs of 8192, 13312 or 13824 points (up to
- *              221184; the shape that needs the fewest waves of resident clusters for num_clouds), in
+ *              points or a thread-block cluster of up to 8 CTAs of 1024 points or of up to 16 CTAs of
+ *              8192, 13312 or 13824 points (up to 221184; the shape that needs the fewest waves of
+ *              resident clusters for num_clouds, the smallest buckets on a tie), in
  *              exact rounds of up to 12 picks; beyond that, or if the device refuses the cluster,
  *              a streaming CTA that keeps the running minima in the workspace.
  * tie_break    GDL_TIE_REFERENCE: the reference kernel's argmax reduction order
