@@ -1458,7 +1458,7 @@ class ClockSampler:
 
 ROOFLINE_NOTES = {
     "fps": "FPS is a serial chain of picks per cloud. The bucketed kernel makes them in exchange rounds "
-           "of up to 12 exact picks (about 5-6 on LiDAR clouds); its bound is the latency of those "
+           "of up to 16 exact picks (about 6 on LiDAR clouds); its bound is the latency of those "
            "rounds: `peak` is the time per pick of a chain with this run's exchange rounds and nothing "
            "to update (the per-round time of the same kernel and launch shape on clouds of duplicated "
            "points, where every round makes one pick, times `exchange_rounds`, per pick); the rest of "
@@ -1685,7 +1685,7 @@ def roofline_of(cfg, timed, stage_ms, E, peaks):
     bound = STAGE_BOUND.get(dom, "hbm")
     r = {"kernel": dom, "bound": bound, "note": ROOFLINE_NOTES.get(dom, "")}
     if bound == "latency":
-        # The FPS chain is a sequence of exchange rounds (up to 12 exact picks each in the bucketed
+        # The FPS chain is a sequence of exchange rounds (up to 16 exact picks each in the bucketed
         # kernel, one in the small-cloud kernel); its floor is the same number of rounds with
         # nothing to update: the time per round of the stage on duplicated points (one pick per
         # round there) times this run's round count.

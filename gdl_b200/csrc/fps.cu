@@ -227,7 +227,7 @@ constexpr int kCtaRecords = 2;               // records a CTA of a cluster sends
 // itself is then NaN, not 0, so no pick may follow it in the same round); either way, a later
 // pick's minimum bits must exceed the bound.
 constexpr uint32_t kNonFinite = 0x80000000u;
-constexpr int kRoundPicks = 12;              // picks one round may make
+constexpr int kRoundPicks = 16;              // picks one round may make
 
 __host__ __device__ constexpr size_t bucket_points_bytes(int T, int P) { return (size_t)16 * T * P; }
 // records per round: one per CTA of the cluster, double-buffered

@@ -75,7 +75,7 @@ int gdl_fp32_peak(float *out, int64_t iters, int32_t packed, int32_t blocks, voi
  *              points or a thread-block cluster of up to 8 CTAs of 1024 points or of up to 16 CTAs of
  *              8192, 13312 or 13824 points (up to 221184; the shape that needs the fewest waves of
  *              resident clusters for num_clouds, the smallest buckets on a tie), in
- *              exact rounds of up to 12 picks; beyond that, or if the device refuses the cluster,
+ *              exact rounds of up to 16 picks; beyond that, or if the device refuses the cluster,
  *              a streaming CTA that keeps the running minima in the workspace.
  * tie_break    GDL_TIE_REFERENCE: the reference kernel's argmax reduction order
  *              (bit-identical to fps_kernel<512>); GDL_TIE_LOWEST_INDEX: torch.argmax.

@@ -1,6 +1,6 @@
 """The bucketed FPS kernel's exchange rounds (gdl_fps_round_count), through the C ABI.
 
-The kernel makes its picks in rounds of up to 12: a record that is provably the next pick of the
+The kernel makes its picks in rounds of up to 16: a record that is provably the next pick of the
 one-at-a-time chain joins the round. On clouds of duplicated points every minimum is 0 after the
 first pick, so no later record qualifies and each round makes exactly one pick; on spread-out
 clouds rounds make several. Either way the picks equal the CPU restatement's.
@@ -18,7 +18,7 @@ from gdl_b200 import synthetic
 pytestmark = [pytest.mark.gpu,
               pytest.mark.skipif(not torch.cuda.is_available(), reason="needs a CUDA device")]
 DEV = "cuda"
-MAX_ROUND_PICKS = 12
+MAX_ROUND_PICKS = 16
 
 
 def _fps_rounds(x, sizes, k):
