@@ -919,6 +919,7 @@ __global__ void __launch_bounds__(kExactThreads) knn_exact_kernel(
     const int32_t *__restrict__ flag_count, int64_t *__restrict__ out_idx, float *__restrict__ out_dist,
     unsigned long long *__restrict__ pairs) {
     __shared__ float sd[kExactStretch];
+    __shared__ float cmin[kExactStretch / 32];  // per 32-candidate chunk: smallest distance, NaN if any
     const int nflag = *flag_count;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     for (int f = blockIdx.x; f < nflag; f += gridDim.x) {  // uniform over the CTA
@@ -931,22 +932,47 @@ __global__ void __launch_bounds__(kExactThreads) knn_exact_kernel(
         for (int64_t c0 = s0; c0 < se; c0 += kExactStretch) {
             const int m = (int)(se - c0 < kExactStretch ? se - c0 : kExactStretch);
             __syncthreads();  // the previous stretch's walk is done
-            for (int i = tid; i < m; i += kExactThreads) {
-                const float *p = source + 3 * (c0 + i);
-                sd[i] = dist2(qx, qy, qz, p[0], p[1], p[2]);
+            for (int i0 = 0; i0 < m; i0 += kExactThreads) {  // whole warps: 32 consecutive candidates
+                const int i = i0 + tid;
+                float d = __int_as_float(0x7f800000);
+                if (i < m) {
+                    const float *p = source + 3 * (c0 + i);
+                    d = dist2(qx, qy, qz, p[0], p[1], p[2]);
+                    sd[i] = d;
+                }
+                float mn = d;
+#pragma unroll
+                for (int o = 16; o > 0; o >>= 1) mn = fminf(mn, __shfl_xor_sync(0xffffffffu, mn, o));
+                const bool nan = __any_sync(0xffffffffu, d != d);
+                if (lane == 0 && i0 + warp * 32 < m) cmin[(i0 >> 5) + warp] = nan ? __int_as_float(0x7fc00000) : mn;
             }
             __syncthreads();
             if (warp == 0) {
-                for (int j0 = 0; j0 < m; j0 += 32) {
-                    const bool in = j0 + lane < m;
-                    const float d = in ? sd[j0 + lane] : 0.0f;
-                    const bool full = h.count >= h.cap;
-                    const bool unordered = __any_sync(0xffffffffu, in && d != d) || (full && h.d[0] != h.d[0]);
-                    unsigned live = __ballot_sync(0xffffffffu, in && (unordered || !(full && d >= h.d[0])));
-                    while (live) {
-                        const int l = __ffs(live) - 1;
-                        live &= live - 1;
-                        h.add(__shfl_sync(0xffffffffu, d, l), (int)(c0 + j0 + l));
+                // Chunks are walked in order; a chunk whose smallest distance is >= the heap's largest
+                // (heap full, nothing NaN) holds no candidate the heap would take, and stays so as the
+                // heap's largest only decreases -- 32 chunks are tested per ballot. The others are
+                // walked candidate by candidate exactly as before.
+                const int nch = (m + 31) >> 5;
+                for (int g0 = 0; g0 < nch; g0 += 32) {
+                    const bool have = g0 + lane < nch;
+                    const float cm = have ? cmin[g0 + lane] : 0.0f;
+                    const bool full0 = h.count >= h.cap;
+                    const float root0 = full0 ? h.d[0] : 0.0f;
+                    unsigned need =
+                        __ballot_sync(0xffffffffu, have && !(full0 && root0 == root0 && cm >= root0));
+                    while (need) {
+                        const int j0 = (g0 + __ffs(need) - 1) << 5;
+                        need &= need - 1;
+                        const bool in = j0 + lane < m;
+                        const float d = in ? sd[j0 + lane] : 0.0f;
+                        const bool full = h.count >= h.cap;
+                        const bool unordered = __any_sync(0xffffffffu, in && d != d) || (full && h.d[0] != h.d[0]);
+                        unsigned live = __ballot_sync(0xffffffffu, in && (unordered || !(full && d >= h.d[0])));
+                        while (live) {
+                            const int l = __ffs(live) - 1;
+                            live &= live - 1;
+                            h.add(__shfl_sync(0xffffffffu, d, l), (int)(c0 + j0 + l));
+                        }
                     }
                 }
             }
