@@ -667,13 +667,14 @@ __global__ void __launch_bounds__(kQueryWarps * 32) rg_query_warp_kernel(
     // most of their candidate columns in L1
     for (int64_t j = p0 + gw; j < p1; j += nwarps) {
         int kept = 0;
-        const int64_t q = __float_as_int(sorted_pts[j].w);
+        const float4 qp = sorted_pts[j];  // the query's coordinates (copied from x) and index
+        const int64_t q = __float_as_int(qp.w);
         const bool live = !(mask && !mask[q]);
         const int b = find_cloud_i(ptr, B, j);
         const GridParams g = gp[b];
         if (live && g.ok) {  // uniform over the warp
             const int64_t s0 = ptr[b], s1 = ptr[b + 1];
-            const float qx = x[3 * q], qy = x[3 * q + 1], qz = x[3 * q + 2];
+            const float qx = qp.x, qy = qp.y, qz = qp.z;
             const int qc0 = cell_coord(qx, g.mn[0], inv), qc1 = cell_coord(qy, g.mn[1], inv),
                       qc2 = cell_coord(qz, g.mn[2], inv);
             const int zlo = qc2 - 1 < 0 ? 0 : qc2 - 1;
