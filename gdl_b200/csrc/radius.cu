@@ -630,14 +630,20 @@ __global__ void rg_cells_kernel(const int64_t *__restrict__ ptr, int32_t B, cons
 }
 
 // One warp per query. Lanes 0-8 find the sorted ranges of the 9 z-columns of the 27-cell
-// neighbourhood in the reference's (dx, dy) order; a warp scan turns them into one candidate
-// list that the lanes test 32 at a time, and ballot/popc append the sources in range to the
-// query's padded row in scan order (rows are sorted at compaction). The reference keeps them
-// all when at most `cap` are in range. Otherwise its heap keeps the `cap` smallest distances
-// whenever the cap-th and the next are different; the warp finds the cap-th distance by a
-// coarse histogram (one rescan), a compaction of the candidates below the cutoff into shared
-// memory (one rescan) and a radix select there, and writes the sources at or below it. A tie
-// at the cut (or a cutoff that leaves too many candidates) replays the reference heap on lane 0.
+// neighbourhood in the reference's (dx, dy) order (and, on grids with a dense cell table, where
+// the query's own z-cell lies in each); the warp tests a column's candidates 32 at a time and
+// ballot/popc append the sources in range to the query's padded row (rows are sorted at
+// compaction). The reference keeps them all when at most `cap` are in range. Otherwise its heap
+// keeps the `cap` smallest distances whenever the cap-th and the next are different, and the
+// warp finds that cut in the same pass: the (distance, source) pairs in range also go to a shared
+// buffer, and whenever the buffer has grown (or would overflow) a histogram of it yields a bound,
+// the largest distance among its smallest >= cap pairs. No pair above the bound can be kept, so
+// the buffer keeps the pairs at or below it, later candidates above it are dropped, and a column,
+// or the outer z-cell of a column, whose cell box lies farther from the query than the bound (or
+// than r, before there is a bound) is not scanned at all. The query's own column goes first,
+// which makes the first bound tight. A radix select of the buffer gives the cap-th distance; a
+// tie at the cut (or ties that fill the buffer) replays the reference heap on lane 0, fed in the
+// reference's scan order.
 constexpr int kQueryWarps = 8;
 constexpr int kScanDepth = 4;  // candidate batches of 32 in flight per warp
 constexpr int kOvfCap = 1024;  // candidates a warp can hold for the selection
@@ -648,12 +654,53 @@ struct QueryWarpSmem {
     int hist[kHistBins];
 };
 
-__global__ void __launch_bounds__(kQueryWarps * 32) rg_query_warp_kernel(
+// The first bin at which the running count of the warp's histogram reaches `rank`, and the count
+// before it (every lane returns both).
+__device__ __forceinline__ int hist_rank_bin(const int *hist, int rank, int lane, int &before) {
+    int v[kHistBins / 32], sum = 0;  // 8 consecutive bins per lane, warp scan
+#pragma unroll
+    for (int i = 0; i < kHistBins / 32; ++i) {
+        v[i] = hist[lane * (kHistBins / 32) + i];
+        sum += v[i];
+    }
+    int pre = sum;
+    for (int o = 1; o < 32; o <<= 1) {
+        const int y = __shfl_up_sync(0xffffffffu, pre, o);
+        if (lane >= o) pre += y;
+    }
+    int run = pre - sum, found = -1, bef = 0;
+#pragma unroll
+    for (int i = 0; i < kHistBins / 32; ++i) {
+        if (found < 0 && run + v[i] >= rank) {
+            found = lane * (kHistBins / 32) + i;
+            bef = run;
+        }
+        run += v[i];
+    }
+    const unsigned have = __ballot_sync(0xffffffffu, found >= 0);
+    const int srcl = __ffs(have) - 1;  // lowest lane: the first bin reaching the rank
+    before = __shfl_sync(0xffffffffu, bef, srcl);
+    return __shfl_sync(0xffffffffu, found, srcl);
+}
+
+// Distances, in cell units, from a query at scaled coordinate u (cell qc = floor(u), the binning
+// arithmetic of cell_coord) to the faces of its cell, less a rounding margin: a point binned into
+// the cell below has u' < qc and one binned above has u' >= qc + 1, by the same arithmetic, whose
+// relative error (three roundings) the margin covers many times over. The cell below is open to
+// clamped points when the query's own cell lies past the grid (qc >= res): no bound then.
+__device__ __forceinline__ void face_gaps(float u, int qc, int res, float &below, float &above) {
+    const float eps = 0x1p-19f * (fabsf(u) + 2.0f);
+    below = qc < res ? fmaxf(u - (float)qc - eps, 0.0f) : 0.0f;
+    above = fmaxf((float)(qc + 1) - u - eps, 0.0f);
+}
+
+__global__ void __launch_bounds__(kQueryWarps * 32, 3) rg_query_warp_kernel(
     const float *__restrict__ x, const int64_t *__restrict__ ptr, int32_t B, int64_t n, const uint8_t *__restrict__ mask,
     float r_sq, float inv, int loop, int cap, const GridParams *__restrict__ gp,
     const uint32_t *__restrict__ sorted_keys, const int32_t *__restrict__ cell_start,
     const float4 *__restrict__ sorted_pts, int32_t *__restrict__ counts, int32_t *__restrict__ padded) {
     // sorted_pts spans every cloud: a point's sorted position lies in its own cloud's range
+    // (positions fit in int32: the host refuses n_points >= INT32_MAX / 64)
     extern __shared__ __align__(16) unsigned char query_smem[];  // kQueryWarps x QueryWarpSmem
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     QueryWarpSmem &W = reinterpret_cast<QueryWarpSmem *>(query_smem)[warp];
@@ -661,6 +708,8 @@ __global__ void __launch_bounds__(kQueryWarps * 32) rg_query_warp_kernel(
     const int64_t nwarps = (int64_t)gridDim.x * kQueryWarps;
     const int64_t p0 = ptr[0], p1 = ptr[B];
     const int64_t gw = (int64_t)blockIdx.x * kQueryWarps + warp;
+    // a box lower bound on a squared distance, scaled down by more than the rounding of dist2
+    const float shrink = r_sq * (1.0f - 0x1p-19f);
     for (int64_t q = gw * 32 + lane; q < n; q += nwarps * 32)  // points outside every cloud
         if (q < p0 || q >= p1) counts[q] = 0;
     // queries in cell order (position j of the sorted points): warps running together share
@@ -675,132 +724,137 @@ __global__ void __launch_bounds__(kQueryWarps * 32) rg_query_warp_kernel(
         if (live && g.ok) {  // uniform over the warp
             const int64_t s0 = ptr[b], s1 = ptr[b + 1];
             const float qx = qp.x, qy = qp.y, qz = qp.z;
-            const int qc0 = cell_coord(qx, g.mn[0], inv), qc1 = cell_coord(qy, g.mn[1], inv),
-                      qc2 = cell_coord(qz, g.mn[2], inv);
+            const float ux = mul_ftz(sub_ftz(qx, g.mn[0]), inv), uy = mul_ftz(sub_ftz(qy, g.mn[1]), inv),
+                        uz = mul_ftz(sub_ftz(qz, g.mn[2]), inv);
+            const int qc0 = __float2int_rd(ux), qc1 = __float2int_rd(uy), qc2 = __float2int_rd(uz);  // cell_coord
             const int zlo = qc2 - 1 < 0 ? 0 : qc2 - 1;
             const int zhi = qc2 + 1 > g.res[2] - 1 ? g.res[2] - 1 : qc2 + 1;
-            int64_t j0 = 0;
-            int len = 0;
+            // lane c < 9: column c's sorted range [j0, j0 + len) and the query's z-cell within it,
+            // [j0 + zm0, j0 + zm1) (the whole column when the grid has no dense cell table)
+            int j0 = 0, len = 0, zm0 = 0, zm1 = 0;
             if (lane < 9) {
                 const int cx = qc0 + lane / 3 - 1, cy = qc1 + lane % 3 - 1;
                 if (zlo <= zhi && cx >= 0 && cx < g.res[0] && cy >= 0 && cy < g.res[1]) {
                     const int colc = (cx * g.res[1] + cy) * g.res[2];
-                    int64_t e;
+                    int e;
                     if (dense_cells(g, s1 - s0)) {
                         const int32_t *cs = cell_start + kCellBudget * s0;
                         j0 = cs[colc + zlo];
                         e = cs[colc + zhi + 1];
+                        if (zlo <= qc2 && qc2 <= zhi) {
+                            zm0 = cs[colc + qc2] - j0;
+                            zm1 = cs[colc + qc2 + 1] - j0;
+                        } else {
+                            zm1 = e - j0;
+                        }
                     } else {
-                        j0 = lower_bound_u32(sorted_keys, s0, s1, (uint32_t)(colc + zlo));
-                        e = lower_bound_u32(sorted_keys, j0, s1, (uint32_t)(colc + zhi) + 1u);
+                        j0 = (int)lower_bound_u32(sorted_keys, s0, s1, (uint32_t)(colc + zlo));
+                        e = (int)lower_bound_u32(sorted_keys, j0, s1, (uint32_t)(colc + zhi) + 1u);
+                        zm1 = e - j0;
                     }
-                    len = (int)(e - j0);
+                    len = e - j0;
                 }
             }
-            int clen[9];
-            int64_t cbeg[9];
-#pragma unroll
-            for (int c = 0; c < 9; ++c) {  // every lane takes the 9 (start, length) pairs
-                clen[c] = __shfl_sync(0xffffffffu, len, c);
-                cbeg[c] = __shfl_sync(0xffffffffu, j0, c);
-            }
-            // the candidates in scan order, column by column, 32 at a time; body(ok, d, o) runs
-            // on every lane for every batch (ok: the lane holds a source in range)
-            // (loads of kScanDepth batches are issued before the first is tested)
-            auto scan = [&](auto &&body) {
-#pragma unroll
-                for (int c = 0; c < 9; ++c) {
-                    for (int k0 = 0; k0 < clen[c]; k0 += 32 * kScanDepth) {
-                        float4 sp[kScanDepth];
-#pragma unroll
-                        for (int u = 0; u < kScanDepth; ++u) {
-                            const int k = k0 + 32 * u + lane;
-                            if (k < clen[c]) sp[u] = sorted_pts[cbeg[c] + k];
-                        }
-#pragma unroll
-                        for (int u = 0; u < kScanDepth; ++u) {
-                            if (k0 + 32 * u >= clen[c]) break;  // uniform over the warp
-                            const int k = k0 + 32 * u + lane;
-                            bool ok = false;
-                            float d = 0.0f;
-                            int o = 0;
-                            if (k < clen[c]) {
-                                o = __float_as_int(sp[u].w);
-                                d = dist2(qx, qy, qz, sp[u].x, sp[u].y, sp[u].z);
-                                ok = (loop || (int64_t)o != q) && d < r_sq;
-                            }
-                            body(ok, d, o);
-                        }
-                    }
-                }
-            };
+            float gxl, gxh, gyl, gyh, gzl, gzh;  // face gaps of the query's cell, cell units
+            face_gaps(ux, qc0, g.res[0], gxl, gxh);
+            face_gaps(uy, qc1, g.res[1], gyl, gyh);
+            face_gaps(uz, qc2, g.res[2], gzl, gzh);
             int32_t *row = padded + q * cap;
-            // pass 1: sources in range in scan order, the first `cap` into the row and the first
-            // kOvfCap (distance, source) pairs into shared memory
-            scan([&](bool ok, float d, int o) {
-                const unsigned hits = __ballot_sync(0xffffffffu, ok);
-                const int pos = kept + __popc(hits & lt_mask);
-                if (ok) {
-                    if (pos < cap) row[pos] = o;
-                    if (pos < kOvfCap) W.buf[pos] = make_float2(d, __int_as_float(o));
+            int m = 0;            // pairs in the buffer: every pair seen in range with d <= bound
+            float bound = r_sq;   // in range is d < r_sq, so every such pair until the first bound
+            bool bounded = false, replay = false;
+            int next_tighten = 2 * cap;
+            // keep the buffered pairs at or below the histogram bin where the running count
+            // reaches cap; the bound becomes the largest distance kept (m >= cap on entry)
+            auto tighten = [&]() {
+                if (!(bound > 0x1p-100f)) {  // a zero bound: only ties remain, the heap decides
+                    replay = true;
+                    return;
                 }
-                kept += __popc(hits);
-            });
-            if (kept > cap) {
-                int m = kept;  // candidates in the buffer
-                bool replay = false;
-                if (kept > kOvfCap) {
-                    // cutoff: the smallest histogram bin edge with at least cap + 1 candidates
-                    // below it; the buffer is refilled with the candidates under it
-                    const float scale = (float)kHistBins / r_sq;
-                    __syncwarp();
-                    for (int h = lane; h < kHistBins; h += 32) W.hist[h] = 0;
-                    __syncwarp();
-                    scan([&](bool ok, float d, int o) {
-                        if (ok) atomicAdd(&W.hist[min((int)(d * scale), kHistBins - 1)], 1);
-                    });
-                    __syncwarp();
-                    int v[kHistBins / 32], sum = 0;  // 8 consecutive bins per lane, warp scan
-#pragma unroll
-                    for (int i = 0; i < kHistBins / 32; ++i) {
-                        v[i] = W.hist[lane * (kHistBins / 32) + i];
-                        sum += v[i];
+                const float scale = (float)kHistBins / bound;
+                __syncwarp();
+                for (int h = lane; h < kHistBins; h += 32) W.hist[h] = 0;
+                __syncwarp();
+                for (int i = lane; i < m; i += 32)
+                    atomicAdd(&W.hist[min((int)(W.buf[i].x * scale), kHistBins - 1)], 1);
+                __syncwarp();
+                int before;
+                const int cut = hist_rank_bin(W.hist, cap, lane, before);
+                int w = 0;
+                float top = 0.0f;
+                for (int base = 0; base < m; base += 32) {
+                    const int i = base + lane;
+                    const float2 e = i < m ? W.buf[i] : make_float2(0.0f, 0.0f);
+                    const bool keep = i < m && min((int)(e.x * scale), kHistBins - 1) <= cut;
+                    const unsigned kh = __ballot_sync(0xffffffffu, keep);  // reads of the batch done
+                    if (keep) {
+                        W.buf[w + __popc(kh & lt_mask)] = e;  // position <= i
+                        top = fmaxf(top, e.x);
                     }
-                    int pre = sum;
-                    for (int o = 1; o < 32; o <<= 1) {
-                        const int y = __shfl_up_sync(0xffffffffu, pre, o);
-                        if (lane >= o) pre += y;
+                    w += __popc(kh);
+                    __syncwarp();
+                }
+                for (int o = 16; o > 0; o >>= 1) top = fmaxf(top, __shfl_xor_sync(0xffffffffu, top, o));
+                m = w;
+                bound = top;
+                bounded = true;
+                next_tighten = 2 * (m > cap ? m : cap);
+            };
+            // columns: the query's own first, then the rest; once the heap replay is decided the
+            // scan stops (the replay rescans every column)
+            for (int ci = 0; ci < 9 && !replay; ++ci) {
+                if (m >= next_tighten) tighten();  // m >= 2 cap: the row is over the cap
+                const int c = ci == 0 ? 4 : (ci <= 4 ? ci - 1 : ci);
+                const int cb = __shfl_sync(0xffffffffu, j0, c);
+                const int cl = __shfl_sync(0xffffffffu, len, c);
+                const int z0 = __shfl_sync(0xffffffffu, zm0, c), z1 = __shfl_sync(0xffffffffu, zm1, c);
+                const int cxo = c / 3, cyo = c - 3 * cxo;
+                const float gx = cxo == 0 ? gxl : (cxo == 2 ? gxh : 0.0f);
+                const float gy = cyo == 0 ? gyl : (cyo == 2 ? gyh : 0.0f);
+                const float gxy = gx * gx + gy * gy;
+                if (replay || cl == 0 || gxy * shrink > bound) continue;  // uniform: nothing to keep
+                const int a = (gxy + gzl * gzl) * shrink > bound ? z0 : 0;   // the z-cell below
+                const int e = (gxy + gzh * gzh) * shrink > bound ? z1 : cl;  // the z-cell above
+                for (int k0 = a; k0 < e; k0 += 32 * kScanDepth) {
+                    if (m > kOvfCap - 32 * kScanDepth) {  // room for the batches below
+                        tighten();
+                        if (m > kOvfCap - 32 * kScanDepth) replay = true;  // ties fill the buffer
+                        if (replay) break;
                     }
-                    int run = pre - sum, found = kHistBins, upto = 0;
+                    float4 sp[kScanDepth];
 #pragma unroll
-                    for (int i = 0; i < kHistBins / 32; ++i) {
-                        run += v[i];
-                        if (found == kHistBins && run >= cap + 1) {
-                            found = lane * (kHistBins / 32) + i;
-                            upto = run;
+                    for (int u = 0; u < kScanDepth; ++u) {
+                        const int k = k0 + 32 * u + lane;
+                        if (k < e) sp[u] = sorted_pts[cb + k];
+                    }
+#pragma unroll
+                    for (int u = 0; u < kScanDepth; ++u) {
+                        if (k0 + 32 * u >= e) break;  // uniform over the warp
+                        const int k = k0 + 32 * u + lane;
+                        bool ok = false;
+                        float d = 0.0f;
+                        int o = 0;
+                        if (k < e) {
+                            o = __float_as_int(sp[u].w);
+                            d = dist2(qx, qy, qz, sp[u].x, sp[u].y, sp[u].z);
+                            ok = (loop || (int64_t)o != q) && d < r_sq;
                         }
-                    }
-                    const unsigned have = __ballot_sync(0xffffffffu, found < kHistBins);
-                    const int srcl = __ffs(have) - 1;  // lowest lane: the first bin reaching cap + 1
-                    const int cut_bin = __shfl_sync(0xffffffffu, found, srcl);
-                    const int nbuf = __shfl_sync(0xffffffffu, upto, srcl);
-                    __syncwarp();
-                    replay = nbuf > kOvfCap;
-                    if (!replay) {
-                        m = 0;
-                        scan([&](bool ok, float d, int o) {
-                            ok = ok && min((int)(d * scale), kHistBins - 1) <= cut_bin;
-                            const unsigned hits = __ballot_sync(0xffffffffu, ok);
-                            const int pos = m + __popc(hits & lt_mask);
-                            if (ok && pos < kOvfCap) W.buf[pos] = make_float2(d, __int_as_float(o));
-                            m += __popc(hits);
-                        });
-                        if (m > kOvfCap) m = kOvfCap;  // cannot happen: the histogram counted these
+                        const unsigned hits = __ballot_sync(0xffffffffu, ok);
+                        const int pos = kept + __popc(hits & lt_mask);
+                        if (ok && pos < cap) row[pos] = o;  // the row while at most cap are in range
+                        kept += __popc(hits);
+                        const bool put = ok && d <= bound;
+                        const unsigned ph = bounded ? __ballot_sync(0xffffffffu, put) : hits;
+                        if (put) W.buf[m + __popc(ph & lt_mask)] = make_float2(d, __int_as_float(o));
+                        m += __popc(ph);
                     }
                 }
+            }
+            if (kept > cap) {
                 __syncwarp();
                 if (!replay) {
-                    // radix select of the cap-th smallest distance (rank cap, 1-based), 8 bits a pass
+                    // radix select of the cap-th smallest distance (rank cap, 1-based), 8 bits a
+                    // pass, over the buffer: every pair in range at or below the bound, m >= cap
                     uint32_t prefix = 0, pmask = 0;
                     int rank = cap;  // rank within the candidates matching the prefix
                     for (int shift = 24; shift >= 0; shift -= 8) {
@@ -811,30 +865,9 @@ __global__ void __launch_bounds__(kQueryWarps * 32) rg_query_warp_kernel(
                             if ((u & pmask) == prefix) atomicAdd(&W.hist[(u >> shift) & 255u], 1);
                         }
                         __syncwarp();
-                        int v[kHistBins / 32], sum = 0;
-#pragma unroll
-                        for (int i = 0; i < kHistBins / 32; ++i) {
-                            v[i] = W.hist[lane * (kHistBins / 32) + i];
-                            sum += v[i];
-                        }
-                        int pre = sum;
-                        for (int o = 1; o < 32; o <<= 1) {
-                            const int y = __shfl_up_sync(0xffffffffu, pre, o);
-                            if (lane >= o) pre += y;
-                        }
-                        int run = pre - sum, found = -1, before = 0;
-#pragma unroll
-                        for (int i = 0; i < kHistBins / 32; ++i) {
-                            if (found < 0 && run + v[i] >= rank) {
-                                found = lane * (kHistBins / 32) + i;
-                                before = run;
-                            }
-                            run += v[i];
-                        }
-                        const unsigned have = __ballot_sync(0xffffffffu, found >= 0);
-                        const int srcl = __ffs(have) - 1;
-                        const int digit = __shfl_sync(0xffffffffu, found, srcl);
-                        rank -= __shfl_sync(0xffffffffu, before, srcl);
+                        int before;
+                        const int digit = hist_rank_bin(W.hist, rank, lane, before);
+                        rank -= before;
                         prefix |= (uint32_t)digit << shift;
                         pmask |= 255u << shift;
                         __syncwarp();
@@ -858,7 +891,13 @@ __global__ void __launch_bounds__(kQueryWarps * 32) rg_query_warp_kernel(
                     }
                     __syncwarp();
                 }
-                if (replay) {  // the reference heap, fed in scan order, on lane 0
+                if (replay) {  // the reference heap, fed in its scan order, on lane 0
+                    int clen[9], cbeg[9];
+#pragma unroll
+                    for (int c = 0; c < 9; ++c) {
+                        clen[c] = __shfl_sync(0xffffffffu, len, c);
+                        cbeg[c] = __shfl_sync(0xffffffffu, j0, c);
+                    }
                     if (lane == 0) {
                         float hd[64];
                         int hid[64];

@@ -146,6 +146,33 @@ def test_radius_matches_oracle(oracle, max_nn, loop, kind, path):
             assert np.array_equal(dst.cpu().numpy()[:E], np.repeat(np.arange(x.shape[0]), np.diff(wrp)))
 
 
+@pytest.mark.parametrize("max_nn", [16, 64])
+@pytest.mark.parametrize("loop", [False, True])
+def test_radius_dense_rows_match_oracle(oracle, max_nn, loop):
+    """Rows with far more than 1024 sources in range on the general path (clouds over 4096
+    points): a tight ball, stacks of duplicated points and a fine lattice among spread points, so
+    that a query warp bounds its selection many times over, skips the cells beyond the bound and
+    meets ties at the cut (the heap replay), with and without a mask."""
+    rng = np.random.default_rng(7)
+    ball = rng.normal(0.0, 0.06, (3000, 3))
+    dup = np.repeat(rng.random((3, 3)) * 0.4, 500, axis=0)
+    lat = rng.integers(0, 8, (2500, 3)) * 0.05
+    spread = rng.random((3000, 3)) * 2 - 1
+    x = np.concatenate([ball, dup, lat, spread]).astype(np.float32)
+    x = np.ascontiguousarray(x[rng.permutation(len(x))])
+    ptr = synthetic.ptr_of([len(x) - 4500, 4500])
+    mask = rng.random(len(x)) > 0.05
+    for r in (0.1, 0.3):
+        for m in (None, mask):
+            wrp, wsrc = oracle.radius_graph(x, ptr, r, max_nn, loop, m, dist=oracle.DIST_CUDA)
+            rp, src, _ = csrc.radius_graph_csr(torch.from_numpy(x).to(DEV), r, torch.from_numpy(ptr).to(DEV),
+                                               max_num_neighbors=max_nn, loop=loop,
+                                               mask=None if m is None else torch.from_numpy(m).to(DEV))
+            rp = rp.cpu().numpy()
+            assert np.array_equal(rp, wrp), (r, m is not None)
+            assert np.array_equal(src.cpu().numpy()[:rp[-1]], wsrc), (r, m is not None)
+
+
 def test_radius_golden_and_kat(golden):
     x = torch.from_numpy(golden["rad_x"]).to(DEV)
     B, n, K = (int(v) for v in golden["rad_meta"])
