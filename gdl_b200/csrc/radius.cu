@@ -648,6 +648,7 @@ constexpr int kQueryWarps = 8;
 constexpr int kScanDepth = 4;  // candidate batches of 32 in flight per warp
 constexpr int kOvfCap = 1024;  // candidates a warp can hold for the selection
 constexpr int kHistBins = 256;
+constexpr int kFlatMax = 256;  // queries with at most this many candidates load them as one list
 
 struct QueryWarpSmem {
     float2 buf[kOvfCap];  // (distance, global index bits)
@@ -800,53 +801,91 @@ __global__ void __launch_bounds__(kQueryWarps * 32, 3) rg_query_warp_kernel(
                 bounded = true;
                 next_tighten = 2 * (m > cap ? m : cap);
             };
-            // columns: the query's own first, then the rest; once the heap replay is decided the
-            // scan stops (the replay rescans every column)
-            for (int ci = 0; ci < 9 && !replay; ++ci) {
-                if (m >= next_tighten) tighten();  // m >= 2 cap: the row is over the cap
-                const int c = ci == 0 ? 4 : (ci <= 4 ? ci - 1 : ci);
-                const int cb = __shfl_sync(0xffffffffu, j0, c);
-                const int cl = __shfl_sync(0xffffffffu, len, c);
-                const int z0 = __shfl_sync(0xffffffffu, zm0, c), z1 = __shfl_sync(0xffffffffu, zm1, c);
-                const int cxo = c / 3, cyo = c - 3 * cxo;
-                const float gx = cxo == 0 ? gxl : (cxo == 2 ? gxh : 0.0f);
-                const float gy = cyo == 0 ? gyl : (cyo == 2 ? gyh : 0.0f);
-                const float gxy = gx * gx + gy * gy;
-                if (replay || cl == 0 || gxy * shrink > bound) continue;  // uniform: nothing to keep
-                const int a = (gxy + gzl * gzl) * shrink > bound ? z0 : 0;   // the z-cell below
-                const int e = (gxy + gzh * gzh) * shrink > bound ? z1 : cl;  // the z-cell above
-                for (int k0 = a; k0 < e; k0 += 32 * kScanDepth) {
-                    if (m > kOvfCap - 32 * kScanDepth) {  // room for the batches below
-                        tighten();
-                        if (m > kOvfCap - 32 * kScanDepth) replay = true;  // ties fill the buffer
-                        if (replay) break;
-                    }
+            // one batch of candidates: test them, append the sources in range to the row while at
+            // most cap are, and the pairs at or below the bound to the buffer (room checked before)
+            auto consume = [&](const float4 &sp, bool have) {
+                bool ok = false;
+                float d = 0.0f;
+                int o = 0;
+                if (have) {
+                    o = __float_as_int(sp.w);
+                    d = dist2(qx, qy, qz, sp.x, sp.y, sp.z);
+                    ok = (loop || (int64_t)o != q) && d < r_sq;
+                }
+                const unsigned hits = __ballot_sync(0xffffffffu, ok);
+                const int pos = kept + __popc(hits & lt_mask);
+                if (ok && pos < cap) row[pos] = o;
+                kept += __popc(hits);
+                const bool put = ok && d <= bound;
+                const unsigned ph = bounded ? __ballot_sync(0xffffffffu, put) : hits;
+                if (put) W.buf[m + __popc(ph & lt_mask)] = make_float2(d, __int_as_float(o));
+                m += __popc(ph);
+            };
+            // candidates of all 9 columns as one list (inclusive prefix of the lengths on lanes 0-8)
+            int incl = len;
+#pragma unroll
+            for (int o = 1; o < 16; o <<= 1) {
+                const int y = __shfl_up_sync(0xffffffffu, incl, o);
+                if (lane >= o) incl += y;
+            }
+            const int total = __shfl_sync(0xffffffffu, incl, 8);
+            if (total <= kFlatMax) {
+                // few candidates: load them all at once instead of column after column (the buffer
+                // holds every pair in range, no bound needed)
+                const int lbase = j0 - (incl - len);  // sorted position of list entry t, column lane
+                int ends[9];
+#pragma unroll
+                for (int c = 0; c < 9; ++c) ends[c] = __shfl_sync(0xffffffffu, incl, c);
+                for (int t0 = 0; t0 < total; t0 += 32 * kScanDepth) {
                     float4 sp[kScanDepth];
 #pragma unroll
                     for (int u = 0; u < kScanDepth; ++u) {
-                        const int k = k0 + 32 * u + lane;
-                        if (k < e) sp[u] = sorted_pts[cb + k];
+                        const int t = t0 + 32 * u + lane;
+                        int col = 0;
+#pragma unroll
+                        for (int c = 0; c < 8; ++c) col += t >= ends[c];
+                        const int at = __shfl_sync(0xffffffffu, lbase, col) + t;
+                        if (t < total) sp[u] = sorted_pts[at];
                     }
 #pragma unroll
                     for (int u = 0; u < kScanDepth; ++u) {
-                        if (k0 + 32 * u >= e) break;  // uniform over the warp
-                        const int k = k0 + 32 * u + lane;
-                        bool ok = false;
-                        float d = 0.0f;
-                        int o = 0;
-                        if (k < e) {
-                            o = __float_as_int(sp[u].w);
-                            d = dist2(qx, qy, qz, sp[u].x, sp[u].y, sp[u].z);
-                            ok = (loop || (int64_t)o != q) && d < r_sq;
+                        if (t0 + 32 * u >= total) break;  // uniform over the warp
+                        consume(sp[u], t0 + 32 * u + lane < total);
+                    }
+                }
+            } else {
+                // columns: the query's own first, then the rest; once the heap replay is decided
+                // the scan stops (the replay rescans every column)
+                for (int ci = 0; ci < 9 && !replay; ++ci) {
+                    if (m >= next_tighten) tighten();  // m >= 2 cap: the row is over the cap
+                    const int c = ci == 0 ? 4 : (ci <= 4 ? ci - 1 : ci);
+                    const int cb = __shfl_sync(0xffffffffu, j0, c);
+                    const int cl = __shfl_sync(0xffffffffu, len, c);
+                    const int z0 = __shfl_sync(0xffffffffu, zm0, c), z1 = __shfl_sync(0xffffffffu, zm1, c);
+                    const int cxo = c / 3, cyo = c - 3 * cxo;
+                    const float gx = cxo == 0 ? gxl : (cxo == 2 ? gxh : 0.0f);
+                    const float gy = cyo == 0 ? gyl : (cyo == 2 ? gyh : 0.0f);
+                    const float gxy = gx * gx + gy * gy;
+                    if (replay || cl == 0 || gxy * shrink > bound) continue;  // uniform: nothing to keep
+                    const int a = (gxy + gzl * gzl) * shrink > bound ? z0 : 0;   // the z-cell below
+                    const int e = (gxy + gzh * gzh) * shrink > bound ? z1 : cl;  // the z-cell above
+                    for (int k0 = a; k0 < e; k0 += 32 * kScanDepth) {
+                        if (m > kOvfCap - 32 * kScanDepth) {  // room for the batches below
+                            tighten();
+                            if (m > kOvfCap - 32 * kScanDepth) replay = true;  // ties fill the buffer
+                            if (replay) break;
                         }
-                        const unsigned hits = __ballot_sync(0xffffffffu, ok);
-                        const int pos = kept + __popc(hits & lt_mask);
-                        if (ok && pos < cap) row[pos] = o;  // the row while at most cap are in range
-                        kept += __popc(hits);
-                        const bool put = ok && d <= bound;
-                        const unsigned ph = bounded ? __ballot_sync(0xffffffffu, put) : hits;
-                        if (put) W.buf[m + __popc(ph & lt_mask)] = make_float2(d, __int_as_float(o));
-                        m += __popc(ph);
+                        float4 sp[kScanDepth];
+#pragma unroll
+                        for (int u = 0; u < kScanDepth; ++u) {
+                            const int k = k0 + 32 * u + lane;
+                            if (k < e) sp[u] = sorted_pts[cb + k];
+                        }
+#pragma unroll
+                        for (int u = 0; u < kScanDepth; ++u) {
+                            if (k0 + 32 * u >= e) break;  // uniform over the warp
+                            consume(sp[u], k0 + 32 * u + lane < e);
+                        }
                     }
                 }
             }
