@@ -601,14 +601,22 @@ __global__ void __launch_bounds__(kSmallThreads) rg_small_compact_kernel(
 
 
 // ------------------------------------------------------------------ any cloud size
-// Dense cell table: cell_start[kCellBudget * ptr[b] + c] = first sorted position of cloud b with
-// key >= c (c = 0..ncells), built when the grid has at most kCellBudget * n_b - 1 cells; a
-// (dx, dy) column's z-cells zlo..zhi are then [cell_start[col + zlo], cell_start[col + zhi + 1]).
-// Clouds with larger grids binary-search the sorted keys instead.
+// Cell table of cloud b, kCellBudget * n_b entries from cell_start[kCellBudget * ptr[b]]:
+//   * dense: the grid has at most kCellBudget * n_b - 1 cells; entry c (c = 0..ncells) is the
+//     first sorted position with key >= c, so a (dx, dy) column's z-cells zlo..zhi are
+//     [entry col + zlo, entry col + zhi + 1);
+//   * columns: a larger grid whose res_x * res_y (x, y) columns fit; entry k (k = 0..res_x res_y)
+//     is the first sorted position with key >= k * res_z, so a query binary-searches only the
+//     few points of each column for its z-range;
+//   * neither: the query binary-searches the cloud's sorted keys.
 constexpr int kCellBudget = 16;
 
 __device__ __forceinline__ bool dense_cells(const GridParams &g, int64_t n_b) {
     return (int64_t)g.ncells + 1 <= kCellBudget * n_b;
+}
+
+__device__ __forceinline__ bool column_cells(const GridParams &g, int64_t n_b) {
+    return (int64_t)g.res[0] * g.res[1] + 1 <= kCellBudget * n_b;
 }
 
 __global__ void rg_cells_kernel(const int64_t *__restrict__ ptr, int32_t B, const GridParams *__restrict__ gp,
@@ -625,8 +633,12 @@ __global__ void rg_cells_kernel(const int64_t *__restrict__ ptr, int32_t B, cons
     const GridParams g = gp[b];
     const int64_t s0 = ptr[b], s1 = ptr[b + 1];
     const int64_t c = t - kCellBudget * s0;
-    if (!dense_cells(g, s1 - s0) || c > g.ncells) return;
-    cell_start[t] = (int32_t)lower_bound_u32(sorted_keys, s0, s1, (uint32_t)c);
+    if (dense_cells(g, s1 - s0)) {
+        if (c <= g.ncells) cell_start[t] = (int32_t)lower_bound_u32(sorted_keys, s0, s1, (uint32_t)c);
+    } else if (column_cells(g, s1 - s0)) {
+        if (c <= (int64_t)g.res[0] * g.res[1])
+            cell_start[t] = (int32_t)lower_bound_u32(sorted_keys, s0, s1, (uint32_t)(c * g.res[2]));
+    }
 }
 
 // One warp per query. Lanes 0-8 find the sorted ranges of the 9 z-columns of the 27-cell
@@ -749,8 +761,16 @@ __global__ void __launch_bounds__(kQueryWarps * 32, 3) rg_query_warp_kernel(
                             zm1 = e - j0;
                         }
                     } else {
-                        j0 = (int)lower_bound_u32(sorted_keys, s0, s1, (uint32_t)(colc + zlo));
-                        e = (int)lower_bound_u32(sorted_keys, j0, s1, (uint32_t)(colc + zhi) + 1u);
+                        // the column's points (or the cloud's), then two independent searches
+                        int64_t lo = s0, hi = s1;
+                        if (column_cells(g, s1 - s0)) {
+                            const int32_t *cs = cell_start + kCellBudget * s0;
+                            const int col = cx * g.res[1] + cy;
+                            lo = cs[col];
+                            hi = cs[col + 1];
+                        }
+                        j0 = (int)lower_bound_u32(sorted_keys, lo, hi, (uint32_t)(colc + zlo));
+                        e = (int)lower_bound_u32(sorted_keys, lo, hi, (uint32_t)(colc + zhi) + 1u);
                         zm1 = e - j0;
                     }
                     len = e - j0;

@@ -173,6 +173,25 @@ def test_radius_dense_rows_match_oracle(oracle, max_nn, loop):
             assert np.array_equal(src.cpu().numpy()[:rp[-1]], wsrc), (r, m is not None)
 
 
+@pytest.mark.parametrize("extent", [40.0, 400.0])
+def test_radius_sparse_grids_match_oracle(oracle, extent):
+    """Clouds whose grids have many more cells than points (clusters spread over a wide box):
+    a 40 m box keeps a table of the grid's (x, y) columns, a 400 m box has none and searches the
+    sorted cell keys directly."""
+    rng = np.random.default_rng(int(extent))
+    centres = rng.random((600, 3)) * np.array([extent, extent, 10.0])
+    x = (np.repeat(centres, 10, axis=0) + rng.normal(0.0, 0.3, (6000, 3))).astype(np.float32)
+    ptr = synthetic.ptr_of([6000])
+    for max_nn in (16, 64):
+        wrp, wsrc = oracle.radius_graph(x, ptr, 0.5, max_nn, False, None, dist=oracle.DIST_CUDA)
+        rp, src, _ = csrc.radius_graph_csr(torch.from_numpy(x).to(DEV), 0.5, torch.from_numpy(ptr).to(DEV),
+                                           max_num_neighbors=max_nn)
+        rp = rp.cpu().numpy()
+        assert rp[-1] > 10000
+        assert np.array_equal(rp, wrp)
+        assert np.array_equal(src.cpu().numpy()[:rp[-1]], wsrc)
+
+
 def test_radius_golden_and_kat(golden):
     x = torch.from_numpy(golden["rad_x"]).to(DEV)
     B, n, K = (int(v) for v in golden["rad_meta"])
