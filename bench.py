@@ -1022,11 +1022,20 @@ class C5:
                 "segment_sum": 4 * min(E, nc) * C + 4 * nc * C + 4 * (E + 2 * nc)}
 
     def e2e_step(self):
+        # the features are needed only by the last stage: their copy runs on a side stream while
+        # FPS runs (copy engine and SMs in parallel); the segment sum waits for it
+        main = torch.cuda.current_stream(self.dev)
+        if getattr(self, "_copy_stream", None) is None:
+            self._copy_stream = torch.cuda.Stream(self.dev)
         pos = self.pos_h.to(self.dev, non_blocking=True)
-        feat = self.feat_h.to(self.dev, non_blocking=True)
+        self._copy_stream.wait_stream(main)  # after the positions: FPS needs them first
+        with torch.cuda.stream(self._copy_stream):
+            feat = self.feat_h.to(self.dev, non_blocking=True)
         idx, cent = csrc.fps_cuda(pos, self.ptr_h, self.k_h, return_pos=True)
         row_ptr, src, _, rp32, src32 = csrc.radius_graph_csr(cent, self.R, self.cptr_h, max_num_neighbors=self.NN,
                                                              int32_csr=True)
+        main.wait_stream(self._copy_stream)
+        feat.record_stream(main)
         out = csrc.segment_reduce_cuda(feat, src32, rp32[:-1], rp32[1:], self.nc, "sum")
         host = out.to("cpu", non_blocking=True)
         torch.cuda.current_stream(self.dev).synchronize()
