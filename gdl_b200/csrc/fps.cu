@@ -338,6 +338,10 @@ __global__ void __launch_bounds__(T, 1) fps_bucket_kernel(const float *__restric
     __shared__ uint2 slotB[NW];  // z, bound
     __shared__ float4 s_pick[M];  // the round's picks
     __shared__ int s_count;       // how many (-1: a wait gave up)
+    // small buckets (P <= 8) test the round's picks against their warp's box first: there a
+    // lane's own tests cost about as much as its update (larger buckets measured slower with it)
+    constexpr bool kWarpBox = P <= 8;
+    __shared__ float s_wbox[kWarpBox ? NW : 1][6];  // each warp's box: the union of its lanes' boxes
     float2 *sx2 = reinterpret_cast<float2 *>(smem);  // pair h of thread t at h * T + t
     float2 *sy2 = sx2 + PH * T;
     float2 *sz2 = sy2 + PH * T;
@@ -452,6 +456,17 @@ __global__ void __launch_bounds__(T, 1) fps_bucket_kernel(const float *__restric
         bz = (bj & 1) ? Z.y : Z.x;
     };
     rekey();
+    // the warp's box: redux.sync over an order-preserving integer image of each coordinate (the
+    // boxes are built from +-inf by fminf / fmaxf, never NaN)
+    if constexpr (kWarpBox) {
+#pragma unroll
+        for (int c = 0; c < 6; ++c) {
+            const int b = __float_as_int(box[c]);
+            const int key = b >= 0 ? b : (b ^ 0x7fffffff);
+            const int r = c < 3 ? __reduce_min_sync(0xffffffffu, key) : __reduce_max_sync(0xffffffffu, key);
+            if (lane == 0) s_wbox[warp][c] = __int_as_float(r >= 0 ? r : (r ^ 0x7fffffff));
+        }
+    }
 
     if (t == 0) {
         if (actual > 0) {  // the first pick: the cloud's first point
@@ -480,11 +495,37 @@ __global__ void __launch_bounds__(T, 1) fps_bucket_kernel(const float *__restric
         {
             const int npick = s_count;
             const float curmax = __uint_as_float((uint32_t)(lkey >> 32));
+            // (small buckets) first lanes 0..npick-1 test one pick each against the warp's box and
+            // its lanes' largest minimum (minima are >= 0, so their bits order as unsigned): the
+            // bound to a box can only grow for a box inside it, so a pick that fails there fails
+            // every lane's own test; the lanes then test only the picks that passed
             uint32_t need = 0u;
+            if constexpr (kWarpBox) {
+                const uint32_t wmax = __reduce_max_sync(0xffffffffu, (uint32_t)(lkey >> 32));
+                bool near = false;
+                if (lane < npick) {
+                    const float4 p = s_pick[lane];
+                    // read every round (volatile): held across the loop the box would cost registers
+                    const volatile float *wbp = s_wbox[warp];
+                    float wb[6];
+#pragma unroll
+                    for (int c = 0; c < 6; ++c) wb[c] = wbp[c];
+                    near = !(box_dist2_lb(p.x, p.y, p.z, wb) >= __uint_as_float(wmax));
+                }
+                uint32_t cand = __ballot_sync(0xffffffffu, near);
 #pragma unroll 1
-            for (int i = 0; i < npick; ++i) {
-                const float4 p = s_pick[i];
-                if (!(box_dist2_lb(p.x, p.y, p.z, box) >= curmax)) need |= 1u << i;
+                while (cand) {
+                    const int i = __ffs(cand) - 1;
+                    cand &= cand - 1u;
+                    const float4 p = s_pick[i];
+                    if (!(box_dist2_lb(p.x, p.y, p.z, box) >= curmax)) need |= 1u << i;
+                }
+            } else {
+#pragma unroll 1
+                for (int i = 0; i < npick; ++i) {
+                    const float4 p = s_pick[i];
+                    if (!(box_dist2_lb(p.x, p.y, p.z, box) >= curmax)) need |= 1u << i;
+                }
             }
             uint32_t wneed = __reduce_or_sync(0xffffffffu, need);
             if (wneed) {
