@@ -708,7 +708,7 @@ __device__ __forceinline__ void face_gaps(float u, int qc, int res, float &below
 }
 
 __global__ void __launch_bounds__(kQueryWarps * 32, 3) rg_query_warp_kernel(
-    const float *__restrict__ x, const int64_t *__restrict__ ptr, int32_t B, int64_t n, const uint8_t *__restrict__ mask,
+    const int64_t *__restrict__ ptr, int32_t B, int64_t n, const uint8_t *__restrict__ mask,
     float r_sq, float inv, int loop, int cap, const GridParams *__restrict__ gp,
     const uint32_t *__restrict__ sorted_keys, const int32_t *__restrict__ cell_start,
     const float4 *__restrict__ sorted_pts, int32_t *__restrict__ counts, int32_t *__restrict__ padded) {
@@ -1102,7 +1102,7 @@ extern "C" int gdl_radius_graph_geometry(const float *x, const int64_t *ptr, int
     const unsigned qgrid = (unsigned)(qblocks < 32 * kSmCount ? qblocks : 32 * kSmCount);
     const size_t qsmem = sizeof(QueryWarpSmem) * kQueryWarps;
     GDL_CUDA_TRY(cudaFuncSetAttribute(rg_query_warp_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)qsmem));
-    rg_query_warp_kernel<<<qgrid, kQueryWarps * 32, qsmem, st>>>(x, ptr, num_clouds, n_points, mask, r_sq, inv, loop, cap,
+    rg_query_warp_kernel<<<qgrid, kQueryWarps * 32, qsmem, st>>>(ptr, num_clouds, n_points, mask, r_sq, inv, loop, cap,
                                                              w.gp, w.sorted_keys, w.cell_start, w.sorted_pts,
                                                              w.counts, w.padded);
     GDL_CUDA_TRY((exclusive_scan<int32_t, int64_t>(w.counts, out_row_ptr, n_points, w.scan_scratch,
